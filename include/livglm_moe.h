@@ -1,0 +1,181 @@
+/*
+ * livglm_moe.h -- C ABI of the B200-native GLM MoE block.
+ *
+ * One MoE block of GLM-5.3-Flash as in kg36/livglm: sigmoid router with
+ * e_score_correction_bias and group-limited top-k, token-to-expert dispatch,
+ * routed limited-SwiGLU experts read straight from the checkpoint's group-32
+ * MXFP4 records, and the weighted combine with the shared expert added.
+ *
+ * Conventions
+ *  - Every pointer argument is a DEVICE pointer unless its comment says
+ *    "host".  bf16 tensors are passed as uint16_t bit patterns.
+ *  - Every call is stream-ordered on `stream` (a cudaStream_t passed as
+ *    void*; NULL is the legacy default stream), performs no host
+ *    synchronisation and allocates no device memory: scratch comes from the
+ *    caller's `workspace` (size from lg_moe_workspace_size), which must be
+ *    256-byte aligned and must not be shared by calls that overlap on the GPU.
+ *  - Return value: LG_OK (0) or an LG_ERR_* code; lg_moe_last_error() gives
+ *    a message for the calling thread.  Argument errors are detected on the
+ *    host before any launch and leave the stream untouched.
+ *  - Routed expert tensors are banks: expert e's tensor starts at
+ *    base + e * stride (bytes) and is byte-identical to the checkpoint's
+ *      model.language_model.layers.{L}.mlp.experts.{e}.{gate,up}_proj.weight_packed  U8 [F, d/2]
+ *      ...{gate,up}_proj.weight_scale   U8 [F, d/32]
+ *      ...down_proj.weight_packed       U8 [d, F/2]
+ *      ...down_proj.weight_scale        U8 [d, F/32]
+ *    (kg36/livglm src/glm53flash/expert_source.py:189-229, contract.py:47-50).
+ *    E2M1 nibbles: the low nibble of byte i is column 2i.  E8M0 scale s means
+ *    2^(s-127); 255 is NaN.
+ */
+#ifndef LIVGLM_MOE_H
+#define LIVGLM_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LG_MOE_ABI_VERSION 1
+
+enum {
+  LG_OK = 0,
+  LG_ERR_INVALID_ARG = 1, /* bad shape, null pointer, misalignment */
+  LG_ERR_UNSUPPORTED = 2, /* geometry outside what the kernels handle */
+  LG_ERR_WORKSPACE = 3,   /* workspace missing or too small */
+  LG_ERR_CUDA = 4,        /* a CUDA launch or runtime call failed */
+  LG_ERR_NCCL = 5,        /* a collective failed */
+  LG_ERR_TIMEOUT = 6      /* a bounded device wait gave up */
+};
+
+/* MoE geometry; field names follow GLMTextConfig
+ * (kg36/livglm src/glm53flash/model_config.py:11-54). */
+typedef struct lg_moe_config {
+  int32_t hidden_size;           /* d */
+  int32_t moe_intermediate_size; /* F, width of one routed expert */
+  int32_t n_routed_experts;      /* E */
+  int32_t num_experts_per_tok;   /* k */
+  int32_t n_shared_experts;      /* shared width Fs = F * n_shared_experts */
+  int32_t n_group;               /* G */
+  int32_t topk_group;            /* g */
+  int32_t norm_topk_prob;        /* 0 or 1 */
+  float routed_scaling_factor;
+  float swiglu_limit; /* <= 0 disables the clamp (expert_ssd.py:103-107) */
+} lg_moe_config;
+
+/* Resident weights of one MoE layer (all device pointers). */
+typedef struct lg_moe_weights {
+  const float *router_weight; /* mlp.gate.weight                 f32 [E, d] */
+  const float *router_bias;   /* mlp.gate.e_score_correction_bias f32 [E] */
+  const uint8_t *gate_packed, *gate_scale;
+  const uint8_t *up_packed, *up_scale;
+  const uint8_t *down_packed, *down_scale;
+  int64_t gate_packed_stride, gate_scale_stride; /* bytes between experts */
+  int64_t up_packed_stride, up_scale_stride;
+  int64_t down_packed_stride, down_scale_stride;
+  const uint16_t *shared_gate; /* mlp.shared_experts.gate_proj.weight bf16 [Fs, d] */
+  const uint16_t *shared_up;   /* mlp.shared_experts.up_proj.weight   bf16 [Fs, d] */
+  const uint16_t *shared_down; /* mlp.shared_experts.down_proj.weight bf16 [d, Fs] */
+} lg_moe_weights;
+
+int lg_moe_abi_version(void);
+
+/* Message for the last failed call on this thread ("" if none). */
+const char *lg_moe_last_error(void);
+
+/* Bytes of scratch one call needs for up to `max_tokens` tokens
+ * (router, dispatch, experts, forward all fit in this size). 0 on error. */
+size_t lg_moe_workspace_size(const lg_moe_config *cfg /* host */, int64_t max_tokens);
+
+/*
+ * Router.  Replaces TopKRouter.__call__ (kg36/livglm src/glm53flash/moe.py:36-63).
+ *   x       bf16 [M, d]
+ *   logits  f32  [M, E]   (may be NULL)
+ *   weights f32  [M, k]   normalised, scaled route weights
+ *   indices u32  [M, k]   ascending choice order, best expert last (moe.py:58)
+ */
+int lg_moe_router(const lg_moe_config *cfg, const uint16_t *x, int64_t M,
+                  const float *router_weight, const float *router_bias,
+                  float *logits, float *weights, uint32_t *indices,
+                  void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Dispatch.  Replaces the first-occurrence compaction of routed ids
+ * (expert_ssd.py:162-170) and the native route plan's unique/compact mapping
+ * (native_expert_ssd.py:475-525) with a stable counting sort of the route
+ * slots s = t*k + j by expert id:
+ *   counts  i32 [E]      routes per expert
+ *   offsets i32 [E + 1]  exclusive prefix sum, offsets[E] = M*k
+ *   perm    i32 [M*k]    perm[offsets[e] + r] = r-th slot (increasing) routed to e
+ * Route slots whose index is >= E are skipped: they are not counted, do not
+ * appear in perm, and (in lg_moe_experts) their output rows stay unwritten.
+ */
+int lg_moe_dispatch(const lg_moe_config *cfg, const uint32_t *indices, int64_t M,
+                    int32_t *counts, int32_t *offsets, int32_t *perm,
+                    void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Routed experts.  Replaces the expert backend call
+ * ExpertSSD.__call__(x, indices) -> [M, k, d] (expert_ssd.py:159-188) and the
+ * native pair QMV + masked QMV (native_expert_ssd.py:698-712):
+ *   y[t, j] = down_e( limited_swiglu( gate_e(x_t), up_e(x_t) ) ), e = indices[t, j]
+ * with bf16 results for gate, up, every SwiGLU op and down.
+ *   x bf16 [M, d]; indices u32 [M, k]; y bf16 [M, k, d]
+ */
+int lg_moe_experts(const lg_moe_config *cfg, const lg_moe_weights *w,
+                   const uint16_t *x, const uint32_t *indices, int64_t M,
+                   uint16_t *y, void *workspace, size_t workspace_bytes,
+                   void *stream);
+
+/*
+ * Shared expert.  Replaces DenseMLP.__call__ with bf16 weights
+ * (layers.py:66-67, 160-171): out = down(limited_swiglu(gate(x), up(x))), bf16.
+ *   x bf16 [M, d]; out bf16 [M, d]
+ */
+int lg_moe_shared(const lg_moe_config *cfg, const lg_moe_weights *w,
+                  const uint16_t *x, int64_t M, uint16_t *out,
+                  void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Combine.  Replaces the merge of ExpertSSDMoE._call_impl (moe.py:199-201):
+ *   out[t] = sum_j f32(y[t, j]) * weights[t, j]  (+ f32(shared[t]))
+ * summed in j order; shared may be NULL.  out f32 [M, d].
+ */
+int lg_moe_combine(const lg_moe_config *cfg, const uint16_t *y,
+                   const float *weights, const uint16_t *shared, int64_t M,
+                   float *out, void *stream);
+
+/*
+ * Whole block.  Replaces ExpertSSDMoE.__call__ (moe.py:96-201) for bf16
+ * hidden states: returns the f32 merge the MLX graph produces.
+ *   x bf16 [M, d]; out f32 [M, d]
+ *   weights_out f32 [M, k] and indices_out u32 [M, k] may be NULL; when given
+ *   they receive the router's outputs (the reference's last_route record).
+ */
+int lg_moe_forward(const lg_moe_config *cfg, const lg_moe_weights *w,
+                   const uint16_t *x, int64_t M, float *out,
+                   float *weights_out, uint32_t *indices_out,
+                   void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Stage tracing.  Counterpart of the reference's per-layer trace spans
+ * (DecodeTrace spans "router_graph_construct", "moe_merge_graph_construct",
+ * moe.py:97-197; trace.py:43-310), measured on the device: while enabled,
+ * every lg_moe_forward records CUDA events around its five stages (router,
+ * dispatch, gate/up, down, combine) into a ring of `capacity_calls` slots
+ * (works inside CUDA graph capture; a replay re-records the captured slot).
+ * capacity_calls <= 0 disables tracing.  Process-wide, not thread-safe.
+ */
+int lg_moe_trace_enable(int capacity_calls);
+
+/* Copies up to max_calls recorded calls, oldest first, as
+ * stage_ms[call * 5 + stage] (milliseconds).  Waits for the events.  Returns
+ * the number of calls copied, or a negative LG_ERR_* code. */
+int lg_moe_trace_read(float *stage_ms /* host */, int max_calls);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LIVGLM_MOE_H */

@@ -1,0 +1,495 @@
+// C ABI of the GLM MoE block (see include/livglm_moe.h).
+//
+// Host-side argument validation mirrors the reference's ContractError checks
+// (kg36/livglm src/glm53flash/model_config.py:142-176) plus the kernels' own
+// layout requirements; nothing is launched when validation fails.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "livglm_moe.h"
+#include "moe_kernels.cuh"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(LG_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return LG_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+constexpr size_t kAlign = 256;
+size_t up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+int validate_cfg(const lg_moe_config* c) {
+  if (!c) return fail(LG_ERR_INVALID_ARG, "config is NULL");
+  const int d = c->hidden_size, F = c->moe_intermediate_size, E = c->n_routed_experts;
+  const int k = c->num_experts_per_tok, G = c->n_group, g = c->topk_group;
+  if (d < 32 || d % 32) return fail(LG_ERR_INVALID_ARG, "hidden_size %d must be a positive multiple of 32", d);
+  if (F < 32 || F % 32) return fail(LG_ERR_INVALID_ARG, "moe_intermediate_size %d must be a positive multiple of 32", F);
+  if (E < 2 || E > 1024) return fail(LG_ERR_UNSUPPORTED, "n_routed_experts %d outside 2..1024", E);
+  if (k < 1 || k > E) return fail(LG_ERR_INVALID_ARG, "invalid routed top-k geometry: k=%d E=%d", k, E);
+  if (k > 32) return fail(LG_ERR_UNSUPPORTED, "num_experts_per_tok %d > 32", k);
+  if (G < 1 || E % G) return fail(LG_ERR_INVALID_ARG, "expert count must be divisible by n_group (%d %% %d)", E, G);
+  if (g < 1 || g > G) return fail(LG_ERR_INVALID_ARG, "invalid topk_group %d for n_group %d", g, G);
+  if (E / G < 2) return fail(LG_ERR_INVALID_ARG, "router groups must contain at least two experts");
+  if (c->n_shared_experts < 0) return fail(LG_ERR_INVALID_ARG, "n_shared_experts < 0");
+  if (static_cast<long long>(F) * c->n_shared_experts > (1 << 20))
+    return fail(LG_ERR_UNSUPPORTED, "shared expert width too large");
+  return LG_OK;
+}
+
+int validate_tokens(int64_t M, const lg_moe_config* c) {
+  if (M < 0) return fail(LG_ERR_INVALID_ARG, "token count %lld < 0", static_cast<long long>(M));
+  const long long big = static_cast<long long>(M) *
+                        (c->hidden_size > c->n_routed_experts ? c->hidden_size : c->n_routed_experts) *
+                        c->num_experts_per_tok;
+  if (big >= (1LL << 40)) return fail(LG_ERR_UNSUPPORTED, "token count %lld too large", static_cast<long long>(M));
+  if (static_cast<long long>(M) * c->num_experts_per_tok >= (1LL << 31))
+    return fail(LG_ERR_UNSUPPORTED, "route count overflows int32");
+  return LG_OK;
+}
+
+struct Layout {
+  size_t logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, total;
+};
+
+Layout layout(const lg_moe_config* c, int64_t M) {
+  const size_t E = c->n_routed_experts, k = c->num_experts_per_tok, d = c->hidden_size;
+  const size_t F = c->moe_intermediate_size, Fs = F * c->n_shared_experts;
+  const size_t m = static_cast<size_t>(M);
+  Layout L{};
+  size_t o = 0;
+  L.logits = o;  o += up(m * E * 4);
+  L.weights = o; o += up(m * k * 4);
+  L.indices = o; o += up(m * k * 4);
+  L.counts = o;  o += up(E * 4);
+  L.offsets = o; o += up((E + 1) * 4);
+  L.perm = o;    o += up(m * k * 4);
+  L.active = o;  o += up((E + 1) * 4);
+  L.act = o;     o += up(m * k * F * 2);
+  L.act_s = o;   o += up(m * Fs * 2);
+  L.y = o;       o += up(m * k * d * 2);
+  L.ys = o;      o += up(m * d * 2);
+  L.total = o;
+  return L;
+}
+
+template <typename T>
+T* at(void* ws, size_t off) { return reinterpret_cast<T*>(static_cast<char*>(ws) + off); }
+
+int check_ws(const lg_moe_config* c, int64_t M, void* ws, size_t bytes) {
+  const size_t need = layout(c, M).total;
+  if (!ws) return fail(LG_ERR_WORKSPACE, "workspace is NULL (need %zu bytes)", need);
+  if (!aligned(ws, kAlign)) return fail(LG_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  if (bytes < need) return fail(LG_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", bytes, need);
+  return LG_OK;
+}
+
+int validate_weights(const lg_moe_config* c, const lg_moe_weights* w, bool routed, bool shared) {
+  if (!w) return fail(LG_ERR_INVALID_ARG, "weights is NULL");
+  if (routed) {
+    const void* ps[6] = {w->gate_packed, w->gate_scale, w->up_packed, w->up_scale, w->down_packed, w->down_scale};
+    for (const void* p : ps)
+      if (!p) return fail(LG_ERR_INVALID_ARG, "routed expert tensor pointer is NULL");
+    if (!aligned(w->gate_packed, 16) || !aligned(w->up_packed, 16) || !aligned(w->down_packed, 16))
+      return fail(LG_ERR_INVALID_ARG, "weight_packed banks must be 16-byte aligned");
+    const long long d = c->hidden_size, F = c->moe_intermediate_size;
+    const long long gp = F * d / 2, gs = F * d / 32, dp = d * F / 2, ds = d * F / 32;
+    if (w->gate_packed_stride % 16 || w->up_packed_stride % 16 || w->down_packed_stride % 16)
+      return fail(LG_ERR_INVALID_ARG, "weight_packed expert strides must be multiples of 16 bytes");
+    if (w->gate_packed_stride < gp || w->up_packed_stride < gp || w->down_packed_stride < dp ||
+        w->gate_scale_stride < gs || w->up_scale_stride < gs || w->down_scale_stride < ds)
+      return fail(LG_ERR_INVALID_ARG, "expert strides smaller than one expert's tensor");
+  }
+  if (shared && c->n_shared_experts > 0) {
+    if (!w->shared_gate || !w->shared_up || !w->shared_down)
+      return fail(LG_ERR_INVALID_ARG, "shared expert weight pointer is NULL");
+    if (!aligned(w->shared_gate, 16) || !aligned(w->shared_up, 16) || !aligned(w->shared_down, 16))
+      return fail(LG_ERR_INVALID_ARG, "shared expert weights must be 16-byte aligned");
+  }
+  return LG_OK;
+}
+
+int num_sms() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+// ---- launches --------------------------------------------------------------
+
+int launch_router(const lg_moe_config* c, const uint16_t* x, int M, const float* Wr,
+                  const float* bias, float* logits, float* weights, uint32_t* indices,
+                  int* counts, cudaStream_t s) {
+  using namespace lg;
+  const int d = c->hidden_size, E = c->n_routed_experts;
+  if (M <= 4) {
+    dim3 grid((M + 0) / 1, (E + 7) / 8);
+    router_logits_kernel<1, 1><<<grid, 256, 0, s>>>(x, Wr, M, d, E, logits);
+  } else {
+    dim3 grid((M + 3) / 4, (E + 31) / 32);
+    router_logits_kernel<4, 4><<<grid, 256, 0, s>>>(x, Wr, M, d, E, logits);
+  }
+  const size_t smem = static_cast<size_t>(kSelectWarps) * (2 * E + c->n_group) * sizeof(float);
+  router_select_kernel<<<(M + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, smem, s>>>(
+      logits, bias, M, E, c->n_group, c->topk_group, c->num_experts_per_tok, c->norm_topk_prob,
+      c->routed_scaling_factor, weights, indices, counts);
+  return cuda_check(cudaGetLastError(), "router launch");
+}
+
+// Routes whose expert id is >= E are skipped (never counted, never placed in
+// perm); their slots' outputs are left unwritten.
+__global__ void histogram_kernel(const uint32_t* __restrict__ idx, int S, int E, int* __restrict__ counts) {
+  for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < S; s += gridDim.x * blockDim.x) {
+    const uint32_t e = idx[s];
+    if (e < static_cast<uint32_t>(E)) atomicAdd(counts + e, 1);
+  }
+}
+
+int launch_dispatch(const lg_moe_config* c, const uint32_t* idx, int M, int* counts,
+                    int* offsets, int* perm, int* active, bool need_hist, cudaStream_t s) {
+  const int E = c->n_routed_experts, S = M * c->num_experts_per_tok;
+  if (need_hist) {
+    cudaMemsetAsync(counts, 0, E * sizeof(int), s);
+    histogram_kernel<<<(S + 255) / 256 < 1024 ? (S + 255) / 256 : 1024, 256, 0, s>>>(idx, S, E, counts);
+  }
+  lg::dispatch_kernel<<<E, 256, 0, s>>>(idx, S, E, counts, offsets, perm, active);
+  return cuda_check(cudaGetLastError(), "dispatch launch");
+}
+
+template <int LPR, int TT>
+int launch_gemv_t(const lg::GemvArgs& a, int max_items, cudaStream_t s) {
+  const int G = (a.K > a.Ks ? a.K : a.Ks) / 32;
+  const int KI = (G + LPR - 1) / LPR;
+  const size_t smem = static_cast<size_t>(TT) * KI * 8 * LPR * sizeof(float4);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(lg::grouped_gemv_kernel<LPR, TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr = true;
+  }
+  int occ = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, lg::grouped_gemv_kernel<LPR, TT>, 256, smem);
+  if (occ < 1) occ = 1;
+  int grid = num_sms() * occ;
+  if (max_items < grid) grid = max_items;
+  if (grid < 1) grid = 1;
+  lg::grouped_gemv_kernel<LPR, TT><<<grid, 256, smem, s>>>(a);
+  return cuda_check(cudaGetLastError(), "grouped gemv launch");
+}
+
+template <int LPR>
+int launch_gemv_tt(const lg::GemvArgs& a, int tt, int max_items, cudaStream_t s) {
+  switch (tt) {
+    case 1: return launch_gemv_t<LPR, 1>(a, max_items, s);
+    case 2: return launch_gemv_t<LPR, 2>(a, max_items, s);
+    default: return launch_gemv_t<LPR, 4>(a, max_items, s);
+  }
+}
+
+int pick_lpr(int K) {
+  const int G = K / 32;
+  for (int l = 32; l >= 4; l >>= 1)
+    if (G % l == 0) return l;
+  return 4;
+}
+
+int launch_gemv(const lg::GemvArgs& a, int M, int max_routes_per_expert, int E, cudaStream_t s) {
+  const int K = a.K > 0 ? a.K : a.Ks;
+  const int lpr = pick_lpr(K);
+  const int rows = 8 * (32 / lpr);
+  int tt = 4;
+  const int need = max_routes_per_expert > M ? max_routes_per_expert : M;
+  if (need <= 1) tt = 1;
+  else if (need <= 2) tt = 2;
+  const int G = (a.K > a.Ks ? a.K : a.Ks) / 32;
+  while (tt > 1 && static_cast<size_t>(tt) * ((G + lpr - 1) / lpr) * 8 * lpr * 16 > 200 * 1024) tt >>= 1;
+  if (static_cast<size_t>(tt) * ((G + lpr - 1) / lpr) * 8 * lpr * 16 > 200 * 1024)
+    return fail(LG_ERR_UNSUPPORTED, "reduction length %d too large for the staged GEMV", K);
+  const long long items = static_cast<long long>(E) * ((a.N + rows - 1) / rows) + (a.Ns + rows - 1) / rows;
+  const int max_items = items > (1 << 30) ? (1 << 30) : static_cast<int>(items);
+  switch (lpr) {
+    case 32: return launch_gemv_tt<32>(a, tt, max_items, s);
+    case 16: return launch_gemv_tt<16>(a, tt, max_items, s);
+    case 8: return launch_gemv_tt<8>(a, tt, max_items, s);
+    default: return launch_gemv_tt<4>(a, tt, max_items, s);
+  }
+}
+
+// Gate/up (+ SwiGLU) pass over routed experts and, when `with_shared`, the
+// shared expert.  Routing tables must be ready.
+int launch_gate_up(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M,
+                   const int* offsets, const int* perm, const int* active, uint16_t* act,
+                   uint16_t* act_s, bool with_routed, bool with_shared, cudaStream_t s) {
+  const int d = c->hidden_size, F = c->moe_intermediate_size, k = c->num_experts_per_tok;
+  const int Fs = F * c->n_shared_experts;
+  const bool sh = with_shared && Fs > 0;
+  lg::GemvArgs a{};
+  a.K = d; a.N = F; a.Ks = d; a.Ns = sh ? Fs : 0; a.k = k; a.M = M; a.pair = 1;
+  a.limit = c->swiglu_limit;
+  if (with_routed) {
+    a.a_packed = w->gate_packed; a.a_scale = w->gate_scale; a.b_packed = w->up_packed; a.b_scale = w->up_scale;
+    a.a_pstride = w->gate_packed_stride; a.a_sstride = w->gate_scale_stride;
+    a.b_pstride = w->up_packed_stride; a.b_sstride = w->up_scale_stride;
+  }
+  a.sa = sh ? w->shared_gate : nullptr; a.sb = sh ? w->shared_up : nullptr;
+  a.xin = x; a.xin_by_token = 1; a.xin_s = x;
+  a.offsets = offsets; a.perm = perm; a.active = active;
+  a.out = act; a.out_by_slot = 0; a.out_s = act_s;
+  return launch_gemv(a, M, M, with_routed ? c->n_routed_experts : 0, s);
+}
+
+// Down pass: routed outputs land in slot order (row t*k + j of y).
+int launch_down(const lg_moe_config* c, const lg_moe_weights* w, int M, const int* offsets,
+                const int* perm, const int* active, const uint16_t* act, const uint16_t* act_s,
+                uint16_t* y, uint16_t* ys, bool with_routed, bool with_shared, cudaStream_t s) {
+  const int d = c->hidden_size, F = c->moe_intermediate_size, k = c->num_experts_per_tok;
+  const int Fs = F * c->n_shared_experts;
+  const bool sh = with_shared && Fs > 0;
+  lg::GemvArgs b{};
+  b.K = F; b.N = d; b.Ks = sh ? Fs : F; b.Ns = sh ? d : 0; b.k = k; b.M = M; b.pair = 0;
+  b.limit = c->swiglu_limit;
+  if (with_routed) {
+    b.a_packed = w->down_packed; b.a_scale = w->down_scale;
+    b.a_pstride = w->down_packed_stride; b.a_sstride = w->down_scale_stride;
+  }
+  b.sa = sh ? w->shared_down : nullptr;
+  b.xin = act; b.xin_by_token = 0; b.xin_s = act_s;
+  b.offsets = offsets; b.perm = perm; b.active = active;
+  b.out = y; b.out_by_slot = 1; b.out_s = ys;
+  return launch_gemv(b, M, M, with_routed ? c->n_routed_experts : 0, s);
+}
+
+int launch_experts(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M,
+                   const int* offsets, const int* perm, const int* active, uint16_t* act,
+                   uint16_t* act_s, uint16_t* y, uint16_t* ys, bool with_routed, bool with_shared,
+                   cudaStream_t s) {
+  int rc = launch_gate_up(c, w, x, M, offsets, perm, active, act, act_s, with_routed, with_shared, s);
+  if (rc) return rc;
+  return launch_down(c, w, M, offsets, perm, active, act, act_s, y, ys, with_routed, with_shared, s);
+}
+
+// ---- stage tracing ------------------------------------------------------------
+// When enabled, lg_moe_forward records a CUDA event before its first stage and
+// after each stage (router, dispatch, gate/up, down, combine) into a ring of
+// per-call slots, the device-side counterpart of the reference's trace spans
+// (moe.py:97-197).  Not thread-safe; meant for measurement runs.
+constexpr int kStages = 5;
+struct Trace {
+  int cap = 0, next = 0, recorded = 0;
+  cudaEvent_t* ev = nullptr;  // cap * (kStages + 1)
+};
+Trace g_trace;
+
+int trace_slot() {
+  if (!g_trace.cap) return -1;
+  const int slot = g_trace.next;
+  g_trace.next = (g_trace.next + 1) % g_trace.cap;
+  if (g_trace.recorded < g_trace.cap) ++g_trace.recorded;
+  return slot;
+}
+void trace_mark(int slot, int i, cudaStream_t s) {
+  if (slot >= 0) cudaEventRecord(g_trace.ev[slot * (kStages + 1) + i], s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int lg_moe_trace_enable(int capacity_calls) {
+  if (g_trace.ev) {
+    for (int i = 0; i < g_trace.cap * (kStages + 1); ++i) cudaEventDestroy(g_trace.ev[i]);
+    delete[] g_trace.ev;
+    g_trace = Trace{};
+  }
+  if (capacity_calls <= 0) return LG_OK;
+  if (capacity_calls > (1 << 16)) return fail(LG_ERR_INVALID_ARG, "trace capacity too large");
+  g_trace.ev = new cudaEvent_t[capacity_calls * (kStages + 1)];
+  for (int i = 0; i < capacity_calls * (kStages + 1); ++i) {
+    const cudaError_t e = cudaEventCreate(&g_trace.ev[i]);
+    if (e != cudaSuccess) {
+      for (int j = 0; j < i; ++j) cudaEventDestroy(g_trace.ev[j]);
+      delete[] g_trace.ev;
+      g_trace = Trace{};
+      return cuda_check(e, "trace event create");
+    }
+  }
+  g_trace.cap = capacity_calls;
+  return LG_OK;
+}
+
+int lg_moe_trace_read(float* stage_ms, int max_calls) {
+  if (!stage_ms && max_calls > 0) return -fail(LG_ERR_INVALID_ARG, "trace: NULL output");
+  const int n = g_trace.recorded < max_calls ? g_trace.recorded : max_calls;
+  for (int c = 0; c < n; ++c) {
+    const int slot = (g_trace.next - g_trace.recorded + c + g_trace.cap) % g_trace.cap;
+    cudaEvent_t* e = g_trace.ev + slot * (kStages + 1);
+    if (cudaEventSynchronize(e[kStages]) != cudaSuccess) return -fail(LG_ERR_CUDA, "trace: event sync failed");
+    for (int i = 0; i < kStages; ++i) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, e[i], e[i + 1]) != cudaSuccess) ms = -1.f;
+      stage_ms[c * kStages + i] = ms;
+    }
+  }
+  return n;
+}
+
+
+int lg_moe_abi_version(void) { return LG_MOE_ABI_VERSION; }
+
+const char* lg_moe_last_error(void) { return g_err; }
+
+size_t lg_moe_workspace_size(const lg_moe_config* cfg, int64_t max_tokens) {
+  if (validate_cfg(cfg) || validate_tokens(max_tokens, cfg)) return 0;
+  return layout(cfg, max_tokens).total;
+}
+
+int lg_moe_router(const lg_moe_config* cfg, const uint16_t* x, int64_t M, const float* router_weight,
+                  const float* router_bias, float* logits, float* weights, uint32_t* indices,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = validate_cfg(cfg)) || (rc = validate_tokens(M, cfg))) return rc;
+  if (M == 0) return LG_OK;
+  if (!x || !router_weight || !router_bias || !weights || !indices)
+    return fail(LG_ERR_INVALID_ARG, "router: NULL tensor pointer");
+  if (!aligned(x, 16) || !aligned(router_weight, 16))
+    return fail(LG_ERR_INVALID_ARG, "router: x and router_weight must be 16-byte aligned");
+  if (!logits) {
+    if ((rc = check_ws(cfg, M, workspace, workspace_bytes))) return rc;
+    logits = at<float>(workspace, layout(cfg, M).logits);
+  }
+  return launch_router(cfg, x, static_cast<int>(M), router_weight, router_bias, logits, weights, indices,
+                       nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int lg_moe_dispatch(const lg_moe_config* cfg, const uint32_t* indices, int64_t M, int32_t* counts,
+                    int32_t* offsets, int32_t* perm, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = validate_cfg(cfg)) || (rc = validate_tokens(M, cfg))) return rc;
+  if (!indices || !counts || !offsets || !perm) return fail(LG_ERR_INVALID_ARG, "dispatch: NULL pointer");
+  if ((rc = check_ws(cfg, M, workspace, workspace_bytes))) return rc;
+  const Layout L = layout(cfg, M);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M == 0) {
+    cudaMemsetAsync(counts, 0, cfg->n_routed_experts * sizeof(int), s);
+    cudaMemsetAsync(offsets, 0, (cfg->n_routed_experts + 1) * sizeof(int), s);
+    return cuda_check(cudaGetLastError(), "dispatch memset");
+  }
+  return launch_dispatch(cfg, indices, static_cast<int>(M), counts, offsets, perm,
+                         at<int>(workspace, L.active), true, s);
+}
+
+int lg_moe_experts(const lg_moe_config* cfg, const lg_moe_weights* w, const uint16_t* x,
+                   const uint32_t* indices, int64_t M, uint16_t* y, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = validate_cfg(cfg)) || (rc = validate_tokens(M, cfg))) return rc;
+  if (M == 0) return LG_OK;
+  if ((rc = validate_weights(cfg, w, true, false))) return rc;
+  if (!x || !indices || !y) return fail(LG_ERR_INVALID_ARG, "experts: NULL tensor pointer");
+  if (!aligned(x, 16) || !aligned(y, 16)) return fail(LG_ERR_INVALID_ARG, "experts: x and y must be 16-byte aligned");
+  if ((rc = check_ws(cfg, M, workspace, workspace_bytes))) return rc;
+  const Layout L = layout(cfg, M);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* counts = at<int>(workspace, L.counts);
+  int* offsets = at<int>(workspace, L.offsets);
+  int* perm = at<int>(workspace, L.perm);
+  int* active = at<int>(workspace, L.active);
+  if ((rc = launch_dispatch(cfg, indices, static_cast<int>(M), counts, offsets, perm, active, true, s))) return rc;
+  return launch_experts(cfg, w, x, static_cast<int>(M), offsets, perm, active, at<uint16_t>(workspace, L.act),
+                        nullptr, y, nullptr, true, false, s);
+}
+
+int lg_moe_shared(const lg_moe_config* cfg, const lg_moe_weights* w, const uint16_t* x, int64_t M,
+                  uint16_t* out, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = validate_cfg(cfg)) || (rc = validate_tokens(M, cfg))) return rc;
+  if (cfg->n_shared_experts < 1) return fail(LG_ERR_INVALID_ARG, "shared: n_shared_experts is 0");
+  if (M == 0) return LG_OK;
+  if ((rc = validate_weights(cfg, w, false, true))) return rc;
+  if (!x || !out) return fail(LG_ERR_INVALID_ARG, "shared: NULL tensor pointer");
+  if (!aligned(x, 16)) return fail(LG_ERR_INVALID_ARG, "shared: x must be 16-byte aligned");
+  if ((rc = check_ws(cfg, M, workspace, workspace_bytes))) return rc;
+  const Layout L = layout(cfg, M);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* active = at<int>(workspace, L.active);
+  cudaMemsetAsync(active, 0, sizeof(int), s);
+  return launch_experts(cfg, w, x, static_cast<int>(M), at<int>(workspace, L.offsets), at<int>(workspace, L.perm),
+                        active, nullptr, at<uint16_t>(workspace, L.act_s), nullptr, out, false, true, s);
+}
+
+int lg_moe_combine(const lg_moe_config* cfg, const uint16_t* y, const float* weights, const uint16_t* shared,
+                   int64_t M, float* out, void* stream) {
+  int rc;
+  if ((rc = validate_cfg(cfg)) || (rc = validate_tokens(M, cfg))) return rc;
+  if (M == 0) return LG_OK;
+  if (!y || !weights || !out) return fail(LG_ERR_INVALID_ARG, "combine: NULL tensor pointer");
+  if (!aligned(y, 8) || !aligned(out, 16) || (shared && !aligned(shared, 8)))
+    return fail(LG_ERR_INVALID_ARG, "combine: misaligned tensor");
+  const int d = cfg->hidden_size;
+  const long long n4 = M * (d / 4);
+  const int grid = static_cast<int>(n4 / 256 + 1 < 4 * num_sms() ? n4 / 256 + 1 : 4 * num_sms());
+  lg::combine_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      y, weights, shared, static_cast<int>(M), cfg->num_experts_per_tok, d, out);
+  return cuda_check(cudaGetLastError(), "combine launch");
+}
+
+int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint16_t* x, int64_t M, float* out,
+                   float* weights_out, uint32_t* indices_out, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  int rc;
+  if ((rc = validate_cfg(cfg)) || (rc = validate_tokens(M, cfg))) return rc;
+  if (M == 0) return LG_OK;
+  if ((rc = validate_weights(cfg, w, true, true))) return rc;
+  if (!x || !out || !w->router_weight || !w->router_bias) return fail(LG_ERR_INVALID_ARG, "forward: NULL pointer");
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w->router_weight, 16))
+    return fail(LG_ERR_INVALID_ARG, "forward: x, out and router_weight must be 16-byte aligned");
+  if ((rc = check_ws(cfg, M, workspace, workspace_bytes))) return rc;
+  const Layout L = layout(cfg, M);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int m = static_cast<int>(M);
+  float* wts = weights_out ? weights_out : at<float>(workspace, L.weights);
+  uint32_t* idx = indices_out ? indices_out : at<uint32_t>(workspace, L.indices);
+  int* counts = at<int>(workspace, L.counts);
+  int* offsets = at<int>(workspace, L.offsets);
+  int* perm = at<int>(workspace, L.perm);
+  int* active = at<int>(workspace, L.active);
+  const int slot = trace_slot();
+  trace_mark(slot, 0, s);
+  if ((rc = cuda_check(cudaMemsetAsync(counts, 0, cfg->n_routed_experts * sizeof(int), s), "memset"))) return rc;
+  if ((rc = launch_router(cfg, x, m, w->router_weight, w->router_bias, at<float>(workspace, L.logits), wts, idx,
+                          counts, s)))
+    return rc;
+  trace_mark(slot, 1, s);
+  if ((rc = launch_dispatch(cfg, idx, m, counts, offsets, perm, active, false, s))) return rc;
+  trace_mark(slot, 2, s);
+  uint16_t* act = at<uint16_t>(workspace, L.act);
+  uint16_t* act_s = at<uint16_t>(workspace, L.act_s);
+  uint16_t* y = at<uint16_t>(workspace, L.y);
+  uint16_t* ys = cfg->n_shared_experts > 0 ? at<uint16_t>(workspace, L.ys) : nullptr;
+  if ((rc = launch_gate_up(cfg, w, x, m, offsets, perm, active, act, act_s, true, true, s))) return rc;
+  trace_mark(slot, 3, s);
+  if ((rc = launch_down(cfg, w, m, offsets, perm, active, act, act_s, y, ys, true, true, s))) return rc;
+  trace_mark(slot, 4, s);
+  rc = lg_moe_combine(cfg, y, wts, ys, M, out, stream);
+  trace_mark(slot, 5, s);
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,457 @@
+// Kernels of the GLM MoE block for sm_100a.
+//
+//   router_logits_kernel   x @ W_r^T in the canonical fp32 order     moe.py:37-38
+//   router_select_kernel   sigmoid, bias, group top-2, top-k, norm   moe.py:39-62
+//   dispatch_kernel        counts / offsets / stable permutation     (build contract)
+//   grouped_gemv_kernel    MXFP4 or bf16 expert rows x routed tokens expert_ssd.py:172-188
+//   combine_kernel         weighted top-k sum + shared add           moe.py:199-201
+#pragma once
+#include "common.cuh"
+
+namespace lg {
+
+// --------------------------------------------------------------------------
+// Router logits: one warp owns TEW experts x TM tokens.  Lane l accumulates
+// the 8-element chunks c = l, l+32, ... in increasing element order with
+// fma, then a 16/8/4/2/1 xor butterfly adds the 32 partials.  This is the
+// summation order the CPU checker restates.
+template <int TM, int TEW>
+__global__ void __launch_bounds__(256)
+router_logits_kernel(const uint16_t* __restrict__ x, const float* __restrict__ W,
+                     int M, int d, int E, float* __restrict__ logits) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * TM;
+  const int e0 = (blockIdx.y * 8 + warp) * TEW;
+  if (e0 >= E) return;
+  float acc[TM][TEW];
+#pragma unroll
+  for (int a = 0; a < TM; ++a)
+#pragma unroll
+    for (int b = 0; b < TEW; ++b) acc[a][b] = 0.0f;
+  const int chunks = d >> 3;
+  for (int c = lane; c < chunks; c += 32) {
+    float xv[TM][8];
+#pragma unroll
+    for (int a = 0; a < TM; ++a) {
+      const int t = t0 + a;
+      if (t < M) {
+        uint4 u = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * d + 8 * c);
+        xv[a][0] = bf16lo(u.x); xv[a][1] = bf16hi(u.x);
+        xv[a][2] = bf16lo(u.y); xv[a][3] = bf16hi(u.y);
+        xv[a][4] = bf16lo(u.z); xv[a][5] = bf16hi(u.z);
+        xv[a][6] = bf16lo(u.w); xv[a][7] = bf16hi(u.w);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) xv[a][q] = 0.0f;
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < TEW; ++b) {
+      const int e = e0 + b;
+      if (e < E) {
+        const float4* wp = reinterpret_cast<const float4*>(W + static_cast<size_t>(e) * d + 8 * c);
+        float4 w0 = wp[0], w1 = wp[1];
+        float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int a = 0; a < TM; ++a)
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[a][b] = __fmaf_rn(xv[a][q], wv[q], acc[a][b]);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+    for (int a = 0; a < TM; ++a)
+#pragma unroll
+      for (int b = 0; b < TEW; ++b)
+        acc[a][b] = __fadd_rn(acc[a][b], __shfl_xor_sync(0xffffffffu, acc[a][b], off));
+  if (lane == 0) {
+#pragma unroll
+    for (int a = 0; a < TM; ++a)
+#pragma unroll
+      for (int b = 0; b < TEW; ++b) {
+        const int t = t0 + a, e = e0 + b;
+        if (t < M && e < E) logits[static_cast<size_t>(t) * E + e] = acc[a][b];
+      }
+  }
+}
+
+// (value, index) order of a stable ascending sort; idx < 0 marks "none".
+__device__ __forceinline__ bool after(float a, int ia, float b, int ib) {
+  if (ib < 0) return ia >= 0;
+  if (ia < 0) return false;
+  return a > b || (a == b && ia > ib);
+}
+__device__ __forceinline__ void warp_best(float& v, int& i) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, v, off);
+    int oi = __shfl_xor_sync(0xffffffffu, i, off);
+    if (after(ov, oi, v, i)) { v = ov; i = oi; }
+  }
+}
+
+// --------------------------------------------------------------------------
+// Router selection: one warp per token.  E <= 1024 (32 experts per lane).
+// Shared memory per warp: scores[E], choice[E], gscore[G].
+constexpr int kSelectWarps = 4;
+__global__ void __launch_bounds__(kSelectWarps * 32)
+router_select_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                     int M, int E, int G, int g, int k, int norm, float scale,
+                     float* __restrict__ weights, uint32_t* __restrict__ indices,
+                     int* __restrict__ counts) {
+  extern __shared__ float sm[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int t = blockIdx.x * kSelectWarps + warp;
+  if (t >= M) return;
+  float* sc = sm + warp * (2 * E + G);
+  float* ch = sc + E;
+  float* gs = ch + E;
+  for (int e = lane; e < E; e += 32) {
+    float s = own_sigmoidf(logits[static_cast<size_t>(t) * E + e]);
+    sc[e] = s;
+    ch[e] = __fadd_rn(s, bias[e]);
+  }
+  __syncwarp();
+  const int per = E / G;
+  for (int gi = lane; gi < G; gi += 32) {
+    int b1 = -1, b2 = -1;
+    float v1 = 0.f, v2 = 0.f;
+    for (int j = 0; j < per; ++j) {
+      const int e = gi * per + j;
+      const float v = ch[e];
+      if (after(v, e, v1, b1)) { b2 = b1; v2 = v1; b1 = e; v1 = v; }
+      else if (after(v, e, v2, b2)) { b2 = e; v2 = v; }
+    }
+    gs[gi] = __fadd_rn(v2, v1);
+  }
+  __syncwarp();
+  // topk_group best groups; lane owns groups lane + 32u (G <= 1024)
+  uint32_t gtaken = 0u;
+  for (int s = 0; s < g; ++s) {
+    float bv = 0.f; int bi = -1;
+    for (int u = 0; lane + 32 * u < G; ++u) {
+      const int gi = lane + 32 * u;
+      if (!((gtaken >> u) & 1u) && after(gs[gi], gi, bv, bi)) { bv = gs[gi]; bi = gi; }
+    }
+    warp_best(bv, bi);
+    if ((bi & 31) == lane) gtaken |= 1u << (bi >> 5);
+  }
+  // broadcast the group mask through shared memory (reuse gs as flags)
+  __syncwarp();
+  for (int u = 0; lane + 32 * u < G; ++u) gs[lane + 32 * u] = ((gtaken >> u) & 1u) ? 1.f : 0.f;
+  __syncwarp();
+  const float ninf = __uint_as_float(0xff800000u);
+  for (int e = lane; e < E; e += 32)
+    if (gs[e / per] == 0.f) ch[e] = ninf;
+  __syncwarp();
+  uint32_t taken = 0u;
+  int mine = -1;  // lane j < k keeps the expert of output slot j
+  for (int s = 0; s < k; ++s) {
+    float bv = 0.f; int bi = -1;
+    for (int u = 0; lane + 32 * u < E; ++u) {
+      const int e = lane + 32 * u;
+      if (!((taken >> u) & 1u) && after(ch[e], e, bv, bi)) { bv = ch[e]; bi = e; }
+    }
+    warp_best(bv, bi);
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (lane == k - 1 - s) mine = bi;
+  }
+  // weights: sequential sum in output order (lane 0), then each lane j < k
+  float wj = (lane < k) ? sc[mine] : 0.f;
+  float denom = 0.f;
+  if (norm) {
+    float sum = __shfl_sync(0xffffffffu, wj, 0);
+    for (int j = 1; j < k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, wj, j));
+    denom = __fadd_rn(sum, 0x1.79ca1p-67f);  // float32(1e-20)
+  }
+  if (lane < k) {
+    float w = norm ? __fdiv_rn(wj, denom) : wj;
+    w = __fmul_rn(w, scale);
+    weights[static_cast<size_t>(t) * k + lane] = w;
+    indices[static_cast<size_t>(t) * k + lane] = static_cast<uint32_t>(mine);
+    if (counts) atomicAdd(counts + mine, 1);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Dispatch: block e scans all route slots and writes, in slot order, the
+// slots routed to expert e (stable counting sort).  It also writes offsets[e]
+// and the compact list of active experts: active[0] = #experts with routes,
+// active[1 + r] = r-th such expert in increasing id.
+__global__ void __launch_bounds__(256)
+dispatch_kernel(const uint32_t* __restrict__ idx, int S, int E,
+                const int* __restrict__ counts, int* __restrict__ offsets,
+                int* __restrict__ perm, int* __restrict__ active) {
+  __shared__ int red[2][8];
+  __shared__ int wsum[8];
+  const int e = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int start = 0, nz = 0;
+  for (int j = threadIdx.x; j < e; j += 256) {
+    const int c = counts[j];
+    start += c;
+    nz += c > 0;
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    start += __shfl_xor_sync(0xffffffffu, start, off);
+    nz += __shfl_xor_sync(0xffffffffu, nz, off);
+  }
+  if (lane == 0) { red[0][warp] = start; red[1][warp] = nz; }
+  __syncthreads();
+  start = 0; nz = 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) { start += red[0][w]; nz += red[1][w]; }
+  const int cnt = counts[e];
+  if (threadIdx.x == 0) {
+    offsets[e] = start;
+    if (e == E - 1) { offsets[E] = start + cnt; active[0] = nz + (cnt > 0); }
+    if (cnt > 0) active[1 + nz] = e;
+  }
+  if (cnt == 0) return;
+  int base = start;
+  for (int s0 = 0; s0 < S; s0 += 256) {
+    const int s = s0 + threadIdx.x;
+    const bool f = s < S && idx[s] == static_cast<uint32_t>(e);
+    const unsigned b = __ballot_sync(0xffffffffu, f);
+    __syncthreads();
+    if (lane == 0) wsum[warp] = __popc(b);
+    __syncthreads();
+    int wpre = 0, tot = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) { const int v = wsum[w]; wpre += (w < warp) ? v : 0; tot += v; }
+    if (f) perm[base + wpre + __popc(b & ((1u << lane) - 1u))] = s;
+    base += tot;
+    if (base - start >= cnt) break;
+  }
+}
+
+// --------------------------------------------------------------------------
+// Grouped GEMV over (expert, row block) work items.
+//
+// Work items 0 .. n_active*nrb-1 are routed: expert e = active[1 + item/nrb],
+// rows rb*ROWS .. +ROWS of its weight matrix, against the rows of the
+// routes offsets[e] .. offsets[e+1]-1 (in permuted order).  The remaining
+// nrb_s items are shared-expert row blocks against all M tokens.
+//
+// A "slot" of LPR lanes owns one weight row; lane `sub` of the slot owns
+// the 32-column groups c = sub, sub + LPR, ...: one 16-byte load of packed
+// E2M1 nibbles plus one E8M0 scale byte per group (64 bytes for bf16 rows).
+// Token rows are staged in shared memory as f32 in a lane-interleaved
+// layout so that the LPR lanes read consecutive float4s.
+struct GemvArgs {
+  int K, N;          // routed: reduction length, rows per expert
+  int Ks, Ns;        // shared: reduction length, rows (Ns = 0: no shared)
+  int k;             // routes per token
+  int M;             // tokens
+  int pair;          // 1: gate+up with SwiGLU epilogue; 0: single matrix
+  float limit;
+  const uint8_t *a_packed, *a_scale, *b_packed, *b_scale;
+  long long a_pstride, a_sstride, b_pstride, b_sstride;
+  const uint16_t *sa, *sb;  // shared weights bf16 [Ns, Ks]
+  const uint16_t* xin;      // routed input rows
+  int xin_by_token;         // 1: row = perm[p] / k (token rows); 0: row = p
+  const uint16_t* xin_s;    // shared input rows [M, Ks]
+  const int *offsets, *perm, *active;
+  uint16_t* out;            // routed output [*, N]
+  int out_by_slot;          // 1: row = perm[p]; 0: row = p
+  uint16_t* out_s;          // shared output [M, Ns]
+};
+
+template <int LPR, int TT>
+__global__ void __launch_bounds__(256)
+grouped_gemv_kernel(GemvArgs a) {
+  extern __shared__ float4 xs[];
+  constexpr int SLOTS = 32 / LPR;
+  constexpr int ROWS = 8 * SLOTS;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int sub = lane & (LPR - 1);
+  const int slot = lane / LPR;
+  const int n_active = a.active[0];
+  const int nrb = (a.N + ROWS - 1) / ROWS;
+  const int nrb_s = (a.Ns + ROWS - 1) / ROWS;
+  const long long n_routed = static_cast<long long>(n_active) * nrb;
+  const long long total = n_routed + nrb_s;
+  for (long long w = blockIdx.x; w < total; w += gridDim.x) {
+    const bool sh = w >= n_routed;
+    int e = 0, rb, r0, nr, K, N;
+    if (!sh) {
+      const int u = static_cast<int>(w / nrb);
+      rb = static_cast<int>(w - static_cast<long long>(u) * nrb);
+      e = a.active[1 + u];
+      r0 = a.offsets[e];
+      nr = a.offsets[e + 1] - r0;
+      K = a.K; N = a.N;
+    } else {
+      rb = static_cast<int>(w - n_routed);
+      r0 = 0; nr = a.M;
+      K = a.Ks; N = a.Ns;
+    }
+    const int G = K >> 5;
+    const int KI = (G + LPR - 1) / LPR;
+    const int row = rb * ROWS + warp * SLOTS + slot;
+    const bool valid = row < N;
+    const int rr = valid ? row : 0;
+    for (int c0 = 0; c0 < nr; c0 += TT) {
+      const int nt = min(TT, nr - c0);
+      __syncthreads();
+      for (int i4 = threadIdx.x; i4 < nt * G * 8; i4 += blockDim.x) {
+        const int t = i4 / (G * 8);
+        const int rem = i4 - t * G * 8;
+        const int c = rem >> 3, q4 = rem & 7;
+        const uint16_t* src;
+        if (!sh) {
+          const int p = r0 + c0 + t;
+          const int srow = a.xin_by_token ? a.perm[p] / a.k : p;
+          src = a.xin + static_cast<size_t>(srow) * K;
+        } else {
+          src = a.xin_s + static_cast<size_t>(c0 + t) * K;
+        }
+        const uint2 u = *reinterpret_cast<const uint2*>(src + 32 * c + 4 * q4);
+        xs[((t * KI + c / LPR) * 8 + q4) * LPR + (c & (LPR - 1))] =
+            make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
+      }
+      __syncthreads();
+      float acc_a[TT], acc_b[TT];
+#pragma unroll
+      for (int t = 0; t < TT; ++t) { acc_a[t] = 0.f; acc_b[t] = 0.f; }
+      for (int i = 0; i < KI; ++i) {
+        const int c = sub + LPR * i;
+        if (c >= G) break;
+        if (!sh) {
+          const size_t poff = static_cast<size_t>(rr) * (K >> 1) + 16 * c;
+          const size_t soff = static_cast<size_t>(rr) * G + c;
+          const uint4 pa = ldg_nc_v4(a.a_packed + e * a.a_pstride + poff);
+          const float sa = e8m0_to_f32(a.a_scale[e * a.a_sstride + soff]);
+          uint4 pb = make_uint4(0, 0, 0, 0);
+          float sb = 0.f;
+          if (a.pair) {
+            pb = ldg_nc_v4(a.b_packed + e * a.b_pstride + poff);
+            sb = e8m0_to_f32(a.b_scale[e * a.b_sstride + soff]);
+          }
+          float ga[TT], gb[TT];
+#pragma unroll
+          for (int t = 0; t < TT; ++t) { ga[t] = 0.f; gb[t] = 0.f; }
+          const uint32_t wa4[4] = {pa.x, pa.y, pa.z, pa.w};
+          const uint32_t wb4[4] = {pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+          for (int wd = 0; wd < 4; ++wd) {
+            float va[8], vb[8];
+            e2m1x8_to_f32(wa4[wd], va);
+            if (a.pair) e2m1x8_to_f32(wb4[wd], vb);
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+              if (t < nt) {
+                const float4 x0 = xs[((t * KI + i) * 8 + 2 * wd) * LPR + sub];
+                const float4 x1 = xs[((t * KI + i) * 8 + 2 * wd + 1) * LPR + sub];
+                const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                for (int q = 0; q < 8; ++q) ga[t] = __fmaf_rn(xv[q], va[q], ga[t]);
+                if (a.pair) {
+#pragma unroll
+                  for (int q = 0; q < 8; ++q) gb[t] = __fmaf_rn(xv[q], vb[q], gb[t]);
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int t = 0; t < TT; ++t) {
+            acc_a[t] = __fmaf_rn(ga[t], sa, acc_a[t]);
+            acc_b[t] = __fmaf_rn(gb[t], sb, acc_b[t]);
+          }
+        } else {
+          const uint16_t* wa = a.sa + static_cast<size_t>(rr) * K + 32 * c;
+          const uint16_t* wb = a.pair ? a.sb + static_cast<size_t>(rr) * K + 32 * c : nullptr;
+#pragma unroll
+          for (int wd = 0; wd < 4; ++wd) {
+            const uint4 ua = ldg_nc_v4(wa + 8 * wd);
+            const float va[8] = {bf16lo(ua.x), bf16hi(ua.x), bf16lo(ua.y), bf16hi(ua.y),
+                                 bf16lo(ua.z), bf16hi(ua.z), bf16lo(ua.w), bf16hi(ua.w)};
+            float vb[8];
+            if (a.pair) {
+              const uint4 ub = ldg_nc_v4(wb + 8 * wd);
+              vb[0] = bf16lo(ub.x); vb[1] = bf16hi(ub.x); vb[2] = bf16lo(ub.y); vb[3] = bf16hi(ub.y);
+              vb[4] = bf16lo(ub.z); vb[5] = bf16hi(ub.z); vb[6] = bf16lo(ub.w); vb[7] = bf16hi(ub.w);
+            }
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+              if (t < nt) {
+                const float4 x0 = xs[((t * KI + i) * 8 + 2 * wd) * LPR + sub];
+                const float4 x1 = xs[((t * KI + i) * 8 + 2 * wd + 1) * LPR + sub];
+                const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                for (int q = 0; q < 8; ++q) acc_a[t] = __fmaf_rn(xv[q], va[q], acc_a[t]);
+                if (a.pair) {
+#pragma unroll
+                  for (int q = 0; q < 8; ++q) acc_b[t] = __fmaf_rn(xv[q], vb[q], acc_b[t]);
+                }
+              }
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int off = LPR / 2; off >= 1; off >>= 1)
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+          acc_a[t] = __fadd_rn(acc_a[t], __shfl_xor_sync(0xffffffffu, acc_a[t], off));
+          acc_b[t] = __fadd_rn(acc_b[t], __shfl_xor_sync(0xffffffffu, acc_b[t], off));
+        }
+      if (valid && sub == 0) {
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+          if (t < nt) {
+            uint16_t v;
+            if (a.pair) v = swiglu_bf16(round_bf16(acc_a[t]), round_bf16(acc_b[t]), a.limit);
+            else v = f32_to_bf16(acc_a[t]);
+            if (!sh) {
+              const int p = r0 + c0 + t;
+              const int orow = a.out_by_slot ? a.perm[p] : p;
+              a.out[static_cast<size_t>(orow) * N + row] = v;
+            } else {
+              a.out_s[static_cast<size_t>(c0 + t) * N + row] = v;
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// Combine: out[t, i] = ((0 + y0*w0) + y1*w1) + ... (+ shared), products and
+// sums each rounded to f32 as in the MLX graph (bf16 * f32 -> f32).
+__global__ void __launch_bounds__(256)
+combine_kernel(const uint16_t* __restrict__ y, const float* __restrict__ w,
+               const uint16_t* __restrict__ ys, int M, int k, int d, float* __restrict__ out) {
+  const int d4 = d >> 2;
+  const long long n = static_cast<long long>(M) * d4;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += 256LL * gridDim.x) {
+    const int t = static_cast<int>(i / d4);
+    const int c = static_cast<int>(i - static_cast<long long>(t) * d4);
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const float wj = w[static_cast<size_t>(t) * k + j];
+      const uint2 u = *reinterpret_cast<const uint2*>(y + (static_cast<size_t>(t) * k + j) * d + 4 * c);
+      s0 = __fadd_rn(s0, __fmul_rn(bf16lo(u.x), wj));
+      s1 = __fadd_rn(s1, __fmul_rn(bf16hi(u.x), wj));
+      s2 = __fadd_rn(s2, __fmul_rn(bf16lo(u.y), wj));
+      s3 = __fadd_rn(s3, __fmul_rn(bf16hi(u.y), wj));
+    }
+    if (ys) {
+      const uint2 u = *reinterpret_cast<const uint2*>(ys + static_cast<size_t>(t) * d + 4 * c);
+      s0 = __fadd_rn(s0, bf16lo(u.x));
+      s1 = __fadd_rn(s1, bf16hi(u.x));
+      s2 = __fadd_rn(s2, bf16lo(u.y));
+      s3 = __fadd_rn(s3, bf16hi(u.y));
+    }
+    reinterpret_cast<float4*>(out)[i] = make_float4(s0, s1, s2, s3);
+  }
+}
+
+}  // namespace lg

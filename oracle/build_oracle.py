@@ -1,0 +1,36 @@
+"""Build recipe for the CPU oracle's C part -- TEST INFRASTRUCTURE ONLY.
+
+Compiles oracle/router_ref.c into oracle/_build/liboracle.so with gcc, with
+floating-point contraction off so every fmaf/add/mul rounds exactly where the
+source says.  The reference itself (kg36/livglm) is Python + MLX and has no
+C/C++ sources for this path, so there is nothing to build under oracle/_ref.
+"""
+
+from __future__ import annotations
+
+import os
+import subprocess
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+SRC = HERE / "router_ref.c"
+OUT = HERE / "_build" / "liboracle.so"
+
+
+def build(force: bool = False) -> Path:
+    if not force and OUT.exists() and OUT.stat().st_mtime >= SRC.stat().st_mtime:
+        return OUT
+    OUT.parent.mkdir(parents=True, exist_ok=True)
+    tmp = OUT.with_suffix(f".{os.getpid()}.tmp")
+    cmd = [
+        "gcc", "-O2", "-std=c11", "-shared", "-fPIC",
+        "-ffp-contract=off", "-fno-fast-math", "-fno-builtin",
+        str(SRC), "-o", str(tmp), "-lm",
+    ]
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, OUT)
+    return OUT
+
+
+if __name__ == "__main__":
+    print(build(force=True))
