@@ -305,7 +305,14 @@ int trace_slot() {
   return slot;
 }
 void trace_mark(int slot, int i, cudaStream_t s) {
-  if (slot >= 0) cudaEventRecord(g_trace.ev[slot * (kStages + 1) + i], s);
+  if (slot < 0) return;
+  cudaEvent_t ev = g_trace.ev[slot * (kStages + 1) + i];
+  // Under stream capture a plain record becomes an internal graph edge; the
+  // external flag makes each replay record the event where the host sees it.
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(s, &st);
+  if (st == cudaStreamCaptureStatusActive) cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal);
+  else cudaEventRecord(ev, s);
 }
 
 }  // namespace
