@@ -159,6 +159,33 @@ int lg_moe_forward(const lg_moe_config *cfg, const lg_moe_weights *w,
                    void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * Whole block without a workspace.  No counterpart in the reference.
+ * For callers that cannot allocate device memory when they run the block
+ * (a host framework that owns all device memory and gives plugins no
+ * allocator, a decode loop where cudaMalloc could synchronise the device,
+ * code holding a lock the allocator also takes): same arguments and result
+ * as lg_moe_forward, but the scratch lives in a fixed 4 MiB device array
+ * inside the library, so this call performs no cudaMalloc/cudaFree and no
+ * other allocation.
+ *  - Limit: M must fit in 4 MiB of scratch (lg_moe_workspace_size(cfg, M)
+ *    <= 4194304; about 40 tokens at d=4096, E=128, k=8, F=1536); larger M
+ *    returns LG_ERR_UNSUPPORTED with a message saying so.
+ *  - The first call on a device resolves the array's device address for the
+ *    current device (cudaGetSymbolAddress); make that first call before any
+ *    stream capture.  The current device must own `stream` and the tensors.
+ *  - Every call on a device shares the one array and it keeps the last
+ *    call's contents; calls that overlap on the GPU (different streams, or
+ *    threads without ordering) race on it.  Each call zeroes what must start
+ *    at zero itself.
+ *  - The array occupies 4 MiB on every GPU where the library's device code
+ *    is loaded, until the process exits.
+ */
+int lg_moe_forward_static_scratch(const lg_moe_config *cfg, const lg_moe_weights *w,
+                                  const uint16_t *x, int64_t M, float *out,
+                                  float *weights_out, uint32_t *indices_out,
+                                  void *stream);
+
+/*
  * Stage tracing.  Counterpart of the reference's per-layer trace spans
  * (DecodeTrace spans "router_graph_construct", "moe_merge_graph_construct",
  * moe.py:97-197; trace.py:43-310), measured on the device: while enabled,

@@ -19,7 +19,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OUT = PKG / "_lib" / "liblivglm_moe.so"
-SOURCES = ["moe_capi.cu"]
+SOURCES = ["moe_capi.cu", "moe_noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

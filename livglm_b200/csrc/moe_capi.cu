@@ -317,6 +317,12 @@ void trace_mark(int slot, int i, cudaStream_t s) {
 
 }  // namespace
 
+// Sets this thread's lg_moe_last_error() message from other translation units
+// of the library (not exported: hidden visibility).
+__attribute__((visibility("hidden"))) int lg_internal_set_error(int code, const char* msg) {
+  return fail(code, "%s", msg);
+}
+
 extern "C" {
 
 int lg_moe_trace_enable(int capacity_calls) {
