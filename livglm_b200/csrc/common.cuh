@@ -106,4 +106,19 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   return r;
 }
 
+// (value, index) order of a stable ascending sort; idx < 0 marks "none".
+__device__ __forceinline__ bool after(float a, int ia, float b, int ib) {
+  if (ib < 0) return ia >= 0;
+  if (ia < 0) return false;
+  return a > b || (a == b && ia > ib);
+}
+__device__ __forceinline__ void warp_best(float& v, int& i) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, v, off);
+    int oi = __shfl_xor_sync(0xffffffffu, i, off);
+    if (after(ov, oi, v, i)) { v = ov; i = oi; }
+  }
+}
+
 }  // namespace lg

@@ -6,8 +6,10 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <utility>
 
 #include "livglm_moe.h"
+#include "decode_kernels.cuh"
 #include "moe_kernels.cuh"
 
 namespace {
@@ -62,7 +64,7 @@ int validate_tokens(int64_t M, const lg_moe_config* c) {
 }
 
 struct Layout {
-  size_t logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, total;
+  size_t logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, total;
 };
 
 Layout layout(const lg_moe_config* c, int64_t M) {
@@ -82,6 +84,7 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   L.act_s = o;   o += up(m * Fs * 2);
   L.y = o;       o += up(m * k * d * 2);
   L.ys = o;      o += up(m * d * 2);
+  L.tickets = o; o += up(d * 4);
   L.total = o;
   return L;
 }
@@ -285,6 +288,119 @@ int launch_experts(const lg_moe_config* c, const lg_moe_weights* w, const uint16
   return launch_down(c, w, M, offsets, perm, active, act, act_s, y, ys, with_routed, with_shared, s);
 }
 
+void trace_mark(int slot, int i, cudaStream_t s);
+
+// ---- decode chain (M <= lg::kDecodeMaxTokens) ----------------------------------
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                      bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename K>
+int occupancy(K kernel, int threads, size_t smem) {
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  int occ = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem);
+  return occ < 1 ? 1 : occ;
+}
+
+size_t decode_down_smem(const lg_moe_config* c, int M) {
+  const size_t F = c->moe_intermediate_size, Fs = F * c->n_shared_experts;
+  const size_t routed = static_cast<size_t>(M) * c->num_experts_per_tok * F * 2;
+  const size_t shared = static_cast<size_t>(M) * Fs * 2;
+  return routed > shared ? routed : shared;
+}
+
+bool decode_fits(const lg_moe_config* c, int64_t M) {
+  return M >= 1 && M <= lg::kDecodeMaxTokens &&
+         static_cast<size_t>(M) * c->hidden_size * 2 <= 160 * 1024 && decode_down_smem(c, static_cast<int>(M)) <= 160 * 1024;
+}
+
+template <int TT>
+int launch_decode_t(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M, float* out,
+                    float* wts, uint32_t* idx, void* ws, const Layout& L, int slot, cudaStream_t s) {
+  using namespace lg;
+  const int d = c->hidden_size, F = c->moe_intermediate_size, E = c->n_routed_experts, k = c->num_experts_per_tok;
+  const int Fs = F * c->n_shared_experts;
+  DecodeArgs a{};
+  a.M = M; a.d = d; a.F = F; a.Fs = Fs; a.E = E; a.k = k; a.G = c->n_group; a.g = c->topk_group;
+  a.norm = c->norm_topk_prob; a.scale = c->routed_scaling_factor; a.limit = c->swiglu_limit;
+  a.x = x; a.Wr = w->router_weight; a.bias = w->router_bias;
+  a.gate_p = w->gate_packed; a.gate_s = w->gate_scale; a.up_p = w->up_packed; a.up_s = w->up_scale;
+  a.down_p = w->down_packed; a.down_s = w->down_scale;
+  a.gate_ps = w->gate_packed_stride; a.gate_ss = w->gate_scale_stride;
+  a.up_ps = w->up_packed_stride; a.up_ss = w->up_scale_stride;
+  a.down_ps = w->down_packed_stride; a.down_ss = w->down_scale_stride;
+  a.sh_gate = w->shared_gate; a.sh_up = w->shared_up; a.sh_down = w->shared_down;
+  a.logits = at<float>(ws, L.logits); a.weights = wts; a.indices = idx;
+  a.counts = at<int>(ws, L.counts); a.offsets = at<int>(ws, L.offsets); a.perm = at<int>(ws, L.perm);
+  a.active = at<int>(ws, L.active);
+  a.act = at<uint16_t>(ws, L.act); a.act_s = at<uint16_t>(ws, L.act_s);
+  a.y = at<uint16_t>(ws, L.y); a.ys = at<uint16_t>(ws, L.ys);
+  a.tickets = at<unsigned>(ws, L.tickets); a.out = out;
+  a.lpr_down = pick_lpr(F);
+  a.lpr_down_s = Fs > 0 ? pick_lpr(Fs) : a.lpr_down;
+  const int rpu_r = 2 * (32 / a.lpr_down), rpu_s = 2 * (32 / a.lpr_down_s);
+  a.cb_rows = Fs > 0 && rpu_s > rpu_r ? rpu_s : rpu_r;
+  const int n_tickets = d / a.cb_rows;
+  // split of the persistent grids between shared and routed work, by bytes
+  const double U = static_cast<double>(E < M * k ? E : M * k);
+  const double routed_row = static_cast<double>(d) * 17.0 / 32.0;
+  const double gu_r = U * 2.0 * F * routed_row, gu_s = 2.0 * Fs * d * 2.0;
+  const double dn_r = U * F * routed_row, dn_s = static_cast<double>(Fs) * d * 2.0;
+  const int sms = num_sms();
+  cudaError_t e;
+  // 1. router logits
+  e = launch_ex(router_logits_decode_kernel<TT>, dim3((E + 7) / 8), dim3(256), 0, s, slot < 0, a);
+  if (e != cudaSuccess) return cuda_check(e, "router logits launch");
+  // 2. select + dispatch
+  const int G = c->n_group;
+  const size_t smem_sel = (2 * E + 3 * G) * 4 + G * 4 + kDecodeMaxTokens * 32 * 4 + 32 * 4 + (3 * E + 2) * 4;
+  e = launch_ex(router_select_dispatch_kernel, dim3(1), dim3(256), smem_sel, s, slot < 0, a, n_tickets);
+  if (e != cudaSuccess) return cuda_check(e, "router select launch");
+  trace_mark(slot, 1, s);
+  trace_mark(slot, 2, s);
+  // 3. gate/up
+  const int KI = (d / 32 + 31) / 32;
+  const size_t smem_gu = static_cast<size_t>(TT) * KI * 4 * 32 * 16;
+  const int grid_gu = sms * occupancy(gate_up_decode_kernel<TT>, 256, smem_gu);
+  a.gu_shared_ctas = Fs > 0 ? static_cast<int>(grid_gu * gu_s / (gu_s + gu_r) + 0.5) : 0;
+  if (Fs > 0 && a.gu_shared_ctas < 1) a.gu_shared_ctas = 1;
+  if (a.gu_shared_ctas > grid_gu - 1) a.gu_shared_ctas = grid_gu - 1;
+  e = launch_ex(gate_up_decode_kernel<TT>, dim3(grid_gu), dim3(256), smem_gu, s, slot < 0, a);
+  if (e != cudaSuccess) return cuda_check(e, "gate/up launch");
+  trace_mark(slot, 3, s);
+  // 4. down + combine
+  const size_t smem_dn = decode_down_smem(c, M);
+  const int grid_dn = sms * occupancy(down_decode_kernel<TT>, 256, smem_dn);
+  a.down_shared_ctas = Fs > 0 ? static_cast<int>(grid_dn * dn_s / (dn_s + dn_r) + 0.5) : 0;
+  if (Fs > 0 && a.down_shared_ctas < 1) a.down_shared_ctas = 1;
+  if (a.down_shared_ctas > grid_dn - 1) a.down_shared_ctas = grid_dn - 1;
+  e = launch_ex(down_decode_kernel<TT>, dim3(grid_dn), dim3(256), smem_dn, s, slot < 0, a);
+  if (e != cudaSuccess) return cuda_check(e, "down launch");
+  trace_mark(slot, 4, s);
+  trace_mark(slot, 5, s);
+  return LG_OK;
+}
+
+int launch_decode(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M, float* out,
+                  float* wts, uint32_t* idx, void* ws, const Layout& L, int slot, cudaStream_t s) {
+  if (M <= 1) return launch_decode_t<1>(c, w, x, M, out, wts, idx, ws, L, slot, s);
+  if (M <= 2) return launch_decode_t<2>(c, w, x, M, out, wts, idx, ws, L, slot, s);
+  return launch_decode_t<4>(c, w, x, M, out, wts, idx, ws, L, slot, s);
+}
+
 // ---- stage tracing ------------------------------------------------------------
 // When enabled, lg_moe_forward records a CUDA event before its first stage and
 // after each stage (router, dispatch, gate/up, down, combine) into a ring of
@@ -485,6 +601,10 @@ int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint
   int* active = at<int>(workspace, L.active);
   const int slot = trace_slot();
   trace_mark(slot, 0, s);
+  if (decode_fits(cfg, M)) {
+    rc = launch_decode(cfg, w, x, m, out, wts, idx, workspace, L, slot, s);
+    return rc;
+  }
   if ((rc = cuda_check(cudaMemsetAsync(counts, 0, cfg->n_routed_experts * sizeof(int), s), "memset"))) return rc;
   if ((rc = launch_router(cfg, x, m, w->router_weight, w->router_bias, at<float>(workspace, L.logits), wts, idx,
                           counts, s)))

@@ -134,7 +134,7 @@ def test_dispatch_bit_exact(cuda, native_lib, M, skew):
 
 # -------------------------------------------------------------- forward ---
 
-@pytest.mark.parametrize("M", [1, 2, 5])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5])
 def test_forward_cfg1_decode(cfg1_layer, cuda, M):
     cfg, t, tn = cfg1_layer
     moe = build_layer(cfg, t)
@@ -161,7 +161,9 @@ def test_forward_cfg1_batched_sampled(cfg1_layer, cuda, M):
 def test_combine_bit_exact_given_inputs(cfg1_layer, cuda):
     cfg, t, tn = cfg1_layer
     moe = build_layer(cfg, t)
-    x = synthetic.hidden_states(cfg, 3, seed=9, device=cuda)
+    # M=5 takes the general (non-decode) chain, the same kernels as the
+    # separate entry points
+    x = synthetic.hidden_states(cfg, 5, seed=9, device=cuda)
     out, w, idx = moe(x, return_route=True)
     y = moe.experts(x, idx)
     sh = moe.shared_experts(x)
@@ -206,18 +208,50 @@ def test_checkpoint_names_drop_in(cuda, native_lib, golden_cfg0):
     assert len(moe.last_route_ids) == z["indices"].size
 
 
+@pytest.mark.parametrize("M", [1, 3, 7])
 @pytest.mark.parametrize("geo", [
     dict(n_routed_experts=48, num_experts_per_tok=1, n_group=1, topk_group=1),
     dict(n_routed_experts=64, num_experts_per_tok=6, n_group=2, topk_group=2, n_shared_experts=2),
     dict(n_routed_experts=32, num_experts_per_tok=8, n_group=4, topk_group=1, moe_intermediate_size=96,
          norm_topk_prob=False, swiglu_limit=0.0),
 ])
-def test_forward_other_geometries(cuda, native_lib, geo):
+def test_forward_other_geometries(cuda, native_lib, geo, M):
     cfg = CONFIGS["cfg0"].replace(**geo)
     t = synthetic.layer_weights(cfg, seed=1, device=cuda)
     tn = bank_to_numpy(t)
-    x = synthetic.hidden_states(cfg, 7, seed=2, device=cuda) * 4
+    x = synthetic.hidden_states(cfg, M, seed=2, device=cuda) * 4
     out, w, idx = build_layer(cfg, t)(x, return_route=True)
     ref = mo.moe_forward(to_numpy(x), tn, cfg)
     np.testing.assert_array_equal(to_numpy(idx), ref["indices"])
     assert_close(to_numpy(out), ref["out"])
+
+
+@pytest.mark.parametrize("M", [1, 2, 6])
+def test_forward_cfg0_small_batches(cuda, native_lib, golden_cfg0, M):
+    """Decode-shaped calls (M <= 4 take the fused decode chain) on config 0."""
+    z = golden_cfg0
+    cfg = CONFIGS["cfg0"]
+    moe = build_layer(cfg, bank_to_device(z, cuda))
+    x = z["x"][:M]
+    out, w, idx = moe(to_device(x, cuda, bf16=True), return_route=True)
+    ref = mo.moe_forward(x, z, cfg)
+    np.testing.assert_array_equal(to_numpy(idx), ref["indices"])
+    np.testing.assert_array_equal(to_numpy(w).view(np.uint32), ref["weights"].view(np.uint32))
+    assert_close(to_numpy(out), ref["out"], max_abs=2e-3)
+
+
+@pytest.mark.parametrize("M", [1, 3])
+def test_forward_large_activations(cuda, native_lib, M):
+    """Hidden states far outside the f16 range exercise the power-of-two
+    prescale of the decode kernels; SwiGLU without a limit keeps the large
+    activations flowing into the down projection."""
+    cfg = CONFIGS["cfg0"].replace(swiglu_limit=0.0)
+    t = synthetic.layer_weights(cfg, seed=3, device=cuda)
+    tn = bank_to_numpy(t)
+    x = synthetic.hidden_states(cfg, M, seed=4, device=cuda) * 65536
+    out, w, idx = build_layer(cfg, t)(x, return_route=True)
+    ref = mo.moe_forward(to_numpy(x), tn, cfg)
+    np.testing.assert_array_equal(to_numpy(idx), ref["indices"])
+    o, r = to_numpy(out), ref["out"]
+    scale = float(np.max(np.abs(r)))
+    assert_close(o / scale, r / scale, max_abs=2e-3)
