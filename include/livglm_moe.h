@@ -17,6 +17,11 @@
  *  - Return value: LG_OK (0) or an LG_ERR_* code; lg_moe_last_error() gives
  *    a message for the calling thread.  Argument errors are detected on the
  *    host before any launch and leave the stream untouched.
+ *  - Device-side failures cannot be returned from a stream-ordered call: the
+ *    first 4 bytes of the workspace are a status word that kernels set when a
+ *    bounded wait gives up (LG_ERR_TIMEOUT in the low byte, the waiting site
+ *    above it).  Zero the workspace once after allocating it; the library
+ *    never clears the status word, so it stays set until the caller clears it.
  *  - Routed expert tensors are banks: expert e's tensor starts at
  *    base + e * stride (bytes) and is byte-identical to the checkpoint's
  *      model.language_model.layers.{L}.mlp.experts.{e}.{gate,up}_proj.weight_packed  U8 [F, d/2]

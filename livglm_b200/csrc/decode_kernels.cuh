@@ -4,11 +4,7 @@
 //   router_logits_decode_kernel    one warp per expert; canonical fp32 order
 //   router_select_dispatch_kernel  one CTA: sigmoid/bias/group-limited top-k,
 //                                  weights, counts/offsets/perm/active
-//   gate_up_decode_kernel          MXFP4 gate+up rows x routed tokens, SwiGLU;
-//                                  bf16 shared expert rows in dedicated CTAs
-//   down_decode_kernel             MXFP4 down rows x routed activations, bf16
-//                                  shared down; the last unit to finish a row
-//                                  block writes the f32 combine (moe.py:199-201)
+//   (gate/up and down: stream_kernels.cuh)
 //
 // Dot products: E2M1 pairs are converted with cvt.rn.f16x2.e2m1x2 and
 // multiplied into f32 accumulators with the mixed-precision
@@ -89,9 +85,8 @@ struct DecodeArgs {
   uint16_t *act, *act_s, *y, *ys;
   unsigned* tickets;  // down combine tickets, one per combine block
   float* out;
-  int gu_shared_ctas, down_shared_ctas;
-  int lpr_down, lpr_down_s;  // lanes per row in the down kernel (routed / shared)
-  int cb_rows;               // rows per combine block
+  int* status;               // device status word (0 = ok)
+  int lpr_down;              // lanes per row in the down kernel (routed rows)
 };
 
 // ---------------------------------------------------------------------------
@@ -256,356 +251,6 @@ __global__ void __launch_bounds__(256) router_select_dispatch_kernel(DecodeArgs 
     int r = 0;
     for (int j = 0; j < s; ++j) r += sel_e[j] == e;
     a.perm[offs[e] + r] = s;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Gate/up.  CTAs [0, gu_shared_ctas) stream the shared expert's bf16 rows
-// (they need no routing, so they start while the router still runs); the
-// others stream routed (expert, row) units.  A warp owns one row pair (gate
-// row f and up row f) at a time; lane l owns the 32-column groups
-// c = l, l+32, ...: one 16-byte packed load and one scale byte per group
-// (four 16-byte loads per group for bf16 rows).
-// Shared memory: activations of all M tokens, [t][i][w][lane] uint4 so that
-// lane l reads group c = l + 32i, word w (8 values) conflict-free.
-template <int TT>
-__global__ void __launch_bounds__(256) gate_up_decode_kernel(DecodeArgs a) {
-  extern __shared__ uint4 gu_xs[];
-  __shared__ unsigned amax_bits[TT];
-  __shared__ float tok_scale[TT];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int K = a.d, G = K >> 5, KI = (G + 31) >> 5;
-  const bool shared_cta = static_cast<int>(blockIdx.x) < a.gu_shared_ctas;
-  const int M = a.M;
-  // ---- stage the M token rows (x is complete: the router waited on it) ----
-  if (threadIdx.x < TT) amax_bits[threadIdx.x] = 0u;
-  __syncthreads();
-  const int n4 = M * G * 4;  // uint4 per row: G groups x 4 words
-  for (int i4 = threadIdx.x; i4 < n4; i4 += blockDim.x) {
-    const int t = i4 / (G * 4), rem = i4 - t * G * 4, c = rem >> 2, w = rem & 3;
-    const uint4 u = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + 32 * c + 8 * w);
-    gu_xs[((t * KI + (c >> 5)) * 4 + w) * 32 + (c & 31)] = u;
-    if (!shared_cta) {
-      float m = fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y))));
-      m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
-      atomicMax(amax_bits + t, __float_as_uint(m));
-    }
-  }
-  __syncthreads();
-  if (shared_cta) {
-    pdl_trigger();
-    const int units = a.Fs;
-    const int wpc = blockDim.x >> 5;
-    const int nw = a.gu_shared_ctas * wpc;
-    for (int f = blockIdx.x * wpc + warp; f < units; f += nw) {
-      float ag[TT], au[TT];
-#pragma unroll
-      for (int t = 0; t < TT; ++t) { ag[t] = 0.f; au[t] = 0.f; }
-      const uint16_t* gr = a.sh_gate + static_cast<size_t>(f) * K;
-      const uint16_t* ur = a.sh_up + static_cast<size_t>(f) * K;
-      for (int i = 0; i < KI; ++i) {
-        const int c = lane + 32 * i;
-        if (c < G) {
-          uint4 wg[4], wu[4];
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            wg[w] = ldg_nc_v4(gr + 32 * c + 8 * w);
-            wu[w] = ldg_nc_v4(ur + 32 * c + 8 * w);
-          }
-#pragma unroll
-          for (int w = 0; w < 4; ++w)
-#pragma unroll
-            for (int t = 0; t < TT; ++t)
-              if (t < M) {
-                const uint4 xv = gu_xs[((t * KI + i) * 4 + w) * 32 + lane];
-                ag[t] = dot8_bf16(wg[w], xv, ag[t]);
-                au[t] = dot8_bf16(wu[w], xv, au[t]);
-              }
-        }
-      }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1)
-#pragma unroll
-        for (int t = 0; t < TT; ++t) {
-          ag[t] = __fadd_rn(ag[t], __shfl_xor_sync(0xffffffffu, ag[t], off));
-          au[t] = __fadd_rn(au[t], __shfl_xor_sync(0xffffffffu, au[t], off));
-        }
-      if (lane < TT && lane < M) {
-        float g = ag[0], u = au[0];
-#pragma unroll
-        for (int t = 1; t < TT; ++t)
-          if (lane == t) { g = ag[t]; u = au[t]; }
-        a.act_s[static_cast<size_t>(lane) * a.Fs + f] = swiglu_bf16(round_bf16(g), round_bf16(u), a.limit);
-      }
-    }
-    return;
-  }
-  // ---- routed: convert the staged rows to f16 in place (prescaled) ----
-  if (threadIdx.x < TT) {
-    const int sh = f16_shift_for(__uint_as_float(amax_bits[threadIdx.x]));
-    tok_scale[threadIdx.x] = pow2i(sh);  // result multiplier
-    amax_bits[threadIdx.x] = static_cast<unsigned>(sh);
-  }
-  __syncthreads();
-  for (int i4 = threadIdx.x; i4 < n4; i4 += blockDim.x) {
-    const int t = i4 / (G * 4), rem = i4 - t * G * 4, c = rem >> 2, w = rem & 3;
-    uint4& v = gu_xs[((t * KI + (c >> 5)) * 4 + w) * 32 + (c & 31)];
-    const float s = pow2i(-static_cast<int>(amax_bits[t]));
-    v = make_uint4(bf16x2_to_f16x2_scaled(v.x, s), bf16x2_to_f16x2_scaled(v.y, s),
-                   bf16x2_to_f16x2_scaled(v.z, s), bf16x2_to_f16x2_scaled(v.w, s));
-  }
-  __syncthreads();
-  pdl_wait();  // routing tables written by the router
-  pdl_trigger();
-  const int n_active = __ldcg(a.active);
-  const long long units = static_cast<long long>(n_active) * a.F;
-  const int wpc = blockDim.x >> 5;
-  const int routed_ctas = gridDim.x - a.gu_shared_ctas;
-  const int nw = routed_ctas * wpc;
-  const int gw = (blockIdx.x - a.gu_shared_ctas) * wpc + warp;
-  for (long long u = gw; u < units; u += nw) {
-    const int ai = static_cast<int>(u / a.F);
-    const int f = static_cast<int>(u - static_cast<long long>(ai) * a.F);
-    const int e = __ldcg(a.active + 1 + ai);
-    const int p0 = __ldcg(a.offsets + e);
-    const int n = __ldcg(a.offsets + e + 1) - p0;
-    int tok[TT];
-#pragma unroll
-    for (int j = 0; j < TT; ++j) tok[j] = j < n ? __ldcg(a.perm + p0 + j) / a.k : 0;
-    const uint8_t* gp = a.gate_p + e * a.gate_ps + static_cast<size_t>(f) * (K >> 1);
-    const uint8_t* up = a.up_p + e * a.up_ps + static_cast<size_t>(f) * (K >> 1);
-    const uint8_t* gsc = a.gate_s + e * a.gate_ss + static_cast<size_t>(f) * G;
-    const uint8_t* usc = a.up_s + e * a.up_ss + static_cast<size_t>(f) * G;
-    float ag[TT], au[TT];
-#pragma unroll
-    for (int t = 0; t < TT; ++t) { ag[t] = 0.f; au[t] = 0.f; }
-    constexpr int kPre = 4;  // groups per lane loaded ahead (K <= 4096 in one batch)
-    for (int i0 = 0; i0 < KI; i0 += kPre) {
-      uint4 pg[kPre], pu[kPre];
-      uint32_t sg[kPre], su[kPre];
-#pragma unroll
-      for (int q = 0; q < kPre; ++q) {
-        const int c = lane + 32 * (i0 + q);
-        if (i0 + q < KI && c < G) {
-          pg[q] = ldg_nc_v4(gp + 16 * c);
-          pu[q] = ldg_nc_v4(up + 16 * c);
-          sg[q] = gsc[c];
-          su[q] = usc[c];
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < kPre; ++q) {
-        const int i = i0 + q;
-        const int c = lane + 32 * i;
-        if (i < KI && c < G) {
-          float gg[TT], gu[TT];
-#pragma unroll
-          for (int t = 0; t < TT; ++t) { gg[t] = 0.f; gu[t] = 0.f; }
-          const uint32_t wg4[4] = {pg[q].x, pg[q].y, pg[q].z, pg[q].w};
-          const uint32_t wu4[4] = {pu[q].x, pu[q].y, pu[q].z, pu[q].w};
-#pragma unroll
-          for (int w = 0; w < 4; ++w)
-#pragma unroll
-            for (int j = 0; j < TT; ++j)
-              if (j < n) {
-                const uint4 xv = gu_xs[((tok[j] * KI + i) * 4 + w) * 32 + lane];
-                gg[j] = dot8_e2m1_f16(wg4[w], xv, gg[j]);
-                gu[j] = dot8_e2m1_f16(wu4[w], xv, gu[j]);
-              }
-          const float s_g = e8m0_to_f32(sg[q]), s_u = e8m0_to_f32(su[q]);
-#pragma unroll
-          for (int j = 0; j < TT; ++j) {
-            ag[j] = __fmaf_rn(gg[j], s_g, ag[j]);
-            au[j] = __fmaf_rn(gu[j], s_u, au[j]);
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1)
-#pragma unroll
-      for (int j = 0; j < TT; ++j) {
-        ag[j] = __fadd_rn(ag[j], __shfl_xor_sync(0xffffffffu, ag[j], off));
-        au[j] = __fadd_rn(au[j], __shfl_xor_sync(0xffffffffu, au[j], off));
-      }
-    if (lane < TT && lane < n) {
-      float g = ag[0], uu = au[0];
-      int tj = tok[0];
-#pragma unroll
-      for (int j = 1; j < TT; ++j)
-        if (lane == j) { g = ag[j]; uu = au[j]; tj = tok[j]; }
-      const float m = tok_scale[tj];
-      a.act[static_cast<size_t>(p0 + lane) * a.F + f] =
-          swiglu_bf16(round_bf16(__fmul_rn(g, m)), round_bf16(__fmul_rn(uu, m)), a.limit);
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Down + combine.  A unit is 2 row-iterations of one warp: 32/LPR rows per
-// iteration, LPR lanes per row, each lane G/LPR groups of the row.  Routed
-// units cover (active expert, row block); CTAs [0, down_shared_ctas) cover the
-// shared expert's bf16 rows.  After writing its rows a unit takes a ticket on
-// its combine block; the unit that completes a block sums, for every token,
-// the k routed rows in route order plus the shared row into `out`.
-// Shared memory: f16 activations of all M*k routes ([p][q4][grp] uint4, with
-// per-route power-of-two prescale) or the M shared rows (bf16, [t][q4][grp]).
-template <int TT>
-__global__ void __launch_bounds__(256) down_decode_kernel(DecodeArgs a) {
-  extern __shared__ uint4 dn_xs[];
-  __shared__ float rscale[kDecodeMaxTokens * 32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const bool shared_cta = static_cast<int>(blockIdx.x) < a.down_shared_ctas;
-  const int M = a.M, k = a.k, d = a.d;
-  const int K = shared_cta ? a.Fs : a.F;
-  const int G = K >> 5;
-  const int LPR = shared_cta ? a.lpr_down_s : a.lpr_down;
-  const int slots = 32 / LPR;
-  const int rows_per_unit = 2 * slots;
-  const int nblk = d / rows_per_unit;
-  const int sub = lane & (LPR - 1), slot = lane / LPR;
-  const int per_lane = (G + LPR - 1) / LPR;
-  pdl_wait();  // activations from the gate/up kernel
-  pdl_trigger();
-  const int n_active = __ldcg(a.active);
-  const int R = shared_cta ? M : M * k;  // staged rows
-  const uint16_t* src = shared_cta ? a.act_s : a.act;
-  // stage: bf16 rows -> [r][q4][grp] uint4 (shared: bf16 kept; routed: f16 prescaled)
-  for (int r = warp; r < R; r += blockDim.x >> 5) {
-    if (shared_cta) {
-      for (int v = lane; v < G * 4; v += 32) {
-        const int grp = v >> 2, q4 = v & 3;
-        dn_xs[(r * 4 + q4) * G + grp] = __ldcg(reinterpret_cast<const uint4*>(src + static_cast<size_t>(r) * K + 32 * grp + 8 * q4));
-      }
-    } else {
-      float m = 0.f;
-      for (int v = lane; v < G * 4; v += 32) {
-        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src + static_cast<size_t>(r) * K + 8 * v));
-        m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y)))));
-        m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
-      }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-      const int sh = f16_shift_for(m);
-      const float s = pow2i(-sh);
-      if (lane == 0) rscale[r] = pow2i(sh);
-      for (int v = lane; v < G * 4; v += 32) {
-        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src + static_cast<size_t>(r) * K + 8 * v));
-        dn_xs[(r * 4 + (v & 3)) * G + (v >> 2)] =
-            make_uint4(bf16x2_to_f16x2_scaled(u.x, s), bf16x2_to_f16x2_scaled(u.y, s),
-                       bf16x2_to_f16x2_scaled(u.z, s), bf16x2_to_f16x2_scaled(u.w, s));
-      }
-    }
-  }
-  __syncthreads();
-  const int wpc = blockDim.x >> 5;
-  const int my_ctas = shared_cta ? a.down_shared_ctas : gridDim.x - a.down_shared_ctas;
-  const int cta_i = shared_cta ? blockIdx.x : blockIdx.x - a.down_shared_ctas;
-  const int nw = my_ctas * wpc;
-  const long long units = shared_cta ? static_cast<long long>(nblk) : static_cast<long long>(n_active) * nblk;
-  const int cb = a.cb_rows;
-  const unsigned expected = static_cast<unsigned>(n_active) * (cb / (2 * (32 / a.lpr_down))) +
-                            (a.Fs > 0 ? static_cast<unsigned>(cb / (2 * (32 / a.lpr_down_s))) : 0u);
-  for (long long u = cta_i * wpc + warp; u < units; u += nw) {
-    const int ai = shared_cta ? 0 : static_cast<int>(u / nblk);
-    const int rb = static_cast<int>(u - static_cast<long long>(ai) * nblk);
-    const int e = shared_cta ? 0 : __ldcg(a.active + 1 + ai);
-    const int p0 = shared_cta ? 0 : __ldcg(a.offsets + e);
-    const int n = shared_cta ? M : __ldcg(a.offsets + e + 1) - p0;
-#pragma unroll
-    for (int it = 0; it < 2; ++it) {
-      const int row = rb * rows_per_unit + it * slots + slot;
-      float acc[TT];
-#pragma unroll
-      for (int j = 0; j < TT; ++j) acc[j] = 0.f;
-      if (shared_cta) {
-        const uint16_t* wr = a.sh_down + static_cast<size_t>(row) * K;
-        for (int q = 0; q < per_lane; ++q) {
-          const int grp = sub + LPR * q;
-          if (grp < G) {
-            uint4 wv[4];
-#pragma unroll
-            for (int w = 0; w < 4; ++w) wv[w] = ldg_nc_v4(wr + 32 * grp + 8 * w);
-#pragma unroll
-            for (int w = 0; w < 4; ++w)
-#pragma unroll
-              for (int j = 0; j < TT; ++j)
-                if (j < n) acc[j] = dot8_bf16(wv[w], dn_xs[(j * 4 + w) * G + grp], acc[j]);
-          }
-        }
-      } else {
-        const uint8_t* wp = a.down_p + e * a.down_ps + static_cast<size_t>(row) * (K >> 1);
-        const uint8_t* ws = a.down_s + e * a.down_ss + static_cast<size_t>(row) * G;
-        constexpr int kPre = 4;
-        for (int q0 = 0; q0 < per_lane; q0 += kPre) {
-          uint4 pk[kPre];
-          uint32_t sc[kPre];
-#pragma unroll
-          for (int q = 0; q < kPre; ++q) {
-            const int grp = sub + LPR * (q0 + q);
-            if (q0 + q < per_lane && grp < G) { pk[q] = ldg_nc_v4(wp + 16 * grp); sc[q] = ws[grp]; }
-          }
-#pragma unroll
-          for (int q = 0; q < kPre; ++q) {
-            const int grp = sub + LPR * (q0 + q);
-            if (q0 + q < per_lane && grp < G) {
-              const uint32_t w4[4] = {pk[q].x, pk[q].y, pk[q].z, pk[q].w};
-              float gsum[TT];
-#pragma unroll
-              for (int j = 0; j < TT; ++j) gsum[j] = 0.f;
-#pragma unroll
-              for (int w = 0; w < 4; ++w)
-#pragma unroll
-                for (int j = 0; j < TT; ++j)
-                  if (j < n) gsum[j] = dot8_e2m1_f16(w4[w], dn_xs[((p0 + j) * 4 + w) * G + grp], gsum[j]);
-              const float s = e8m0_to_f32(sc[q]);
-#pragma unroll
-              for (int j = 0; j < TT; ++j) acc[j] = __fmaf_rn(gsum[j], s, acc[j]);
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int off = LPR / 2; off >= 1; off >>= 1)
-#pragma unroll
-        for (int j = 0; j < TT; ++j) acc[j] = __fadd_rn(acc[j], __shfl_xor_sync(0xffffffffu, acc[j], off));
-      if (sub < TT && sub < n) {
-        float v = acc[0];
-#pragma unroll
-        for (int j = 1; j < TT; ++j)
-          if (sub == j) v = acc[j];
-        if (shared_cta) {
-          a.ys[static_cast<size_t>(sub) * d + row] = f32_to_bf16(v);
-        } else {
-          const int p = p0 + sub;
-          a.y[static_cast<size_t>(__ldcg(a.perm + p)) * d + row] = f32_to_bf16(__fmul_rn(v, rscale[p]));
-        }
-      }
-    }
-    // ---- combine-block ticket ----
-    __syncwarp();
-    unsigned ticket = 0;
-    const int blk = (rb * rows_per_unit) / cb;
-    if (lane == 0) {
-      __threadfence();
-      ticket = atomicAdd(a.tickets + blk, 1u);
-    }
-    ticket = __shfl_sync(0xffffffffu, ticket, 0);
-    if (ticket == expected - 1) {
-      __threadfence();
-      for (int o = lane; o < cb * M; o += 32) {
-        const int t = o / cb, row = blk * cb + (o - t * cb);
-        float s = 0.f;
-        for (int j = 0; j < k; ++j) {
-          const float wj = __ldcg(a.weights + static_cast<size_t>(t) * k + j);
-          const unsigned short yb = __ldcg(reinterpret_cast<const unsigned short*>(a.y) + (static_cast<size_t>(t) * k + j) * d + row);
-          s = __fadd_rn(s, __fmul_rn(bf16_to_f32(yb), wj));
-        }
-        if (a.Fs > 0) s = __fadd_rn(s, bf16_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(a.ys) + static_cast<size_t>(t) * d + row)));
-        a.out[static_cast<size_t>(t) * d + row] = s;
-      }
-      if (lane == 0) a.tickets[blk] = 0u;
-    }
   }
 }
 

@@ -6,10 +6,11 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <utility>
 
 #include "livglm_moe.h"
-#include "decode_kernels.cuh"
+#include "stream_kernels.cuh"
 #include "moe_kernels.cuh"
 
 namespace {
@@ -64,7 +65,7 @@ int validate_tokens(int64_t M, const lg_moe_config* c) {
 }
 
 struct Layout {
-  size_t logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, total;
+  size_t status, logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, total;
 };
 
 Layout layout(const lg_moe_config* c, int64_t M) {
@@ -73,6 +74,7 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   const size_t m = static_cast<size_t>(M);
   Layout L{};
   size_t o = 0;
+  L.status = o;  o += up(4);
   L.logits = o;  o += up(m * E * 4);
   L.weights = o; o += up(m * k * 4);
   L.indices = o; o += up(m * k * 4);
@@ -309,22 +311,60 @@ cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
 
 template <typename K>
 int occupancy(K kernel, int threads, size_t smem) {
-  if (smem > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   int occ = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem);
   return occ < 1 ? 1 : occ;
 }
 
-size_t decode_down_smem(const lg_moe_config* c, int M) {
-  const size_t F = c->moe_intermediate_size, Fs = F * c->n_shared_experts;
-  const size_t routed = static_cast<size_t>(M) * c->num_experts_per_tok * F * 2;
-  const size_t shared = static_cast<size_t>(M) * Fs * 2;
-  return routed > shared ? routed : shared;
+constexpr size_t kSmemBudget = 227 * 1024 - 2048;  // dynamic bytes left after static shared
+
+struct StreamPlan {
+  lg::StreamCfg gu, dn;
+  size_t gu_smem, dn_smem;
+};
+
+bool plan_stream(const lg_moe_config* c, int M, int TT, StreamPlan* P) {
+  const size_t d = c->hidden_size, F = c->moe_intermediate_size, Fs = F * c->n_shared_experts;
+  const size_t G = d / 32, KI = (G + 31) / 32, WPL = (d / 4 / 8 + 31) / 32;
+  const size_t GF = F / 32, WS = (Fs / 8 + 31) / 32, R = static_cast<size_t>(M) * c->num_experts_per_tok;
+  // gate/up
+  const size_t gu_stage = std::max<size_t>(Fs > 0 ? 2 * lg::kGuRowsShared * d * 2 : 0,
+                                           2 * lg::kGuRowsRouted * (d / 2) + 2 * lg::kGuRowsRouted * G);
+  const size_t gu_x = TT * KI * 128 * 16 + TT * 4 * WPL * 32 * 16;
+  const size_t gu_aux = 2 * lg::kGuRowsShared * 4 * TT * 2 * 4;
+  const size_t gu_fixed = gu_x + gu_aux;
+  if (gu_fixed + 2 * gu_stage > kSmemBudget) return false;
+  P->gu.stages = static_cast<int>(std::min<size_t>(lg::kMaxStages, (kSmemBudget - gu_fixed) / gu_stage));
+  P->gu.stage_bytes = static_cast<int>(gu_stage);
+  P->gu.x_off = P->gu.stages * P->gu.stage_bytes;
+  P->gu.aux_off = static_cast<int>(P->gu.x_off + gu_x);
+  P->gu_smem = P->gu.aux_off + gu_aux;
+  // down
+  const size_t dn_stage = std::max<size_t>(Fs > 0 ? lg::kDnRowsShared * Fs * 2 : 0,
+                                           lg::kDnRowsRouted * (F / 2) + lg::kDnRowsRouted * GF);
+  const size_t dn_x = R * F * 2 + static_cast<size_t>(M) * WS * 32 * 16;
+  const size_t dn_aux = ((R * 4 + 15) / 16) * 16;
+  if (dn_x + dn_aux + 2 * dn_stage > kSmemBudget) return false;
+  P->dn.stages = static_cast<int>(std::min<size_t>(lg::kMaxStages, (kSmemBudget - dn_x - dn_aux) / dn_stage));
+  P->dn.stage_bytes = static_cast<int>(dn_stage);
+  P->dn.x_off = P->dn.stages * P->dn.stage_bytes;
+  P->dn.aux_off = static_cast<int>(P->dn.x_off + dn_x);
+  P->dn_smem = P->dn.aux_off + dn_aux;
+  return true;
 }
 
-bool decode_fits(const lg_moe_config* c, int64_t M) {
-  return M >= 1 && M <= lg::kDecodeMaxTokens &&
-         static_cast<size_t>(M) * c->hidden_size * 2 <= 160 * 1024 && decode_down_smem(c, static_cast<int>(M)) <= 160 * 1024;
+// The decode chain needs bulk-copyable chunks: 16-byte aligned bases and
+// expert strides (scales included), d % 64 == 0.
+bool decode_fits(const lg_moe_config* c, const lg_moe_weights* w, int64_t M) {
+  if (M < 1 || M > lg::kDecodeMaxTokens) return false;
+  if (c->hidden_size % 64) return false;
+  if (c->num_experts_per_tok * M > lg::kDecodeMaxTokens * 32) return false;
+  if (!aligned(w->gate_scale, 16) || !aligned(w->up_scale, 16) || !aligned(w->down_scale, 16)) return false;
+  if (w->gate_scale_stride % 16 || w->up_scale_stride % 16 || w->down_scale_stride % 16) return false;
+  StreamPlan P;
+  const int TT = M <= 1 ? 1 : M <= 2 ? 2 : 4;
+  return plan_stream(c, static_cast<int>(M), TT, &P);
 }
 
 template <int TT>
@@ -333,6 +373,8 @@ int launch_decode_t(const lg_moe_config* c, const lg_moe_weights* w, const uint1
   using namespace lg;
   const int d = c->hidden_size, F = c->moe_intermediate_size, E = c->n_routed_experts, k = c->num_experts_per_tok;
   const int Fs = F * c->n_shared_experts;
+  StreamPlan P;
+  if (!plan_stream(c, M, TT, &P)) return fail(LG_ERR_UNSUPPORTED, "decode chain does not fit in shared memory");
   DecodeArgs a{};
   a.M = M; a.d = d; a.F = F; a.Fs = Fs; a.E = E; a.k = k; a.G = c->n_group; a.g = c->topk_group;
   a.norm = c->norm_topk_prob; a.scale = c->routed_scaling_factor; a.limit = c->swiglu_limit;
@@ -349,45 +391,30 @@ int launch_decode_t(const lg_moe_config* c, const lg_moe_weights* w, const uint1
   a.act = at<uint16_t>(ws, L.act); a.act_s = at<uint16_t>(ws, L.act_s);
   a.y = at<uint16_t>(ws, L.y); a.ys = at<uint16_t>(ws, L.ys);
   a.tickets = at<unsigned>(ws, L.tickets); a.out = out;
+  a.status = at<int>(ws, L.status);
   a.lpr_down = pick_lpr(F);
-  a.lpr_down_s = Fs > 0 ? pick_lpr(Fs) : a.lpr_down;
-  const int rpu_r = 2 * (32 / a.lpr_down), rpu_s = 2 * (32 / a.lpr_down_s);
-  a.cb_rows = Fs > 0 && rpu_s > rpu_r ? rpu_s : rpu_r;
-  const int n_tickets = d / a.cb_rows;
-  // split of the persistent grids between shared and routed work, by bytes
-  const double U = static_cast<double>(E < M * k ? E : M * k);
-  const double routed_row = static_cast<double>(d) * 17.0 / 32.0;
-  const double gu_r = U * 2.0 * F * routed_row, gu_s = 2.0 * Fs * d * 2.0;
-  const double dn_r = U * F * routed_row, dn_s = static_cast<double>(Fs) * d * 2.0;
+  const int n_tickets = d / kDnRowsRouted;
   const int sms = num_sms();
+  const bool pdl = slot < 0;
   cudaError_t e;
   // 1. router logits
-  e = launch_ex(router_logits_decode_kernel<TT>, dim3((E + 7) / 8), dim3(256), 0, s, slot < 0, a);
+  e = launch_ex(router_logits_decode_kernel<TT>, dim3((E + 7) / 8), dim3(256), 0, s, pdl, a);
   if (e != cudaSuccess) return cuda_check(e, "router logits launch");
   // 2. select + dispatch
   const int G = c->n_group;
   const size_t smem_sel = (2 * E + 3 * G) * 4 + G * 4 + kDecodeMaxTokens * 32 * 4 + 32 * 4 + (3 * E + 2) * 4;
-  e = launch_ex(router_select_dispatch_kernel, dim3(1), dim3(256), smem_sel, s, slot < 0, a, n_tickets);
+  e = launch_ex(router_select_dispatch_kernel, dim3(1), dim3(256), smem_sel, s, pdl, a, n_tickets);
   if (e != cudaSuccess) return cuda_check(e, "router select launch");
   trace_mark(slot, 1, s);
   trace_mark(slot, 2, s);
   // 3. gate/up
-  const int KI = (d / 32 + 31) / 32;
-  const size_t smem_gu = static_cast<size_t>(TT) * KI * 4 * 32 * 16;
-  const int grid_gu = sms * occupancy(gate_up_decode_kernel<TT>, 256, smem_gu);
-  a.gu_shared_ctas = Fs > 0 ? static_cast<int>(grid_gu * gu_s / (gu_s + gu_r) + 0.5) : 0;
-  if (Fs > 0 && a.gu_shared_ctas < 1) a.gu_shared_ctas = 1;
-  if (a.gu_shared_ctas > grid_gu - 1) a.gu_shared_ctas = grid_gu - 1;
-  e = launch_ex(gate_up_decode_kernel<TT>, dim3(grid_gu), dim3(256), smem_gu, s, slot < 0, a);
+  occupancy(gate_up_stream_kernel<TT>, kStreamThreads, P.gu_smem);
+  e = launch_ex(gate_up_stream_kernel<TT>, dim3(sms), dim3(kStreamThreads), P.gu_smem, s, pdl, a, P.gu);
   if (e != cudaSuccess) return cuda_check(e, "gate/up launch");
   trace_mark(slot, 3, s);
   // 4. down + combine
-  const size_t smem_dn = decode_down_smem(c, M);
-  const int grid_dn = sms * occupancy(down_decode_kernel<TT>, 256, smem_dn);
-  a.down_shared_ctas = Fs > 0 ? static_cast<int>(grid_dn * dn_s / (dn_s + dn_r) + 0.5) : 0;
-  if (Fs > 0 && a.down_shared_ctas < 1) a.down_shared_ctas = 1;
-  if (a.down_shared_ctas > grid_dn - 1) a.down_shared_ctas = grid_dn - 1;
-  e = launch_ex(down_decode_kernel<TT>, dim3(grid_dn), dim3(256), smem_dn, s, slot < 0, a);
+  occupancy(down_stream_kernel<TT>, kStreamThreads, P.dn_smem);
+  e = launch_ex(down_stream_kernel<TT>, dim3(sms), dim3(kStreamThreads), P.dn_smem, s, pdl, a, P.dn);
   if (e != cudaSuccess) return cuda_check(e, "down launch");
   trace_mark(slot, 4, s);
   trace_mark(slot, 5, s);
@@ -601,7 +628,7 @@ int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint
   int* active = at<int>(workspace, L.active);
   const int slot = trace_slot();
   trace_mark(slot, 0, s);
-  if (decode_fits(cfg, M)) {
+  if (decode_fits(cfg, w, M)) {
     rc = launch_decode(cfg, w, x, m, out, wts, idx, workspace, L, slot, s);
     return rc;
   }

@@ -1,0 +1,77 @@
+// Bulk-copy pipeline primitives for sm_100a: mbarrier ring + cp.async.bulk
+// (TMA bulk copies global -> shared, no multicast).
+//
+// Every wait is bounded: after kWaitLimitNs of %globaltimer time a waiter
+// gives up, records an LG_ERR_TIMEOUT status word with the stage that gave
+// up, and returns false so the kernel can leave instead of hanging.
+#pragma once
+#include "common.cuh"
+
+namespace lg {
+
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+// status word codes: LG_ERR_TIMEOUT (6) in the low byte, the waiting site above it
+enum WaitSite : int {
+  kSiteGuFull = 1 << 8, kSiteGuEmpty = 2 << 8, kSiteGuDrain = 3 << 8,
+  kSiteDnFull = 4 << 8, kSiteDnEmpty = 5 << 8, kSiteDnDrain = 6 << 8,
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, int* status, int site) {
+  if (mbar_try_wait(b, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(b, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (status) atomicExch(status, 6 | site);
+      return false;
+    }
+  }
+  return true;
+}
+// contiguous global -> shared copy completing `bytes` of transactions on `bar`;
+// dst, src and bytes must be multiples of 16
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// named barrier over the consumer warps only (id 1)
+__device__ __forceinline__ void consumer_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+}  // namespace lg

@@ -1,0 +1,506 @@
+// Streaming expert kernels for decode shapes (M <= kDecodeMaxTokens), one CTA
+// per SM: a producer warp moves contiguous weight chunks (~32 KB) into a ring
+// of shared-memory stages with cp.async.bulk; 8 consumer warps compute from
+// shared memory.  With the whole ring in flight per SM, HBM latency is
+// covered without tying up registers.
+//
+//   gate_up_stream_kernel  chunks: shared expert, 2 bf16 rows of gate and up
+//                          (4 warps per row, one K-quarter each); routed
+//                          experts, 8 MXFP4 rows of gate and up (warp per row)
+//   down_stream_kernel     chunks: shared expert, 8 bf16 rows (warp per row);
+//                          routed experts, 32 MXFP4 rows (LPR lanes per row);
+//                          the chunk that completes a 32-row block writes the
+//                          f32 combine of that block (moe.py:199-201)
+//
+// Chunk lists are [shared chunks..., routed chunks...] dealt round-robin over
+// the CTAs.  Shared chunks need no routing, so they run before
+// griddepcontrol.wait; routed chunks are enumerated after it.
+//
+// Error handling: all mbarrier waits are bounded (pipeline.cuh).  A warp whose
+// wait gives up marks the status word and keeps walking the same chunk list
+// without loading or computing, so every consumer still reaches every named
+// barrier and the CTA exits.
+#pragma once
+#include "decode_kernels.cuh"
+#include "pipeline.cuh"
+
+namespace lg {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kStreamThreads = kConsumerThreads + 32;
+constexpr int kMaxStages = 8;
+constexpr int kGuRowsRouted = 8;
+constexpr int kGuRowsShared = 2;
+constexpr int kDnRowsRouted = 32;
+constexpr int kDnRowsShared = 8;
+
+struct StreamCfg {
+  int stages;
+  int stage_bytes;
+  int x_off;    // byte offset of staged activations
+  int aux_off;  // byte offset of the reduction / scale scratch
+};
+
+// ---------------------------------------------------------------------------
+template <int TT>
+__global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(DecodeArgs a, StreamCfg sc) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) uint64_t full[kMaxStages];
+  __shared__ __align__(8) uint64_t empty[kMaxStages];
+  __shared__ unsigned amax_bits[TT];
+  __shared__ float tok_mult[TT];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = a.d, G = K >> 5, KI = (G + 31) >> 5;
+  const int M = a.M, F = a.F, Fs = a.Fs;
+  const int S = sc.stages;
+  const int KQ = K >> 2;                    // shared-chunk quarter width
+  const int WPL = (KQ / 8 + 31) / 32;       // 8-element words per lane per quarter
+  uint4* xh = reinterpret_cast<uint4*>(smem + sc.x_off);   // f16 [t][i][w][lane]
+  uint4* xb = xh + TT * KI * 128;                          // bf16 [t][q][w4][lane]
+  float* red = reinterpret_cast<float*>(smem + sc.aux_off);  // [2][2 rows][4 q][TT][2]
+  const int n_sh = Fs > 0 ? Fs / kGuRowsShared : 0;
+  const int nrb = F / kGuRowsRouted;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumerWarps); }
+    mbar_fence_init();
+  }
+  if (threadIdx.x < TT) amax_bits[threadIdx.x] = 0u;
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {  // ---------------- producer ----------------
+    if (lane == 0) {
+      bool ok = true;
+      int it = 0;
+      int j = blockIdx.x;
+      const unsigned sh_bytes = kGuRowsShared * K * 2;
+      for (; j < n_sh; j += gridDim.x, ++it) {
+        const int s = it % S;
+        const unsigned round = it / S;
+        if (ok && round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, a.status, kSiteGuEmpty);
+        if (!ok) continue;
+        unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+        mbar_arrive_expect_tx(&full[s], 2 * sh_bytes);
+        bulk_g2s(st, a.sh_gate + static_cast<size_t>(j) * kGuRowsShared * K, sh_bytes, &full[s]);
+        bulk_g2s(st + sh_bytes, a.sh_up + static_cast<size_t>(j) * kGuRowsShared * K, sh_bytes, &full[s]);
+      }
+      pdl_wait();
+      pdl_trigger();
+      const int n_r = __ldcg(a.active) * nrb;
+      const unsigned pk = kGuRowsRouted * (K >> 1), sk = kGuRowsRouted * G;
+      for (; j - n_sh < n_r; j += gridDim.x, ++it) {
+        const int s = it % S;
+        const unsigned round = it / S;
+        if (ok && round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, a.status, kSiteGuEmpty);
+        if (!ok) continue;
+        const int jr = j - n_sh;
+        const int e = __ldcg(a.active + 1 + jr / nrb);
+        const size_t f0 = static_cast<size_t>(jr % nrb) * kGuRowsRouted;
+        unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+        mbar_arrive_expect_tx(&full[s], 2 * pk + 2 * sk);
+        bulk_g2s(st, a.gate_p + e * a.gate_ps + f0 * (K >> 1), pk, &full[s]);
+        bulk_g2s(st + pk, a.up_p + e * a.up_ps + f0 * (K >> 1), pk, &full[s]);
+        bulk_g2s(st + 2 * pk, a.gate_s + e * a.gate_ss + f0 * G, sk, &full[s]);
+        bulk_g2s(st + 2 * pk + sk, a.up_s + e * a.up_ss + f0 * G, sk, &full[s]);
+      }
+      if (!ok) {  // consumers stopped: let copies already issued land before leaving
+        for (int q = (it > S ? it - S : 0); q < it; ++q)
+          mbar_wait(&full[q % S], (q / S) & 1, a.status, kSiteGuDrain);
+      }
+    } else {
+      pdl_wait();
+      pdl_trigger();
+    }
+    return;
+  }
+
+  // ------------------------------- consumers -------------------------------
+  const int ct = threadIdx.x;  // 0 .. kConsumerThreads-1
+  // stage bf16 rows for shared chunks: element qq*KQ + 8*(lane + 32*w4) + 0..7
+  if (n_sh > 0) {
+    const int per_row = 4 * WPL * 32;
+    for (int i4 = ct; i4 < M * per_row; i4 += kConsumerThreads) {
+      const int t = i4 / per_row, rem = i4 - t * per_row;
+      const int qq = rem / (WPL * 32), r2 = rem - qq * WPL * 32, w4 = r2 >> 5, ln = r2 & 31;
+      const int el = 8 * (ln + 32 * w4);
+      if (el < KQ)
+        xb[(t * 4 + qq) * WPL * 32 + w4 * 32 + ln] =
+            *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + qq * KQ + el);
+    }
+  }
+  // stage f16 rows for routed chunks (with per-token power-of-two prescale)
+  for (int i4 = ct; i4 < M * G * 4; i4 += kConsumerThreads) {
+    const int t = i4 / (G * 4), rem = i4 - t * G * 4, c = rem >> 2;
+    const uint4 u = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + 8 * rem);
+    float m = fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y))));
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
+    atomicMax(amax_bits + t, __float_as_uint(m));
+    (void)c;
+  }
+  consumer_sync(kConsumerThreads);
+  if (ct < M) tok_mult[ct] = pow2i(f16_shift_for(__uint_as_float(amax_bits[ct])));
+  consumer_sync(kConsumerThreads);
+  for (int i4 = ct; i4 < M * G * 4; i4 += kConsumerThreads) {
+    const int t = i4 / (G * 4), rem = i4 - t * G * 4, c = rem >> 2, w = rem & 3;
+    const uint4 u = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + 8 * rem);
+    const float s = __fdiv_rn(1.0f, tok_mult[t]);
+    xh[((t * KI + (c >> 5)) * 4 + w) * 32 + (c & 31)] =
+        make_uint4(bf16x2_to_f16x2_scaled(u.x, s), bf16x2_to_f16x2_scaled(u.y, s),
+                   bf16x2_to_f16x2_scaled(u.z, s), bf16x2_to_f16x2_scaled(u.w, s));
+  }
+  consumer_sync(kConsumerThreads);
+
+  bool ok = true;
+  int it = 0, shi = 0;
+  int j = blockIdx.x;
+  // shared-expert chunks: rows 2j, 2j+1; warp -> (row w/4, K quarter w%4)
+  for (; j < n_sh; j += gridDim.x, ++it, ++shi) {
+    const int s = it % S;
+    if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteGuFull);
+    const int rr = warp >> 2, qq = warp & 3;
+    float ag[TT], au[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) { ag[t] = 0.f; au[t] = 0.f; }
+    if (ok) {
+      const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+      const unsigned char* gr = st + static_cast<size_t>(rr) * K * 2 + static_cast<size_t>(qq) * KQ * 2;
+      const unsigned char* ur = gr + static_cast<size_t>(kGuRowsShared) * K * 2;
+      for (int w4 = 0; w4 < WPL; ++w4) {
+        const int el = 8 * (lane + 32 * w4);
+        if (el < KQ) {
+          const uint4 wg = *reinterpret_cast<const uint4*>(gr + 2 * el);
+          const uint4 wu = *reinterpret_cast<const uint4*>(ur + 2 * el);
+#pragma unroll
+          for (int t = 0; t < TT; ++t)
+            if (t < M) {
+              const uint4 xv = xb[(t * 4 + qq) * WPL * 32 + w4 * 32 + lane];
+              ag[t] = dot8_bf16(wg, xv, ag[t]);
+              au[t] = dot8_bf16(wu, xv, au[t]);
+            }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
+        ag[t] = __fadd_rn(ag[t], __shfl_xor_sync(0xffffffffu, ag[t], off));
+        au[t] = __fadd_rn(au[t], __shfl_xor_sync(0xffffffffu, au[t], off));
+      }
+    float* rb = red + (shi & 1) * (kGuRowsShared * 4 * TT * 2);
+    if (lane == 0) {
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
+        rb[((rr * 4 + qq) * TT + t) * 2 + 0] = ag[t];
+        rb[((rr * 4 + qq) * TT + t) * 2 + 1] = au[t];
+      }
+    }
+    consumer_sync(kConsumerThreads);
+    if (ok && warp < kGuRowsShared && lane < M) {
+      float g = 0.f, u = 0.f;
+      for (int q = 0; q < 4; ++q) {
+        g = __fadd_rn(g, rb[((warp * 4 + q) * TT + lane) * 2 + 0]);
+        u = __fadd_rn(u, rb[((warp * 4 + q) * TT + lane) * 2 + 1]);
+      }
+      a.act_s[static_cast<size_t>(lane) * Fs + j * kGuRowsShared + warp] =
+          swiglu_bf16(round_bf16(g), round_bf16(u), a.limit);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+  const int n_r = __ldcg(a.active) * nrb;
+  for (; j - n_sh < n_r; j += gridDim.x, ++it) {
+    const int s = it % S;
+    if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteGuFull);
+    const int jr = j - n_sh;
+    const int e = __ldcg(a.active + 1 + jr / nrb);
+    const int f = (jr % nrb) * kGuRowsRouted + warp;
+    const int p0 = __ldcg(a.offsets + e);
+    const int n = __ldcg(a.offsets + e + 1) - p0;
+    int tok[TT];
+#pragma unroll
+    for (int q = 0; q < TT; ++q) tok[q] = q < n ? __ldcg(a.perm + p0 + q) / a.k : 0;
+    float ag[TT], au[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) { ag[t] = 0.f; au[t] = 0.f; }
+    if (ok) {
+      const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+      const size_t pk = static_cast<size_t>(kGuRowsRouted) * (K >> 1);
+      const unsigned char* gp = st + static_cast<size_t>(warp) * (K >> 1);
+      const unsigned char* up = gp + pk;
+      const unsigned char* gs = st + 2 * pk + warp * G;
+      const unsigned char* us = gs + kGuRowsRouted * G;
+      for (int i = 0; i < KI; ++i) {
+        const int c = lane + 32 * i;
+        if (c < G) {
+          const uint4 pg = *reinterpret_cast<const uint4*>(gp + 16 * c);
+          const uint4 pu = *reinterpret_cast<const uint4*>(up + 16 * c);
+          const float s_g = e8m0_to_f32(gs[c]), s_u = e8m0_to_f32(us[c]);
+          const uint32_t wg4[4] = {pg.x, pg.y, pg.z, pg.w};
+          const uint32_t wu4[4] = {pu.x, pu.y, pu.z, pu.w};
+          float gg[TT], gu[TT];
+#pragma unroll
+          for (int t = 0; t < TT; ++t) { gg[t] = 0.f; gu[t] = 0.f; }
+#pragma unroll
+          for (int w = 0; w < 4; ++w)
+#pragma unroll
+            for (int q = 0; q < TT; ++q)
+              if (q < n) {
+                const uint4 xv = xh[((tok[q] * KI + i) * 4 + w) * 32 + lane];
+                gg[q] = dot8_e2m1_f16(wg4[w], xv, gg[q]);
+                gu[q] = dot8_e2m1_f16(wu4[w], xv, gu[q]);
+              }
+#pragma unroll
+          for (int q = 0; q < TT; ++q) {
+            ag[q] = __fmaf_rn(gg[q], s_g, ag[q]);
+            au[q] = __fmaf_rn(gu[q], s_u, au[q]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+      for (int q = 0; q < TT; ++q) {
+        ag[q] = __fadd_rn(ag[q], __shfl_xor_sync(0xffffffffu, ag[q], off));
+        au[q] = __fadd_rn(au[q], __shfl_xor_sync(0xffffffffu, au[q], off));
+      }
+    if (ok && lane < TT && lane < n) {
+      float g = ag[0], uu = au[0];
+      int tj = tok[0];
+#pragma unroll
+      for (int q = 1; q < TT; ++q)
+        if (lane == q) { g = ag[q]; uu = au[q]; tj = tok[q]; }
+      const float m = tok_mult[tj];
+      a.act[static_cast<size_t>(p0 + lane) * F + f] =
+          swiglu_bf16(round_bf16(__fmul_rn(g, m)), round_bf16(__fmul_rn(uu, m)), a.limit);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <int TT>
+__global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeArgs a, StreamCfg sc) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) uint64_t full[kMaxStages];
+  __shared__ __align__(8) uint64_t empty[kMaxStages];
+  __shared__ unsigned ticket_s;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int M = a.M, k = a.k, d = a.d, F = a.F, Fs = a.Fs;
+  const int G = F >> 5;
+  const int S = sc.stages;
+  const int LPR = a.lpr_down;
+  const int slots = 32 / LPR;
+  const int sub = lane & (LPR - 1), slot = lane / LPR;
+  const int per_lane = (G + LPR - 1) / LPR;
+  const int WS = (Fs / 8 + 31) / 32;  // 8-element words per lane of a shared row
+  const int n_sh = Fs > 0 ? d / kDnRowsShared : 0;
+  const int nrb = d / kDnRowsRouted;
+  const int R = M * k;
+  uint4* xr = reinterpret_cast<uint4*>(smem + sc.x_off);  // f16 [p][q4][grp]
+  uint4* xsb = xr + R * G * 4;                             // bf16 [t][w4][lane]
+  float* rscale = reinterpret_cast<float*>(smem + sc.aux_off);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumerWarps); }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {  // ---------------- producer ----------------
+    // weights depend on nothing earlier and the routing tables are complete
+    // (the gate/up kernel waited on the router before letting this kernel
+    // launch), so streaming starts before griddepcontrol.wait.
+    if (lane == 0) {
+      bool ok = true;
+      int it = 0;
+      const int n_r = __ldcg(a.active) * nrb;
+      const unsigned shb = kDnRowsShared * Fs * 2;
+      const unsigned pk = kDnRowsRouted * (F >> 1), sk = kDnRowsRouted * G;
+      for (int j = blockIdx.x; j < n_sh + n_r; j += gridDim.x, ++it) {
+        const int s = it % S;
+        const unsigned round = it / S;
+        if (ok && round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, a.status, kSiteDnEmpty);
+        if (!ok) continue;
+        unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+        if (j < n_sh) {
+          mbar_arrive_expect_tx(&full[s], shb);
+          bulk_g2s(st, a.sh_down + static_cast<size_t>(j) * kDnRowsShared * Fs, shb, &full[s]);
+        } else {
+          const int jr = j - n_sh;
+          const int e = __ldcg(a.active + 1 + jr / nrb);
+          const size_t r0 = static_cast<size_t>(jr % nrb) * kDnRowsRouted;
+          mbar_arrive_expect_tx(&full[s], pk + sk);
+          bulk_g2s(st, a.down_p + e * a.down_ps + r0 * (F >> 1), pk, &full[s]);
+          bulk_g2s(st + pk, a.down_s + e * a.down_ss + r0 * G, sk, &full[s]);
+        }
+      }
+      if (!ok) {
+        for (int q = (it > S ? it - S : 0); q < it; ++q)
+          mbar_wait(&full[q % S], (q / S) & 1, a.status, kSiteDnDrain);
+      }
+    }
+    pdl_wait();
+    pdl_trigger();
+    return;
+  }
+
+  // ------------------------------- consumers -------------------------------
+  const int ct = threadIdx.x;
+  pdl_wait();  // activations from the gate/up kernel
+  pdl_trigger();
+  const int n_active = __ldcg(a.active);
+  const int n_r = n_active * nrb;
+  // stage routed activations as f16 with a per-route power-of-two prescale
+  for (int r = warp; r < R; r += kConsumerWarps) {
+    const uint16_t* src = a.act + static_cast<size_t>(r) * F;
+    float m = 0.f;
+    for (int v = lane; v < G * 4; v += 32) {
+      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src + 8 * v));
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y)))));
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const int sh = f16_shift_for(m);
+    const float s = pow2i(-sh);
+    if (lane == 0) rscale[r] = pow2i(sh);
+    for (int v = lane; v < G * 4; v += 32) {
+      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src + 8 * v));
+      xr[(r * 4 + (v & 3)) * G + (v >> 2)] =
+          make_uint4(bf16x2_to_f16x2_scaled(u.x, s), bf16x2_to_f16x2_scaled(u.y, s),
+                     bf16x2_to_f16x2_scaled(u.z, s), bf16x2_to_f16x2_scaled(u.w, s));
+    }
+  }
+  // stage shared activations (bf16) as [t][w4][lane], element 8*(lane + 32*w4)
+  if (Fs > 0) {
+    for (int i4 = ct; i4 < M * WS * 32; i4 += kConsumerThreads) {
+      const int t = i4 / (WS * 32), rem = i4 - t * WS * 32;
+      const int el = 8 * rem;  // rem = lane + 32*w4
+      if (el < Fs) xsb[i4] = __ldcg(reinterpret_cast<const uint4*>(a.act_s + static_cast<size_t>(t) * Fs + el));
+    }
+  }
+  consumer_sync(kConsumerThreads);
+
+  bool ok = true;
+  const unsigned expected = static_cast<unsigned>(n_active) + (Fs > 0 ? kDnRowsRouted / kDnRowsShared : 0u);
+  int it = 0;
+  for (int j = blockIdx.x; j < n_sh + n_r; j += gridDim.x, ++it) {
+    const int s = it % S;
+    if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteDnFull);
+    const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+    int blk;
+    if (j < n_sh) {  // shared: warp -> row j*8 + warp, whole Fs
+      const int row = j * kDnRowsShared + warp;
+      blk = row / kDnRowsRouted;
+      float acc[TT];
+#pragma unroll
+      for (int t = 0; t < TT; ++t) acc[t] = 0.f;
+      if (ok) {
+        const unsigned char* wr = st + static_cast<size_t>(warp) * Fs * 2;
+        for (int w4 = 0; w4 < WS; ++w4) {
+          const int el = 8 * (lane + 32 * w4);
+          if (el < Fs) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(wr + 2 * el);
+#pragma unroll
+            for (int t = 0; t < TT; ++t)
+              if (t < M) acc[t] = dot8_bf16(wv, xsb[t * WS * 32 + w4 * 32 + lane], acc[t]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+        for (int t = 0; t < TT; ++t) acc[t] = __fadd_rn(acc[t], __shfl_xor_sync(0xffffffffu, acc[t], off));
+      if (ok && lane < M) {
+        float v = acc[0];
+#pragma unroll
+        for (int t = 1; t < TT; ++t)
+          if (lane == t) v = acc[t];
+        a.ys[static_cast<size_t>(lane) * d + row] = f32_to_bf16(v);
+      }
+    } else {  // routed: rows r0 .. r0+31 of expert e; warp iteration covers `slots` rows
+      const int jr = j - n_sh;
+      const int e = __ldcg(a.active + 1 + jr / nrb);
+      const int r0 = (jr % nrb) * kDnRowsRouted;
+      blk = r0 / kDnRowsRouted;
+      const int p0 = __ldcg(a.offsets + e);
+      const int n = __ldcg(a.offsets + e + 1) - p0;
+      int slot_of[TT];
+#pragma unroll
+      for (int q = 0; q < TT; ++q) slot_of[q] = q < n ? __ldcg(a.perm + p0 + q) : 0;
+      const size_t pk = static_cast<size_t>(kDnRowsRouted) * (F >> 1);
+      for (int rl = warp * slots + slot; rl < kDnRowsRouted; rl += kConsumerWarps * slots) {
+        float acc[TT];
+#pragma unroll
+        for (int q = 0; q < TT; ++q) acc[q] = 0.f;
+        if (ok) {
+          const unsigned char* wp = st + static_cast<size_t>(rl) * (F >> 1);
+          const unsigned char* ws = st + pk + rl * G;
+          for (int qg = 0; qg < per_lane; ++qg) {
+            const int grp = sub + LPR * qg;
+            if (grp < G) {
+              const uint4 pkv = *reinterpret_cast<const uint4*>(wp + 16 * grp);
+              const float scl = e8m0_to_f32(ws[grp]);
+              const uint32_t w4v[4] = {pkv.x, pkv.y, pkv.z, pkv.w};
+              float gsum[TT];
+#pragma unroll
+              for (int q = 0; q < TT; ++q) gsum[q] = 0.f;
+#pragma unroll
+              for (int w = 0; w < 4; ++w)
+#pragma unroll
+                for (int q = 0; q < TT; ++q)
+                  if (q < n) gsum[q] = dot8_e2m1_f16(w4v[w], xr[((p0 + q) * 4 + w) * G + grp], gsum[q]);
+#pragma unroll
+              for (int q = 0; q < TT; ++q) acc[q] = __fmaf_rn(gsum[q], scl, acc[q]);
+            }
+          }
+        }
+#pragma unroll
+        for (int off = LPR / 2; off >= 1; off >>= 1)
+#pragma unroll
+          for (int q = 0; q < TT; ++q) acc[q] = __fadd_rn(acc[q], __shfl_xor_sync(0xffffffffu, acc[q], off));
+        if (ok && sub < TT && sub < n) {
+          float v = acc[0];
+          int sl = slot_of[0];
+#pragma unroll
+          for (int q = 1; q < TT; ++q)
+            if (sub == q) { v = acc[q]; sl = slot_of[q]; }
+          a.y[static_cast<size_t>(sl) * d + r0 + rl] = f32_to_bf16(__fmul_rn(v, rscale[p0 + sub]));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // ---- combine-block ticket: the chunk that completes block `blk` sums it ----
+    __threadfence();
+    consumer_sync(kConsumerThreads);
+    if (ct == 0) ticket_s = atomicAdd(a.tickets + blk, 1u);
+    consumer_sync(kConsumerThreads);
+    if (ticket_s == expected - 1) {
+      __threadfence();
+      for (int o = ct; o < kDnRowsRouted * M; o += kConsumerThreads) {
+        const int t = o / kDnRowsRouted, row = blk * kDnRowsRouted + (o - t * kDnRowsRouted);
+        float acc = 0.f;
+        for (int q = 0; q < k; ++q) {
+          const float wq = __ldcg(a.weights + static_cast<size_t>(t) * k + q);
+          const unsigned short yb =
+              __ldcg(reinterpret_cast<const unsigned short*>(a.y) + (static_cast<size_t>(t) * k + q) * d + row);
+          acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(yb), wq));
+        }
+        if (Fs > 0)
+          acc = __fadd_rn(acc, bf16_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(a.ys) +
+                                                 static_cast<size_t>(t) * d + row)));
+        a.out[static_cast<size_t>(t) * d + row] = acc;
+      }
+      if (ct == 0) a.tickets[blk] = 0u;
+    }
+  }
+}
+
+}  // namespace lg

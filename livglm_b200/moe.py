@@ -54,7 +54,10 @@ def _rows_bf16(hidden_states: torch.Tensor, hidden: int) -> torch.Tensor:
 
 
 class Workspace:
-    """Caller-owned scratch for the C ABI, grown outside the hot calls."""
+    """Caller-owned scratch for the C ABI, grown outside the hot calls.
+
+    Allocated zero-filled: its first 4 bytes are the library's device status
+    word (0 = ok; set when a bounded device wait gives up)."""
 
     def __init__(self) -> None:
         self.buf: torch.Tensor | None = None
@@ -64,8 +67,14 @@ class Workspace:
         if need == 0:
             _native.check(_native.LG_ERR_INVALID_ARG, "workspace size")
         if self.buf is None or self.buf.numel() < need or self.buf.device != device:
-            self.buf = torch.empty(need, dtype=torch.uint8, device=device)
+            self.buf = torch.zeros(need, dtype=torch.uint8, device=device)
         return self.buf.data_ptr(), self.buf.numel()
+
+    def status(self) -> int:
+        """The device status word (synchronises with the device)."""
+        if self.buf is None:
+            return 0
+        return int(self.buf[:4].view(torch.int32).item())
 
 
 def require_weight(value, name: str):
@@ -378,6 +387,11 @@ class ExpertSSDMoE:
         if return_route:
             return result, weights, indices
         return result
+
+    def device_status(self) -> int:
+        """Status word of this layer's workspace: 0, or LG_ERR_TIMEOUT | site << 8
+        if a bounded device wait gave up."""
+        return self._ws.status()
 
     @property
     def last_route_ids(self) -> tuple[int, ...]:

@@ -144,6 +144,7 @@ def test_forward_cfg1_decode(cfg1_layer, cuda, M):
     np.testing.assert_array_equal(to_numpy(idx), ref["indices"])
     np.testing.assert_array_equal(to_numpy(w).view(np.uint32), ref["weights"].view(np.uint32))
     assert_close(to_numpy(out), ref["out"])
+    assert moe.device_status() == 0
 
 
 @pytest.mark.parametrize("M", [256, 4096])
@@ -172,13 +173,14 @@ def test_combine_bit_exact_given_inputs(cfg1_layer, cuda):
     np.testing.assert_array_equal(to_numpy(out).view(np.uint32), ref.view(np.uint32))
 
 
-def test_forward_deterministic_and_shape_preserving(cfg1_layer, cuda):
+@pytest.mark.parametrize("M", [1, 2, 6])
+def test_forward_deterministic_and_shape_preserving(cfg1_layer, cuda, M):
     cfg, t, _ = cfg1_layer
     moe = build_layer(cfg, t)
-    x = synthetic.hidden_states(cfg, 6, seed=3, device=cuda).reshape(2, 3, cfg.hidden_size)
+    x = synthetic.hidden_states(cfg, 3 * M, seed=3, device=cuda).reshape(M, 3, cfg.hidden_size)
     a = moe(x)
     b = moe(x)
-    assert a.shape == (2, 3, cfg.hidden_size) and a.dtype == torch.float32
+    assert a.shape == (M, 3, cfg.hidden_size) and a.dtype == torch.float32
     assert torch.equal(a, b)
     empty = moe(x[:0])
     assert empty.shape == (0, 3, cfg.hidden_size)
