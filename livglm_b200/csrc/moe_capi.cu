@@ -332,7 +332,7 @@ bool plan_stream(const lg_moe_config* c, int M, int TT, StreamPlan* P) {
   const size_t gu_stage = std::max<size_t>(Fs > 0 ? 2 * lg::kGuRowsShared * d * 2 : 0,
                                            2 * lg::kGuRowsRouted * (d / 2) + 2 * lg::kGuRowsRouted * G);
   const size_t gu_x = TT * KI * 128 * 16 + TT * 4 * WPL * 32 * 16;
-  const size_t gu_aux = 2 * lg::kGuRowsShared * 4 * TT * 2 * 4;
+  const size_t gu_aux = lg::kGroups * 2 * lg::kGuRowsShared * 4 * TT * 2 * 4;
   const size_t gu_fixed = gu_x + gu_aux;
   if (gu_fixed + 2 * gu_stage > kSmemBudget) return false;
   P->gu.stages = static_cast<int>(std::min<size_t>(lg::kMaxStages, (kSmemBudget - gu_fixed) / gu_stage));

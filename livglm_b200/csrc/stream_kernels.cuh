@@ -1,8 +1,8 @@
 // Streaming expert kernels for decode shapes (M <= kDecodeMaxTokens), one CTA
 // per SM: a producer warp moves contiguous weight chunks (~32 KB) into a ring
-// of shared-memory stages with cp.async.bulk; 8 consumer warps compute from
-// shared memory.  With the whole ring in flight per SM, HBM latency is
-// covered without tying up registers.
+// of shared-memory stages with cp.async.bulk; two groups of 8 consumer warps
+// take alternate stages and compute from shared memory.  With the ring in
+// flight per SM, HBM latency is covered without tying up registers.
 //
 //   gate_up_stream_kernel  chunks: shared expert, 2 bf16 rows of gate and up
 //                          (4 warps per row, one K-quarter each); routed
@@ -12,9 +12,11 @@
 //                          the chunk that completes a 32-row block writes the
 //                          f32 combine of that block (moe.py:199-201)
 //
-// Chunk lists are [shared chunks..., routed chunks...] dealt round-robin over
-// the CTAs.  Shared chunks need no routing, so they run before
-// griddepcontrol.wait; routed chunks are enumerated after it.
+// Chunk it of a CTA is chunk j = blockIdx.x + it * gridDim.x of the list
+// [shared chunks..., routed chunks...]; consumer group it % 2 takes it.
+// Shared chunks need no routing, so they run before griddepcontrol.wait;
+// routed chunks are enumerated after it.  Each 32-column group is summed in
+// four independent word chains to keep the FMA pipes busy.
 //
 // Error handling: all mbarrier waits are bounded (pipeline.cuh).  A warp whose
 // wait gives up marks the status word and keeps walking the same chunk list
@@ -26,14 +28,18 @@
 
 namespace lg {
 
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 8;  // warps of one consumer group
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kStreamThreads = kConsumerThreads + 32;
+constexpr int kGroups = 2;  // consumer groups take alternate stages
+constexpr int kStreamThreads = kGroups * kConsumerThreads + 32;
+constexpr int kProducerWarp = kGroups * kConsumerWarps;
 constexpr int kMaxStages = 8;
 constexpr int kGuRowsRouted = 8;
 constexpr int kGuRowsShared = 2;
 constexpr int kDnRowsRouted = 32;
 constexpr int kDnRowsShared = 8;
+// named barriers: 1 + group (one consumer group), 3 (all consumers)
+constexpr int kBarAllConsumers = 3;
 
 struct StreamCfg {
   int stages;
@@ -41,6 +47,25 @@ struct StreamCfg {
   int x_off;    // byte offset of staged activations
   int aux_off;  // byte offset of the reduction / scale scratch
 };
+
+// sum of 32 E2M1 x f16 products of one group in four word chains
+template <int TT>
+__device__ __forceinline__ void group_dot_e2m1(const uint4& pw, const uint4* xv0, int xstride, int n,
+                                               float (&gsum)[TT]) {
+  const uint32_t w4[4] = {pw.x, pw.y, pw.z, pw.w};
+  float c[4][TT];
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int q = 0; q < TT; ++q) c[w][q] = 0.f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int q = 0; q < TT; ++q)
+      if (q < n) c[w][q] = dot8_e2m1_f16(w4[w], xv0[q * xstride + w * 32], c[w][q]);
+#pragma unroll
+  for (int q = 0; q < TT; ++q) gsum[q] = __fadd_rn(__fadd_rn(c[0][q], c[1][q]), __fadd_rn(c[2][q], c[3][q]));
+}
 
 // ---------------------------------------------------------------------------
 template <int TT>
@@ -50,15 +75,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
   __shared__ __align__(8) uint64_t empty[kMaxStages];
   __shared__ unsigned amax_bits[TT];
   __shared__ float tok_mult[TT];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = a.d, G = K >> 5, KI = (G + 31) >> 5;
   const int M = a.M, F = a.F, Fs = a.Fs;
   const int S = sc.stages;
-  const int KQ = K >> 2;                    // shared-chunk quarter width
-  const int WPL = (KQ / 8 + 31) / 32;       // 8-element words per lane per quarter
-  uint4* xh = reinterpret_cast<uint4*>(smem + sc.x_off);   // f16 [t][i][w][lane]
-  uint4* xb = xh + TT * KI * 128;                          // bf16 [t][q][w4][lane]
-  float* red = reinterpret_cast<float*>(smem + sc.aux_off);  // [2][2 rows][4 q][TT][2]
+  const int KQ = K >> 2;               // shared-chunk quarter width
+  const int WPL = (KQ / 8 + 31) / 32;  // 8-element words per lane per quarter
+  uint4* xh = reinterpret_cast<uint4*>(smem + sc.x_off);  // f16 [t][i][w][lane]
+  uint4* xb = xh + TT * KI * 128;                         // bf16 [t][q][w4][lane]
+  float* red = reinterpret_cast<float*>(smem + sc.aux_off);  // [group][2][2 rows][4 q][TT][2]
   const int n_sh = Fs > 0 ? Fs / kGuRowsShared : 0;
   const int nrb = F / kGuRowsRouted;
   if (threadIdx.x == 0) {
@@ -68,7 +93,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
   if (threadIdx.x < TT) amax_bits[threadIdx.x] = 0u;
   __syncthreads();
 
-  if (warp == kConsumerWarps) {  // ---------------- producer ----------------
+  if (warp_id == kProducerWarp) {  // -------------- producer --------------
     if (lane == 0) {
       bool ok = true;
       int it = 0;
@@ -115,11 +140,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
   }
 
   // ------------------------------- consumers -------------------------------
-  const int ct = threadIdx.x;  // 0 .. kConsumerThreads-1
+  const int grp = warp_id / kConsumerWarps;  // consumer group
+  const int warp = warp_id % kConsumerWarps;  // warp within the group
+  const int ct = threadIdx.x;                 // 0 .. kGroups*kConsumerThreads-1
+  constexpr int kAll = kGroups * kConsumerThreads;
   // stage bf16 rows for shared chunks: element qq*KQ + 8*(lane + 32*w4) + 0..7
   if (n_sh > 0) {
     const int per_row = 4 * WPL * 32;
-    for (int i4 = ct; i4 < M * per_row; i4 += kConsumerThreads) {
+    for (int i4 = ct; i4 < M * per_row; i4 += kAll) {
       const int t = i4 / per_row, rem = i4 - t * per_row;
       const int qq = rem / (WPL * 32), r2 = rem - qq * WPL * 32, w4 = r2 >> 5, ln = r2 & 31;
       const int el = 8 * (ln + 32 * w4);
@@ -128,19 +156,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
             *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + qq * KQ + el);
     }
   }
-  // stage f16 rows for routed chunks (with per-token power-of-two prescale)
-  for (int i4 = ct; i4 < M * G * 4; i4 += kConsumerThreads) {
-    const int t = i4 / (G * 4), rem = i4 - t * G * 4, c = rem >> 2;
+  // f16 rows for routed chunks, with a per-token power-of-two prescale
+  for (int i4 = ct; i4 < M * G * 4; i4 += kAll) {
+    const int t = i4 / (G * 4), rem = i4 - t * G * 4;
     const uint4 u = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + 8 * rem);
     float m = fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y))));
     m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
     atomicMax(amax_bits + t, __float_as_uint(m));
-    (void)c;
   }
-  consumer_sync(kConsumerThreads);
+  named_sync(kBarAllConsumers, kAll);
   if (ct < M) tok_mult[ct] = pow2i(f16_shift_for(__uint_as_float(amax_bits[ct])));
-  consumer_sync(kConsumerThreads);
-  for (int i4 = ct; i4 < M * G * 4; i4 += kConsumerThreads) {
+  named_sync(kBarAllConsumers, kAll);
+  for (int i4 = ct; i4 < M * G * 4; i4 += kAll) {
     const int t = i4 / (G * 4), rem = i4 - t * G * 4, c = rem >> 2, w = rem & 3;
     const uint4 u = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + 8 * rem);
     const float s = __fdiv_rn(1.0f, tok_mult[t]);
@@ -148,23 +175,27 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
         make_uint4(bf16x2_to_f16x2_scaled(u.x, s), bf16x2_to_f16x2_scaled(u.y, s),
                    bf16x2_to_f16x2_scaled(u.z, s), bf16x2_to_f16x2_scaled(u.w, s));
   }
-  consumer_sync(kConsumerThreads);
+  named_sync(kBarAllConsumers, kAll);
 
   bool ok = true;
-  int it = 0, shi = 0;
-  int j = blockIdx.x;
+  int shi = 0;
+  int it = grp;
+  int j = blockIdx.x + it * gridDim.x;
   // shared-expert chunks: rows 2j, 2j+1; warp -> (row w/4, K quarter w%4)
-  for (; j < n_sh; j += gridDim.x, ++it, ++shi) {
+  for (; j < n_sh; it += kGroups, j += kGroups * gridDim.x, ++shi) {
     const int s = it % S;
     if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteGuFull);
     const int rr = warp >> 2, qq = warp & 3;
-    float ag[TT], au[TT];
+    float ag[4][TT], au[4][TT];
 #pragma unroll
-    for (int t = 0; t < TT; ++t) { ag[t] = 0.f; au[t] = 0.f; }
+    for (int w = 0; w < 4; ++w)
+#pragma unroll
+      for (int t = 0; t < TT; ++t) { ag[w][t] = 0.f; au[w][t] = 0.f; }
     if (ok) {
       const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
       const unsigned char* gr = st + static_cast<size_t>(rr) * K * 2 + static_cast<size_t>(qq) * KQ * 2;
       const unsigned char* ur = gr + static_cast<size_t>(kGuRowsShared) * K * 2;
+#pragma unroll 4
       for (int w4 = 0; w4 < WPL; ++w4) {
         const int el = 8 * (lane + 32 * w4);
         if (el < KQ) {
@@ -174,30 +205,36 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
           for (int t = 0; t < TT; ++t)
             if (t < M) {
               const uint4 xv = xb[(t * 4 + qq) * WPL * 32 + w4 * 32 + lane];
-              ag[t] = dot8_bf16(wg, xv, ag[t]);
-              au[t] = dot8_bf16(wu, xv, au[t]);
+              ag[w4 & 3][t] = dot8_bf16(wg, xv, ag[w4 & 3][t]);
+              au[w4 & 3][t] = dot8_bf16(wu, xv, au[w4 & 3][t]);
             }
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+    float gt[TT], ut[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      gt[t] = __fadd_rn(__fadd_rn(ag[0][t], ag[1][t]), __fadd_rn(ag[2][t], ag[3][t]));
+      ut[t] = __fadd_rn(__fadd_rn(au[0][t], au[1][t]), __fadd_rn(au[2][t], au[3][t]));
+    }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1)
 #pragma unroll
       for (int t = 0; t < TT; ++t) {
-        ag[t] = __fadd_rn(ag[t], __shfl_xor_sync(0xffffffffu, ag[t], off));
-        au[t] = __fadd_rn(au[t], __shfl_xor_sync(0xffffffffu, au[t], off));
+        gt[t] = __fadd_rn(gt[t], __shfl_xor_sync(0xffffffffu, gt[t], off));
+        ut[t] = __fadd_rn(ut[t], __shfl_xor_sync(0xffffffffu, ut[t], off));
       }
-    float* rb = red + (shi & 1) * (kGuRowsShared * 4 * TT * 2);
+    float* rb = red + ((grp * 2 + (shi & 1)) * kGuRowsShared * 4 * TT * 2);
     if (lane == 0) {
 #pragma unroll
       for (int t = 0; t < TT; ++t) {
-        rb[((rr * 4 + qq) * TT + t) * 2 + 0] = ag[t];
-        rb[((rr * 4 + qq) * TT + t) * 2 + 1] = au[t];
+        rb[((rr * 4 + qq) * TT + t) * 2 + 0] = gt[t];
+        rb[((rr * 4 + qq) * TT + t) * 2 + 1] = ut[t];
       }
     }
-    consumer_sync(kConsumerThreads);
+    named_sync(1 + grp, kConsumerThreads);
     if (ok && warp < kGuRowsShared && lane < M) {
       float g = 0.f, u = 0.f;
       for (int q = 0; q < 4; ++q) {
@@ -211,7 +248,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
   pdl_wait();
   pdl_trigger();
   const int n_r = __ldcg(a.active) * nrb;
-  for (; j - n_sh < n_r; j += gridDim.x, ++it) {
+  for (; j - n_sh < n_r; it += kGroups, j += kGroups * gridDim.x) {
     const int s = it % S;
     if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteGuFull);
     const int jr = j - n_sh;
@@ -232,26 +269,33 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
       const unsigned char* up = gp + pk;
       const unsigned char* gs = st + 2 * pk + warp * G;
       const unsigned char* us = gs + kGuRowsRouted * G;
+#pragma unroll 2
       for (int i = 0; i < KI; ++i) {
         const int c = lane + 32 * i;
         if (c < G) {
           const uint4 pg = *reinterpret_cast<const uint4*>(gp + 16 * c);
           const uint4 pu = *reinterpret_cast<const uint4*>(up + 16 * c);
           const float s_g = e8m0_to_f32(gs[c]), s_u = e8m0_to_f32(us[c]);
-          const uint32_t wg4[4] = {pg.x, pg.y, pg.z, pg.w};
-          const uint32_t wu4[4] = {pu.x, pu.y, pu.z, pu.w};
+          const uint4* xv0 = xh + i * 128 + lane;
           float gg[TT], gu[TT];
+          // x of token tok[q] sits at xh[(tok*KI + i)*128 + w*32 + lane]
+          if (n == 1 || TT == 1) {
+            group_dot_e2m1<TT>(pg, xv0 + tok[0] * KI * 128, 0, n, gg);
+            group_dot_e2m1<TT>(pu, xv0 + tok[0] * KI * 128, 0, n, gu);
+          } else {
 #pragma unroll
-          for (int t = 0; t < TT; ++t) { gg[t] = 0.f; gu[t] = 0.f; }
-#pragma unroll
-          for (int w = 0; w < 4; ++w)
-#pragma unroll
-            for (int q = 0; q < TT; ++q)
+            for (int q = 0; q < TT; ++q) {
+              float g1[1], u1[1];
               if (q < n) {
-                const uint4 xv = xh[((tok[q] * KI + i) * 4 + w) * 32 + lane];
-                gg[q] = dot8_e2m1_f16(wg4[w], xv, gg[q]);
-                gu[q] = dot8_e2m1_f16(wu4[w], xv, gu[q]);
+                group_dot_e2m1<1>(pg, xv0 + tok[q] * KI * 128, 0, 1, g1);
+                group_dot_e2m1<1>(pu, xv0 + tok[q] * KI * 128, 0, 1, u1);
+              } else {
+                g1[0] = 0.f; u1[0] = 0.f;
               }
+              gg[q] = g1[0];
+              gu[q] = u1[0];
+            }
+          }
 #pragma unroll
           for (int q = 0; q < TT; ++q) {
             ag[q] = __fmaf_rn(gg[q], s_g, ag[q]);
@@ -288,8 +332,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages];
   __shared__ __align__(8) uint64_t empty[kMaxStages];
-  __shared__ unsigned ticket_s;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ unsigned ticket_s[kGroups];
+  const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int M = a.M, k = a.k, d = a.d, F = a.F, Fs = a.Fs;
   const int G = F >> 5;
   const int S = sc.stages;
@@ -302,7 +346,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   const int nrb = d / kDnRowsRouted;
   const int R = M * k;
   uint4* xr = reinterpret_cast<uint4*>(smem + sc.x_off);  // f16 [p][q4][grp]
-  uint4* xsb = xr + R * G * 4;                             // bf16 [t][w4][lane]
+  uint4* xsb = xr + R * G * 4;                            // bf16 [t][w4][lane]
   float* rscale = reinterpret_cast<float*>(smem + sc.aux_off);
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumerWarps); }
@@ -310,8 +354,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   }
   __syncthreads();
 
-  if (warp == kConsumerWarps) {  // ---------------- producer ----------------
-    // weights depend on nothing earlier and the routing tables are complete
+  if (warp_id == kProducerWarp) {  // -------------- producer --------------
+    // Weights depend on nothing earlier and the routing tables are complete
     // (the gate/up kernel waited on the router before letting this kernel
     // launch), so streaming starts before griddepcontrol.wait.
     if (lane == 0) {
@@ -349,13 +393,17 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   }
 
   // ------------------------------- consumers -------------------------------
+  const int grp = warp_id / kConsumerWarps;
+  const int warp = warp_id % kConsumerWarps;
   const int ct = threadIdx.x;
+  constexpr int kAll = kGroups * kConsumerThreads;
+  const int gt = ct - grp * kConsumerThreads;  // thread within the group
   pdl_wait();  // activations from the gate/up kernel
   pdl_trigger();
   const int n_active = __ldcg(a.active);
   const int n_r = n_active * nrb;
-  // stage routed activations as f16 with a per-route power-of-two prescale
-  for (int r = warp; r < R; r += kConsumerWarps) {
+  // routed activations as f16 with a per-route power-of-two prescale
+  for (int r = warp_id; r < R; r += kGroups * kConsumerWarps) {
     const uint16_t* src = a.act + static_cast<size_t>(r) * F;
     float m = 0.f;
     for (int v = lane; v < G * 4; v += 32) {
@@ -375,20 +423,20 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
                      bf16x2_to_f16x2_scaled(u.z, s), bf16x2_to_f16x2_scaled(u.w, s));
     }
   }
-  // stage shared activations (bf16) as [t][w4][lane], element 8*(lane + 32*w4)
+  // shared activations (bf16) as [t][w4][lane], element 8*(lane + 32*w4)
   if (Fs > 0) {
-    for (int i4 = ct; i4 < M * WS * 32; i4 += kConsumerThreads) {
+    for (int i4 = ct; i4 < M * WS * 32; i4 += kAll) {
       const int t = i4 / (WS * 32), rem = i4 - t * WS * 32;
-      const int el = 8 * rem;  // rem = lane + 32*w4
+      const int el = 8 * rem;
       if (el < Fs) xsb[i4] = __ldcg(reinterpret_cast<const uint4*>(a.act_s + static_cast<size_t>(t) * Fs + el));
     }
   }
-  consumer_sync(kConsumerThreads);
+  named_sync(kBarAllConsumers, kAll);
 
   bool ok = true;
   const unsigned expected = static_cast<unsigned>(n_active) + (Fs > 0 ? kDnRowsRouted / kDnRowsShared : 0u);
-  int it = 0;
-  for (int j = blockIdx.x; j < n_sh + n_r; j += gridDim.x, ++it) {
+  for (int it = grp, j = blockIdx.x + grp * gridDim.x; j < n_sh + n_r;
+       it += kGroups, j += kGroups * gridDim.x) {
     const int s = it % S;
     if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteDnFull);
     const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
@@ -396,35 +444,41 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
     if (j < n_sh) {  // shared: warp -> row j*8 + warp, whole Fs
       const int row = j * kDnRowsShared + warp;
       blk = row / kDnRowsRouted;
-      float acc[TT];
+      float acc[4][TT];
 #pragma unroll
-      for (int t = 0; t < TT; ++t) acc[t] = 0.f;
+      for (int w = 0; w < 4; ++w)
+#pragma unroll
+        for (int t = 0; t < TT; ++t) acc[w][t] = 0.f;
       if (ok) {
         const unsigned char* wr = st + static_cast<size_t>(warp) * Fs * 2;
+#pragma unroll 4
         for (int w4 = 0; w4 < WS; ++w4) {
           const int el = 8 * (lane + 32 * w4);
           if (el < Fs) {
             const uint4 wv = *reinterpret_cast<const uint4*>(wr + 2 * el);
 #pragma unroll
             for (int t = 0; t < TT; ++t)
-              if (t < M) acc[t] = dot8_bf16(wv, xsb[t * WS * 32 + w4 * 32 + lane], acc[t]);
+              if (t < M) acc[w4 & 3][t] = dot8_bf16(wv, xsb[t * WS * 32 + w4 * 32 + lane], acc[w4 & 3][t]);
           }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
+      float v[TT];
+#pragma unroll
+      for (int t = 0; t < TT; ++t) v[t] = __fadd_rn(__fadd_rn(acc[0][t], acc[1][t]), __fadd_rn(acc[2][t], acc[3][t]));
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1)
 #pragma unroll
-        for (int t = 0; t < TT; ++t) acc[t] = __fadd_rn(acc[t], __shfl_xor_sync(0xffffffffu, acc[t], off));
+        for (int t = 0; t < TT; ++t) v[t] = __fadd_rn(v[t], __shfl_xor_sync(0xffffffffu, v[t], off));
       if (ok && lane < M) {
-        float v = acc[0];
+        float o = v[0];
 #pragma unroll
         for (int t = 1; t < TT; ++t)
-          if (lane == t) v = acc[t];
-        a.ys[static_cast<size_t>(lane) * d + row] = f32_to_bf16(v);
+          if (lane == t) o = v[t];
+        a.ys[static_cast<size_t>(lane) * d + row] = f32_to_bf16(o);
       }
-    } else {  // routed: rows r0 .. r0+31 of expert e; warp iteration covers `slots` rows
+    } else {  // routed: rows r0 .. r0+31 of expert e; a warp iteration covers `slots` rows
       const int jr = j - n_sh;
       const int e = __ldcg(a.active + 1 + jr / nrb);
       const int r0 = (jr % nrb) * kDnRowsRouted;
@@ -442,20 +496,29 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
         if (ok) {
           const unsigned char* wp = st + static_cast<size_t>(rl) * (F >> 1);
           const unsigned char* ws = st + pk + rl * G;
+#pragma unroll 2
           for (int qg = 0; qg < per_lane; ++qg) {
-            const int grp = sub + LPR * qg;
-            if (grp < G) {
-              const uint4 pkv = *reinterpret_cast<const uint4*>(wp + 16 * grp);
-              const float scl = e8m0_to_f32(ws[grp]);
-              const uint32_t w4v[4] = {pkv.x, pkv.y, pkv.z, pkv.w};
+            const int gi = sub + LPR * qg;
+            if (gi < G) {
+              const uint4 pkv = *reinterpret_cast<const uint4*>(wp + 16 * gi);
+              const float scl = e8m0_to_f32(ws[gi]);
               float gsum[TT];
+              // x of route p0+q: xr[((p0+q)*4 + w)*G + gi]
+              const uint4* xv0 = xr + p0 * 4 * G + gi;
+              float c[4][TT];
 #pragma unroll
-              for (int q = 0; q < TT; ++q) gsum[q] = 0.f;
+              for (int w = 0; w < 4; ++w)
+#pragma unroll
+                for (int q = 0; q < TT; ++q) c[w][q] = 0.f;
+              const uint32_t w4v[4] = {pkv.x, pkv.y, pkv.z, pkv.w};
 #pragma unroll
               for (int w = 0; w < 4; ++w)
 #pragma unroll
                 for (int q = 0; q < TT; ++q)
-                  if (q < n) gsum[q] = dot8_e2m1_f16(w4v[w], xr[((p0 + q) * 4 + w) * G + grp], gsum[q]);
+                  if (q < n) c[w][q] = dot8_e2m1_f16(w4v[w], xv0[(q * 4 + w) * G], c[w][q]);
+#pragma unroll
+              for (int q = 0; q < TT; ++q)
+                gsum[q] = __fadd_rn(__fadd_rn(c[0][q], c[1][q]), __fadd_rn(c[2][q], c[3][q]));
 #pragma unroll
               for (int q = 0; q < TT; ++q) acc[q] = __fmaf_rn(gsum[q], scl, acc[q]);
             }
@@ -479,12 +542,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
     }
     // ---- combine-block ticket: the chunk that completes block `blk` sums it ----
     __threadfence();
-    consumer_sync(kConsumerThreads);
-    if (ct == 0) ticket_s = atomicAdd(a.tickets + blk, 1u);
-    consumer_sync(kConsumerThreads);
-    if (ticket_s == expected - 1) {
+    named_sync(1 + grp, kConsumerThreads);
+    if (gt == 0) ticket_s[grp] = atomicAdd(a.tickets + blk, 1u);
+    named_sync(1 + grp, kConsumerThreads);
+    if (ticket_s[grp] == expected - 1) {
       __threadfence();
-      for (int o = ct; o < kDnRowsRouted * M; o += kConsumerThreads) {
+      for (int o = gt; o < kDnRowsRouted * M; o += kConsumerThreads) {
         const int t = o / kDnRowsRouted, row = blk * kDnRowsRouted + (o - t * kDnRowsRouted);
         float acc = 0.f;
         for (int q = 0; q < k; ++q) {
@@ -498,8 +561,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
                                                  static_cast<size_t>(t) * d + row)));
         a.out[static_cast<size_t>(t) * d + row] = acc;
       }
-      if (ct == 0) a.tickets[blk] = 0u;
+      if (gt == 0) a.tickets[blk] = 0u;
     }
+    named_sync(1 + grp, kConsumerThreads);  // ticket_s reuse
   }
 }
 
