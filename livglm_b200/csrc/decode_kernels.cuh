@@ -90,27 +90,61 @@ struct DecodeArgs {
 };
 
 // ---------------------------------------------------------------------------
+// Router logits for decode: CTA = kRouterExperts warps = kRouterExperts
+// experts.  The CTA's router-weight rows (contiguous) are bulk-copied into
+// shared memory before griddepcontrol.wait, so they stream while the previous
+// kernel on the stream finishes; only x is read after the wait.  Lane l forms
+// the canonical partial over chunks l, l+32, ... then the xor butterfly.
+constexpr int kRouterExperts = 4;
 template <int TT>
-__global__ void __launch_bounds__(256) router_logits_decode_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(kRouterExperts * 32) router_logits_decode_kernel(DecodeArgs a) {
+  extern __shared__ __align__(128) unsigned char rsm[];
+  __shared__ __align__(8) uint64_t wbar;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int e = blockIdx.x * 8 + warp;
-  const bool live = e < a.E;
-  const float* wrow = a.Wr + static_cast<size_t>(live ? e : 0) * a.d;
-  if (live) {  // router weights do not depend on earlier kernels: pull them into L2 now
-    for (int line = lane; line < a.d / 32; line += 32)
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(wrow + 32 * line));
+  const int e0 = blockIdx.x * kRouterExperts;
+  const int ne = min(kRouterExperts, a.E - e0);
+  const float* ws = reinterpret_cast<const float*>(rsm);
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(&wbar))), "r"(1));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    const unsigned row = static_cast<unsigned>(a.d) * 4u;
+    const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&wbar));
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(row * ne) : "memory");
+    for (int r = 0; r < ne; ++r)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+                       "r"(static_cast<uint32_t>(__cvta_generic_to_shared(rsm + r * row))),
+                   "l"(a.Wr + static_cast<size_t>(e0 + r) * a.d), "r"(row), "r"(bar)
+                   : "memory");
   }
+  __syncthreads();
   pdl_wait();
   pdl_trigger();
-  if (!live) return;
+  // bounded wait for the weight rows
+  {
+    const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&wbar));
+    uint32_t done = 0;
+    unsigned long long t0 = 0;
+    for (;;) {
+      asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                   : "=r"(done) : "r"(bar) : "memory");
+      if (done) break;
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (!t0) t0 = t;
+      else if (t - t0 > 2000000000ull) { if (a.status) atomicExch(a.status, 6 | (7 << 8)); return; }
+    }
+  }
+  if (warp >= ne) return;
+  const int e = e0 + warp;
+  const float* wrow = ws + static_cast<size_t>(warp) * a.d;
   float acc[TT];
 #pragma unroll
   for (int t = 0; t < TT; ++t) acc[t] = 0.f;
   const int chunks = a.d >> 3;
 #pragma unroll 4
   for (int c = lane; c < chunks; c += 32) {
-    const float4* wp = reinterpret_cast<const float4*>(wrow + 8 * c);
-    const float4 w0 = wp[0], w1 = wp[1];
+    const float4 w0 = *reinterpret_cast<const float4*>(wrow + 8 * c);
+    const float4 w1 = *reinterpret_cast<const float4*>(wrow + 8 * c + 4);
     const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
@@ -157,7 +191,6 @@ __global__ void __launch_bounds__(256) router_select_dispatch_kernel(DecodeArgs 
   const int tid = threadIdx.x;
   pdl_trigger();
   pdl_wait();
-  for (int i = tid; i < n_tickets; i += blockDim.x) a.tickets[i] = 0u;
   const int per = E / G;
   const float ninf = __uint_as_float(0xff800000u);
   for (int t = 0; t < M; ++t) {
@@ -172,6 +205,7 @@ __global__ void __launch_bounds__(256) router_select_dispatch_kernel(DecodeArgs 
         const int g0 = (e / per) * per;
         const float v = ch[e];
         int r = 0;
+#pragma unroll 8
         for (int j = 0; j < per; ++j) r += after(ch[g0 + j], g0 + j, v, e);
         if (r == 0) gt1[e / per] = v;
         if (r == 1) gt2[e / per] = v;
@@ -192,6 +226,7 @@ __global__ void __launch_bounds__(256) router_select_dispatch_kernel(DecodeArgs 
     for (int e = tid; e < E; e += blockDim.x) {
       const float v = ch[e];
       int r = 0;
+#pragma unroll 8
       for (int j = 0; j < E; ++j) r += after(ch[j], j, v, e);
       if (r < k) {
         sel_e[t * k + (k - 1 - r)] = e;

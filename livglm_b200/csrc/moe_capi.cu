@@ -332,7 +332,8 @@ bool plan_stream(const lg_moe_config* c, int M, int TT, StreamPlan* P) {
   const size_t gu_stage = std::max<size_t>(Fs > 0 ? 2 * lg::kGuRowsShared * d * 2 : 0,
                                            2 * lg::kGuRowsRouted * (d / 2) + 2 * lg::kGuRowsRouted * G);
   const size_t gu_x = TT * KI * 128 * 16 + TT * 4 * WPL * 32 * 16;
-  const size_t gu_aux = lg::kGroups * 2 * lg::kGuRowsShared * 4 * TT * 2 * 4;
+  const size_t tables = (2 * (static_cast<size_t>(c->n_routed_experts) + 1) + R) * 4;
+  const size_t gu_aux = lg::kGroups * 2 * lg::kGuRowsShared * 4 * TT * 2 * 4 + tables;
   const size_t gu_fixed = gu_x + gu_aux;
   if (gu_fixed + 2 * gu_stage > kSmemBudget) return false;
   P->gu.stages = static_cast<int>(std::min<size_t>(lg::kMaxStages, (kSmemBudget - gu_fixed) / gu_stage));
@@ -344,7 +345,7 @@ bool plan_stream(const lg_moe_config* c, int M, int TT, StreamPlan* P) {
   const size_t dn_stage = std::max<size_t>(Fs > 0 ? lg::kDnRowsShared * Fs * 2 : 0,
                                            lg::kDnRowsRouted * (F / 2) + lg::kDnRowsRouted * GF);
   const size_t dn_x = R * F * 2 + static_cast<size_t>(M) * WS * 32 * 16;
-  const size_t dn_aux = ((R * 4 + 15) / 16) * 16;
+  const size_t dn_aux = ((R + 3) & ~size_t(3)) * 4 + tables;
   if (dn_x + dn_aux + 2 * dn_stage > kSmemBudget) return false;
   P->dn.stages = static_cast<int>(std::min<size_t>(lg::kMaxStages, (kSmemBudget - dn_x - dn_aux) / dn_stage));
   P->dn.stage_bytes = static_cast<int>(dn_stage);
@@ -359,6 +360,7 @@ bool plan_stream(const lg_moe_config* c, int M, int TT, StreamPlan* P) {
 bool decode_fits(const lg_moe_config* c, const lg_moe_weights* w, int64_t M) {
   if (M < 1 || M > lg::kDecodeMaxTokens) return false;
   if (c->hidden_size % 64) return false;
+  if (static_cast<size_t>(lg::kRouterExperts) * c->hidden_size * 4 > 200 * 1024) return false;
   if (c->num_experts_per_tok * M > lg::kDecodeMaxTokens * 32) return false;
   if (!aligned(w->gate_scale, 16) || !aligned(w->up_scale, 16) || !aligned(w->down_scale, 16)) return false;
   if (w->gate_scale_stride % 16 || w->up_scale_stride % 16 || w->down_scale_stride % 16) return false;
@@ -398,7 +400,10 @@ int launch_decode_t(const lg_moe_config* c, const lg_moe_weights* w, const uint1
   const bool pdl = slot < 0;
   cudaError_t e;
   // 1. router logits
-  e = launch_ex(router_logits_decode_kernel<TT>, dim3((E + 7) / 8), dim3(256), 0, s, pdl, a);
+  const size_t smem_rl = static_cast<size_t>(kRouterExperts) * d * 4;
+  occupancy(router_logits_decode_kernel<TT>, kRouterExperts * 32, smem_rl);
+  e = launch_ex(router_logits_decode_kernel<TT>, dim3((E + kRouterExperts - 1) / kRouterExperts),
+                dim3(kRouterExperts * 32), smem_rl, s, pdl, a);
   if (e != cudaSuccess) return cuda_check(e, "router logits launch");
   // 2. select + dispatch
   const int G = c->n_group;
@@ -417,6 +422,11 @@ int launch_decode_t(const lg_moe_config* c, const lg_moe_weights* w, const uint1
   e = launch_ex(down_stream_kernel<TT>, dim3(sms), dim3(kStreamThreads), P.dn_smem, s, pdl, a, P.dn);
   if (e != cudaSuccess) return cuda_check(e, "down launch");
   trace_mark(slot, 4, s);
+  // 5. combine
+  const int n4 = M * (d / 4);
+  e = launch_ex(combine_decode_kernel, dim3((n4 + 255) / 256 < 2 * sms ? (n4 + 255) / 256 : 2 * sms), dim3(256), 0, s,
+                pdl, a);
+  if (e != cudaSuccess) return cuda_check(e, "combine launch");
   trace_mark(slot, 5, s);
   return LG_OK;
 }

@@ -8,9 +8,11 @@
 //                          (4 warps per row, one K-quarter each); routed
 //                          experts, 8 MXFP4 rows of gate and up (warp per row)
 //   down_stream_kernel     chunks: shared expert, 8 bf16 rows (warp per row);
-//                          routed experts, 32 MXFP4 rows (LPR lanes per row);
-//                          the chunk that completes a 32-row block writes the
-//                          f32 combine of that block (moe.py:199-201)
+//                          routed experts, 32 MXFP4 rows (LPR lanes per row)
+//   combine_decode_kernel  f32 merge of routed rows and shared row
+//
+// The producer warp copies the routing tables into shared memory once per
+// CTA and hands them to the consumers through an mbarrier.
 //
 // Chunk it of a CTA is chunk j = blockIdx.x + it * gridDim.x of the list
 // [shared chunks..., routed chunks...]; consumer group it % 2 takes it.
@@ -48,6 +50,18 @@ struct StreamCfg {
   int aux_off;  // byte offset of the reduction / scale scratch
 };
 
+// Copy the routing tables (active list, offsets, perm) into shared memory
+// with the 32 lanes of the calling warp, then arrive on `bar` (count 1).
+__device__ __forceinline__ void copy_tables(const DecodeArgs& a, int* s_active, int* s_offsets, int* s_perm,
+                                            int lane, uint64_t* bar) {
+  const int n_active = __ldcg(a.active);
+  for (int i = lane; i <= n_active; i += 32) s_active[i] = __ldcg(a.active + i);
+  for (int i = lane; i <= a.E; i += 32) s_offsets[i] = __ldcg(a.offsets + i);
+  for (int i = lane; i < a.M * a.k; i += 32) s_perm[i] = __ldcg(a.perm + i);
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
+
 // sum of 32 E2M1 x f16 products of one group in four word chains
 template <int TT>
 __device__ __forceinline__ void group_dot_e2m1(const uint4& pw, const uint4* xv0, int xstride, int n,
@@ -84,20 +98,25 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
   uint4* xh = reinterpret_cast<uint4*>(smem + sc.x_off);  // f16 [t][i][w][lane]
   uint4* xb = xh + TT * KI * 128;                         // bf16 [t][q][w4][lane]
   float* red = reinterpret_cast<float*>(smem + sc.aux_off);  // [group][2][2 rows][4 q][TT][2]
+  int* s_active = reinterpret_cast<int*>(red + kGroups * 2 * kGuRowsShared * 4 * TT * 2);
+  int* s_offsets = s_active + a.E + 1;
+  int* s_perm = s_offsets + a.E + 1;
+  __shared__ __align__(8) uint64_t tbl;
   const int n_sh = Fs > 0 ? Fs / kGuRowsShared : 0;
   const int nrb = F / kGuRowsRouted;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumerWarps); }
+    mbar_init(&tbl, 1);
     mbar_fence_init();
   }
   if (threadIdx.x < TT) amax_bits[threadIdx.x] = 0u;
   __syncthreads();
 
   if (warp_id == kProducerWarp) {  // -------------- producer --------------
+    bool ok = true;
+    int it = 0;
+    int j = blockIdx.x;
     if (lane == 0) {
-      bool ok = true;
-      int it = 0;
-      int j = blockIdx.x;
       const unsigned sh_bytes = kGuRowsShared * K * 2;
       for (; j < n_sh; j += gridDim.x, ++it) {
         const int s = it % S;
@@ -109,9 +128,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
         bulk_g2s(st, a.sh_gate + static_cast<size_t>(j) * kGuRowsShared * K, sh_bytes, &full[s]);
         bulk_g2s(st + sh_bytes, a.sh_up + static_cast<size_t>(j) * kGuRowsShared * K, sh_bytes, &full[s]);
       }
-      pdl_wait();
-      pdl_trigger();
-      const int n_r = __ldcg(a.active) * nrb;
+    }
+    __syncwarp();
+    pdl_wait();  // routing tables written by the router
+    pdl_trigger();
+    copy_tables(a, s_active, s_offsets, s_perm, lane, &tbl);
+    if (lane == 0) {
+      const int n_r = s_active[0] * nrb;
       const unsigned pk = kGuRowsRouted * (K >> 1), sk = kGuRowsRouted * G;
       for (; j - n_sh < n_r; j += gridDim.x, ++it) {
         const int s = it % S;
@@ -119,7 +142,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
         if (ok && round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, a.status, kSiteGuEmpty);
         if (!ok) continue;
         const int jr = j - n_sh;
-        const int e = __ldcg(a.active + 1 + jr / nrb);
+        const int e = s_active[1 + jr / nrb];
         const size_t f0 = static_cast<size_t>(jr % nrb) * kGuRowsRouted;
         unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
         mbar_arrive_expect_tx(&full[s], 2 * pk + 2 * sk);
@@ -132,9 +155,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
         for (int q = (it > S ? it - S : 0); q < it; ++q)
           mbar_wait(&full[q % S], (q / S) & 1, a.status, kSiteGuDrain);
       }
-    } else {
-      pdl_wait();
-      pdl_trigger();
     }
     return;
   }
@@ -195,19 +215,22 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
       const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
       const unsigned char* gr = st + static_cast<size_t>(rr) * K * 2 + static_cast<size_t>(qq) * KQ * 2;
       const unsigned char* ur = gr + static_cast<size_t>(kGuRowsShared) * K * 2;
-#pragma unroll 4
-      for (int w4 = 0; w4 < WPL; ++w4) {
-        const int el = 8 * (lane + 32 * w4);
-        if (el < KQ) {
-          const uint4 wg = *reinterpret_cast<const uint4*>(gr + 2 * el);
-          const uint4 wu = *reinterpret_cast<const uint4*>(ur + 2 * el);
+      for (int w0 = 0; w0 < WPL; w0 += 4) {
 #pragma unroll
-          for (int t = 0; t < TT; ++t)
-            if (t < M) {
-              const uint4 xv = xb[(t * 4 + qq) * WPL * 32 + w4 * 32 + lane];
-              ag[w4 & 3][t] = dot8_bf16(wg, xv, ag[w4 & 3][t]);
-              au[w4 & 3][t] = dot8_bf16(wu, xv, au[w4 & 3][t]);
-            }
+        for (int u4 = 0; u4 < 4; ++u4) {
+          const int w4 = w0 + u4;
+          const int el = 8 * (lane + 32 * w4);
+          if (w4 < WPL && el < KQ) {
+            const uint4 wg = *reinterpret_cast<const uint4*>(gr + 2 * el);
+            const uint4 wu = *reinterpret_cast<const uint4*>(ur + 2 * el);
+#pragma unroll
+            for (int t = 0; t < TT; ++t)
+              if (t < M) {
+                const uint4 xv = xb[(t * 4 + qq) * WPL * 32 + w4 * 32 + lane];
+                ag[u4][t] = dot8_bf16(wg, xv, ag[u4][t]);
+                au[u4][t] = dot8_bf16(wu, xv, au[u4][t]);
+              }
+          }
         }
       }
     }
@@ -247,18 +270,19 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
   }
   pdl_wait();
   pdl_trigger();
-  const int n_r = __ldcg(a.active) * nrb;
+  if (ok) ok = mbar_wait(&tbl, 0, a.status, kSiteGuFull);
+  const int n_r = ok ? s_active[0] * nrb : 0;
   for (; j - n_sh < n_r; it += kGroups, j += kGroups * gridDim.x) {
     const int s = it % S;
     if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteGuFull);
     const int jr = j - n_sh;
-    const int e = __ldcg(a.active + 1 + jr / nrb);
+    const int e = s_active[1 + jr / nrb];
     const int f = (jr % nrb) * kGuRowsRouted + warp;
-    const int p0 = __ldcg(a.offsets + e);
-    const int n = __ldcg(a.offsets + e + 1) - p0;
+    const int p0 = s_offsets[e];
+    const int n = s_offsets[e + 1] - p0;
     int tok[TT];
 #pragma unroll
-    for (int q = 0; q < TT; ++q) tok[q] = q < n ? __ldcg(a.perm + p0 + q) / a.k : 0;
+    for (int q = 0; q < TT; ++q) tok[q] = q < n ? s_perm[p0 + q] / a.k : 0;
     float ag[TT], au[TT];
 #pragma unroll
     for (int t = 0; t < TT; ++t) { ag[t] = 0.f; au[t] = 0.f; }
@@ -332,7 +356,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages];
   __shared__ __align__(8) uint64_t empty[kMaxStages];
-  __shared__ unsigned ticket_s[kGroups];
   const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int M = a.M, k = a.k, d = a.d, F = a.F, Fs = a.Fs;
   const int G = F >> 5;
@@ -348,8 +371,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   uint4* xr = reinterpret_cast<uint4*>(smem + sc.x_off);  // f16 [p][q4][grp]
   uint4* xsb = xr + R * G * 4;                            // bf16 [t][w4][lane]
   float* rscale = reinterpret_cast<float*>(smem + sc.aux_off);
+  int* s_active = reinterpret_cast<int*>(rscale + ((R + 3) & ~3));
+  int* s_offsets = s_active + a.E + 1;
+  int* s_perm = s_offsets + a.E + 1;
+  __shared__ __align__(8) uint64_t tbl;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumerWarps); }
+    mbar_init(&tbl, 1);
     mbar_fence_init();
   }
   __syncthreads();
@@ -358,10 +386,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
     // Weights depend on nothing earlier and the routing tables are complete
     // (the gate/up kernel waited on the router before letting this kernel
     // launch), so streaming starts before griddepcontrol.wait.
+    copy_tables(a, s_active, s_offsets, s_perm, lane, &tbl);
     if (lane == 0) {
       bool ok = true;
       int it = 0;
-      const int n_r = __ldcg(a.active) * nrb;
+      const int n_r = s_active[0] * nrb;
       const unsigned shb = kDnRowsShared * Fs * 2;
       const unsigned pk = kDnRowsRouted * (F >> 1), sk = kDnRowsRouted * G;
       for (int j = blockIdx.x; j < n_sh + n_r; j += gridDim.x, ++it) {
@@ -375,7 +404,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
           bulk_g2s(st, a.sh_down + static_cast<size_t>(j) * kDnRowsShared * Fs, shb, &full[s]);
         } else {
           const int jr = j - n_sh;
-          const int e = __ldcg(a.active + 1 + jr / nrb);
+          const int e = s_active[1 + jr / nrb];
           const size_t r0 = static_cast<size_t>(jr % nrb) * kDnRowsRouted;
           mbar_arrive_expect_tx(&full[s], pk + sk);
           bulk_g2s(st, a.down_p + e * a.down_ps + r0 * (F >> 1), pk, &full[s]);
@@ -397,10 +426,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   const int warp = warp_id % kConsumerWarps;
   const int ct = threadIdx.x;
   constexpr int kAll = kGroups * kConsumerThreads;
-  const int gt = ct - grp * kConsumerThreads;  // thread within the group
   pdl_wait();  // activations from the gate/up kernel
   pdl_trigger();
-  const int n_active = __ldcg(a.active);
+  bool ok = mbar_wait(&tbl, 0, a.status, kSiteDnFull);
+  const int n_active = ok ? s_active[0] : 0;
   const int n_r = n_active * nrb;
   // routed activations as f16 with a per-route power-of-two prescale
   for (int r = warp_id; r < R; r += kGroups * kConsumerWarps) {
@@ -433,17 +462,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   }
   named_sync(kBarAllConsumers, kAll);
 
-  bool ok = true;
-  const unsigned expected = static_cast<unsigned>(n_active) + (Fs > 0 ? kDnRowsRouted / kDnRowsShared : 0u);
   for (int it = grp, j = blockIdx.x + grp * gridDim.x; j < n_sh + n_r;
        it += kGroups, j += kGroups * gridDim.x) {
     const int s = it % S;
     if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteDnFull);
     const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
-    int blk;
     if (j < n_sh) {  // shared: warp -> row j*8 + warp, whole Fs
       const int row = j * kDnRowsShared + warp;
-      blk = row / kDnRowsRouted;
       float acc[4][TT];
 #pragma unroll
       for (int w = 0; w < 4; ++w)
@@ -451,14 +476,17 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
         for (int t = 0; t < TT; ++t) acc[w][t] = 0.f;
       if (ok) {
         const unsigned char* wr = st + static_cast<size_t>(warp) * Fs * 2;
-#pragma unroll 4
-        for (int w4 = 0; w4 < WS; ++w4) {
-          const int el = 8 * (lane + 32 * w4);
-          if (el < Fs) {
-            const uint4 wv = *reinterpret_cast<const uint4*>(wr + 2 * el);
+        for (int w0 = 0; w0 < WS; w0 += 4) {
 #pragma unroll
-            for (int t = 0; t < TT; ++t)
-              if (t < M) acc[w4 & 3][t] = dot8_bf16(wv, xsb[t * WS * 32 + w4 * 32 + lane], acc[w4 & 3][t]);
+          for (int u4 = 0; u4 < 4; ++u4) {
+            const int w4 = w0 + u4;
+            const int el = 8 * (lane + 32 * w4);
+            if (w4 < WS && el < Fs) {
+              const uint4 wv = *reinterpret_cast<const uint4*>(wr + 2 * el);
+#pragma unroll
+              for (int t = 0; t < TT; ++t)
+                if (t < M) acc[u4][t] = dot8_bf16(wv, xsb[t * WS * 32 + w4 * 32 + lane], acc[u4][t]);
+            }
           }
         }
       }
@@ -480,14 +508,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
       }
     } else {  // routed: rows r0 .. r0+31 of expert e; a warp iteration covers `slots` rows
       const int jr = j - n_sh;
-      const int e = __ldcg(a.active + 1 + jr / nrb);
+      const int e = s_active[1 + jr / nrb];
       const int r0 = (jr % nrb) * kDnRowsRouted;
-      blk = r0 / kDnRowsRouted;
-      const int p0 = __ldcg(a.offsets + e);
-      const int n = __ldcg(a.offsets + e + 1) - p0;
+      const int p0 = s_offsets[e];
+      const int n = s_offsets[e + 1] - p0;
       int slot_of[TT];
 #pragma unroll
-      for (int q = 0; q < TT; ++q) slot_of[q] = q < n ? __ldcg(a.perm + p0 + q) : 0;
+      for (int q = 0; q < TT; ++q) slot_of[q] = q < n ? s_perm[p0 + q] : 0;
       const size_t pk = static_cast<size_t>(kDnRowsRouted) * (F >> 1);
       for (int rl = warp * slots + slot; rl < kDnRowsRouted; rl += kConsumerWarps * slots) {
         float acc[TT];
@@ -540,30 +567,34 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
-    // ---- combine-block ticket: the chunk that completes block `blk` sums it ----
-    __threadfence();
-    named_sync(1 + grp, kConsumerThreads);
-    if (gt == 0) ticket_s[grp] = atomicAdd(a.tickets + blk, 1u);
-    named_sync(1 + grp, kConsumerThreads);
-    if (ticket_s[grp] == expected - 1) {
-      __threadfence();
-      for (int o = gt; o < kDnRowsRouted * M; o += kConsumerThreads) {
-        const int t = o / kDnRowsRouted, row = blk * kDnRowsRouted + (o - t * kDnRowsRouted);
-        float acc = 0.f;
-        for (int q = 0; q < k; ++q) {
-          const float wq = __ldcg(a.weights + static_cast<size_t>(t) * k + q);
-          const unsigned short yb =
-              __ldcg(reinterpret_cast<const unsigned short*>(a.y) + (static_cast<size_t>(t) * k + q) * d + row);
-          acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(yb), wq));
-        }
-        if (Fs > 0)
-          acc = __fadd_rn(acc, bf16_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(a.ys) +
-                                                 static_cast<size_t>(t) * d + row)));
-        a.out[static_cast<size_t>(t) * d + row] = acc;
-      }
-      if (gt == 0) a.tickets[blk] = 0u;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// f32 merge of the routed rows (route order) and the shared row, moe.py:199-201.
+__global__ void __launch_bounds__(256) combine_decode_kernel(DecodeArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int d = a.d, k = a.k;
+  for (int o = blockIdx.x * blockDim.x + threadIdx.x; o < a.M * (d >> 2); o += gridDim.x * blockDim.x) {
+    const int t = o / (d >> 2), c = o - t * (d >> 2);
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    for (int q = 0; q < k; ++q) {
+      const float wq = __ldcg(a.weights + static_cast<size_t>(t) * k + q);
+      const uint2 u = __ldcg(reinterpret_cast<const uint2*>(a.y + (static_cast<size_t>(t) * k + q) * d + 4 * c));
+      s0 = __fadd_rn(s0, __fmul_rn(bf16lo(u.x), wq));
+      s1 = __fadd_rn(s1, __fmul_rn(bf16hi(u.x), wq));
+      s2 = __fadd_rn(s2, __fmul_rn(bf16lo(u.y), wq));
+      s3 = __fadd_rn(s3, __fmul_rn(bf16hi(u.y), wq));
     }
-    named_sync(1 + grp, kConsumerThreads);  // ticket_s reuse
+    if (a.Fs > 0) {
+      const uint2 u = __ldcg(reinterpret_cast<const uint2*>(a.ys + static_cast<size_t>(t) * d + 4 * c));
+      s0 = __fadd_rn(s0, bf16lo(u.x));
+      s1 = __fadd_rn(s1, bf16hi(u.x));
+      s2 = __fadd_rn(s2, bf16lo(u.y));
+      s3 = __fadd_rn(s3, bf16hi(u.y));
+    }
+    reinterpret_cast<float4*>(a.out)[o] = make_float4(s0, s1, s2, s3);
   }
 }
 
