@@ -332,7 +332,7 @@ bool plan_stream(const lg_moe_config* c, int M, int TT, StreamPlan* P) {
   const size_t gu_stage = std::max<size_t>(Fs > 0 ? 2 * lg::kGuRowsShared * d * 2 : 0,
                                            2 * lg::kGuRowsRouted * (d / 2) + 2 * lg::kGuRowsRouted * G);
   const size_t gu_x = TT * KI * 128 * 16 + TT * 4 * WPL * 32 * 16;
-  const size_t tables = (2 * (static_cast<size_t>(c->n_routed_experts) + 1) + R) * 4;
+  const size_t tables = (2 * ((static_cast<size_t>(c->n_routed_experts) + 1 + 3) & ~size_t(3)) + R + 4) * 4;
   const size_t gu_aux = lg::kGroups * 2 * lg::kGuRowsShared * 4 * TT * 2 * 4 + tables;
   const size_t gu_fixed = gu_x + gu_aux;
   if (gu_fixed + 2 * gu_stage > kSmemBudget) return false;
@@ -361,6 +361,8 @@ bool decode_fits(const lg_moe_config* c, const lg_moe_weights* w, int64_t M) {
   if (M < 1 || M > lg::kDecodeMaxTokens) return false;
   if (c->hidden_size % 64) return false;
   if (static_cast<size_t>(lg::kRouterExperts) * c->hidden_size * 4 > 200 * 1024) return false;
+  // register-staged activation rows: d*M/8 <= 4 * 512 uint4, F/8 <= 8 * 32
+  if (static_cast<size_t>(c->hidden_size) * M / 8 > 4 * 512 || c->moe_intermediate_size / 8 > 8 * 32) return false;
   if (c->num_experts_per_tok * M > lg::kDecodeMaxTokens * 32) return false;
   if (!aligned(w->gate_scale, 16) || !aligned(w->up_scale, 16) || !aligned(w->down_scale, 16)) return false;
   if (w->gate_scale_stride % 16 || w->up_scale_stride % 16 || w->down_scale_stride % 16) return false;

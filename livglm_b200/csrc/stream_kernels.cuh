@@ -50,16 +50,17 @@ struct StreamCfg {
   int aux_off;  // byte offset of the reduction / scale scratch
 };
 
-// Copy the routing tables (active list, offsets, perm) into shared memory
-// with the 32 lanes of the calling warp, then arrive on `bar` (count 1).
+// Bulk-copy the routing tables (active list, offsets, perm) into shared
+// memory; completion is signalled on `bar`.  Sizes are rounded up to 16 bytes
+// (the workspace pads every region to 256 bytes, so the tail reads stay inside
+// it).  Called by one thread.
 __device__ __forceinline__ void copy_tables(const DecodeArgs& a, int* s_active, int* s_offsets, int* s_perm,
-                                            int lane, uint64_t* bar) {
-  const int n_active = __ldcg(a.active);
-  for (int i = lane; i <= n_active; i += 32) s_active[i] = __ldcg(a.active + i);
-  for (int i = lane; i <= a.E; i += 32) s_offsets[i] = __ldcg(a.offsets + i);
-  for (int i = lane; i < a.M * a.k; i += 32) s_perm[i] = __ldcg(a.perm + i);
-  __syncwarp();
-  if (lane == 0) mbar_arrive(bar);
+                                            uint64_t* bar) {
+  const unsigned na = ((a.E + 1) * 4 + 15) & ~15u, no = na, np = ((a.M * a.k) * 4 + 15) & ~15u;
+  mbar_arrive_expect_tx(bar, na + no + np);
+  bulk_g2s(s_active, a.active, na, bar);
+  bulk_g2s(s_offsets, a.offsets, no, bar);
+  bulk_g2s(s_perm, a.perm, np, bar);
 }
 
 // sum of 32 E2M1 x f16 products of one group in four word chains
@@ -99,8 +100,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
   uint4* xb = xh + TT * KI * 128;                         // bf16 [t][q][w4][lane]
   float* red = reinterpret_cast<float*>(smem + sc.aux_off);  // [group][2][2 rows][4 q][TT][2]
   int* s_active = reinterpret_cast<int*>(red + kGroups * 2 * kGuRowsShared * 4 * TT * 2);
-  int* s_offsets = s_active + a.E + 1;
-  int* s_perm = s_offsets + a.E + 1;
+  int* s_offsets = s_active + (((a.E + 1) + 3) & ~3);
+  int* s_perm = s_offsets + (((a.E + 1) + 3) & ~3);
   __shared__ __align__(8) uint64_t tbl;
   const int n_sh = Fs > 0 ? Fs / kGuRowsShared : 0;
   const int nrb = F / kGuRowsRouted;
@@ -132,9 +133,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
     __syncwarp();
     pdl_wait();  // routing tables written by the router
     pdl_trigger();
-    copy_tables(a, s_active, s_offsets, s_perm, lane, &tbl);
     if (lane == 0) {
-      const int n_r = s_active[0] * nrb;
+      copy_tables(a, s_active, s_offsets, s_perm, &tbl);
+      if (ok) ok = mbar_wait(&tbl, 0, a.status, kSiteGuEmpty);
+      const int n_r = ok ? s_active[0] * nrb : 0;
       const unsigned pk = kGuRowsRouted * (K >> 1), sk = kGuRowsRouted * G;
       for (; j - n_sh < n_r; j += gridDim.x, ++it) {
         const int s = it % S;
@@ -176,24 +178,42 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
             *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + qq * KQ + el);
     }
   }
-  // f16 rows for routed chunks, with a per-token power-of-two prescale
-  for (int i4 = ct; i4 < M * G * 4; i4 += kAll) {
-    const int t = i4 / (G * 4), rem = i4 - t * G * 4;
-    const uint4 u = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + 8 * rem);
-    float m = fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y))));
-    m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
-    atomicMax(amax_bits + t, __float_as_uint(m));
+  // f16 rows for routed chunks, with a per-token power-of-two prescale:
+  // one load per element into registers, block max, then convert
+  constexpr int kStageRegs = 4;  // uint4 per thread held across the max (M*G*4 <= 4*kAll)
+  uint4 xr[kStageRegs];
+#pragma unroll
+  for (int q = 0; q < kStageRegs; ++q) {
+    const int i4 = ct + q * kAll;
+    if (i4 < M * G * 4) {
+      const int t = i4 / (G * 4), rem = i4 - t * G * 4;
+      xr[q] = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + 8 * rem);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < kStageRegs; ++q) {
+    const int i4 = ct + q * kAll;
+    if (i4 < M * G * 4) {
+      const uint4 u = xr[q];
+      float m = fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y))));
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
+      atomicMax(amax_bits + i4 / (G * 4), __float_as_uint(m));
+    }
   }
   named_sync(kBarAllConsumers, kAll);
   if (ct < M) tok_mult[ct] = pow2i(f16_shift_for(__uint_as_float(amax_bits[ct])));
   named_sync(kBarAllConsumers, kAll);
-  for (int i4 = ct; i4 < M * G * 4; i4 += kAll) {
-    const int t = i4 / (G * 4), rem = i4 - t * G * 4, c = rem >> 2, w = rem & 3;
-    const uint4 u = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + 8 * rem);
-    const float s = __fdiv_rn(1.0f, tok_mult[t]);
-    xh[((t * KI + (c >> 5)) * 4 + w) * 32 + (c & 31)] =
-        make_uint4(bf16x2_to_f16x2_scaled(u.x, s), bf16x2_to_f16x2_scaled(u.y, s),
-                   bf16x2_to_f16x2_scaled(u.z, s), bf16x2_to_f16x2_scaled(u.w, s));
+#pragma unroll
+  for (int q = 0; q < kStageRegs; ++q) {
+    const int i4 = ct + q * kAll;
+    if (i4 < M * G * 4) {
+      const int t = i4 / (G * 4), rem = i4 - t * G * 4, c = rem >> 2, w = rem & 3;
+      const uint4 u = xr[q];
+      const float sc2 = __fdiv_rn(1.0f, tok_mult[t]);
+      xh[((t * KI + (c >> 5)) * 4 + w) * 32 + (c & 31)] =
+          make_uint4(bf16x2_to_f16x2_scaled(u.x, sc2), bf16x2_to_f16x2_scaled(u.y, sc2),
+                     bf16x2_to_f16x2_scaled(u.z, sc2), bf16x2_to_f16x2_scaled(u.w, sc2));
+    }
   }
   named_sync(kBarAllConsumers, kAll);
 
@@ -372,8 +392,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   uint4* xsb = xr + R * G * 4;                            // bf16 [t][w4][lane]
   float* rscale = reinterpret_cast<float*>(smem + sc.aux_off);
   int* s_active = reinterpret_cast<int*>(rscale + ((R + 3) & ~3));
-  int* s_offsets = s_active + a.E + 1;
-  int* s_perm = s_offsets + a.E + 1;
+  int* s_offsets = s_active + (((a.E + 1) + 3) & ~3);
+  int* s_perm = s_offsets + (((a.E + 1) + 3) & ~3);
   __shared__ __align__(8) uint64_t tbl;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumerWarps); }
@@ -386,11 +406,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
     // Weights depend on nothing earlier and the routing tables are complete
     // (the gate/up kernel waited on the router before letting this kernel
     // launch), so streaming starts before griddepcontrol.wait.
-    copy_tables(a, s_active, s_offsets, s_perm, lane, &tbl);
     if (lane == 0) {
-      bool ok = true;
+      copy_tables(a, s_active, s_offsets, s_perm, &tbl);
+      bool ok = mbar_wait(&tbl, 0, a.status, kSiteDnEmpty);
       int it = 0;
-      const int n_r = s_active[0] * nrb;
+      const int n_r = ok ? s_active[0] * nrb : 0;
       const unsigned shb = kDnRowsShared * Fs * 2;
       const unsigned pk = kDnRowsRouted * (F >> 1), sk = kDnRowsRouted * G;
       for (int j = blockIdx.x; j < n_sh + n_r; j += gridDim.x, ++it) {
@@ -431,25 +451,41 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   bool ok = mbar_wait(&tbl, 0, a.status, kSiteDnFull);
   const int n_active = ok ? s_active[0] : 0;
   const int n_r = n_active * nrb;
-  // routed activations as f16 with a per-route power-of-two prescale
+  // routed activations as f16 with a per-route power-of-two prescale; a warp
+  // holds its row in registers (G*4 <= 32*kRowRegs uint4) across the max
+  constexpr int kRowRegs = 8;
   for (int r = warp_id; r < R; r += kGroups * kConsumerWarps) {
     const uint16_t* src = a.act + static_cast<size_t>(r) * F;
+    uint4 v8[kRowRegs];
     float m = 0.f;
-    for (int v = lane; v < G * 4; v += 32) {
-      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src + 8 * v));
-      m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y)))));
-      m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
+#pragma unroll
+    for (int q = 0; q < kRowRegs; ++q) {
+      const int v = lane + 32 * q;
+      if (v < G * 4) v8[q] = __ldcg(reinterpret_cast<const uint4*>(src + 8 * v));
+    }
+#pragma unroll
+    for (int q = 0; q < kRowRegs; ++q) {
+      const int v = lane + 32 * q;
+      if (v < G * 4) {
+        const uint4 u = v8[q];
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y)))));
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
+      }
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
     const int sh = f16_shift_for(m);
-    const float s = pow2i(-sh);
+    const float sc2 = pow2i(-sh);
     if (lane == 0) rscale[r] = pow2i(sh);
-    for (int v = lane; v < G * 4; v += 32) {
-      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src + 8 * v));
-      xr[(r * 4 + (v & 3)) * G + (v >> 2)] =
-          make_uint4(bf16x2_to_f16x2_scaled(u.x, s), bf16x2_to_f16x2_scaled(u.y, s),
-                     bf16x2_to_f16x2_scaled(u.z, s), bf16x2_to_f16x2_scaled(u.w, s));
+#pragma unroll
+    for (int q = 0; q < kRowRegs; ++q) {
+      const int v = lane + 32 * q;
+      if (v < G * 4) {
+        const uint4 u = v8[q];
+        xr[(r * 4 + (v & 3)) * G + (v >> 2)] =
+            make_uint4(bf16x2_to_f16x2_scaled(u.x, sc2), bf16x2_to_f16x2_scaled(u.y, sc2),
+                       bf16x2_to_f16x2_scaled(u.z, sc2), bf16x2_to_f16x2_scaled(u.w, sc2));
+      }
     }
   }
   // shared activations (bf16) as [t][w4][lane], element 8*(lane + 32*w4)
