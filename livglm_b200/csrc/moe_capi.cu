@@ -324,35 +324,55 @@ struct StreamPlan {
   size_t gu_smem, dn_smem;
 };
 
+// Byte stride for rows staged one by one so that lanes (g, q) reading 4 bytes
+// at row g, offset 4q hit 32 distinct banks: stride/4 must be 4 * odd mod 32.
+int conflict_free_stride(int row_bytes) {
+  for (int pad = 0; pad <= 112; pad += 16)
+    if ((((row_bytes + pad) / 4) % 32) % 8 == 4) return row_bytes + pad;
+  return row_bytes;
+}
+
+void plan_rows(int row_bytes, int g_bytes, lg::StreamCfg* sc) {
+  sc->rs = conflict_free_stride(row_bytes);
+  if (g_bytes % 16 == 0) { sc->ss_rows = 1; sc->ss = conflict_free_stride(g_bytes); }
+  else { sc->ss_rows = 0; sc->ss = g_bytes; }
+}
+
 bool plan_stream(const lg_moe_config* c, int M, int TT, StreamPlan* P) {
   const size_t d = c->hidden_size, F = c->moe_intermediate_size, Fs = F * c->n_shared_experts;
-  const size_t G = d / 32, KI = (G + 31) / 32, WPL = (d / 4 / 8 + 31) / 32;
+  const size_t E = c->n_routed_experts;
+  const size_t G = d / 32, WPL = (d / 4 / 8 + 31) / 32;
   const size_t GF = F / 32, WS = (Fs / 8 + 31) / 32, R = static_cast<size_t>(M) * c->num_experts_per_tok;
+  const size_t tables = (2 * ((E + 1 + 3) & ~size_t(3)) + R + 4) * 4;
   // gate/up
+  plan_rows(static_cast<int>(d / 2), static_cast<int>(G), &P->gu);
   const size_t gu_stage = std::max<size_t>(Fs > 0 ? 2 * lg::kGuRowsShared * d * 2 : 0,
-                                           2 * lg::kGuRowsRouted * (d / 2) + 2 * lg::kGuRowsRouted * G);
-  const size_t gu_x = TT * KI * 128 * 16 + TT * 4 * WPL * 32 * 16;
-  const size_t tables = (2 * ((static_cast<size_t>(c->n_routed_experts) + 1 + 3) & ~size_t(3)) + R + 4) * 4;
-  const size_t gu_aux = lg::kGroups * 2 * lg::kGuRowsShared * 4 * TT * 2 * 4 + tables;
+                                           2 * lg::kGuRowsRouted * (P->gu.rs + P->gu.ss));
+  const size_t gu_x = TT * d * 2 + TT * 4 * WPL * 32 * 16;
+  const size_t gu_aux = (lg::kGroups * 2 * lg::kGuRowsShared * 4 * TT * 2 +
+                         lg::kGroups * 2 * lg::kConsumerWarps * 8 * TT * 2) * 4 + tables;
   const size_t gu_fixed = gu_x + gu_aux;
   if (gu_fixed + 2 * gu_stage > kSmemBudget) return false;
   P->gu.stages = static_cast<int>(std::min<size_t>(lg::kMaxStages, (kSmemBudget - gu_fixed) / gu_stage));
-  P->gu.stage_bytes = static_cast<int>(gu_stage);
+  P->gu.stage_bytes = static_cast<int>((gu_stage + 127) & ~size_t(127));
+  P->gu.stages = static_cast<int>(std::min<size_t>(P->gu.stages, (kSmemBudget - gu_fixed) / P->gu.stage_bytes));
   P->gu.x_off = P->gu.stages * P->gu.stage_bytes;
   P->gu.aux_off = static_cast<int>(P->gu.x_off + gu_x);
   P->gu_smem = P->gu.aux_off + gu_aux;
   // down
+  plan_rows(static_cast<int>(F / 2), static_cast<int>(GF), &P->dn);
   const size_t dn_stage = std::max<size_t>(Fs > 0 ? lg::kDnRowsShared * Fs * 2 : 0,
-                                           lg::kDnRowsRouted * (F / 2) + lg::kDnRowsRouted * GF);
+                                           lg::kDnRowsRouted * (P->dn.rs + P->dn.ss));
   const size_t dn_x = R * F * 2 + static_cast<size_t>(M) * WS * 32 * 16;
-  const size_t dn_aux = ((R + 3) & ~size_t(3)) * 4 + tables;
+  const size_t dn_aux = (((R + 3) & ~size_t(3)) + lg::kGroups * 2 * lg::kConsumerWarps * lg::kDnRowsRouted * TT) * 4 +
+                        tables;
   if (dn_x + dn_aux + 2 * dn_stage > kSmemBudget) return false;
-  P->dn.stages = static_cast<int>(std::min<size_t>(lg::kMaxStages, (kSmemBudget - dn_x - dn_aux) / dn_stage));
-  P->dn.stage_bytes = static_cast<int>(dn_stage);
+  P->dn.stage_bytes = static_cast<int>((dn_stage + 127) & ~size_t(127));
+  P->dn.stages = static_cast<int>(std::min<size_t>(lg::kMaxStages, (kSmemBudget - dn_x - dn_aux) / P->dn.stage_bytes));
   P->dn.x_off = P->dn.stages * P->dn.stage_bytes;
   P->dn.aux_off = static_cast<int>(P->dn.x_off + dn_x);
   P->dn_smem = P->dn.aux_off + dn_aux;
-  return true;
+  return P->gu.stages >= 2 && P->dn.stages >= 2;
 }
 
 // The decode chain needs bulk-copyable chunks: 16-byte aligned bases and
@@ -363,6 +383,7 @@ bool decode_fits(const lg_moe_config* c, const lg_moe_weights* w, int64_t M) {
   if (static_cast<size_t>(lg::kRouterExperts) * c->hidden_size * 4 > 200 * 1024) return false;
   // register-staged activation rows: d*M/8 <= 4 * 512 uint4, F/8 <= 8 * 32
   if (static_cast<size_t>(c->hidden_size) * M / 8 > 4 * 512 || c->moe_intermediate_size / 8 > 8 * 32) return false;
+  if (c->num_experts_per_tok * M > lg::kDecodeMaxTokens * 32) return false;
   if (c->num_experts_per_tok * M > lg::kDecodeMaxTokens * 32) return false;
   if (!aligned(w->gate_scale, 16) || !aligned(w->up_scale, 16) || !aligned(w->down_scale, 16)) return false;
   if (w->gate_scale_stride % 16 || w->up_scale_stride % 16 || w->down_scale_stride % 16) return false;

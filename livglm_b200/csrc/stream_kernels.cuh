@@ -48,7 +48,44 @@ struct StreamCfg {
   int stage_bytes;
   int x_off;    // byte offset of staged activations
   int aux_off;  // byte offset of the reduction / scale scratch
+  int rs;       // padded byte stride of a routed weight row in a stage
+  int ss;       // byte stride of a routed scale row in a stage
+  int ss_rows;  // 1: scale rows copied one by one (padded); 0: one contiguous block
 };
+
+// m16n8k16 tensor-core MMA, f16 x f16 -> f32 (fragment layout of the PTX ISA:
+// a0/a2 rows g, a1/a3 rows g+8; a0/a1 k 2q..2q+1, a2/a3 k 2q+8..2q+9;
+// b0 k 2q..2q+1, b1 k 2q+8..2q+9, column g; d0/d1 row g, d2/d3 row g+8,
+// columns 2q, 2q+1; g = lane/4, q = lane%4)
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(w));
+}
+// One 32-column group of a 16-row tile against up to 8 activation columns.
+// Lane (g, q) holds the 4 bytes [4q, 4q+4) of the group's 16 bytes in rows g
+// (wlo) and g+8 (whi): columns 8q..8q+7.  k-slots 2q+i <-> column 8q+i and
+// 2q+8+i <-> column 8q+2+i (first MMA), then columns 8q+4..8q+7 (second), so
+// the activation fragment is the 8 contiguous f16 at columns 8q..8q+7 of the
+// lane's column g.  d += A * B for the group.
+__device__ __forceinline__ void group_mma(float (&d)[4], uint32_t wlo, uint32_t whi, const uint4& xv) {
+  uint32_t hl[4], hh[4];
+  e2m1x8_to_f16x2(wlo, hl);
+  e2m1x8_to_f16x2(whi, hh);
+  mma16816(d, hl[0], hh[0], hl[1], hh[1], xv.x, xv.y);
+  mma16816(d, hl[2], hh[2], hl[3], hh[3], xv.z, xv.w);
+}
 
 // Bulk-copy the routing tables (active list, offsets, perm) into shared
 // memory; completion is signalled on `bar`.  Sizes are rounded up to 16 bytes
@@ -82,27 +119,49 @@ __device__ __forceinline__ void group_dot_e2m1(const uint4& pw, const uint4* xv0
   for (int q = 0; q < TT; ++q) gsum[q] = __fadd_rn(__fadd_rn(c[0][q], c[1][q]), __fadd_rn(c[2][q], c[3][q]));
 }
 
+// Issue the bulk copies of `rows` weight rows (row_bytes each, global stride
+// row_bytes) into padded shared rows (stride rs), and of their scale rows
+// (g_bytes each) either row by row (stride ss) or as one block; lanes of the
+// producer warp split the rows.  Returns the bytes the stage will receive.
+__device__ __forceinline__ void issue_rows(unsigned char* dst, const uint8_t* src, int rows, int row_bytes,
+                                           int rs, int lane, uint64_t* bar) {
+  for (int r = lane; r < rows; r += 32)
+    bulk_g2s(dst + static_cast<size_t>(r) * rs, src + static_cast<size_t>(r) * row_bytes, row_bytes, bar);
+}
+__device__ __forceinline__ void issue_scales(unsigned char* dst, const uint8_t* src, int rows, int g_bytes, int ss,
+                                             int ss_rows, int lane, uint64_t* bar) {
+  if (ss_rows) {
+    for (int r = lane; r < rows; r += 32)
+      bulk_g2s(dst + static_cast<size_t>(r) * ss, src + static_cast<size_t>(r) * g_bytes, g_bytes, bar);
+  } else if (lane == 0) {
+    bulk_g2s(dst, src, rows * g_bytes, bar);
+  }
+}
+
 // ---------------------------------------------------------------------------
 template <int TT>
 __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(DecodeArgs a, StreamCfg sc) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages];
   __shared__ __align__(8) uint64_t empty[kMaxStages];
+  __shared__ __align__(8) uint64_t tbl;
   __shared__ unsigned amax_bits[TT];
   __shared__ float tok_mult[TT];
   const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int K = a.d, G = K >> 5, KI = (G + 31) >> 5;
+  const int K = a.d, G = K >> 5;
   const int M = a.M, F = a.F, Fs = a.Fs;
   const int S = sc.stages;
   const int KQ = K >> 2;               // shared-chunk quarter width
   const int WPL = (KQ / 8 + 31) / 32;  // 8-element words per lane per quarter
-  uint4* xh = reinterpret_cast<uint4*>(smem + sc.x_off);  // f16 [t][i][w][lane]
-  uint4* xb = xh + TT * KI * 128;                         // bf16 [t][q][w4][lane]
-  float* red = reinterpret_cast<float*>(smem + sc.aux_off);  // [group][2][2 rows][4 q][TT][2]
-  int* s_active = reinterpret_cast<int*>(red + kGroups * 2 * kGuRowsShared * 4 * TT * 2);
+  uint16_t* xh = reinterpret_cast<uint16_t*>(smem + sc.x_off);  // f16 [t][K]
+  uint4* xb = reinterpret_cast<uint4*>(xh + TT * K);              // bf16 [t][q][w4][lane]
+  float* red = reinterpret_cast<float*>(smem + sc.aux_off);
+  // red: shared-chunk partials [group][2][2 rows][4 q][TT][2], then routed
+  // partials [group][2][8 warps][8 rows][TT][2]
+  float* red_r = red + kGroups * 2 * kGuRowsShared * 4 * TT * 2;
+  int* s_active = reinterpret_cast<int*>(red_r + kGroups * 2 * kConsumerWarps * 8 * TT * 2);
   int* s_offsets = s_active + (((a.E + 1) + 3) & ~3);
   int* s_perm = s_offsets + (((a.E + 1) + 3) & ~3);
-  __shared__ __align__(8) uint64_t tbl;
   const int n_sh = Fs > 0 ? Fs / kGuRowsShared : 0;
   const int nrb = F / kGuRowsRouted;
   if (threadIdx.x == 0) {
@@ -117,54 +176,65 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
     bool ok = true;
     int it = 0;
     int j = blockIdx.x;
-    if (lane == 0) {
-      const unsigned sh_bytes = kGuRowsShared * K * 2;
-      for (; j < n_sh; j += gridDim.x, ++it) {
-        const int s = it % S;
-        const unsigned round = it / S;
+    const unsigned sh_bytes = kGuRowsShared * K * 2;
+    for (; j < n_sh; j += gridDim.x, ++it) {
+      const int s = it % S;
+      const unsigned round = it / S;
+      if (lane == 0) {
         if (ok && round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, a.status, kSiteGuEmpty);
-        if (!ok) continue;
-        unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], 2 * sh_bytes);
-        bulk_g2s(st, a.sh_gate + static_cast<size_t>(j) * kGuRowsShared * K, sh_bytes, &full[s]);
-        bulk_g2s(st + sh_bytes, a.sh_up + static_cast<size_t>(j) * kGuRowsShared * K, sh_bytes, &full[s]);
+        if (ok) {
+          unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+          mbar_arrive_expect_tx(&full[s], 2 * sh_bytes);
+          bulk_g2s(st, a.sh_gate + static_cast<size_t>(j) * kGuRowsShared * K, sh_bytes, &full[s]);
+          bulk_g2s(st + sh_bytes, a.sh_up + static_cast<size_t>(j) * kGuRowsShared * K, sh_bytes, &full[s]);
+        }
       }
     }
-    __syncwarp();
+    ok = __shfl_sync(0xffffffffu, ok, 0);
     pdl_wait();  // routing tables written by the router
     pdl_trigger();
     if (lane == 0) {
       copy_tables(a, s_active, s_offsets, s_perm, &tbl);
       if (ok) ok = mbar_wait(&tbl, 0, a.status, kSiteGuEmpty);
-      const int n_r = ok ? s_active[0] * nrb : 0;
-      const unsigned pk = kGuRowsRouted * (K >> 1), sk = kGuRowsRouted * G;
-      for (; j - n_sh < n_r; j += gridDim.x, ++it) {
-        const int s = it % S;
-        const unsigned round = it / S;
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    const int n_r = ok ? s_active[0] * nrb : 0;
+    const int rb = K >> 1;
+    const unsigned bytes = 2u * kGuRowsRouted * rb + 2u * kGuRowsRouted * G;
+    for (; j - n_sh < n_r; j += gridDim.x, ++it) {
+      const int s = it % S;
+      const unsigned round = it / S;
+      if (lane == 0) {
         if (ok && round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, a.status, kSiteGuEmpty);
-        if (!ok) continue;
-        const int jr = j - n_sh;
-        const int e = s_active[1 + jr / nrb];
-        const size_t f0 = static_cast<size_t>(jr % nrb) * kGuRowsRouted;
-        unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], 2 * pk + 2 * sk);
-        bulk_g2s(st, a.gate_p + e * a.gate_ps + f0 * (K >> 1), pk, &full[s]);
-        bulk_g2s(st + pk, a.up_p + e * a.up_ps + f0 * (K >> 1), pk, &full[s]);
-        bulk_g2s(st + 2 * pk, a.gate_s + e * a.gate_ss + f0 * G, sk, &full[s]);
-        bulk_g2s(st + 2 * pk + sk, a.up_s + e * a.up_ss + f0 * G, sk, &full[s]);
+        if (ok) mbar_arrive_expect_tx(&full[s], bytes);
       }
-      if (!ok) {  // consumers stopped: let copies already issued land before leaving
-        for (int q = (it > S ? it - S : 0); q < it; ++q)
-          mbar_wait(&full[q % S], (q / S) & 1, a.status, kSiteGuDrain);
-      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) continue;
+      const int jr = j - n_sh;
+      const int e = s_active[1 + jr / nrb];
+      const size_t f0 = static_cast<size_t>(jr % nrb) * kGuRowsRouted;
+      unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+      // rows 0..7: gate rows f0..f0+7; rows 8..15: up rows; then 16 scale rows
+      issue_rows(st, a.gate_p + e * a.gate_ps + f0 * rb, kGuRowsRouted, rb, sc.rs, lane, &full[s]);
+      issue_rows(st + kGuRowsRouted * sc.rs, a.up_p + e * a.up_ps + f0 * rb, kGuRowsRouted, rb, sc.rs, lane,
+                 &full[s]);
+      unsigned char* sst = st + 2 * kGuRowsRouted * sc.rs;
+      issue_scales(sst, a.gate_s + e * a.gate_ss + f0 * G, kGuRowsRouted, G, sc.ss, sc.ss_rows, lane, &full[s]);
+      issue_scales(sst + kGuRowsRouted * sc.ss, a.up_s + e * a.up_ss + f0 * G, kGuRowsRouted, G, sc.ss,
+                   sc.ss_rows, lane, &full[s]);
+    }
+    if (!ok && lane == 0) {  // consumers stopped: let copies already issued land before leaving
+      for (int q = (it > S ? it - S : 0); q < it; ++q)
+        mbar_wait(&full[q % S], (q / S) & 1, a.status, kSiteGuDrain);
     }
     return;
   }
 
   // ------------------------------- consumers -------------------------------
-  const int grp = warp_id / kConsumerWarps;  // consumer group
+  const int grp = warp_id / kConsumerWarps;   // consumer group
   const int warp = warp_id % kConsumerWarps;  // warp within the group
   const int ct = threadIdx.x;                 // 0 .. kGroups*kConsumerThreads-1
+  const int gt = ct - grp * kConsumerThreads;
   constexpr int kAll = kGroups * kConsumerThreads;
   // stage bf16 rows for shared chunks: element qq*KQ + 8*(lane + 32*w4) + 0..7
   if (n_sh > 0) {
@@ -178,26 +248,23 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
             *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + qq * KQ + el);
     }
   }
-  // f16 rows for routed chunks, with a per-token power-of-two prescale:
-  // one load per element into registers, block max, then convert
-  constexpr int kStageRegs = 4;  // uint4 per thread held across the max (M*G*4 <= 4*kAll)
+  // f16 rows for routed chunks with a per-token power-of-two prescale: one
+  // load per element into registers, block max, then convert
+  constexpr int kStageRegs = 4;  // M*K/8 <= kStageRegs*kAll
   uint4 xr[kStageRegs];
 #pragma unroll
   for (int q = 0; q < kStageRegs; ++q) {
     const int i4 = ct + q * kAll;
-    if (i4 < M * G * 4) {
-      const int t = i4 / (G * 4), rem = i4 - t * G * 4;
-      xr[q] = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + 8 * rem);
-    }
+    if (i4 < M * K / 8) xr[q] = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(i4) * 8);
   }
 #pragma unroll
   for (int q = 0; q < kStageRegs; ++q) {
     const int i4 = ct + q * kAll;
-    if (i4 < M * G * 4) {
+    if (i4 < M * K / 8) {
       const uint4 u = xr[q];
       float m = fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y))));
       m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
-      atomicMax(amax_bits + i4 / (G * 4), __float_as_uint(m));
+      atomicMax(amax_bits + (i4 * 8) / K, __float_as_uint(m));
     }
   }
   named_sync(kBarAllConsumers, kAll);
@@ -206,11 +273,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
 #pragma unroll
   for (int q = 0; q < kStageRegs; ++q) {
     const int i4 = ct + q * kAll;
-    if (i4 < M * G * 4) {
-      const int t = i4 / (G * 4), rem = i4 - t * G * 4, c = rem >> 2, w = rem & 3;
+    if (i4 < M * K / 8) {
       const uint4 u = xr[q];
-      const float sc2 = __fdiv_rn(1.0f, tok_mult[t]);
-      xh[((t * KI + (c >> 5)) * 4 + w) * 32 + (c & 31)] =
+      const float sc2 = __fdiv_rn(1.0f, tok_mult[(i4 * 8) / K]);
+      reinterpret_cast<uint4*>(xh)[i4] =
           make_uint4(bf16x2_to_f16x2_scaled(u.x, sc2), bf16x2_to_f16x2_scaled(u.y, sc2),
                      bf16x2_to_f16x2_scaled(u.z, sc2), bf16x2_to_f16x2_scaled(u.w, sc2));
     }
@@ -218,7 +284,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
   named_sync(kBarAllConsumers, kAll);
 
   bool ok = true;
-  int shi = 0;
+  int shi = 0, rti = 0;
   int it = grp;
   int j = blockIdx.x + it * gridDim.x;
   // shared-expert chunks: rows 2j, 2j+1; warp -> (row w/4, K quarter w%4)
@@ -256,25 +322,25 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    float gt[TT], ut[TT];
+    float g4[TT], u4s[TT];
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
-      gt[t] = __fadd_rn(__fadd_rn(ag[0][t], ag[1][t]), __fadd_rn(ag[2][t], ag[3][t]));
-      ut[t] = __fadd_rn(__fadd_rn(au[0][t], au[1][t]), __fadd_rn(au[2][t], au[3][t]));
+      g4[t] = __fadd_rn(__fadd_rn(ag[0][t], ag[1][t]), __fadd_rn(ag[2][t], ag[3][t]));
+      u4s[t] = __fadd_rn(__fadd_rn(au[0][t], au[1][t]), __fadd_rn(au[2][t], au[3][t]));
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1)
 #pragma unroll
       for (int t = 0; t < TT; ++t) {
-        gt[t] = __fadd_rn(gt[t], __shfl_xor_sync(0xffffffffu, gt[t], off));
-        ut[t] = __fadd_rn(ut[t], __shfl_xor_sync(0xffffffffu, ut[t], off));
+        g4[t] = __fadd_rn(g4[t], __shfl_xor_sync(0xffffffffu, g4[t], off));
+        u4s[t] = __fadd_rn(u4s[t], __shfl_xor_sync(0xffffffffu, u4s[t], off));
       }
     float* rb = red + ((grp * 2 + (shi & 1)) * kGuRowsShared * 4 * TT * 2);
     if (lane == 0) {
 #pragma unroll
       for (int t = 0; t < TT; ++t) {
-        rb[((rr * 4 + qq) * TT + t) * 2 + 0] = gt[t];
-        rb[((rr * 4 + qq) * TT + t) * 2 + 1] = ut[t];
+        rb[((rr * 4 + qq) * TT + t) * 2 + 0] = g4[t];
+        rb[((rr * 4 + qq) * TT + t) * 2 + 1] = u4s[t];
       }
     }
     named_sync(1 + grp, kConsumerThreads);
@@ -292,80 +358,68 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
   pdl_trigger();
   if (ok) ok = mbar_wait(&tbl, 0, a.status, kSiteGuFull);
   const int n_r = ok ? s_active[0] * nrb : 0;
-  for (; j - n_sh < n_r; it += kGroups, j += kGroups * gridDim.x) {
+  // routed chunks: 16-row tile = 8 gate rows over 8 up rows; the K groups are
+  // split over the 8 warps of the group; columns = routes of the expert
+  const int g8 = lane >> 2, q4 = lane & 3;
+  const int gpw = (G + kConsumerWarps - 1) / kConsumerWarps;
+  for (; j - n_sh < n_r; it += kGroups, j += kGroups * gridDim.x, ++rti) {
     const int s = it % S;
     if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteGuFull);
     const int jr = j - n_sh;
     const int e = s_active[1 + jr / nrb];
-    const int f = (jr % nrb) * kGuRowsRouted + warp;
+    const int f0 = (jr % nrb) * kGuRowsRouted;
     const int p0 = s_offsets[e];
     const int n = s_offsets[e + 1] - p0;
-    int tok[TT];
-#pragma unroll
-    for (int q = 0; q < TT; ++q) tok[q] = q < n ? s_perm[p0 + q] / a.k : 0;
-    float ag[TT], au[TT];
-#pragma unroll
-    for (int t = 0; t < TT; ++t) { ag[t] = 0.f; au[t] = 0.f; }
+    const int col_tok = s_perm[p0 + (g8 < n ? g8 : 0)] / a.k;  // token of this lane's column
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
     if (ok) {
       const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
-      const size_t pk = static_cast<size_t>(kGuRowsRouted) * (K >> 1);
-      const unsigned char* gp = st + static_cast<size_t>(warp) * (K >> 1);
-      const unsigned char* up = gp + pk;
-      const unsigned char* gs = st + 2 * pk + warp * G;
-      const unsigned char* us = gs + kGuRowsRouted * G;
-#pragma unroll 2
-      for (int i = 0; i < KI; ++i) {
-        const int c = lane + 32 * i;
-        if (c < G) {
-          const uint4 pg = *reinterpret_cast<const uint4*>(gp + 16 * c);
-          const uint4 pu = *reinterpret_cast<const uint4*>(up + 16 * c);
-          const float s_g = e8m0_to_f32(gs[c]), s_u = e8m0_to_f32(us[c]);
-          const uint4* xv0 = xh + i * 128 + lane;
-          float gg[TT], gu[TT];
-          // x of token tok[q] sits at xh[(tok*KI + i)*128 + w*32 + lane]
-          if (n == 1 || TT == 1) {
-            group_dot_e2m1<TT>(pg, xv0 + tok[0] * KI * 128, 0, n, gg);
-            group_dot_e2m1<TT>(pu, xv0 + tok[0] * KI * 128, 0, n, gu);
-          } else {
-#pragma unroll
-            for (int q = 0; q < TT; ++q) {
-              float g1[1], u1[1];
-              if (q < n) {
-                group_dot_e2m1<1>(pg, xv0 + tok[q] * KI * 128, 0, 1, g1);
-                group_dot_e2m1<1>(pu, xv0 + tok[q] * KI * 128, 0, 1, u1);
-              } else {
-                g1[0] = 0.f; u1[0] = 0.f;
-              }
-              gg[q] = g1[0];
-              gu[q] = u1[0];
-            }
-          }
-#pragma unroll
-          for (int q = 0; q < TT; ++q) {
-            ag[q] = __fmaf_rn(gg[q], s_g, ag[q]);
-            au[q] = __fmaf_rn(gu[q], s_u, au[q]);
-          }
-        }
+      const unsigned char* wlo = st + static_cast<size_t>(g8) * sc.rs + 4 * q4;                  // gate row g
+      const unsigned char* whi = st + static_cast<size_t>(kGuRowsRouted + g8) * sc.rs + 4 * q4;  // up row g
+      const unsigned char* sst = st + 2 * kGuRowsRouted * sc.rs;
+      const unsigned char* slo = sst + (sc.ss_rows ? g8 * sc.ss : g8 * G);
+      const unsigned char* shi = sst + (sc.ss_rows ? (kGuRowsRouted + g8) * sc.ss : (kGuRowsRouted + g8) * G);
+      const uint16_t* xrow = xh + static_cast<size_t>(col_tok) * K + 8 * q4;
+      const int c0 = warp * gpw, c1 = min(G, c0 + gpw);
+#pragma unroll 4
+      for (int c = c0; c < c1; ++c) {
+        const uint32_t wl = *reinterpret_cast<const uint32_t*>(wlo + 16 * c);
+        const uint32_t wh = *reinterpret_cast<const uint32_t*>(whi + 16 * c);
+        const uint4 xv = *reinterpret_cast<const uint4*>(xrow + 32 * c);
+        const float sl = e8m0_to_f32(slo[c]), sh = e8m0_to_f32(shi[c]);
+        float t4[4] = {0.f, 0.f, 0.f, 0.f};
+        group_mma(t4, wl, wh, xv);
+        d[0] = __fmaf_rn(t4[0], sl, d[0]);
+        d[1] = __fmaf_rn(t4[1], sl, d[1]);
+        d[2] = __fmaf_rn(t4[2], sh, d[2]);
+        d[3] = __fmaf_rn(t4[3], sh, d[3]);
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+    // cross-warp reduction of the K split: partials [warp][row][col][gate/up]
+    float* rr2 = red_r + ((grp * 2 + (rti & 1)) * kConsumerWarps + warp) * 8 * TT * 2;
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1)
-#pragma unroll
-      for (int q = 0; q < TT; ++q) {
-        ag[q] = __fadd_rn(ag[q], __shfl_xor_sync(0xffffffffu, ag[q], off));
-        au[q] = __fadd_rn(au[q], __shfl_xor_sync(0xffffffffu, au[q], off));
+    for (int h = 0; h < 2; ++h) {
+      const int col = 2 * q4 + h;
+      if (col < n && col < TT) {
+        rr2[(g8 * TT + col) * 2 + 0] = d[h];
+        rr2[(g8 * TT + col) * 2 + 1] = d[2 + h];
       }
-    if (ok && lane < TT && lane < n) {
-      float g = ag[0], uu = au[0];
-      int tj = tok[0];
-#pragma unroll
-      for (int q = 1; q < TT; ++q)
-        if (lane == q) { g = ag[q]; uu = au[q]; tj = tok[q]; }
+    }
+    named_sync(1 + grp, kConsumerThreads);
+    if (ok && gt < 8 * n) {
+      const int row = gt / n, col = gt - row * n;
+      const float* base = red_r + (grp * 2 + (rti & 1)) * kConsumerWarps * 8 * TT * 2;
+      float g = 0.f, u = 0.f;
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        g = __fadd_rn(g, base[(w * 8 * TT + row * TT + col) * 2 + 0]);
+        u = __fadd_rn(u, base[(w * 8 * TT + row * TT + col) * 2 + 1]);
+      }
+      const int tj = s_perm[p0 + col] / a.k;
       const float m = tok_mult[tj];
-      a.act[static_cast<size_t>(p0 + lane) * F + f] =
-          swiglu_bf16(round_bf16(__fmul_rn(g, m)), round_bf16(__fmul_rn(uu, m)), a.limit);
+      a.act[static_cast<size_t>(p0 + col) * F + f0 + row] =
+          swiglu_bf16(round_bf16(__fmul_rn(g, m)), round_bf16(__fmul_rn(u, m)), a.limit);
     }
   }
 }
@@ -376,25 +430,22 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages];
   __shared__ __align__(8) uint64_t empty[kMaxStages];
+  __shared__ __align__(8) uint64_t tbl;
   const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int M = a.M, k = a.k, d = a.d, F = a.F, Fs = a.Fs;
   const int G = F >> 5;
   const int S = sc.stages;
-  const int LPR = a.lpr_down;
-  const int slots = 32 / LPR;
-  const int sub = lane & (LPR - 1), slot = lane / LPR;
-  const int per_lane = (G + LPR - 1) / LPR;
   const int WS = (Fs / 8 + 31) / 32;  // 8-element words per lane of a shared row
   const int n_sh = Fs > 0 ? d / kDnRowsShared : 0;
   const int nrb = d / kDnRowsRouted;
   const int R = M * k;
-  uint4* xr = reinterpret_cast<uint4*>(smem + sc.x_off);  // f16 [p][q4][grp]
-  uint4* xsb = xr + R * G * 4;                            // bf16 [t][w4][lane]
+  uint16_t* xr = reinterpret_cast<uint16_t*>(smem + sc.x_off);  // f16 [p][F]
+  uint4* xsb = reinterpret_cast<uint4*>(xr + static_cast<size_t>(R) * F);  // bf16 [t][w4][lane]
   float* rscale = reinterpret_cast<float*>(smem + sc.aux_off);
-  int* s_active = reinterpret_cast<int*>(rscale + ((R + 3) & ~3));
+  float* red_r = rscale + ((R + 3) & ~3);  // [group][2][8 warps][32 rows][TT]
+  int* s_active = reinterpret_cast<int*>(red_r + kGroups * 2 * kConsumerWarps * kDnRowsRouted * TT);
   int* s_offsets = s_active + (((a.E + 1) + 3) & ~3);
   int* s_perm = s_offsets + (((a.E + 1) + 3) & ~3);
-  __shared__ __align__(8) uint64_t tbl;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumerWarps); }
     mbar_init(&tbl, 1);
@@ -406,35 +457,41 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
     // Weights depend on nothing earlier and the routing tables are complete
     // (the gate/up kernel waited on the router before letting this kernel
     // launch), so streaming starts before griddepcontrol.wait.
+    bool ok = true;
     if (lane == 0) {
       copy_tables(a, s_active, s_offsets, s_perm, &tbl);
-      bool ok = mbar_wait(&tbl, 0, a.status, kSiteDnEmpty);
-      int it = 0;
-      const int n_r = ok ? s_active[0] * nrb : 0;
-      const unsigned shb = kDnRowsShared * Fs * 2;
-      const unsigned pk = kDnRowsRouted * (F >> 1), sk = kDnRowsRouted * G;
-      for (int j = blockIdx.x; j < n_sh + n_r; j += gridDim.x, ++it) {
-        const int s = it % S;
-        const unsigned round = it / S;
+      ok = mbar_wait(&tbl, 0, a.status, kSiteDnEmpty);
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    int it = 0;
+    const int n_r = ok ? s_active[0] * nrb : 0;
+    const unsigned shb = kDnRowsShared * Fs * 2;
+    const int rb = F >> 1;
+    const unsigned rbytes = kDnRowsRouted * (rb + G);
+    for (int j = blockIdx.x; j < n_sh + n_r; j += gridDim.x, ++it) {
+      const int s = it % S;
+      const unsigned round = it / S;
+      if (lane == 0) {
         if (ok && round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, a.status, kSiteDnEmpty);
-        if (!ok) continue;
-        unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
-        if (j < n_sh) {
-          mbar_arrive_expect_tx(&full[s], shb);
-          bulk_g2s(st, a.sh_down + static_cast<size_t>(j) * kDnRowsShared * Fs, shb, &full[s]);
-        } else {
-          const int jr = j - n_sh;
-          const int e = s_active[1 + jr / nrb];
-          const size_t r0 = static_cast<size_t>(jr % nrb) * kDnRowsRouted;
-          mbar_arrive_expect_tx(&full[s], pk + sk);
-          bulk_g2s(st, a.down_p + e * a.down_ps + r0 * (F >> 1), pk, &full[s]);
-          bulk_g2s(st + pk, a.down_s + e * a.down_ss + r0 * G, sk, &full[s]);
-        }
+        if (ok) mbar_arrive_expect_tx(&full[s], j < n_sh ? shb : rbytes);
       }
-      if (!ok) {
-        for (int q = (it > S ? it - S : 0); q < it; ++q)
-          mbar_wait(&full[q % S], (q / S) & 1, a.status, kSiteDnDrain);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) continue;
+      unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+      if (j < n_sh) {
+        if (lane == 0) bulk_g2s(st, a.sh_down + static_cast<size_t>(j) * kDnRowsShared * Fs, shb, &full[s]);
+      } else {
+        const int jr = j - n_sh;
+        const int e = s_active[1 + jr / nrb];
+        const size_t r0 = static_cast<size_t>(jr % nrb) * kDnRowsRouted;
+        issue_rows(st, a.down_p + e * a.down_ps + r0 * rb, kDnRowsRouted, rb, sc.rs, lane, &full[s]);
+        issue_scales(st + kDnRowsRouted * sc.rs, a.down_s + e * a.down_ss + r0 * G, kDnRowsRouted, G, sc.ss,
+                     sc.ss_rows, lane, &full[s]);
       }
+    }
+    if (!ok && lane == 0) {
+      for (int q = (it > S ? it - S : 0); q < it; ++q)
+        mbar_wait(&full[q % S], (q / S) & 1, a.status, kSiteDnDrain);
     }
     pdl_wait();
     pdl_trigger();
@@ -445,6 +502,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   const int grp = warp_id / kConsumerWarps;
   const int warp = warp_id % kConsumerWarps;
   const int ct = threadIdx.x;
+  const int gt = ct - grp * kConsumerThreads;
   constexpr int kAll = kGroups * kConsumerThreads;
   pdl_wait();  // activations from the gate/up kernel
   pdl_trigger();
@@ -452,7 +510,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   const int n_active = ok ? s_active[0] : 0;
   const int n_r = n_active * nrb;
   // routed activations as f16 with a per-route power-of-two prescale; a warp
-  // holds its row in registers (G*4 <= 32*kRowRegs uint4) across the max
+  // holds its row in registers (F/8 <= 32*kRowRegs uint4) across the max
   constexpr int kRowRegs = 8;
   for (int r = warp_id; r < R; r += kGroups * kConsumerWarps) {
     const uint16_t* src = a.act + static_cast<size_t>(r) * F;
@@ -461,12 +519,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
 #pragma unroll
     for (int q = 0; q < kRowRegs; ++q) {
       const int v = lane + 32 * q;
-      if (v < G * 4) v8[q] = __ldcg(reinterpret_cast<const uint4*>(src + 8 * v));
+      if (v < F / 8) v8[q] = __ldcg(reinterpret_cast<const uint4*>(src + 8 * v));
     }
 #pragma unroll
     for (int q = 0; q < kRowRegs; ++q) {
       const int v = lane + 32 * q;
-      if (v < G * 4) {
+      if (v < F / 8) {
         const uint4 u = v8[q];
         m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y)))));
         m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
@@ -480,9 +538,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
 #pragma unroll
     for (int q = 0; q < kRowRegs; ++q) {
       const int v = lane + 32 * q;
-      if (v < G * 4) {
+      if (v < F / 8) {
         const uint4 u = v8[q];
-        xr[(r * 4 + (v & 3)) * G + (v >> 2)] =
+        reinterpret_cast<uint4*>(xr + static_cast<size_t>(r) * F)[v] =
             make_uint4(bf16x2_to_f16x2_scaled(u.x, sc2), bf16x2_to_f16x2_scaled(u.y, sc2),
                        bf16x2_to_f16x2_scaled(u.z, sc2), bf16x2_to_f16x2_scaled(u.w, sc2));
       }
@@ -498,8 +556,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   }
   named_sync(kBarAllConsumers, kAll);
 
-  for (int it = grp, j = blockIdx.x + grp * gridDim.x; j < n_sh + n_r;
-       it += kGroups, j += kGroups * gridDim.x) {
+  const int g8 = lane >> 2, q4 = lane & 3;
+  const int gpw = (G + kConsumerWarps - 1) / kConsumerWarps;
+  int rti = 0;
+  for (int it = grp, j = blockIdx.x + grp * gridDim.x; j < n_sh + n_r; it += kGroups, j += kGroups * gridDim.x) {
     const int s = it % S;
     if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteDnFull);
     const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
@@ -542,66 +602,69 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
           if (lane == t) o = v[t];
         a.ys[static_cast<size_t>(lane) * d + row] = f32_to_bf16(o);
       }
-    } else {  // routed: rows r0 .. r0+31 of expert e; a warp iteration covers `slots` rows
+    } else {  // routed: rows r0 .. r0+31 (two 16-row tiles) of expert e, K split over warps
       const int jr = j - n_sh;
       const int e = s_active[1 + jr / nrb];
       const int r0 = (jr % nrb) * kDnRowsRouted;
       const int p0 = s_offsets[e];
       const int n = s_offsets[e + 1] - p0;
-      int slot_of[TT];
-#pragma unroll
-      for (int q = 0; q < TT; ++q) slot_of[q] = q < n ? s_perm[p0 + q] : 0;
-      const size_t pk = static_cast<size_t>(kDnRowsRouted) * (F >> 1);
-      for (int rl = warp * slots + slot; rl < kDnRowsRouted; rl += kConsumerWarps * slots) {
-        float acc[TT];
-#pragma unroll
-        for (int q = 0; q < TT; ++q) acc[q] = 0.f;
-        if (ok) {
-          const unsigned char* wp = st + static_cast<size_t>(rl) * (F >> 1);
-          const unsigned char* ws = st + pk + rl * G;
+      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+      if (ok) {
+        const uint16_t* xrow = xr + static_cast<size_t>(p0 + (g8 < n ? g8 : 0)) * F + 8 * q4;
+        const unsigned char* w0r = st + static_cast<size_t>(g8) * sc.rs + 4 * q4;
+        const unsigned char* w1r = w0r + 8 * static_cast<size_t>(sc.rs);
+        const unsigned char* w2r = w0r + 16 * static_cast<size_t>(sc.rs);
+        const unsigned char* w3r = w0r + 24 * static_cast<size_t>(sc.rs);
+        const unsigned char* sst = st + kDnRowsRouted * sc.rs;
+        const int sstr = sc.ss_rows ? sc.ss : G;
+        const unsigned char* s0 = sst + g8 * sstr;
+        const int c0 = warp * gpw, c1 = min(G, c0 + gpw);
 #pragma unroll 2
-          for (int qg = 0; qg < per_lane; ++qg) {
-            const int gi = sub + LPR * qg;
-            if (gi < G) {
-              const uint4 pkv = *reinterpret_cast<const uint4*>(wp + 16 * gi);
-              const float scl = e8m0_to_f32(ws[gi]);
-              float gsum[TT];
-              // x of route p0+q: xr[((p0+q)*4 + w)*G + gi]
-              const uint4* xv0 = xr + p0 * 4 * G + gi;
-              float c[4][TT];
-#pragma unroll
-              for (int w = 0; w < 4; ++w)
-#pragma unroll
-                for (int q = 0; q < TT; ++q) c[w][q] = 0.f;
-              const uint32_t w4v[4] = {pkv.x, pkv.y, pkv.z, pkv.w};
-#pragma unroll
-              for (int w = 0; w < 4; ++w)
-#pragma unroll
-                for (int q = 0; q < TT; ++q)
-                  if (q < n) c[w][q] = dot8_e2m1_f16(w4v[w], xv0[(q * 4 + w) * G], c[w][q]);
-#pragma unroll
-              for (int q = 0; q < TT; ++q)
-                gsum[q] = __fadd_rn(__fadd_rn(c[0][q], c[1][q]), __fadd_rn(c[2][q], c[3][q]));
-#pragma unroll
-              for (int q = 0; q < TT; ++q) acc[q] = __fmaf_rn(gsum[q], scl, acc[q]);
-            }
-          }
-        }
-#pragma unroll
-        for (int off = LPR / 2; off >= 1; off >>= 1)
-#pragma unroll
-          for (int q = 0; q < TT; ++q) acc[q] = __fadd_rn(acc[q], __shfl_xor_sync(0xffffffffu, acc[q], off));
-        if (ok && sub < TT && sub < n) {
-          float v = acc[0];
-          int sl = slot_of[0];
-#pragma unroll
-          for (int q = 1; q < TT; ++q)
-            if (sub == q) { v = acc[q]; sl = slot_of[q]; }
-          a.y[static_cast<size_t>(sl) * d + r0 + rl] = f32_to_bf16(__fmul_rn(v, rscale[p0 + sub]));
+        for (int c = c0; c < c1; ++c) {
+          const uint4 xv = *reinterpret_cast<const uint4*>(xrow + 32 * c);
+          const uint32_t wa = *reinterpret_cast<const uint32_t*>(w0r + 16 * c);
+          const uint32_t wb = *reinterpret_cast<const uint32_t*>(w1r + 16 * c);
+          const uint32_t wc = *reinterpret_cast<const uint32_t*>(w2r + 16 * c);
+          const uint32_t wd = *reinterpret_cast<const uint32_t*>(w3r + 16 * c);
+          const float sa = e8m0_to_f32(s0[c]), sb = e8m0_to_f32(s0[8 * sstr + c]);
+          const float sc_ = e8m0_to_f32(s0[16 * sstr + c]), sd = e8m0_to_f32(s0[24 * sstr + c]);
+          float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
+          group_mma(t0, wa, wb, xv);
+          group_mma(t1, wc, wd, xv);
+          d0[0] = __fmaf_rn(t0[0], sa, d0[0]);
+          d0[1] = __fmaf_rn(t0[1], sa, d0[1]);
+          d0[2] = __fmaf_rn(t0[2], sb, d0[2]);
+          d0[3] = __fmaf_rn(t0[3], sb, d0[3]);
+          d1[0] = __fmaf_rn(t1[0], sc_, d1[0]);
+          d1[1] = __fmaf_rn(t1[1], sc_, d1[1]);
+          d1[2] = __fmaf_rn(t1[2], sd, d1[2]);
+          d1[3] = __fmaf_rn(t1[3], sd, d1[3]);
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
+      float* rr2 = red_r + ((grp * 2 + (rti & 1)) * kConsumerWarps + warp) * kDnRowsRouted * TT;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int col = 2 * q4 + h;
+        if (col < n && col < TT) {
+          rr2[(g8)*TT + col] = d0[h];
+          rr2[(g8 + 8) * TT + col] = d0[2 + h];
+          rr2[(g8 + 16) * TT + col] = d1[h];
+          rr2[(g8 + 24) * TT + col] = d1[2 + h];
+        }
+      }
+      named_sync(1 + grp, kConsumerThreads);
+      if (ok) {
+        const float* base = red_r + (grp * 2 + (rti & 1)) * kConsumerWarps * kDnRowsRouted * TT;
+        for (int o = gt; o < kDnRowsRouted * n; o += kConsumerThreads) {
+          const int row = o / n, col = o - row * n;
+          float v = 0.f;
+          for (int w = 0; w < kConsumerWarps; ++w) v = __fadd_rn(v, base[(w * kDnRowsRouted + row) * TT + col]);
+          a.y[static_cast<size_t>(s_perm[p0 + col]) * d + r0 + row] = f32_to_bf16(__fmul_rn(v, rscale[p0 + col]));
+        }
+      }
+      ++rti;
     }
   }
 }
