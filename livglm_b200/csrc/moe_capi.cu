@@ -332,12 +332,6 @@ int conflict_free_stride(int row_bytes) {
   return row_bytes;
 }
 
-void plan_rows(int row_bytes, int g_bytes, lg::StreamCfg* sc) {
-  sc->rs = conflict_free_stride(row_bytes);
-  if (g_bytes % 16 == 0) { sc->ss_rows = 1; sc->ss = conflict_free_stride(g_bytes); }
-  else { sc->ss_rows = 0; sc->ss = g_bytes; }
-}
-
 bool plan_stream(const lg_moe_config* c, int M, int TT, StreamPlan* P) {
   const size_t d = c->hidden_size, F = c->moe_intermediate_size, Fs = F * c->n_shared_experts;
   const size_t E = c->n_routed_experts;
@@ -345,9 +339,10 @@ bool plan_stream(const lg_moe_config* c, int M, int TT, StreamPlan* P) {
   const size_t GF = F / 32, WS = (Fs / 8 + 31) / 32, R = static_cast<size_t>(M) * c->num_experts_per_tok;
   const size_t tables = (2 * ((E + 1 + 3) & ~size_t(3)) + R + 4) * 4;
   // gate/up
-  plan_rows(static_cast<int>(d / 2), static_cast<int>(G), &P->gu);
+  P->gu.rs = conflict_free_stride(static_cast<int>(d / 2));
+  P->gu.ss = static_cast<int>(G); P->gu.ss_rows = 0;
   const size_t gu_stage = std::max<size_t>(Fs > 0 ? 2 * lg::kGuRowsShared * d * 2 : 0,
-                                           2 * lg::kGuRowsRouted * (P->gu.rs + P->gu.ss));
+                                           2 * lg::kGuRowsRouted * (P->gu.rs + G));
   const size_t gu_x = TT * d * 2 + TT * 4 * WPL * 32 * 16;
   const size_t gu_aux = (lg::kGroups * 2 * lg::kGuRowsShared * 4 * TT * 2 +
                          lg::kGroups * 2 * lg::kConsumerWarps * 8 * TT * 2) * 4 + tables;
@@ -360,9 +355,11 @@ bool plan_stream(const lg_moe_config* c, int M, int TT, StreamPlan* P) {
   P->gu.aux_off = static_cast<int>(P->gu.x_off + gu_x);
   P->gu_smem = P->gu.aux_off + gu_aux;
   // down
-  plan_rows(static_cast<int>(F / 2), static_cast<int>(GF), &P->dn);
+  // down: blocks of 4 rows; block stride/4 must be 4*odd mod 32 (see the kernel)
+  P->dn.rs = conflict_free_stride(static_cast<int>(2 * F));
+  P->dn.ss = static_cast<int>(GF); P->dn.ss_rows = 0;
   const size_t dn_stage = std::max<size_t>(Fs > 0 ? lg::kDnRowsShared * Fs * 2 : 0,
-                                           lg::kDnRowsRouted * (P->dn.rs + P->dn.ss));
+                                           (lg::kDnRowsRouted / 4) * P->dn.rs + lg::kDnRowsRouted * GF);
   const size_t dn_x = R * F * 2 + static_cast<size_t>(M) * WS * 32 * 16;
   const size_t dn_aux = (((R + 3) & ~size_t(3)) + lg::kGroups * 2 * lg::kConsumerWarps * lg::kDnRowsRouted * TT) * 4 +
                         tables;

@@ -218,10 +218,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
       issue_rows(st, a.gate_p + e * a.gate_ps + f0 * rb, kGuRowsRouted, rb, sc.rs, lane, &full[s]);
       issue_rows(st + kGuRowsRouted * sc.rs, a.up_p + e * a.up_ps + f0 * rb, kGuRowsRouted, rb, sc.rs, lane,
                  &full[s]);
-      unsigned char* sst = st + 2 * kGuRowsRouted * sc.rs;
-      issue_scales(sst, a.gate_s + e * a.gate_ss + f0 * G, kGuRowsRouted, G, sc.ss, sc.ss_rows, lane, &full[s]);
-      issue_scales(sst + kGuRowsRouted * sc.ss, a.up_s + e * a.up_ss + f0 * G, kGuRowsRouted, G, sc.ss,
-                   sc.ss_rows, lane, &full[s]);
+      unsigned char* sst = st + 2 * kGuRowsRouted * sc.rs;  // gate scales [8][G], then up scales [8][G]
+      if (lane == 0) bulk_g2s(sst, a.gate_s + e * a.gate_ss + f0 * G, kGuRowsRouted * G, &full[s]);
+      if (lane == 1) bulk_g2s(sst + kGuRowsRouted * G, a.up_s + e * a.up_ss + f0 * G, kGuRowsRouted * G, &full[s]);
     }
     if (!ok && lane == 0) {  // consumers stopped: let copies already issued land before leaving
       for (int q = (it > S ? it - S : 0); q < it; ++q)
@@ -377,22 +376,42 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
       const unsigned char* wlo = st + static_cast<size_t>(g8) * sc.rs + 4 * q4;                  // gate row g
       const unsigned char* whi = st + static_cast<size_t>(kGuRowsRouted + g8) * sc.rs + 4 * q4;  // up row g
       const unsigned char* sst = st + 2 * kGuRowsRouted * sc.rs;
-      const unsigned char* slo = sst + (sc.ss_rows ? g8 * sc.ss : g8 * G);
-      const unsigned char* shi = sst + (sc.ss_rows ? (kGuRowsRouted + g8) * sc.ss : (kGuRowsRouted + g8) * G);
+      const unsigned char* slo = sst + g8 * G;
+      const unsigned char* shi = sst + (kGuRowsRouted + g8) * G;
       const uint16_t* xrow = xh + static_cast<size_t>(col_tok) * K + 8 * q4;
       const int c0 = warp * gpw, c1 = min(G, c0 + gpw);
-#pragma unroll 4
-      for (int c = c0; c < c1; ++c) {
-        const uint32_t wl = *reinterpret_cast<const uint32_t*>(wlo + 16 * c);
-        const uint32_t wh = *reinterpret_cast<const uint32_t*>(whi + 16 * c);
-        const uint4 xv = *reinterpret_cast<const uint4*>(xrow + 32 * c);
-        const float sl = e8m0_to_f32(slo[c]), sh = e8m0_to_f32(shi[c]);
-        float t4[4] = {0.f, 0.f, 0.f, 0.f};
-        group_mma(t4, wl, wh, xv);
-        d[0] = __fmaf_rn(t4[0], sl, d[0]);
-        d[1] = __fmaf_rn(t4[1], sl, d[1]);
-        d[2] = __fmaf_rn(t4[2], sh, d[2]);
-        d[3] = __fmaf_rn(t4[3], sh, d[3]);
+      if (gpw == 16 && (G & 15) == 0) {  // the warp's 16 scale bytes per row in one load
+        const uint4 vl = *reinterpret_cast<const uint4*>(slo + c0);
+        const uint4 vh = *reinterpret_cast<const uint4*>(shi + c0);
+        const uint32_t sl4[4] = {vl.x, vl.y, vl.z, vl.w}, sh4[4] = {vh.x, vh.y, vh.z, vh.w};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c = c0 + i;
+          const uint32_t wl = *reinterpret_cast<const uint32_t*>(wlo + 16 * c);
+          const uint32_t wh = *reinterpret_cast<const uint32_t*>(whi + 16 * c);
+          const uint4 xv = *reinterpret_cast<const uint4*>(xrow + 32 * c);
+          const float sl = e8m0_to_f32((sl4[i >> 2] >> (8 * (i & 3))) & 0xffu);
+          const float sh = e8m0_to_f32((sh4[i >> 2] >> (8 * (i & 3))) & 0xffu);
+          float t4[4] = {0.f, 0.f, 0.f, 0.f};
+          group_mma(t4, wl, wh, xv);
+          d[0] = __fmaf_rn(t4[0], sl, d[0]);
+          d[1] = __fmaf_rn(t4[1], sl, d[1]);
+          d[2] = __fmaf_rn(t4[2], sh, d[2]);
+          d[3] = __fmaf_rn(t4[3], sh, d[3]);
+        }
+      } else {
+        for (int c = c0; c < c1; ++c) {
+          const uint32_t wl = *reinterpret_cast<const uint32_t*>(wlo + 16 * c);
+          const uint32_t wh = *reinterpret_cast<const uint32_t*>(whi + 16 * c);
+          const uint4 xv = *reinterpret_cast<const uint4*>(xrow + 32 * c);
+          const float sl = e8m0_to_f32(slo[c]), sh = e8m0_to_f32(shi[c]);
+          float t4[4] = {0.f, 0.f, 0.f, 0.f};
+          group_mma(t4, wl, wh, xv);
+          d[0] = __fmaf_rn(t4[0], sl, d[0]);
+          d[1] = __fmaf_rn(t4[1], sl, d[1]);
+          d[2] = __fmaf_rn(t4[2], sh, d[2]);
+          d[3] = __fmaf_rn(t4[3], sh, d[3]);
+        }
       }
     }
     __syncwarp();
@@ -484,9 +503,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
         const int jr = j - n_sh;
         const int e = s_active[1 + jr / nrb];
         const size_t r0 = static_cast<size_t>(jr % nrb) * kDnRowsRouted;
-        issue_rows(st, a.down_p + e * a.down_ps + r0 * rb, kDnRowsRouted, rb, sc.rs, lane, &full[s]);
-        issue_scales(st + kDnRowsRouted * sc.rs, a.down_s + e * a.down_ss + r0 * G, kDnRowsRouted, G, sc.ss,
-                     sc.ss_rows, lane, &full[s]);
+        // 8 blocks of 4 consecutive rows at padded stride sc.rs, then the
+        // chunk's scale rows as one block [32][G]
+        issue_rows(st, a.down_p + e * a.down_ps + r0 * rb, kDnRowsRouted / 4, 4 * rb, sc.rs, lane, &full[s]);
+        if (lane == 31)
+          bulk_g2s(st + (kDnRowsRouted / 4) * sc.rs, a.down_s + e * a.down_ss + r0 * G, kDnRowsRouted * G, &full[s]);
       }
     }
     if (!ok && lane == 0) {
@@ -608,16 +629,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
       const int r0 = (jr % nrb) * kDnRowsRouted;
       const int p0 = s_offsets[e];
       const int n = s_offsets[e + 1] - p0;
+      // tile t (0, 1): MMA row m < 8 is row 4m + 2t, row m + 8 is row 4m + 2t + 1;
+      // the 8 rows of one fragment load sit in 8 differently padded blocks
       float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
       if (ok) {
         const uint16_t* xrow = xr + static_cast<size_t>(p0 + (g8 < n ? g8 : 0)) * F + 8 * q4;
-        const unsigned char* w0r = st + static_cast<size_t>(g8) * sc.rs + 4 * q4;
-        const unsigned char* w1r = w0r + 8 * static_cast<size_t>(sc.rs);
-        const unsigned char* w2r = w0r + 16 * static_cast<size_t>(sc.rs);
-        const unsigned char* w3r = w0r + 24 * static_cast<size_t>(sc.rs);
-        const unsigned char* sst = st + kDnRowsRouted * sc.rs;
-        const int sstr = sc.ss_rows ? sc.ss : G;
-        const unsigned char* s0 = sst + g8 * sstr;
+        const int rb = F >> 1;
+        const unsigned char* blkp = st + static_cast<size_t>(g8) * sc.rs + 4 * q4;
+        const unsigned char* w0r = blkp;           // row 4g
+        const unsigned char* w1r = blkp + rb;      // row 4g + 1
+        const unsigned char* w2r = blkp + 2 * rb;  // row 4g + 2
+        const unsigned char* w3r = blkp + 3 * rb;  // row 4g + 3
+        const unsigned char* s0 = st + (kDnRowsRouted / 4) * sc.rs + (4 * g8) * G;
         const int c0 = warp * gpw, c1 = min(G, c0 + gpw);
 #pragma unroll 2
         for (int c = c0; c < c1; ++c) {
@@ -626,11 +649,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
           const uint32_t wb = *reinterpret_cast<const uint32_t*>(w1r + 16 * c);
           const uint32_t wc = *reinterpret_cast<const uint32_t*>(w2r + 16 * c);
           const uint32_t wd = *reinterpret_cast<const uint32_t*>(w3r + 16 * c);
-          const float sa = e8m0_to_f32(s0[c]), sb = e8m0_to_f32(s0[8 * sstr + c]);
-          const float sc_ = e8m0_to_f32(s0[16 * sstr + c]), sd = e8m0_to_f32(s0[24 * sstr + c]);
+          const float sa = e8m0_to_f32(s0[c]), sb = e8m0_to_f32(s0[G + c]);
+          const float sc_ = e8m0_to_f32(s0[2 * G + c]), sd = e8m0_to_f32(s0[3 * G + c]);
           float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
-          group_mma(t0, wa, wb, xv);
-          group_mma(t1, wc, wd, xv);
+          group_mma(t0, wa, wb, xv);  // rows 4g (m = g) and 4g+1 (m = g+8)
+          group_mma(t1, wc, wd, xv);  // rows 4g+2 and 4g+3
           d0[0] = __fmaf_rn(t0[0], sa, d0[0]);
           d0[1] = __fmaf_rn(t0[1], sa, d0[1]);
           d0[2] = __fmaf_rn(t0[2], sb, d0[2]);
@@ -648,10 +671,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
       for (int h = 0; h < 2; ++h) {
         const int col = 2 * q4 + h;
         if (col < n && col < TT) {
-          rr2[(g8)*TT + col] = d0[h];
-          rr2[(g8 + 8) * TT + col] = d0[2 + h];
-          rr2[(g8 + 16) * TT + col] = d1[h];
-          rr2[(g8 + 24) * TT + col] = d1[2 + h];
+          rr2[(4 * g8 + 0) * TT + col] = d0[h];
+          rr2[(4 * g8 + 1) * TT + col] = d0[2 + h];
+          rr2[(4 * g8 + 2) * TT + col] = d1[h];
+          rr2[(4 * g8 + 3) * TT + col] = d1[2 + h];
         }
       }
       named_sync(1 + grp, kConsumerThreads);
