@@ -20,8 +20,12 @@
  *  - Device-side failures cannot be returned from a stream-ordered call: the
  *    first 4 bytes of the workspace are a status word that kernels set when a
  *    bounded wait gives up (LG_ERR_TIMEOUT in the low byte, the waiting site
- *    above it).  Zero the workspace once after allocating it; the library
- *    never clears the status word, so it stays set until the caller clears it.
+ *    above it).  Zero the workspace once after allocating it: besides the
+ *    status word it holds the grid counters of the fused decode kernel, which
+ *    every call leaves at zero for the next one (a call that finds them
+ *    nonzero computes garbage and sets LG_ERR_WORKSPACE in the status word).
+ *    The library never clears the status word; it stays set until the caller
+ *    clears it.
  *  - Routed expert tensors are banks: expert e's tensor starts at
  *    base + e * stride (bytes) and is byte-identical to the checkpoint's
  *      model.language_model.layers.{L}.mlp.experts.{e}.{gate,up}_proj.weight_packed  U8 [F, d/2]

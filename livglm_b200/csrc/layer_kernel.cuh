@@ -1,0 +1,1278 @@
+// Fused decode MoE block for 1..4 tokens: one persistent cooperative kernel.
+//
+// Every CTA (one per SM) runs a single bulk-copy ring: one producer warp
+// issues the copies, eight consumer warps work on every stage.  The ring
+// carries, in this order, everything the CTA reads from HBM:
+//
+//   phase 1  router rows (f32)      -> logits            (moe.py:37-38)
+//            shared gate/up rows    -> shared act        (layers.py:160-171)
+//            routed gate/up rows    -> routed act        (expert_ssd.py:96-107)
+//   phase 2  shared down rows       -> shared y          (layers.py:160-171)
+//            routed down rows       -> routed y          (expert_ssd.py:96-107)
+//            then the weighted merge of this CTA's output rows (moe.py:199-201)
+//
+// Two grid-wide counters order the phases.  The producer warp of every CTA
+// adds its router rows to `logits` once its consumers wrote them, waits until
+// all E logits exist and computes the routing (sigmoid, bias, group-limited
+// top-k, weights, the stable dispatch of the M*k routes) itself, so no CTA
+// waits for another one's tables.  Each CTA adds one to `act` when its
+// phase-1 results are written; consumers wait for all CTAs before the down
+// phase while the producer keeps streaming down weights into the ring.  The
+// last CTA to finish resets the counters, so every call starts from zero.
+// All CTAs must be resident at once: the kernel is launched cooperatively
+// with one CTA per SM, and every wait gives up after kWaitLimitNs with a
+// status word.
+//
+// Work split: router rows e = b, b+P, ...; gate/up chunks j = b, b+P, ...
+// over the shared chunks followed by the routed chunks of the active experts
+// (expert-major); down rows [r_lo, r_hi) of CTA b for the shared expert and
+// every active expert, so the merge of those rows is local and in route order.
+//
+// Latency: with the ring streaming, one L2 round trip costs microseconds, so
+// every global read off the ring (x, bias, logits, act) is issued as one batch
+// of independent loads, and the dot products interleave 4-8 independent
+// accumulation chains per thread (two consumer warps per SM sub-partition
+// cannot hide dependent-FMA latency otherwise).
+//
+// Arithmetic.  Router: the canonical fp32 order (32 lane partials, butterfly)
+// that the CPU checker restates, so routing is bit-exact.  MXFP4 rows: E2M1
+// pairs -> f16x2 (cvt.rn.f16x2.e2m1x2, exact) times f16 activations with
+// packed f16x2 FMAs over 8-product chains, each chain's two halves summed in
+// f32 and scaled by the E8M0 group scale in f32.  Activation rows are scaled
+// by a power of two so that max|v| < 2^8 (chains stay below 2^14, no f16
+// overflow) and the scale is undone exactly in f32.  bf16 rows (shared
+// expert): mixed fma.rn.f32.bf16 into f32.
+#pragma once
+#include "decode_kernels.cuh"
+#include "pipeline.cuh"
+
+namespace lg {
+namespace layer {
+
+constexpr int kWarps = 8;                  // consumer warps; all of them work on every stage
+constexpr int kConsumers = kWarps * 32;
+constexpr int kCtl = 4;                    // control warps: copy issue, routing (one token each)
+constexpr int kThreads = kConsumers + kCtl * 32;
+constexpr int kBarCons = 1;                // named barrier over the consumer warps
+constexpr int kBarCtl = 2;                 // named barrier over the control warps
+constexpr int kNRed = 4;                   // cross-warp reduction buffers
+constexpr int kMaxStages = 8;
+constexpr int kGuRows = 8;      // routed gate/up rows per chunk
+constexpr int kShGuRows = 2;    // shared gate/up rows per chunk
+constexpr int kShDnRows = 8;    // shared down rows per chunk (warp per row)
+constexpr int kDnRowsMax = 32;  // routed down rows per chunk (16 row sets x 2)
+constexpr int kMaxRoutes = 32;  // M * k
+constexpr int kMaxExperts = 256;
+constexpr int kMaxGroups = 32;
+constexpr int kXRegs = 4;       // uint4 per consumer thread when staging x
+constexpr int kActRegs = 12;    // uint4 per consumer thread when staging act
+constexpr int kActSRegs = 2;    // uint4 per consumer thread when staging act_s
+
+// status sites (LG_ERR_TIMEOUT | site << 8)
+constexpr int kSiteFull = 7 << 8, kSiteEmpty = 8 << 8, kSiteDrain = 9 << 8;
+constexpr int kSiteLogits = 10 << 8, kSiteAct = 11 << 8, kSiteTable = 12 << 8;
+constexpr int kSiteSync = 13 << 8;
+constexpr int kSiteRed = 14 << 8;  // with LG_ERR_WORKSPACE: grid counters were not zero on entry
+
+struct Args {
+  int M, d, F, Fs, E, k, G, g, norm;
+  float scale, limit;
+  const uint16_t* x;
+  const float *Wr, *bias;
+  const uint8_t *gate_p, *gate_s, *up_p, *up_s, *down_p, *down_s;
+  long long gate_ps, gate_ss, up_ps, up_ss, down_ps, down_ss;
+  const uint16_t *sh_gate, *sh_up, *sh_down;
+  float* logits;    // [M, E] workspace
+  float* w_out;     // [M, k] or NULL
+  uint32_t* i_out;  // [M, k] or NULL
+  uint16_t* act;    // [M*k, F] workspace, route-position order
+  uint16_t* act_s;  // [M, Fs] workspace
+  float* out;       // [M, d]
+  int* status;
+  unsigned* sync;   // [0] logits rows done, [1] CTAs past phase 1, [2] CTAs done
+};
+
+// Host-computed shared-memory plan (all offsets in bytes from the dynamic base).
+struct Plan {
+  int stages, stage_bytes;
+  int x_off;     // union: x (phase 1) / act (phase 2)
+  int y_off;     // y rows [M*k + TT][rows_max] f32
+  int rpr;       // router rows per router chunk
+  int unit;      // down-partition row unit (rows * F/32 is a multiple of 16)
+  int sub_rows;  // routed down rows per chunk
+  int sh_rows;   // shared down rows per chunk
+  int rows_max;  // most down rows of one CTA
+};
+
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// bounded wait until *p >= target
+__device__ __forceinline__ bool spin_geq(const unsigned* p, unsigned target, int* status, int site) {
+  if (ld_acquire(p) >= target) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (ld_acquire(p) < target) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicExch(status, 6 | site);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
+// try_wait that may suspend the thread in the barrier for up to `hint_ns`
+// (instead of a busy poll that takes issue slots and shared-memory bandwidth
+// from the warps doing work)
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* b, unsigned parity, unsigned hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait by one lane, then every lane of the warp observes the completed
+// phase itself (each gets the acquire).  Returns the same result in all lanes.
+__device__ __forceinline__ bool wait_warp(uint64_t* b, unsigned parity, int* status, int site, int lane) {
+  unsigned good = 1u;
+  if (lane == 0 && !mbar_try_wait_sleep(b, parity, 20000u)) {
+    const unsigned long long t0 = globaltimer_ns();
+    while (!mbar_try_wait_sleep(b, parity, 20000u)) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicExch(status, 6 | site);
+        good = 0u;
+        break;
+      }
+    }
+  }
+  good = __shfl_sync(0xffffffffu, good, 0);
+  // the phase is complete, so this returns at once; the cap only bounds it
+  for (int n = 0; good && n < (1 << 20) && !mbar_try_wait(b, parity); ++n) {
+  }
+  return good != 0u;
+}
+
+__device__ __forceinline__ uint4 lds128(const unsigned char* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ unsigned fold4(const uint4& v) { return v.x ^ v.y ^ v.z ^ v.w; }
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+// volatile: keeps the conversions in program order, so the scheduler does not
+// hoist every row's converted weights at once (which spills registers)
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
+  asm volatile("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+               "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+               "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+               "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+               : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+               : "r"(w));
+}
+__device__ __forceinline__ float f16x2_sum(uint32_t h) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+  return __fadd_rn(f.x, f.y);
+}
+
+// NR x NC MXFP4 groups w[r][c] (16 packed bytes = 32 E2M1 values each)
+// against TP activation rows: part[r][c][q] = the 32 products of group (r, c)
+// with activation row q, column group c.  Activation words (8 f16) of row q,
+// group c are at x[c][q] + wq * xs, wq = 0..3.  Each (r, c, q) accumulates in
+// two f16x2 chains of 8 products (words 0-1, words 2-3); all NR*NC*TP chains
+// are interleaved.
+template <int NR, int NC, int TP>
+__device__ __forceinline__ void mx_dot(const uint4 (&w)[NR][NC], const uint4* const (&x)[NC][TP], int xs,
+                                       float (&part)[NR][NC][TP]) {
+  uint32_t ch[NR][NC][TP][2];
+#pragma unroll
+  for (int r = 0; r < NR; ++r)
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int q = 0; q < TP; ++q) { ch[r][c][q][0] = 0u; ch[r][c][q][1] = 0u; }
+#pragma unroll
+  for (int wq = 0; wq < 4; ++wq) {
+    uint4 xv[NC][TP];
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int q = 0; q < TP; ++q) xv[c][q] = x[c][q][wq * xs];
+    uint32_t h[NR][NC][4];
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+#pragma unroll
+      for (int c = 0; c < NC; ++c) e2m1x8_to_f16x2(word_of(w[r][c], wq), h[r][c]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int r = 0; r < NR; ++r)
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+#pragma unroll
+          for (int q = 0; q < TP; ++q)
+            ch[r][c][q][wq >> 1] = hfma2(h[r][c][j], word_of(xv[c][q], j), ch[r][c][q][wq >> 1]);
+  }
+#pragma unroll
+  for (int r = 0; r < NR; ++r)
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+#pragma unroll
+      for (int q = 0; q < TP; ++q) part[r][c][q] = __fadd_rn(f16x2_sum(ch[r][c][q][0]), f16x2_sum(ch[r][c][q][1]));
+}
+
+// NV bf16 groups w[v] (4 uint4 = 32 values each) against TP bf16 activation
+// groups (words at x[q] + wq * xs): part[v][q], one f32 chain per word.
+template <int NV, int TP>
+__device__ __forceinline__ void bf_dot(const uint4 (&w)[NV][4], const uint4* const (&x)[TP], int xs,
+                                       float (&part)[NV][TP]) {
+  float ch[NV][4][TP];
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+#pragma unroll
+    for (int wq = 0; wq < 4; ++wq)
+#pragma unroll
+      for (int q = 0; q < TP; ++q) ch[v][wq][q] = 0.f;
+  uint4 xv[4][TP];
+#pragma unroll
+  for (int wq = 0; wq < 4; ++wq)
+#pragma unroll
+    for (int q = 0; q < TP; ++q) xv[wq][q] = x[q][wq * xs];
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+#pragma unroll
+    for (int wq = 0; wq < 4; ++wq)
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+#pragma unroll
+        for (int q = 0; q < TP; ++q)
+          ch[v][wq][q] = fma_bf16(word_of(w[v][wq], e), word_of(xv[wq][q], e), ch[v][wq][q]);
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+#pragma unroll
+    for (int q = 0; q < TP; ++q)
+      part[v][q] = __fadd_rn(__fadd_rn(ch[v][0][q], ch[v][1][q]), __fadd_rn(ch[v][2][q], ch[v][3][q]));
+}
+
+// Reduce V values over SEG lanes (aligned segments of a warp) by halving:
+// afterwards lane l holds in v[0] the segment total of value index
+// (l % SEG) / (SEG / V).  Deterministic order.
+template <int N, int O>
+struct Halve {
+  template <int V>
+  static __device__ __forceinline__ void run(float (&v)[V], int lane) {
+    if constexpr (O >= 1) {
+      if constexpr (N > 1) {
+        const bool upper = (lane & O) != 0;
+#pragma unroll
+        for (int i = 0; i < N / 2; ++i) {
+          const float send = upper ? v[i] : v[i + N / 2];
+          const float keep = upper ? v[i + N / 2] : v[i];
+          v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, O));
+        }
+        Halve<N / 2, O / 2>::run(v, lane);
+      } else {
+        v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], O));
+        Halve<1, O / 2>::run(v, lane);
+      }
+    }
+  }
+};
+template <int V, int SEG>
+__device__ __forceinline__ void reduce_scatter(float (&v)[V], int lane) {
+  static_assert(V <= SEG && (V & (V - 1)) == 0, "V must be a power of two <= SEG");
+  Halve<V, SEG / 2>::run(v, lane);
+}
+
+// power-of-two activation scale: max|v| * 2^-shift < 2^8
+__device__ __forceinline__ int act_shift(float amax) {
+  const int e = static_cast<int>((__float_as_uint(amax) >> 23) & 0xffu) - 127;
+  if (amax == 0.0f) return 0;
+  const int s = e - 7;
+  return s < -120 ? -120 : (s > 120 ? 120 : s);
+}
+__device__ __forceinline__ float absmax8_bf16(const uint4& u) {
+  float m = fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y))));
+  return fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
+}
+__device__ __forceinline__ uint4 bf16x8_to_f16x8_scaled(const uint4& u, float s) {
+  return make_uint4(bf16x2_to_f16x2_scaled(u.x, s), bf16x2_to_f16x2_scaled(u.y, s), bf16x2_to_f16x2_scaled(u.z, s),
+                    bf16x2_to_f16x2_scaled(u.w, s));
+}
+
+// ---------------------------------------------------------------------------
+// Routing of one CTA, computed by the producer warp from the global logits.
+// Restates TopKRouter.__call__ (moe.py:39-62) with the stable (value, index)
+// order of the CPU checker; results go to shared memory.
+struct Tables {
+  int ae[kMaxRoutes];    // active experts, ascending id
+  int ap0[kMaxRoutes];   // first route position of active expert
+  int an[kMaxRoutes];    // routes of active expert
+  int perm[kMaxRoutes];  // route position -> slot t*k + j
+  int sel[kMaxRoutes];   // slot -> expert
+  float w[kMaxRoutes];   // slot -> route weight
+  int n_active;
+  float bias[kMaxExperts];
+  float sc[kMaxExperts];
+  float ch[kMaxExperts];
+};
+
+// Segmented (value, index) argmax over aligned groups of `seg` lanes
+// (seg a power of two <= 32): every lane ends with its segment's best.
+__device__ __forceinline__ void seg_best(float& v, int& i, int seg) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    if (off < seg) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, i, off);
+      if (after(ov, oi, v, i)) { v = ov; i = oi; }
+    }
+  }
+}
+
+// Routing of token t by one warp, every score in registers: lane l holds
+// experts l + 32q.  Same results as the sequential scans of the checker for
+// the stable (value, index) order: group top-2 by two segmented argmaxes
+// (groups of `per` lanes, per | 32), kept groups by rank, top-k by k warp
+// argmaxes.  Writes T.sel[t*k + j] and T.w[t*k + j].  Returns false (and does
+// nothing) for group sizes that are not a divisor of 32.
+__device__ __forceinline__ bool route_token_warp(const Args& a, Tables& T, int t, int lane, bool write_out) {
+  constexpr int V = kMaxExperts / 32;
+  const int E = a.E, G = a.G, k = a.k, per = E / G;
+  if (a.g < G && (per > 32 || (32 % per) != 0)) return false;
+  const float ninf = __uint_as_float(0xff800000u);
+  float lg[V], sc[V], ch[V];
+#pragma unroll
+  for (int q = 0; q < V; ++q) {
+    const int e = lane + 32 * q;
+    lg[q] = e < E ? __ldcg(a.logits + static_cast<size_t>(t) * E + e) : 0.f;
+  }
+#pragma unroll
+  for (int q = 0; q < V; ++q) {
+    const int e = lane + 32 * q;
+    sc[q] = e < E ? own_sigmoidf(lg[q]) : 0.f;
+    ch[q] = e < E ? __fadd_rn(sc[q], T.bias[e]) : ninf;
+  }
+  if (a.g < G) {
+    // group score = second best + best of the group, in the group's lanes
+    float gsc[V];
+#pragma unroll
+    for (int q = 0; q < V; ++q) {
+      const int e = lane + 32 * q;
+      float v1 = ch[q];
+      int i1 = e < E ? e : -1;
+      seg_best(v1, i1, per);
+      float v2 = ch[q];
+      int i2 = (e < E && e != i1) ? e : -1;
+      seg_best(v2, i2, per);
+      gsc[q] = __fadd_rn(v2, v1);
+    }
+    // lane gi < G takes the score of group gi, then its rank among the groups
+    float mine = ninf;
+    const int src = (lane * per) & 31, qs = (lane * per) >> 5;
+#pragma unroll
+    for (int q = 0; q < V; ++q) {
+      const float sv = __shfl_sync(0xffffffffu, gsc[q], src);
+      if (q == qs) mine = sv;
+    }
+    int rank = 0;
+    for (int gj = 0; gj < G; ++gj) {
+      const float sj = __shfl_sync(0xffffffffu, mine, gj);
+      rank += after(sj, gj, mine, lane) ? 1 : 0;
+    }
+    const unsigned keep = __ballot_sync(0xffffffffu, lane < G && rank < a.g);
+#pragma unroll
+    for (int q = 0; q < V; ++q) {
+      const int e = lane + 32 * q;
+      if (e < E && !((keep >> (e / per)) & 1u)) ch[q] = ninf;
+    }
+  }
+  // top-k, best first; slot k-1-s gets the s-th best
+  unsigned taken = 0u;
+  float wj = 0.f;
+  for (int s = 0; s < k; ++s) {
+    float v = 0.f;
+    int i = -1;
+#pragma unroll
+    for (int q = 0; q < V; ++q) {
+      const int e = lane + 32 * q;
+      if (e < E && !((taken >> q) & 1u) && (i < 0 || after(ch[q], e, v, i))) { v = ch[q]; i = e; }
+    }
+    warp_best(v, i);
+    const int qo = i >> 5;
+    float c = 0.f;
+#pragma unroll
+    for (int q = 0; q < V; ++q)
+      if (q == qo) c = sc[q];
+    const float sw = __shfl_sync(0xffffffffu, c, i & 31);
+    if ((i & 31) == lane) taken |= 1u << qo;
+    if (lane == k - 1 - s) wj = sw;
+    if (lane == 0) T.sel[t * k + (k - 1 - s)] = i;
+  }
+  // weights: sequential sum over the k routes in output order
+  float denom = 1.f;
+  if (a.norm) {
+    float sum = __shfl_sync(0xffffffffu, wj, 0);
+    for (int j = 1; j < k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, wj, j));
+    denom = __fadd_rn(sum, 0x1.79ca1p-67f);
+  }
+  __syncwarp();
+  if (lane < k) {
+    const float w = __fmul_rn(a.norm ? __fdiv_rn(wj, denom) : wj, a.scale);
+    T.w[t * k + lane] = w;
+    if (write_out && a.w_out) a.w_out[static_cast<size_t>(t) * k + lane] = w;
+    if (write_out && a.i_out) a.i_out[static_cast<size_t>(t) * k + lane] = static_cast<uint32_t>(T.sel[t * k + lane]);
+  }
+  __syncwarp();
+  return true;
+}
+
+// Same routing by one warp for all tokens, scanning shared memory: the path
+// for group sizes that do not divide 32.
+__device__ __forceinline__ void route_tokens_scan(const Args& a, Tables& T, int lane, bool write_out) {
+  const int E = a.E, G = a.G, k = a.k, per = E / G;
+  const float ninf = __uint_as_float(0xff800000u);
+  for (int t = 0; t < a.M; ++t) {
+    for (int e = lane; e < E; e += 32) {
+      const float s = own_sigmoidf(__ldcg(a.logits + static_cast<size_t>(t) * E + e));
+      T.sc[e] = s;
+      T.ch[e] = __fadd_rn(s, T.bias[e]);
+    }
+    __syncwarp();
+    if (a.g < G) {
+      float gsc = 0.f;
+      if (lane < G) {
+        int b1 = -1, b2 = -1;
+        for (int j = 0; j < per; ++j) {
+          const int e = lane * per + j;
+          if (b1 < 0 || after(T.ch[e], e, T.ch[b1], b1)) { b2 = b1; b1 = e; }
+          else if (b2 < 0 || after(T.ch[e], e, T.ch[b2], b2)) { b2 = e; }
+        }
+        gsc = __fadd_rn(T.ch[b2], T.ch[b1]);
+      }
+      bool kept = false;
+      for (int s = 0; s < a.g; ++s) {
+        float v = gsc;
+        int i = (lane < G && !kept) ? lane : -1;
+        warp_best(v, i);
+        if (lane == i) kept = true;
+      }
+      const unsigned keep = __ballot_sync(0xffffffffu, kept);
+      __syncwarp();
+      for (int e = lane; e < E; e += 32)
+        if (!((keep >> (e / per)) & 1u)) T.ch[e] = ninf;
+      __syncwarp();
+    }
+    unsigned taken = 0u;
+    for (int s = 0; s < k; ++s) {
+      float v = 0.f;
+      int i = -1;
+      for (int q = 0; lane + 32 * q < E; ++q) {
+        const int e = lane + 32 * q;
+        if (!((taken >> q) & 1u) && (i < 0 || after(T.ch[e], e, v, i))) { v = T.ch[e]; i = e; }
+      }
+      warp_best(v, i);
+      if (i >= 0 && (i & 31) == lane) taken |= 1u << (i >> 5);
+      if (lane == 0) T.sel[t * k + (k - 1 - s)] = i;
+    }
+    __syncwarp();
+    const float wj = lane < k ? T.sc[T.sel[t * k + lane]] : 0.f;
+    float denom = 1.f;
+    if (a.norm) {
+      float sum = __shfl_sync(0xffffffffu, wj, 0);
+      for (int j = 1; j < k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, wj, j));
+      denom = __fadd_rn(sum, 0x1.79ca1p-67f);
+    }
+    if (lane < k) {
+      const float w = __fmul_rn(a.norm ? __fdiv_rn(wj, denom) : wj, a.scale);
+      T.w[t * k + lane] = w;
+      if (write_out && a.w_out) a.w_out[static_cast<size_t>(t) * k + lane] = w;
+      if (write_out && a.i_out) a.i_out[static_cast<size_t>(t) * k + lane] = static_cast<uint32_t>(T.sel[t * k + lane]);
+    }
+    __syncwarp();
+  }
+}
+
+// Stable counting sort of the S = M*k route slots by expert (S <= 32: lane =
+// slot): route positions, active experts in ascending id, their first
+// position and route count.
+__device__ __forceinline__ void dispatch_routes(const Args& a, Tables& T, int lane) {
+  const int S = a.M * a.k;
+  const bool valid = lane < S;
+  const int e = valid ? T.sel[lane] : 0x40000000 + lane;
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int rank = __popc(peers & ((1u << lane) - 1u));
+  int below = 0, act_below = 0;
+  const unsigned leaders = __ballot_sync(0xffffffffu, valid && rank == 0);
+  for (int j = 0; j < S; ++j) {
+    const int ej = __shfl_sync(0xffffffffu, e, j);
+    below += ej < e;
+    act_below += ((leaders >> j) & 1u) && ej < e;
+  }
+  if (valid) {
+    T.perm[below + rank] = lane;
+    if (rank == 0) {
+      T.ae[act_below] = e;
+      T.ap0[act_below] = below;
+      T.an[act_below] = __popc(peers);
+    }
+  }
+  if (lane == 0) T.n_active = __popc(leaders);
+  __syncwarp();
+}
+
+// Down rows [r_lo, r_hi) of CTA b: the d rows in units of pl.unit, split
+// evenly over the P CTAs.
+struct DownRange {
+  int r_lo, r_hi, rows, n_sdp, n_sub;
+  __device__ __forceinline__ DownRange(const Args& a, const Plan& pl, int b, int P) {
+    const int nunits = a.d / pl.unit;
+    r_lo = pl.unit * static_cast<int>((static_cast<long long>(b) * nunits) / P);
+    r_hi = pl.unit * static_cast<int>((static_cast<long long>(b + 1) * nunits) / P);
+    rows = r_hi - r_lo;
+    n_sdp = a.Fs > 0 ? (rows + pl.sh_rows - 1) / pl.sh_rows : 0;
+    n_sub = (rows + pl.sub_rows - 1) / pl.sub_rows;
+  }
+};
+
+// ---------------------------------------------------------------------------
+template <int TT>
+__global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) uint64_t full[kMaxStages];
+  __shared__ __align__(8) uint64_t empty[kMaxStages];
+  __shared__ __align__(8) uint64_t tbl;     // routing tables ready
+  __shared__ __align__(8) uint64_t lgdone;  // this CTA's logits written
+  __shared__ Tables T;
+  __shared__ float red[kNRed][kWarps][32];
+  __shared__ int red_cnt[kNRed], red_gen[kNRed];
+  __shared__ int s_go;
+  __shared__ unsigned rel_sink[kConsumers];
+  __shared__ unsigned amax_x[TT];
+  __shared__ float tok_mult[TT];
+  __shared__ unsigned amax_r[kMaxRoutes];
+  __shared__ float rscale[kMaxRoutes];
+  __shared__ int s_nact, s_fail;
+
+  const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int P = gridDim.x, b = blockIdx.x;
+  const int M = a.M, d = a.d, F = a.F, Fs = a.Fs, E = a.E, k = a.k;
+  const int G = d >> 5, G2 = F >> 5, G2s = Fs >> 5;
+  const int S = pl.stages, R = M * k;
+  const int nrb = F / kGuRows, n_sh = Fs / kShGuRows;
+  // chunk sequence: router rows, shared gate/up, routed gate/up, shared down,
+  // routed down (expert-major); the routed parts follow the routing tables
+  const int nrr = b < E ? (E - b + P - 1) / P : 0;
+  const int n_rt = (nrr + pl.rpr - 1) / pl.rpr;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kWarps); }
+    mbar_init(&tbl, 1);
+    mbar_init(&lgdone, kWarps * (n_rt > 0 ? n_rt : 1));
+    mbar_fence_init();
+    T.n_active = 0;
+  }
+  if (threadIdx.x < TT) amax_x[threadIdx.x] = 0u;
+  if (threadIdx.x < kMaxRoutes) amax_r[threadIdx.x] = 0u;
+  if (threadIdx.x < kNRed) { red_cnt[threadIdx.x] = 0; red_gen[threadIdx.x] = 0; }
+  __syncthreads();
+
+  // ============================ control warps ============================
+  // warp kWarps issues the copies (lane 0) and builds the dispatch; the four
+  // control warps route one token each
+  if (warp_id >= kWarps) {
+    const int cw = warp_id - kWarps;
+    bool ok = true;
+    int it = 0;
+    bool signaled = n_rt == 0;
+    // this CTA's logits are written: publish them to the grid
+    auto signal_logits = [&]() {
+      __threadfence();
+      atomicAdd(a.sync + 0, static_cast<unsigned>(nrr));
+      signaled = true;
+    };
+    // lane 0: bounded wait until stage `it` is free (its previous chunk
+    // released by every consumer warp), publishing the logits meanwhile
+    auto stage_free = [&]() -> bool {
+      if (!ok) return false;
+      if (it < S) return true;
+      const unsigned par = ((it / S) - 1) & 1;
+      unsigned long long t0 = 0;
+      while (!mbar_try_wait_sleep(&empty[it % S], par, signaled ? 20000u : 500u)) {
+        if (!signaled && mbar_try_wait(&lgdone, 0)) signal_logits();
+        const unsigned long long t = globaltimer_ns();
+        if (!t0) t0 = t;
+        else if (t - t0 > kWaitLimitNs) {
+          atomicExch(a.status, 6 | kSiteEmpty);
+          ok = false;
+          return false;
+        }
+      }
+      return true;
+    };
+    if (cw == 0 && lane == 0) {
+      const unsigned rrow = static_cast<unsigned>(d) * 4u;
+      for (int rc = 0; rc < n_rt; ++rc, ++it) {
+        if (!stage_free()) continue;
+        const int r0 = rc * pl.rpr, nr = min(pl.rpr, nrr - r0);
+        unsigned char* st = smem + static_cast<size_t>(it % S) * pl.stage_bytes;
+        mbar_arrive_expect_tx(&full[it % S], rrow * nr);
+        for (int r = 0; r < nr; ++r)
+          bulk_g2s(st + r * rrow, a.Wr + static_cast<size_t>(b + P * (r0 + r)) * d, rrow, &full[it % S]);
+      }
+      const unsigned shb = kShGuRows * static_cast<unsigned>(d) * 2u;
+      for (int j = b; j < n_sh; j += P, ++it) {
+        if (!stage_free()) continue;
+        unsigned char* st = smem + static_cast<size_t>(it % S) * pl.stage_bytes;
+        mbar_arrive_expect_tx(&full[it % S], 2 * shb);
+        bulk_g2s(st, a.sh_gate + static_cast<size_t>(j) * kShGuRows * d, shb, &full[it % S]);
+        bulk_g2s(st + shb, a.sh_up + static_cast<size_t>(j) * kShGuRows * d, shb, &full[it % S]);
+      }
+      // publish this CTA's logits, then wait for every logit row
+      if (ok && !signaled) {
+        if (mbar_wait(&lgdone, 0, a.status, kSiteLogits)) signal_logits();
+        else ok = false;
+      }
+      s_go = (ok && spin_geq(a.sync + 0, static_cast<unsigned>(E), a.status, kSiteLogits)) ? 1 : 0;
+    }
+    if (cw == 1) {  // score-correction bias, one batch of loads
+      float bv[kMaxExperts / 32];
+#pragma unroll
+      for (int q = 0; q < kMaxExperts / 32; ++q) bv[q] = lane + 32 * q < E ? a.bias[lane + 32 * q] : 0.f;
+#pragma unroll
+      for (int q = 0; q < kMaxExperts / 32; ++q) T.bias[lane + 32 * q] = bv[q];
+    }
+    named_sync(kBarCtl, kCtl * 32);
+    const bool go = s_go != 0;
+    const int per = E / a.G;
+    const bool scan = a.g < a.G && (per > 32 || (32 % per) != 0);
+    if (go) {
+      __threadfence();
+      if (!scan) {
+        if (cw < M) route_token_warp(a, T, cw, lane, b == 0);
+      } else if (cw == 0) {
+        route_tokens_scan(a, T, lane, b == 0);
+      }
+    }
+    named_sync(kBarCtl, kCtl * 32);
+    if (cw != 0) return;
+    if (go) dispatch_routes(a, T, lane);
+    else ok = false;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&tbl);
+    if (lane == 0) {
+      const int n_r = T.n_active * nrb;
+      const unsigned pk = kGuRows * static_cast<unsigned>(d) / 2u, sk = kGuRows * static_cast<unsigned>(G);
+      int j = b;
+      while (j < n_sh) j += P;
+      for (; j < n_sh + n_r; j += P, ++it) {
+        if (!stage_free()) continue;
+        const int jr = j - n_sh;
+        const int ai = jr / nrb;
+        const long long e = T.ae[ai];
+        const size_t f0 = static_cast<size_t>(jr - ai * nrb) * kGuRows;
+        unsigned char* st = smem + static_cast<size_t>(it % S) * pl.stage_bytes;
+        uint64_t* fb = &full[it % S];
+        mbar_arrive_expect_tx(fb, 2 * pk + 2 * sk);
+        bulk_g2s(st, a.gate_p + e * a.gate_ps + f0 * (d / 2), pk, fb);
+        bulk_g2s(st + pk, a.up_p + e * a.up_ps + f0 * (d / 2), pk, fb);
+        bulk_g2s(st + 2 * pk, a.gate_s + e * a.gate_ss + f0 * G, sk, fb);
+        bulk_g2s(st + 2 * pk + sk, a.up_s + e * a.up_ss + f0 * G, sk, fb);
+      }
+      // down weights need nothing from the gate/up phase
+      const DownRange dr(a, pl, b, P);
+      for (int pc = 0; pc < dr.n_sdp; ++pc, ++it) {
+        if (!stage_free()) continue;
+        const int r0 = dr.r_lo + pc * pl.sh_rows, nr = min(pl.sh_rows, dr.r_hi - r0);
+        const unsigned bytes = static_cast<unsigned>(nr) * Fs * 2u;
+        unsigned char* st = smem + static_cast<size_t>(it % S) * pl.stage_bytes;
+        mbar_arrive_expect_tx(&full[it % S], bytes);
+        bulk_g2s(st, a.sh_down + static_cast<size_t>(r0) * Fs, bytes, &full[it % S]);
+      }
+      for (int ai = 0; ai < T.n_active; ++ai) {
+        const long long e = T.ae[ai];
+        for (int sc = 0; sc < dr.n_sub; ++sc, ++it) {
+          if (!stage_free()) continue;
+          const int r0 = dr.r_lo + sc * pl.sub_rows, nr = min(pl.sub_rows, dr.r_hi - r0);
+          const unsigned pb = static_cast<unsigned>(nr) * (F / 2), sb = static_cast<unsigned>(nr) * G2;
+          unsigned char* st = smem + static_cast<size_t>(it % S) * pl.stage_bytes;
+          uint64_t* fb = &full[it % S];
+          mbar_arrive_expect_tx(fb, pb + sb);
+          bulk_g2s(st, a.down_p + e * a.down_ps + static_cast<size_t>(r0) * (F / 2), pb, fb);
+          bulk_g2s(st + pb, a.down_s + e * a.down_ss + static_cast<size_t>(r0) * G2, sb, fb);
+        }
+      }
+      if (!ok) {  // copies already issued land before the CTA leaves
+        for (int q = (it > S ? it - S : 0); q < it; ++q)
+          mbar_wait(&full[q % S], (q / S) & 1, a.status, kSiteDrain);
+      }
+    }
+    return;
+  }
+
+  // =============================== consumers ==============================
+  const int wg = warp_id, ct = threadIdx.x;
+  uint4* xh = reinterpret_cast<uint4*>(smem + pl.x_off);  // f16 [t][wq][c], scaled
+  uint4* xb = xh + TT * 4 * G;                             // bf16 [t][wq][c]
+  float* ysm = reinterpret_cast<float*>(smem + pl.y_off);  // [R + TT][rows_max]
+
+  // ---- stage x: bf16 copy, then f16 scaled so max|x| < 2^8 ----
+  {
+    const int n4 = M * (d >> 3);
+    uint4 xr[kXRegs];
+#pragma unroll
+    for (int q = 0; q < kXRegs; ++q) {
+      const int i4 = ct + q * kConsumers;
+      if (i4 < n4) {
+        const int t = i4 / (d >> 3);
+        xr[q] = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * d + 8 * (i4 - t * (d >> 3)));
+      }
+    }
+    // per-token max |x|: one shared atomic per warp when a warp's 32 lanes
+    // cover one token (d/8 a multiple of 32), else one per lane
+    const bool warp_rows = ((d >> 3) & 31) == 0;
+#pragma unroll
+    for (int q = 0; q < kXRegs; ++q) {
+      const int i4 = ct + q * kConsumers;
+      const int t = i4 / (d >> 3), i8 = i4 - t * (d >> 3);
+      const unsigned m = i4 < n4 ? __float_as_uint(absmax8_bf16(xr[q])) : 0u;
+      if (i4 < n4) xb[(t * 4 + (i8 & 3)) * G + (i8 >> 2)] = xr[q];
+      if (warp_rows) {
+        const unsigned wm = __reduce_max_sync(0xffffffffu, m);
+        if (lane == 0 && i4 < n4) atomicMax(amax_x + t, wm);
+      } else if (i4 < n4) {
+        atomicMax(amax_x + t, m);
+      }
+    }
+    named_sync(kBarCons, kConsumers);
+    if (ct < M) tok_mult[ct] = pow2i(act_shift(__uint_as_float(amax_x[ct])));
+    named_sync(kBarCons, kConsumers);
+#pragma unroll
+    for (int q = 0; q < kXRegs; ++q) {
+      const int i4 = ct + q * kConsumers;
+      if (i4 < n4) {
+        const int t = i4 / (d >> 3), i8 = i4 - t * (d >> 3);
+        xh[(t * 4 + (i8 & 3)) * G + (i8 >> 2)] = bf16x8_to_f16x8_scaled(xr[q], __fdiv_rn(1.0f, tok_mult[t]));
+      }
+    }
+    named_sync(kBarCons, kConsumers);
+  }
+
+  bool ok = true;
+  int it = 0;
+  // Cross-warp reductions without a CTA barrier: use u of buffer rb waits
+  // until the previous use was finished, every warp adds its partials, and
+  // the warp that arrives last finishes the chunk and frees the buffer.
+  int rchunk = 0;
+  auto red_begin = [&](int rb, int use) {
+    if (lane == 0) {
+      for (int n = 0; *reinterpret_cast<volatile int*>(&red_gen[rb]) != use; ++n) {
+        if (n > (1 << 24)) {
+          atomicExch(a.status, 6 | kSiteRed);
+          ok = false;
+          break;
+        }
+        __nanosleep(32);
+      }
+      __threadfence_block();
+    }
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  };
+  auto red_arrive = [&](int rb, int use) -> bool {
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      last = atomicAdd(&red_cnt[rb], 1) == kWarps * (use + 1) - 1;
+      if (last) __threadfence_block();
+    }
+    return __shfl_sync(0xffffffffu, last, 0) != 0;
+  };
+  auto red_end = [&](int rb, int use) {
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      atomicExch(&red_gen[rb], use + 1);
+    }
+  };
+  const int c0 = ct & 127, rs = ct >> 7;  // gate/up: column-group lane, row set 0..1
+  const int CI = (G + 127) >> 7;
+  auto release = [&](int s) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  };
+  // Early release: the slice a thread copied out of the stage must be in its
+  // registers before the stage goes back to the producer.  A store of a value
+  // computed from every copied word sits before the release, which orders
+  // prior stores; without it the loads were observed executing after lane
+  // 0's arrive (the compiler is free to sink them, they only feed registers).
+  auto release_after = [&](int s, unsigned dep) {
+    *reinterpret_cast<volatile unsigned*>(&rel_sink[ct]) = dep;  // volatile: never elided
+    release(s);
+  };
+
+  // ---------------------------- phase 1 ----------------------------
+  // router rows: warp -> row, canonical lane partials + butterfly
+  for (int rc = 0; rc < n_rt; ++rc, ++it) {
+    const int s = it % S;
+    if (ok) ok = wait_warp(&full[s], (it / S) & 1, a.status, kSiteFull, lane);
+    const int r0 = rc * pl.rpr, nr = min(pl.rpr, nrr - r0);
+    const float* ws = reinterpret_cast<const float*>(smem + static_cast<size_t>(s) * pl.stage_bytes);
+    for (int r = wg; ok && r < nr; r += kWarps) {
+      const float* wrow = ws + static_cast<size_t>(r) * d;
+      float acc[TT];
+#pragma unroll
+      for (int t = 0; t < TT; ++t) acc[t] = 0.f;
+      for (int c8 = lane; c8 < (d >> 3); c8 += 32) {
+        const float4 w0 = *reinterpret_cast<const float4*>(wrow + 8 * c8);
+        const float4 w1 = *reinterpret_cast<const float4*>(wrow + 8 * c8 + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+          if (t < M) {
+            const uint4 u = xb[(t * 4 + (c8 & 3)) * G + (c8 >> 2)];
+            const float xv[8] = {bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y),
+                                 bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w)};
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc[t] = __fmaf_rn(xv[q], wv[q], acc[t]);
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+        for (int t = 0; t < TT; ++t) acc[t] = __fadd_rn(acc[t], __shfl_xor_sync(0xffffffffu, acc[t], off));
+      if (lane == 0) {
+        const int e = b + P * (r0 + r);
+#pragma unroll
+        for (int t = 0; t < TT; ++t)
+          if (t < M) a.logits[static_cast<size_t>(t) * E + e] = acc[t];
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&empty[s]);
+      mbar_arrive(&lgdone);  // release: this warp's logits are written
+    }
+  }
+
+  // shared gate/up, rows 2j and 2j+1: thread -> row rs (gate and up),
+  // column groups c0 + 128*ci
+  int j = b;
+  for (; j < n_sh; j += P, ++it) {
+    const int s = it % S;
+    if (ok) ok = wait_warp(&full[s], (it / S) & 1, a.status, kSiteFull, lane);
+    const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
+    const unsigned char* grow = st + static_cast<size_t>(rs) * d * 2;
+    const unsigned char* urow = st + static_cast<size_t>(kShGuRows + rs) * d * 2;
+    float acc[2][TT];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int t = 0; t < TT; ++t) acc[h][t] = 0.f;
+    const bool early = CI == 1;
+    uint4 wv[2][4];
+    if (early) {
+      unsigned dep = 0u;
+      if (ok && c0 < G) {
+#pragma unroll
+        for (int wq = 0; wq < 4; ++wq) {
+          wv[0][wq] = lds128(grow + c0 * 64 + 16 * wq);
+          wv[1][wq] = lds128(urow + c0 * 64 + 16 * wq);
+          dep ^= fold4(wv[0][wq]) ^ fold4(wv[1][wq]);
+        }
+      }
+      release_after(s, dep);
+    }
+    if (ok) {
+      for (int ci = 0; ci < CI; ++ci) {
+        const int c = c0 + 128 * ci;
+        if (c >= G) break;
+        if (!early) {
+#pragma unroll
+          for (int wq = 0; wq < 4; ++wq) {
+            wv[0][wq] = lds128(grow + c * 64 + 16 * wq);
+            wv[1][wq] = lds128(urow + c * 64 + 16 * wq);
+          }
+        }
+        const uint4* xp[TT];
+#pragma unroll
+        for (int t = 0; t < TT; ++t) xp[t] = xb + (min(t, M - 1) * 4) * G + c;
+        float part[2][TT];
+        bf_dot<2, TT>(wv, xp, G, part);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int t = 0; t < TT; ++t) acc[h][t] = __fadd_rn(acc[h][t], part[h][t]);
+      }
+    }
+    if (!early) release(s);
+    float v[2 * TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      v[t] = acc[0][t];
+      v[TT + t] = acc[1][t];
+    }
+    reduce_scatter<2 * TT, 32>(v, lane);
+    const int rb = rchunk % kNRed, use = rchunk / kNRed;
+    ++rchunk;
+    red_begin(rb, use);
+    if ((lane & (32 / (2 * TT) - 1)) == 0) red[rb][wg][lane / (32 / (2 * TT))] = v[0];
+    if (red_arrive(rb, use)) {
+      if (ok && lane < kShGuRows * TT) {
+        const int r = lane / TT, t = lane - (lane / TT) * TT;
+        if (t < M) {
+          float g = 0.f, u = 0.f;
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+            g = __fadd_rn(g, red[rb][r * 4 + w4][t]);
+            u = __fadd_rn(u, red[rb][r * 4 + w4][TT + t]);
+          }
+          a.act_s[static_cast<size_t>(t) * Fs + j * kShGuRows + r] = swiglu_bf16(round_bf16(g), round_bf16(u), a.limit);
+        }
+      }
+      red_end(rb, use);
+    }
+  }
+
+  // routing tables from the producer warp; one agreed active-expert count
+  if (ok) ok = wait_warp(&tbl, 0, a.status, kSiteTable, lane);
+  named_sync(kBarCons, kConsumers);
+  if (ct == 0) s_nact = T.n_active;
+  named_sync(kBarCons, kConsumers);
+  const int n_act = s_nact;
+
+  // routed gate/up: thread -> rows rs*4 .. rs*4+3 of the chunk's 8, gate and up
+  {
+    const int n_r = n_act * nrb;
+    const size_t pk = static_cast<size_t>(kGuRows) * (d >> 1);
+    for (; j < n_sh + n_r; j += P, ++it) {
+      const int s = it % S;
+      if (ok) ok = wait_warp(&full[s], (it / S) & 1, a.status, kSiteFull, lane);
+      const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
+      const int jr = j - n_sh;
+      const int ai = jr / nrb;
+      const int f0 = (jr - ai * nrb) * kGuRows;
+      const int p0 = T.ap0[ai], n = T.an[ai];
+      int tok[TT];
+#pragma unroll
+      for (int q = 0; q < TT; ++q) tok[q] = T.perm[p0 + (q < n ? q : 0)] / k;
+      float acc[8][TT];  // row-vector v = h*4 + r: h gate/up, row rs*4 + r
+#pragma unroll
+      for (int v = 0; v < 8; ++v)
+#pragma unroll
+        for (int q = 0; q < TT; ++q) acc[v][q] = 0.f;
+      constexpr int TP = TT < 2 ? TT : 2;  // tokens per pass
+      const bool early = CI == 1;
+      uint4 w[8][1];
+      float scl[8];
+      auto load_slice = [&](int c) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int Rw = rs * 4 + r;
+            w[h * 4 + r][0] = lds128(st + h * pk + static_cast<size_t>(Rw) * (d >> 1) + 16 * c);
+            scl[h * 4 + r] = e8m0_to_f32(st[2 * pk + h * kGuRows * G + Rw * G + c]);
+          }
+      };
+      if (early) {
+        unsigned dep = 0u;
+        if (ok && c0 < G) {
+          load_slice(c0);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) dep ^= fold4(w[v][0]) ^ __float_as_uint(scl[v]);
+        }
+        release_after(s, dep);
+      }
+      if (ok) {
+        for (int ci = 0; ci < CI; ++ci) {
+          const int c = c0 + 128 * ci;
+          if (c >= G) break;
+          if (!early) load_slice(c);
+#pragma unroll
+          for (int q0 = 0; q0 < TT; q0 += TP) {
+            if (q0 >= n) break;
+            const uint4* xp[1][TP];
+#pragma unroll
+            for (int tq = 0; tq < TP; ++tq) xp[0][tq] = xh + (tok[q0 + tq] * 4) * G + c;
+            float part[8][1][TP];
+            mx_dot<8, 1, TP>(w, xp, G, part);
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+#pragma unroll
+              for (int tq = 0; tq < TP; ++tq) acc[v][q0 + tq] = __fmaf_rn(part[v][0][tq], scl[v], acc[v][q0 + tq]);
+          }
+        }
+      }
+      if (!early) release(s);
+      float vv[8 * TT];  // index (r*2 + h)*TT + q
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int q = 0; q < TT; ++q) vv[(r * 2 + h) * TT + q] = acc[h * 4 + r][q];
+      reduce_scatter<8 * TT, 32>(vv, lane);
+      const int rb = rchunk % kNRed, use = rchunk / kNRed;
+      ++rchunk;
+      red_begin(rb, use);
+      if ((lane & (32 / (8 * TT) - 1)) == 0) red[rb][wg][lane / (32 / (8 * TT))] = vv[0];
+      if (red_arrive(rb, use)) {
+        if (ok && lane < kGuRows * TT) {
+          const int Rw = lane / TT, q = lane - (lane / TT) * TT;
+          if (q < n) {
+            const int set = Rw >> 2, r = Rw & 3;
+            float g = 0.f, u = 0.f;
+#pragma unroll
+            for (int w4 = 0; w4 < 4; ++w4) {
+              g = __fadd_rn(g, red[rb][set * 4 + w4][(r * 2) * TT + q]);
+              u = __fadd_rn(u, red[rb][set * 4 + w4][(r * 2 + 1) * TT + q]);
+            }
+            int tq = tok[0];
+#pragma unroll
+            for (int qq = 1; qq < TT; ++qq)
+              if (q == qq) tq = tok[qq];
+            const float m = tok_mult[tq];
+            a.act[static_cast<size_t>(p0 + q) * F + f0 + Rw] =
+                swiglu_bf16(round_bf16(__fmul_rn(g, m)), round_bf16(__fmul_rn(u, m)), a.limit);
+          }
+        }
+        red_end(rb, use);
+      }
+    }
+  }
+
+  // ------------------------- phase 1 -> phase 2 -------------------------
+  named_sync(kBarCons, kConsumers);
+  if (ct == 0) {
+    __threadfence();
+    atomicAdd(a.sync + 1, 1u);
+    s_fail = (ok && spin_geq(a.sync + 1, static_cast<unsigned>(P), a.status, kSiteAct)) ? 0 : 1;
+    __threadfence();
+  }
+  named_sync(kBarCons, kConsumers);
+  if (s_fail) ok = false;
+  // stage act (f16, scaled per route) and act_s (bf16) into the union area
+  uint4* xa = reinterpret_cast<uint4*>(smem + pl.x_off);  // f16 [p][wq][c]
+  uint4* xs = xa + R * 4 * G2;                             // bf16 [t][wq][c]
+  {
+    const int n4 = ok ? R * (F >> 3) : 0;
+    const int n4s = ok ? M * (Fs >> 3) : 0;
+    uint4 ar[kActRegs], sr[kActSRegs];
+#pragma unroll
+    for (int q = 0; q < kActRegs; ++q) {
+      const int i4 = ct + q * kConsumers;
+      if (i4 < n4) {
+        const int p = i4 / (F >> 3);
+        ar[q] = __ldcg(reinterpret_cast<const uint4*>(a.act + static_cast<size_t>(p) * F + 8 * (i4 - p * (F >> 3))));
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kActSRegs; ++q) {
+      const int i4 = ct + q * kConsumers;
+      if (i4 < n4s) {
+        const int t = i4 / (Fs >> 3);
+        sr[q] = __ldcg(reinterpret_cast<const uint4*>(a.act_s + static_cast<size_t>(t) * Fs + 8 * (i4 - t * (Fs >> 3))));
+      }
+    }
+    const bool warp_rows = ((F >> 3) & 31) == 0;
+#pragma unroll
+    for (int q = 0; q < kActRegs; ++q) {
+      const int i4 = ct + q * kConsumers;
+      const unsigned m = i4 < n4 ? __float_as_uint(absmax8_bf16(ar[q])) : 0u;
+      if (warp_rows) {
+        const unsigned wm = __reduce_max_sync(0xffffffffu, m);
+        if (lane == 0 && i4 < n4) atomicMax(amax_r + i4 / (F >> 3), wm);
+      } else if (i4 < n4) {
+        atomicMax(amax_r + i4 / (F >> 3), m);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kActSRegs; ++q) {
+      const int i4 = ct + q * kConsumers;
+      if (i4 < n4s) {
+        const int t = i4 / (Fs >> 3), i8 = i4 - t * (Fs >> 3);
+        xs[(t * 4 + (i8 & 3)) * G2s + (i8 >> 2)] = sr[q];
+      }
+    }
+    named_sync(kBarCons, kConsumers);
+    if (ct < R) rscale[ct] = pow2i(act_shift(__uint_as_float(amax_r[ct])));
+    named_sync(kBarCons, kConsumers);
+#pragma unroll
+    for (int q = 0; q < kActRegs; ++q) {
+      const int i4 = ct + q * kConsumers;
+      if (i4 < n4) {
+        const int p = i4 / (F >> 3), i8 = i4 - p * (F >> 3);
+        xa[(p * 4 + (i8 & 3)) * G2 + (i8 >> 2)] = bf16x8_to_f16x8_scaled(ar[q], __fdiv_rn(1.0f, rscale[p]));
+      }
+    }
+    named_sync(kBarCons, kConsumers);
+  }
+
+  // ---------------------------- phase 2 ----------------------------
+  const DownRange dr(a, pl, b, P);
+  const int r_lo = dr.r_lo, rows = dr.rows;
+  // shared down: warp -> row, lanes over column groups
+  const int CIs = (G2s + 31) >> 5;
+  for (int pc = 0; pc < dr.n_sdp; ++pc, ++it) {
+    const int s = it % S;
+    if (ok) ok = wait_warp(&full[s], (it / S) & 1, a.status, kSiteFull, lane);
+    const int rl0 = pc * pl.sh_rows, nr = min(pl.sh_rows, rows - rl0);
+    const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
+    float acc[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) acc[t] = 0.f;
+    if (ok && wg < nr) {
+      const unsigned char* wrow = st + static_cast<size_t>(wg) * Fs * 2;
+      for (int ci = 0; ci < CIs; ++ci) {
+        const int c = lane + 32 * ci;
+        if (c < G2s) {
+          uint4 wv[1][4];
+#pragma unroll
+          for (int wq = 0; wq < 4; ++wq) wv[0][wq] = lds128(wrow + c * 64 + 16 * wq);
+          const uint4* xp[TT];
+#pragma unroll
+          for (int t = 0; t < TT; ++t) xp[t] = xs + (min(t, M - 1) * 4) * G2s + c;
+          float part[1][TT];
+          bf_dot<1, TT>(wv, xp, G2s, part);
+#pragma unroll
+          for (int t = 0; t < TT; ++t) acc[t] = __fadd_rn(acc[t], part[0][t]);
+        }
+      }
+    }
+    release(s);
+    reduce_scatter<TT, 32>(acc, lane);
+    if (ok && wg < nr && (lane & (32 / TT - 1)) == 0) {
+      const int t = lane / (32 / TT);
+      if (t < M) ysm[static_cast<size_t>(R + t) * pl.rows_max + rl0 + wg] = round_bf16(acc[0]);
+    }
+  }
+
+  // routed down: 16 column-group lanes (3 groups each) x 16 row sets of two rows
+  {
+    const int cd = ct & 15, rd = ct >> 4;
+    const int CI2 = (G2 + 15) >> 4;
+    const int NB = (CI2 + 2) / 3;  // blocks of three column groups
+    for (int ai = 0; ai < n_act; ++ai) {
+      const int p0 = T.ap0[ai], n = T.an[ai];
+      for (int sc = 0; sc < dr.n_sub; ++sc, ++it) {
+        const int s = it % S;
+        if (ok) ok = wait_warp(&full[s], (it / S) & 1, a.status, kSiteFull, lane);
+        const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
+        const int rl0 = sc * pl.sub_rows, nr = min(pl.sub_rows, rows - rl0);
+        const size_t pb = static_cast<size_t>(nr) * (F >> 1);
+        float acc[2][TT];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int q = 0; q < TT; ++q) acc[h][q] = 0.f;
+        constexpr int TP = TT < 2 ? TT : 2;
+        const bool early = NB == 1;
+        uint4 w[2][3];
+        float scl[2][3];
+        auto load_slice = [&](int cb) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int cc = 0; cc < 3; ++cc) {
+              const int row = rd + 16 * h, c = cd + 16 * (cb * 3 + cc);
+              const bool in = row < nr && c < G2;
+              w[h][cc] = in ? lds128(st + static_cast<size_t>(row) * (F >> 1) + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
+              scl[h][cc] = in ? e8m0_to_f32(st[pb + row * G2 + c]) : 0.f;
+            }
+        };
+        if (early) {
+          unsigned dep = 0u;
+          if (ok) {
+            load_slice(0);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int cc = 0; cc < 3; ++cc) dep ^= fold4(w[h][cc]) ^ __float_as_uint(scl[h][cc]);
+          }
+          release_after(s, dep);
+        }
+        if (ok) {
+          for (int cb = 0; cb < NB; ++cb) {
+            if (!early) load_slice(cb);
+#pragma unroll
+            for (int q0 = 0; q0 < TT; q0 += TP) {
+              if (q0 >= n) break;
+              const uint4* xp[3][TP];
+#pragma unroll
+              for (int cc = 0; cc < 3; ++cc) {
+                const int c = min(cd + 16 * (cb * 3 + cc), G2 - 1);
+#pragma unroll
+                for (int tq = 0; tq < TP; ++tq) xp[cc][tq] = xa + ((p0 + min(q0 + tq, n - 1)) * 4) * G2 + c;
+              }
+              float part[2][3][TP];
+              mx_dot<2, 3, TP>(w, xp, G2, part);
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int cc = 0; cc < 3; ++cc)
+#pragma unroll
+                  for (int tq = 0; tq < TP; ++tq)
+                    acc[h][q0 + tq] = __fmaf_rn(part[h][cc][tq], scl[h][cc], acc[h][q0 + tq]);
+            }
+          }
+        }
+        if (!early) release(s);
+        float v[2 * TT];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int q = 0; q < TT; ++q) v[h * TT + q] = acc[h][q];
+        reduce_scatter<2 * TT, 16>(v, lane);
+        if (ok && (lane & (16 / (2 * TT) - 1)) == 0) {
+          const int vi = (lane & 15) / (16 / (2 * TT));
+          const int h = vi / TT, q = vi - (vi / TT) * TT;
+          const int row = rd + 16 * h;
+          if (row < nr && q < n)
+            ysm[static_cast<size_t>(T.perm[p0 + q]) * pl.rows_max + rl0 + row] =
+                round_bf16(__fmul_rn(v[0], rscale[p0 + q]));
+        }
+      }
+    }
+  }
+
+  // ---- merge this CTA's rows: routes in j order, then the shared row ----
+  named_sync(kBarCons, kConsumers);
+  if (ok) {
+    for (int o = ct; o < M * rows; o += kConsumers) {
+      const int t = o / rows, rl = o - t * rows;
+      float sacc = 0.f;
+      for (int q = 0; q < k; ++q) {
+        const int sl = t * k + q;
+        sacc = __fadd_rn(sacc, __fmul_rn(ysm[static_cast<size_t>(sl) * pl.rows_max + rl], T.w[sl]));
+      }
+      if (Fs > 0) sacc = __fadd_rn(sacc, ysm[static_cast<size_t>(R + t) * pl.rows_max + rl]);
+      a.out[static_cast<size_t>(t) * d + r_lo + rl] = sacc;
+    }
+  }
+  // The last CTA out checks that the counters saw exactly this call (a
+  // workspace that was not zeroed before its first use fails here, once) and
+  // resets them for the next call.
+  if (ct == 0) {
+    __threadfence();
+    if (atomicAdd(a.sync + 2, 1u) == static_cast<unsigned>(P) - 1u) {
+      const unsigned nl = atomicExch(a.sync + 0, 0u), na = atomicExch(a.sync + 1, 0u);
+      atomicExch(a.sync + 2, 0u);
+      if (nl != static_cast<unsigned>(E) || na != static_cast<unsigned>(P)) atomicExch(a.status, 3 | kSiteSync);
+    }
+  }
+}
+
+}  // namespace layer
+}  // namespace lg

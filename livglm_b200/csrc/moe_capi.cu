@@ -10,6 +10,7 @@
 #include <utility>
 
 #include "livglm_moe.h"
+#include "layer_kernel.cuh"
 #include "stream_kernels.cuh"
 #include "moe_kernels.cuh"
 
@@ -65,7 +66,7 @@ int validate_tokens(int64_t M, const lg_moe_config* c) {
 }
 
 struct Layout {
-  size_t status, logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, total;
+  size_t status, logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, sync, total;
 };
 
 Layout layout(const lg_moe_config* c, int64_t M) {
@@ -87,6 +88,7 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   L.y = o;       o += up(m * k * d * 2);
   L.ys = o;      o += up(m * d * 2);
   L.tickets = o; o += up(d * 4);
+  L.sync = o;    o += up(4 * 4);
   L.total = o;
   return L;
 }
@@ -324,52 +326,35 @@ struct StreamPlan {
   size_t gu_smem, dn_smem;
 };
 
-// Byte stride for rows staged one by one so that lanes (g, q) reading 4 bytes
-// at row g, offset 4q hit 32 distinct banks: stride/4 must be 4 * odd mod 32.
-int conflict_free_stride(int row_bytes) {
-  for (int pad = 0; pad <= 112; pad += 16)
-    if ((((row_bytes + pad) / 4) % 32) % 8 == 4) return row_bytes + pad;
-  return row_bytes;
-}
-
 bool plan_stream(const lg_moe_config* c, int M, int TT, StreamPlan* P) {
   const size_t d = c->hidden_size, F = c->moe_intermediate_size, Fs = F * c->n_shared_experts;
-  const size_t E = c->n_routed_experts;
-  const size_t G = d / 32, WPL = (d / 4 / 8 + 31) / 32;
+  const size_t G = d / 32, KI = (G + 31) / 32, WPL = (d / 4 / 8 + 31) / 32;
   const size_t GF = F / 32, WS = (Fs / 8 + 31) / 32, R = static_cast<size_t>(M) * c->num_experts_per_tok;
-  const size_t tables = (2 * ((E + 1 + 3) & ~size_t(3)) + R + 4) * 4;
   // gate/up
-  P->gu.rs = conflict_free_stride(static_cast<int>(d / 2));
-  P->gu.ss = static_cast<int>(G); P->gu.ss_rows = 0;
   const size_t gu_stage = std::max<size_t>(Fs > 0 ? 2 * lg::kGuRowsShared * d * 2 : 0,
-                                           2 * lg::kGuRowsRouted * (P->gu.rs + G));
-  const size_t gu_x = TT * d * 2 + TT * 4 * WPL * 32 * 16;
-  const size_t gu_aux = (lg::kGroups * 2 * lg::kGuRowsShared * 4 * TT * 2 +
-                         lg::kGroups * 2 * lg::kConsumerWarps * 8 * TT * 2) * 4 + tables;
+                                           2 * lg::kGuRowsRouted * (d / 2) + 2 * lg::kGuRowsRouted * G);
+  const size_t gu_x = TT * KI * 128 * 16 + TT * 4 * WPL * 32 * 16;
+  const size_t tables = (2 * ((static_cast<size_t>(c->n_routed_experts) + 1 + 3) & ~size_t(3)) + R + 4) * 4;
+  const size_t gu_aux = lg::kGroups * 2 * lg::kGuRowsShared * 4 * TT * 2 * 4 + tables;
   const size_t gu_fixed = gu_x + gu_aux;
   if (gu_fixed + 2 * gu_stage > kSmemBudget) return false;
   P->gu.stages = static_cast<int>(std::min<size_t>(lg::kMaxStages, (kSmemBudget - gu_fixed) / gu_stage));
-  P->gu.stage_bytes = static_cast<int>((gu_stage + 127) & ~size_t(127));
-  P->gu.stages = static_cast<int>(std::min<size_t>(P->gu.stages, (kSmemBudget - gu_fixed) / P->gu.stage_bytes));
+  P->gu.stage_bytes = static_cast<int>(gu_stage);
   P->gu.x_off = P->gu.stages * P->gu.stage_bytes;
   P->gu.aux_off = static_cast<int>(P->gu.x_off + gu_x);
   P->gu_smem = P->gu.aux_off + gu_aux;
   // down
-  // down: blocks of 4 rows; block stride/4 must be 4*odd mod 32 (see the kernel)
-  P->dn.rs = conflict_free_stride(static_cast<int>(2 * F));
-  P->dn.ss = static_cast<int>(GF); P->dn.ss_rows = 0;
   const size_t dn_stage = std::max<size_t>(Fs > 0 ? lg::kDnRowsShared * Fs * 2 : 0,
-                                           (lg::kDnRowsRouted / 4) * P->dn.rs + lg::kDnRowsRouted * GF);
+                                           lg::kDnRowsRouted * (F / 2) + lg::kDnRowsRouted * GF);
   const size_t dn_x = R * F * 2 + static_cast<size_t>(M) * WS * 32 * 16;
-  const size_t dn_aux = (((R + 3) & ~size_t(3)) + lg::kGroups * 2 * lg::kConsumerWarps * lg::kDnRowsRouted * TT) * 4 +
-                        tables;
+  const size_t dn_aux = ((R + 3) & ~size_t(3)) * 4 + tables;
   if (dn_x + dn_aux + 2 * dn_stage > kSmemBudget) return false;
-  P->dn.stage_bytes = static_cast<int>((dn_stage + 127) & ~size_t(127));
-  P->dn.stages = static_cast<int>(std::min<size_t>(lg::kMaxStages, (kSmemBudget - dn_x - dn_aux) / P->dn.stage_bytes));
+  P->dn.stages = static_cast<int>(std::min<size_t>(lg::kMaxStages, (kSmemBudget - dn_x - dn_aux) / dn_stage));
+  P->dn.stage_bytes = static_cast<int>(dn_stage);
   P->dn.x_off = P->dn.stages * P->dn.stage_bytes;
   P->dn.aux_off = static_cast<int>(P->dn.x_off + dn_x);
   P->dn_smem = P->dn.aux_off + dn_aux;
-  return P->gu.stages >= 2 && P->dn.stages >= 2;
+  return true;
 }
 
 // The decode chain needs bulk-copyable chunks: 16-byte aligned bases and
@@ -380,7 +365,6 @@ bool decode_fits(const lg_moe_config* c, const lg_moe_weights* w, int64_t M) {
   if (static_cast<size_t>(lg::kRouterExperts) * c->hidden_size * 4 > 200 * 1024) return false;
   // register-staged activation rows: d*M/8 <= 4 * 512 uint4, F/8 <= 8 * 32
   if (static_cast<size_t>(c->hidden_size) * M / 8 > 4 * 512 || c->moe_intermediate_size / 8 > 8 * 32) return false;
-  if (c->num_experts_per_tok * M > lg::kDecodeMaxTokens * 32) return false;
   if (c->num_experts_per_tok * M > lg::kDecodeMaxTokens * 32) return false;
   if (!aligned(w->gate_scale, 16) || !aligned(w->up_scale, 16) || !aligned(w->down_scale, 16)) return false;
   if (w->gate_scale_stride % 16 || w->up_scale_stride % 16 || w->down_scale_stride % 16) return false;
@@ -456,6 +440,143 @@ int launch_decode(const lg_moe_config* c, const lg_moe_weights* w, const uint16_
   if (M <= 1) return launch_decode_t<1>(c, w, x, M, out, wts, idx, ws, L, slot, s);
   if (M <= 2) return launch_decode_t<2>(c, w, x, M, out, wts, idx, ws, L, slot, s);
   return launch_decode_t<4>(c, w, x, M, out, wts, idx, ws, L, slot, s);
+}
+
+// ---- fused decode layer (M <= 4): one cooperative kernel ----------------------
+int gcd_int(int x, int y) {
+  while (y) { const int t = x % y; x = y; y = t; }
+  return x;
+}
+
+template <int TT>
+size_t layer_static_smem() {
+  static size_t v = 0;
+  static bool done = false;
+  if (!done) {
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, lg::layer::layer_kernel<TT>) == cudaSuccess) v = fa.sharedSizeBytes;
+    done = true;
+  }
+  return v;
+}
+
+size_t round128(size_t v) { return (v + 127) / 128 * 128; }
+
+// Shared-memory plan: ring stages of the largest chunk, the union of the
+// phase-1 activations and the phase-2 activations, the per-CTA y rows.
+bool plan_layer(const lg_moe_config* c, int M, int TT, size_t static_smem, int grid, lg::layer::Plan* P,
+                size_t* dyn) {
+  using namespace lg::layer;
+  const size_t d = c->hidden_size, F = c->moe_intermediate_size, Fs = F * c->n_shared_experts;
+  const size_t G = d / 32, G2 = F / 32, R = static_cast<size_t>(M) * c->num_experts_per_tok;
+  size_t stage = std::max<size_t>(d * 4, 2 * kGuRows * (d / 2) + 2 * kGuRows * G);
+  if (Fs > 0) stage = std::max<size_t>(stage, 2 * kShGuRows * d * 2);
+  stage = round128(stage);
+  const size_t x_bytes = round128(std::max<size_t>(2 * static_cast<size_t>(TT) * d * 2, R * F * 2 + M * Fs * 2));
+  const int unit = 16 / gcd_int(static_cast<int>(G2), 16);
+  const int nunits = static_cast<int>(d) / unit;
+  const int rows_max = unit * ((nunits + grid - 1) / grid);
+  const size_t y_bytes = round128((R + TT) * static_cast<size_t>(rows_max) * 4);
+  const size_t budget = 227 * 1024 - static_smem;
+  if (x_bytes + y_bytes + 2 * stage > budget) return false;
+  const int stages = static_cast<int>(std::min<size_t>(kMaxStages, (budget - x_bytes - y_bytes) / stage));
+  const int sub = static_cast<int>(std::min<size_t>(kDnRowsMax, stage / (F / 2 + G2))) / unit * unit;
+  if (sub < unit) return false;
+  const int sh = Fs > 0 ? static_cast<int>(std::min<size_t>(kShDnRows, stage / (Fs * 2))) : 1;
+  if (sh < 1) return false;
+  P->stages = stages;
+  P->stage_bytes = static_cast<int>(stage);
+  P->x_off = static_cast<int>(stages * stage);
+  P->y_off = static_cast<int>(P->x_off + x_bytes);
+  P->rpr = static_cast<int>(stage / (d * 4));
+  P->unit = unit;
+  P->sub_rows = sub;
+  P->sh_rows = sh;
+  P->rows_max = rows_max;
+  *dyn = P->y_off + y_bytes;
+  return true;
+}
+
+template <int TT>
+bool layer_fits_t(const lg_moe_config* c, int M) {
+  lg::layer::Plan P;
+  size_t dyn = 0;
+  return plan_layer(c, M, TT, layer_static_smem<TT>(), num_sms(), &P, &dyn);
+}
+
+// The fused kernel needs: 1..4 tokens, M*k <= 32 routes, E <= 256 router
+// experts in <= 32 groups, d % 64 == 0, register-staged activations
+// (M*d <= 16384, M*k*F <= 49152), 16-byte aligned scale banks (every bulk copy
+// starts and ends on 16 bytes) and a shared-memory plan.
+bool layer_fits(const lg_moe_config* c, const lg_moe_weights* w, int64_t M) {
+  using namespace lg::layer;
+  if (M < 1 || M > lg::kDecodeMaxTokens) return false;
+  const long long R = M * c->num_experts_per_tok;
+  if (R > kMaxRoutes || c->n_routed_experts > kMaxExperts || c->n_group > kMaxGroups) return false;
+  if (c->hidden_size % 64) return false;
+  if (static_cast<long long>(c->hidden_size) * M > 8LL * kConsumers * kXRegs) return false;
+  if (R * c->moe_intermediate_size > 8LL * kConsumers * kActRegs) return false;
+  if (!aligned(w->gate_scale, 16) || !aligned(w->up_scale, 16) || !aligned(w->down_scale, 16)) return false;
+  if (w->gate_scale_stride % 16 || w->up_scale_stride % 16 || w->down_scale_stride % 16) return false;
+  const int m = static_cast<int>(M);
+  return m <= 1 ? layer_fits_t<1>(c, m) : m <= 2 ? layer_fits_t<2>(c, m) : layer_fits_t<4>(c, m);
+}
+
+template <int TT>
+int launch_layer_t(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M, float* out,
+                   float* wts, uint32_t* idx, void* ws, const Layout& L, int slot, cudaStream_t s) {
+  using namespace lg::layer;
+  const int grid = num_sms();
+  Plan pl;
+  size_t dyn = 0;
+  if (!plan_layer(c, M, TT, layer_static_smem<TT>(), grid, &pl, &dyn))
+    return fail(LG_ERR_UNSUPPORTED, "fused decode layer does not fit in shared memory");
+  Args a{};
+  a.M = M; a.d = c->hidden_size; a.F = c->moe_intermediate_size; a.Fs = a.F * c->n_shared_experts;
+  a.E = c->n_routed_experts; a.k = c->num_experts_per_tok; a.G = c->n_group; a.g = c->topk_group;
+  a.norm = c->norm_topk_prob; a.scale = c->routed_scaling_factor; a.limit = c->swiglu_limit;
+  a.x = x; a.Wr = w->router_weight; a.bias = w->router_bias;
+  a.gate_p = w->gate_packed; a.gate_s = w->gate_scale; a.up_p = w->up_packed; a.up_s = w->up_scale;
+  a.down_p = w->down_packed; a.down_s = w->down_scale;
+  a.gate_ps = w->gate_packed_stride; a.gate_ss = w->gate_scale_stride;
+  a.up_ps = w->up_packed_stride; a.up_ss = w->up_scale_stride;
+  a.down_ps = w->down_packed_stride; a.down_ss = w->down_scale_stride;
+  a.sh_gate = w->shared_gate; a.sh_up = w->shared_up; a.sh_down = w->shared_down;
+  a.logits = at<float>(ws, L.logits); a.w_out = wts; a.i_out = idx;
+  a.act = at<uint16_t>(ws, L.act); a.act_s = at<uint16_t>(ws, L.act_s);
+  a.out = out; a.status = at<int>(ws, L.status); a.sync = at<unsigned>(ws, L.sync);
+  cudaError_t e = cudaFuncSetAttribute(layer_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(dyn));
+  if (e != cudaSuccess) return cuda_check(e, "fused layer smem attribute");
+  int occ = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, layer_kernel<TT>, kThreads, dyn);
+  if (e != cudaSuccess) return cuda_check(e, "fused layer occupancy");
+  if (occ < 1) return fail(LG_ERR_UNSUPPORTED, "fused decode layer: no CTA fits on an SM");
+  trace_mark(slot, 1, s);
+  trace_mark(slot, 2, s);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = dyn;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, layer_kernel<TT>, a, pl);
+  if (e != cudaSuccess) return cuda_check(e, "fused layer launch");
+  trace_mark(slot, 3, s);
+  trace_mark(slot, 4, s);
+  trace_mark(slot, 5, s);
+  return LG_OK;
+}
+
+int launch_layer(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M, float* out,
+                 float* wts, uint32_t* idx, void* ws, const Layout& L, int slot, cudaStream_t s) {
+  if (M <= 1) return launch_layer_t<1>(c, w, x, M, out, wts, idx, ws, L, slot, s);
+  if (M <= 2) return launch_layer_t<2>(c, w, x, M, out, wts, idx, ws, L, slot, s);
+  return launch_layer_t<4>(c, w, x, M, out, wts, idx, ws, L, slot, s);
 }
 
 // ---- stage tracing ------------------------------------------------------------
@@ -658,6 +779,7 @@ int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint
   int* active = at<int>(workspace, L.active);
   const int slot = trace_slot();
   trace_mark(slot, 0, s);
+  if (layer_fits(cfg, w, M)) return launch_layer(cfg, w, x, m, out, weights_out, indices_out, workspace, L, slot, s);
   if (decode_fits(cfg, w, M)) {
     rc = launch_decode(cfg, w, x, m, out, wts, idx, workspace, L, slot, s);
     return rc;

@@ -60,6 +60,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, int* sta
   }
   return true;
 }
+// mbar_wait by every lane of a warp with a warp-uniform result, so the
+// shuffles that follow never see lanes that disagree about a timeout
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* b, unsigned parity, int* status, int site) {
+  return __all_sync(0xffffffffu, mbar_wait(b, parity, status, site));
+}
 // contiguous global -> shared copy completing `bytes` of transactions on `bar`;
 // dst, src and bytes must be multiples of 16
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
@@ -69,9 +74,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
-// named barrier `id` (1..15) over `nthreads` threads of the CTA
+// named barrier `id` (1..15) over `nthreads` threads of the CTA.  The
+// non-.aligned form: threads arrive one by one, so it is correct right after
+// code where one lane of a warp took a different path (bar.sync, the .aligned
+// form, requires a converged warp).
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 }  // namespace lg

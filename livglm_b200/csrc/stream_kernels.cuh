@@ -48,44 +48,7 @@ struct StreamCfg {
   int stage_bytes;
   int x_off;    // byte offset of staged activations
   int aux_off;  // byte offset of the reduction / scale scratch
-  int rs;       // padded byte stride of a routed weight row in a stage
-  int ss;       // byte stride of a routed scale row in a stage
-  int ss_rows;  // 1: scale rows copied one by one (padded); 0: one contiguous block
 };
-
-// m16n8k16 tensor-core MMA, f16 x f16 -> f32 (fragment layout of the PTX ISA:
-// a0/a2 rows g, a1/a3 rows g+8; a0/a1 k 2q..2q+1, a2/a3 k 2q+8..2q+9;
-// b0 k 2q..2q+1, b1 k 2q+8..2q+9, column g; d0/d1 row g, d2/d3 row g+8,
-// columns 2q, 2q+1; g = lane/4, q = lane%4)
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
-  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
-      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
-      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
-      : "r"(w));
-}
-// One 32-column group of a 16-row tile against up to 8 activation columns.
-// Lane (g, q) holds the 4 bytes [4q, 4q+4) of the group's 16 bytes in rows g
-// (wlo) and g+8 (whi): columns 8q..8q+7.  k-slots 2q+i <-> column 8q+i and
-// 2q+8+i <-> column 8q+2+i (first MMA), then columns 8q+4..8q+7 (second), so
-// the activation fragment is the 8 contiguous f16 at columns 8q..8q+7 of the
-// lane's column g.  d += A * B for the group.
-__device__ __forceinline__ void group_mma(float (&d)[4], uint32_t wlo, uint32_t whi, const uint4& xv) {
-  uint32_t hl[4], hh[4];
-  e2m1x8_to_f16x2(wlo, hl);
-  e2m1x8_to_f16x2(whi, hh);
-  mma16816(d, hl[0], hh[0], hl[1], hh[1], xv.x, xv.y);
-  mma16816(d, hl[2], hh[2], hl[3], hh[3], xv.z, xv.w);
-}
 
 // Bulk-copy the routing tables (active list, offsets, perm) into shared
 // memory; completion is signalled on `bar`.  Sizes are rounded up to 16 bytes
@@ -119,49 +82,27 @@ __device__ __forceinline__ void group_dot_e2m1(const uint4& pw, const uint4* xv0
   for (int q = 0; q < TT; ++q) gsum[q] = __fadd_rn(__fadd_rn(c[0][q], c[1][q]), __fadd_rn(c[2][q], c[3][q]));
 }
 
-// Issue the bulk copies of `rows` weight rows (row_bytes each, global stride
-// row_bytes) into padded shared rows (stride rs), and of their scale rows
-// (g_bytes each) either row by row (stride ss) or as one block; lanes of the
-// producer warp split the rows.  Returns the bytes the stage will receive.
-__device__ __forceinline__ void issue_rows(unsigned char* dst, const uint8_t* src, int rows, int row_bytes,
-                                           int rs, int lane, uint64_t* bar) {
-  for (int r = lane; r < rows; r += 32)
-    bulk_g2s(dst + static_cast<size_t>(r) * rs, src + static_cast<size_t>(r) * row_bytes, row_bytes, bar);
-}
-__device__ __forceinline__ void issue_scales(unsigned char* dst, const uint8_t* src, int rows, int g_bytes, int ss,
-                                             int ss_rows, int lane, uint64_t* bar) {
-  if (ss_rows) {
-    for (int r = lane; r < rows; r += 32)
-      bulk_g2s(dst + static_cast<size_t>(r) * ss, src + static_cast<size_t>(r) * g_bytes, g_bytes, bar);
-  } else if (lane == 0) {
-    bulk_g2s(dst, src, rows * g_bytes, bar);
-  }
-}
-
 // ---------------------------------------------------------------------------
 template <int TT>
 __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(DecodeArgs a, StreamCfg sc) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages];
   __shared__ __align__(8) uint64_t empty[kMaxStages];
-  __shared__ __align__(8) uint64_t tbl;
   __shared__ unsigned amax_bits[TT];
   __shared__ float tok_mult[TT];
   const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int K = a.d, G = K >> 5;
+  const int K = a.d, G = K >> 5, KI = (G + 31) >> 5;
   const int M = a.M, F = a.F, Fs = a.Fs;
   const int S = sc.stages;
   const int KQ = K >> 2;               // shared-chunk quarter width
   const int WPL = (KQ / 8 + 31) / 32;  // 8-element words per lane per quarter
-  uint16_t* xh = reinterpret_cast<uint16_t*>(smem + sc.x_off);  // f16 [t][K]
-  uint4* xb = reinterpret_cast<uint4*>(xh + TT * K);              // bf16 [t][q][w4][lane]
-  float* red = reinterpret_cast<float*>(smem + sc.aux_off);
-  // red: shared-chunk partials [group][2][2 rows][4 q][TT][2], then routed
-  // partials [group][2][8 warps][8 rows][TT][2]
-  float* red_r = red + kGroups * 2 * kGuRowsShared * 4 * TT * 2;
-  int* s_active = reinterpret_cast<int*>(red_r + kGroups * 2 * kConsumerWarps * 8 * TT * 2);
+  uint4* xh = reinterpret_cast<uint4*>(smem + sc.x_off);  // f16 [t][i][w][lane]
+  uint4* xb = xh + TT * KI * 128;                         // bf16 [t][q][w4][lane]
+  float* red = reinterpret_cast<float*>(smem + sc.aux_off);  // [group][2][2 rows][4 q][TT][2]
+  int* s_active = reinterpret_cast<int*>(red + kGroups * 2 * kGuRowsShared * 4 * TT * 2);
   int* s_offsets = s_active + (((a.E + 1) + 3) & ~3);
   int* s_perm = s_offsets + (((a.E + 1) + 3) & ~3);
+  __shared__ __align__(8) uint64_t tbl;
   const int n_sh = Fs > 0 ? Fs / kGuRowsShared : 0;
   const int nrb = F / kGuRowsRouted;
   if (threadIdx.x == 0) {
@@ -176,64 +117,54 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
     bool ok = true;
     int it = 0;
     int j = blockIdx.x;
-    const unsigned sh_bytes = kGuRowsShared * K * 2;
-    for (; j < n_sh; j += gridDim.x, ++it) {
-      const int s = it % S;
-      const unsigned round = it / S;
-      if (lane == 0) {
+    if (lane == 0) {
+      const unsigned sh_bytes = kGuRowsShared * K * 2;
+      for (; j < n_sh; j += gridDim.x, ++it) {
+        const int s = it % S;
+        const unsigned round = it / S;
         if (ok && round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, a.status, kSiteGuEmpty);
-        if (ok) {
-          unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
-          mbar_arrive_expect_tx(&full[s], 2 * sh_bytes);
-          bulk_g2s(st, a.sh_gate + static_cast<size_t>(j) * kGuRowsShared * K, sh_bytes, &full[s]);
-          bulk_g2s(st + sh_bytes, a.sh_up + static_cast<size_t>(j) * kGuRowsShared * K, sh_bytes, &full[s]);
-        }
+        if (!ok) continue;
+        unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+        mbar_arrive_expect_tx(&full[s], 2 * sh_bytes);
+        bulk_g2s(st, a.sh_gate + static_cast<size_t>(j) * kGuRowsShared * K, sh_bytes, &full[s]);
+        bulk_g2s(st + sh_bytes, a.sh_up + static_cast<size_t>(j) * kGuRowsShared * K, sh_bytes, &full[s]);
       }
     }
-    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
     pdl_wait();  // routing tables written by the router
     pdl_trigger();
     if (lane == 0) {
       copy_tables(a, s_active, s_offsets, s_perm, &tbl);
       if (ok) ok = mbar_wait(&tbl, 0, a.status, kSiteGuEmpty);
-    }
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    const int n_r = ok ? s_active[0] * nrb : 0;
-    const int rb = K >> 1;
-    const unsigned bytes = 2u * kGuRowsRouted * rb + 2u * kGuRowsRouted * G;
-    for (; j - n_sh < n_r; j += gridDim.x, ++it) {
-      const int s = it % S;
-      const unsigned round = it / S;
-      if (lane == 0) {
+      const int n_r = ok ? s_active[0] * nrb : 0;
+      const unsigned pk = kGuRowsRouted * (K >> 1), sk = kGuRowsRouted * G;
+      for (; j - n_sh < n_r; j += gridDim.x, ++it) {
+        const int s = it % S;
+        const unsigned round = it / S;
         if (ok && round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, a.status, kSiteGuEmpty);
-        if (ok) mbar_arrive_expect_tx(&full[s], bytes);
+        if (!ok) continue;
+        const int jr = j - n_sh;
+        const int e = s_active[1 + jr / nrb];
+        const size_t f0 = static_cast<size_t>(jr % nrb) * kGuRowsRouted;
+        unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+        mbar_arrive_expect_tx(&full[s], 2 * pk + 2 * sk);
+        bulk_g2s(st, a.gate_p + e * a.gate_ps + f0 * (K >> 1), pk, &full[s]);
+        bulk_g2s(st + pk, a.up_p + e * a.up_ps + f0 * (K >> 1), pk, &full[s]);
+        bulk_g2s(st + 2 * pk, a.gate_s + e * a.gate_ss + f0 * G, sk, &full[s]);
+        bulk_g2s(st + 2 * pk + sk, a.up_s + e * a.up_ss + f0 * G, sk, &full[s]);
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) continue;
-      const int jr = j - n_sh;
-      const int e = s_active[1 + jr / nrb];
-      const size_t f0 = static_cast<size_t>(jr % nrb) * kGuRowsRouted;
-      unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
-      // rows 0..7: gate rows f0..f0+7; rows 8..15: up rows; then 16 scale rows
-      issue_rows(st, a.gate_p + e * a.gate_ps + f0 * rb, kGuRowsRouted, rb, sc.rs, lane, &full[s]);
-      issue_rows(st + kGuRowsRouted * sc.rs, a.up_p + e * a.up_ps + f0 * rb, kGuRowsRouted, rb, sc.rs, lane,
-                 &full[s]);
-      unsigned char* sst = st + 2 * kGuRowsRouted * sc.rs;  // gate scales [8][G], then up scales [8][G]
-      if (lane == 0) bulk_g2s(sst, a.gate_s + e * a.gate_ss + f0 * G, kGuRowsRouted * G, &full[s]);
-      if (lane == 1) bulk_g2s(sst + kGuRowsRouted * G, a.up_s + e * a.up_ss + f0 * G, kGuRowsRouted * G, &full[s]);
-    }
-    if (!ok && lane == 0) {  // consumers stopped: let copies already issued land before leaving
-      for (int q = (it > S ? it - S : 0); q < it; ++q)
-        mbar_wait(&full[q % S], (q / S) & 1, a.status, kSiteGuDrain);
+      if (!ok) {  // consumers stopped: let copies already issued land before leaving
+        for (int q = (it > S ? it - S : 0); q < it; ++q)
+          mbar_wait(&full[q % S], (q / S) & 1, a.status, kSiteGuDrain);
+      }
     }
     return;
   }
 
   // ------------------------------- consumers -------------------------------
-  const int grp = warp_id / kConsumerWarps;   // consumer group
+  const int grp = warp_id / kConsumerWarps;  // consumer group
   const int warp = warp_id % kConsumerWarps;  // warp within the group
   const int ct = threadIdx.x;                 // 0 .. kGroups*kConsumerThreads-1
-  const int gt = ct - grp * kConsumerThreads;
   constexpr int kAll = kGroups * kConsumerThreads;
   // stage bf16 rows for shared chunks: element qq*KQ + 8*(lane + 32*w4) + 0..7
   if (n_sh > 0) {
@@ -247,23 +178,26 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
             *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + qq * KQ + el);
     }
   }
-  // f16 rows for routed chunks with a per-token power-of-two prescale: one
-  // load per element into registers, block max, then convert
-  constexpr int kStageRegs = 4;  // M*K/8 <= kStageRegs*kAll
+  // f16 rows for routed chunks, with a per-token power-of-two prescale:
+  // one load per element into registers, block max, then convert
+  constexpr int kStageRegs = 4;  // uint4 per thread held across the max (M*G*4 <= 4*kAll)
   uint4 xr[kStageRegs];
 #pragma unroll
   for (int q = 0; q < kStageRegs; ++q) {
     const int i4 = ct + q * kAll;
-    if (i4 < M * K / 8) xr[q] = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(i4) * 8);
+    if (i4 < M * G * 4) {
+      const int t = i4 / (G * 4), rem = i4 - t * G * 4;
+      xr[q] = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * K + 8 * rem);
+    }
   }
 #pragma unroll
   for (int q = 0; q < kStageRegs; ++q) {
     const int i4 = ct + q * kAll;
-    if (i4 < M * K / 8) {
+    if (i4 < M * G * 4) {
       const uint4 u = xr[q];
       float m = fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y))));
       m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
-      atomicMax(amax_bits + (i4 * 8) / K, __float_as_uint(m));
+      atomicMax(amax_bits + i4 / (G * 4), __float_as_uint(m));
     }
   }
   named_sync(kBarAllConsumers, kAll);
@@ -272,10 +206,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
 #pragma unroll
   for (int q = 0; q < kStageRegs; ++q) {
     const int i4 = ct + q * kAll;
-    if (i4 < M * K / 8) {
+    if (i4 < M * G * 4) {
+      const int t = i4 / (G * 4), rem = i4 - t * G * 4, c = rem >> 2, w = rem & 3;
       const uint4 u = xr[q];
-      const float sc2 = __fdiv_rn(1.0f, tok_mult[(i4 * 8) / K]);
-      reinterpret_cast<uint4*>(xh)[i4] =
+      const float sc2 = __fdiv_rn(1.0f, tok_mult[t]);
+      xh[((t * KI + (c >> 5)) * 4 + w) * 32 + (c & 31)] =
           make_uint4(bf16x2_to_f16x2_scaled(u.x, sc2), bf16x2_to_f16x2_scaled(u.y, sc2),
                      bf16x2_to_f16x2_scaled(u.z, sc2), bf16x2_to_f16x2_scaled(u.w, sc2));
     }
@@ -283,31 +218,46 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
   named_sync(kBarAllConsumers, kAll);
 
   bool ok = true;
-  int shi = 0, rti = 0;
+  int shi = 0;
   int it = grp;
   int j = blockIdx.x + it * gridDim.x;
   // shared-expert chunks: rows 2j, 2j+1; warp -> (row w/4, K quarter w%4)
   for (; j < n_sh; it += kGroups, j += kGroups * gridDim.x, ++shi) {
     const int s = it % S;
-    if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteGuFull);
+    if (ok) ok = mbar_wait_warp(&full[s], (it / S) & 1, a.status, kSiteGuFull);
     const int rr = warp >> 2, qq = warp & 3;
     float ag[4][TT], au[4][TT];
 #pragma unroll
     for (int w = 0; w < 4; ++w)
 #pragma unroll
       for (int t = 0; t < TT; ++t) { ag[w][t] = 0.f; au[w][t] = 0.f; }
+    const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+    const unsigned char* gr = st + static_cast<size_t>(rr) * K * 2 + static_cast<size_t>(qq) * KQ * 2;
+    const unsigned char* ur = gr + static_cast<size_t>(kGuRowsShared) * K * 2;
+    const bool regs = WPL <= 4;  // copy this lane's slice out and release the stage first
+    uint4 wgr[4], wur[4];
+    if (ok && regs) {
+#pragma unroll
+      for (int u4 = 0; u4 < 4; ++u4) {
+        const int el = 8 * (lane + 32 * u4);
+        if (u4 < WPL && el < KQ) {
+          wgr[u4] = *reinterpret_cast<const uint4*>(gr + 2 * el);
+          wur[u4] = *reinterpret_cast<const uint4*>(ur + 2 * el);
+        }
+      }
+    }
+    __syncwarp();
+    const bool early = regs || !ok;
+    if (early && lane == 0) mbar_arrive(&empty[s]);
     if (ok) {
-      const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
-      const unsigned char* gr = st + static_cast<size_t>(rr) * K * 2 + static_cast<size_t>(qq) * KQ * 2;
-      const unsigned char* ur = gr + static_cast<size_t>(kGuRowsShared) * K * 2;
       for (int w0 = 0; w0 < WPL; w0 += 4) {
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
           const int w4 = w0 + u4;
           const int el = 8 * (lane + 32 * w4);
           if (w4 < WPL && el < KQ) {
-            const uint4 wg = *reinterpret_cast<const uint4*>(gr + 2 * el);
-            const uint4 wu = *reinterpret_cast<const uint4*>(ur + 2 * el);
+            const uint4 wg = regs ? wgr[u4] : *reinterpret_cast<const uint4*>(gr + 2 * el);
+            const uint4 wu = regs ? wur[u4] : *reinterpret_cast<const uint4*>(ur + 2 * el);
 #pragma unroll
             for (int t = 0; t < TT; ++t)
               if (t < M) {
@@ -319,27 +269,29 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    float g4[TT], u4s[TT];
+    if (!early) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    float gt[TT], ut[TT];
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
-      g4[t] = __fadd_rn(__fadd_rn(ag[0][t], ag[1][t]), __fadd_rn(ag[2][t], ag[3][t]));
-      u4s[t] = __fadd_rn(__fadd_rn(au[0][t], au[1][t]), __fadd_rn(au[2][t], au[3][t]));
+      gt[t] = __fadd_rn(__fadd_rn(ag[0][t], ag[1][t]), __fadd_rn(ag[2][t], ag[3][t]));
+      ut[t] = __fadd_rn(__fadd_rn(au[0][t], au[1][t]), __fadd_rn(au[2][t], au[3][t]));
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1)
 #pragma unroll
       for (int t = 0; t < TT; ++t) {
-        g4[t] = __fadd_rn(g4[t], __shfl_xor_sync(0xffffffffu, g4[t], off));
-        u4s[t] = __fadd_rn(u4s[t], __shfl_xor_sync(0xffffffffu, u4s[t], off));
+        gt[t] = __fadd_rn(gt[t], __shfl_xor_sync(0xffffffffu, gt[t], off));
+        ut[t] = __fadd_rn(ut[t], __shfl_xor_sync(0xffffffffu, ut[t], off));
       }
     float* rb = red + ((grp * 2 + (shi & 1)) * kGuRowsShared * 4 * TT * 2);
     if (lane == 0) {
 #pragma unroll
       for (int t = 0; t < TT; ++t) {
-        rb[((rr * 4 + qq) * TT + t) * 2 + 0] = g4[t];
-        rb[((rr * 4 + qq) * TT + t) * 2 + 1] = u4s[t];
+        rb[((rr * 4 + qq) * TT + t) * 2 + 0] = gt[t];
+        rb[((rr * 4 + qq) * TT + t) * 2 + 1] = ut[t];
       }
     }
     named_sync(1 + grp, kConsumerThreads);
@@ -355,93 +307,165 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_stream_kernel(Decod
   }
   pdl_wait();
   pdl_trigger();
-  if (ok) ok = mbar_wait(&tbl, 0, a.status, kSiteGuFull);
+  if (ok) ok = mbar_wait_warp(&tbl, 0, a.status, kSiteGuFull);
   const int n_r = ok ? s_active[0] * nrb : 0;
-  // routed chunks: 16-row tile = 8 gate rows over 8 up rows; the K groups are
-  // split over the 8 warps of the group; columns = routes of the expert
-  const int g8 = lane >> 2, q4 = lane & 3;
-  const int gpw = (G + kConsumerWarps - 1) / kConsumerWarps;
-  for (; j - n_sh < n_r; it += kGroups, j += kGroups * gridDim.x, ++rti) {
+  for (; j - n_sh < n_r; it += kGroups, j += kGroups * gridDim.x) {
     const int s = it % S;
-    if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteGuFull);
+    if (ok) ok = mbar_wait_warp(&full[s], (it / S) & 1, a.status, kSiteGuFull);
     const int jr = j - n_sh;
     const int e = s_active[1 + jr / nrb];
-    const int f0 = (jr % nrb) * kGuRowsRouted;
+    const int f = (jr % nrb) * kGuRowsRouted + warp;
     const int p0 = s_offsets[e];
     const int n = s_offsets[e + 1] - p0;
-    const int col_tok = s_perm[p0 + (g8 < n ? g8 : 0)] / a.k;  // token of this lane's column
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-    if (ok) {
-      const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
-      const unsigned char* wlo = st + static_cast<size_t>(g8) * sc.rs + 4 * q4;                  // gate row g
-      const unsigned char* whi = st + static_cast<size_t>(kGuRowsRouted + g8) * sc.rs + 4 * q4;  // up row g
-      const unsigned char* sst = st + 2 * kGuRowsRouted * sc.rs;
-      const unsigned char* slo = sst + g8 * G;
-      const unsigned char* shi = sst + (kGuRowsRouted + g8) * G;
-      const uint16_t* xrow = xh + static_cast<size_t>(col_tok) * K + 8 * q4;
-      const int c0 = warp * gpw, c1 = min(G, c0 + gpw);
-      if (gpw == 16 && (G & 15) == 0) {  // the warp's 16 scale bytes per row in one load
-        const uint4 vl = *reinterpret_cast<const uint4*>(slo + c0);
-        const uint4 vh = *reinterpret_cast<const uint4*>(shi + c0);
-        const uint32_t sl4[4] = {vl.x, vl.y, vl.z, vl.w}, sh4[4] = {vh.x, vh.y, vh.z, vh.w};
+    int tok[TT];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int c = c0 + i;
-          const uint32_t wl = *reinterpret_cast<const uint32_t*>(wlo + 16 * c);
-          const uint32_t wh = *reinterpret_cast<const uint32_t*>(whi + 16 * c);
-          const uint4 xv = *reinterpret_cast<const uint4*>(xrow + 32 * c);
-          const float sl = e8m0_to_f32((sl4[i >> 2] >> (8 * (i & 3))) & 0xffu);
-          const float sh = e8m0_to_f32((sh4[i >> 2] >> (8 * (i & 3))) & 0xffu);
-          float t4[4] = {0.f, 0.f, 0.f, 0.f};
-          group_mma(t4, wl, wh, xv);
-          d[0] = __fmaf_rn(t4[0], sl, d[0]);
-          d[1] = __fmaf_rn(t4[1], sl, d[1]);
-          d[2] = __fmaf_rn(t4[2], sh, d[2]);
-          d[3] = __fmaf_rn(t4[3], sh, d[3]);
-        }
-      } else {
-        for (int c = c0; c < c1; ++c) {
-          const uint32_t wl = *reinterpret_cast<const uint32_t*>(wlo + 16 * c);
-          const uint32_t wh = *reinterpret_cast<const uint32_t*>(whi + 16 * c);
-          const uint4 xv = *reinterpret_cast<const uint4*>(xrow + 32 * c);
-          const float sl = e8m0_to_f32(slo[c]), sh = e8m0_to_f32(shi[c]);
-          float t4[4] = {0.f, 0.f, 0.f, 0.f};
-          group_mma(t4, wl, wh, xv);
-          d[0] = __fmaf_rn(t4[0], sl, d[0]);
-          d[1] = __fmaf_rn(t4[1], sl, d[1]);
-          d[2] = __fmaf_rn(t4[2], sh, d[2]);
-          d[3] = __fmaf_rn(t4[3], sh, d[3]);
+    for (int q = 0; q < TT; ++q) tok[q] = q < n ? s_perm[p0 + q] / a.k : 0;
+    float ag[TT], au[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) { ag[t] = 0.f; au[t] = 0.f; }
+    // This lane's slice of the stage (16 packed bytes of gate and of up and a
+    // scale byte each, per group) goes to registers first and the stage is
+    // released before the arithmetic, so the ring refills during compute.
+    constexpr int kRegGroups = 4;
+    const bool regs = KI <= kRegGroups;
+    const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+    const size_t pk = static_cast<size_t>(kGuRowsRouted) * (K >> 1);
+    const unsigned char* gp = st + static_cast<size_t>(warp) * (K >> 1);
+    const unsigned char* up = gp + pk;
+    const unsigned char* gs = st + 2 * pk + warp * G;
+    const unsigned char* us = gs + kGuRowsRouted * G;
+    uint4 pgr[kRegGroups], pur[kRegGroups];
+    uint32_t sgr[kRegGroups], sur[kRegGroups];
+    if (ok && regs) {
+#pragma unroll
+      for (int i = 0; i < kRegGroups; ++i) {
+        const int c = lane + 32 * i;
+        if (i < KI && c < G) {
+          pgr[i] = *reinterpret_cast<const uint4*>(gp + 16 * c);
+          pur[i] = *reinterpret_cast<const uint4*>(up + 16 * c);
+          sgr[i] = gs[c];
+          sur[i] = us[c];
         }
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    // cross-warp reduction of the K split: partials [warp][row][col][gate/up]
-    float* rr2 = red_r + ((grp * 2 + (rti & 1)) * kConsumerWarps + warp) * 8 * TT * 2;
+    const bool early = regs || !ok;
+    if (early && lane == 0) mbar_arrive(&empty[s]);
+    // one 32-column group: 4-chain dot products for every routed token
+    auto group = [&](const uint4& pg, const uint4& pu, uint32_t sgb, uint32_t sub_, int i) {
+      const float s_g = e8m0_to_f32(sgb), s_u = e8m0_to_f32(sub_);
+      const uint4* xv0 = xh + i * 128 + lane;  // token t: + t*KI*128, word w: + w*32
+      float gg[TT], gu[TT];
+      if (n == 1 || TT == 1) {
+        group_dot_e2m1<TT>(pg, xv0 + tok[0] * KI * 128, 0, n, gg);
+        group_dot_e2m1<TT>(pu, xv0 + tok[0] * KI * 128, 0, n, gu);
+      } else {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int col = 2 * q4 + h;
-      if (col < n && col < TT) {
-        rr2[(g8 * TT + col) * 2 + 0] = d[h];
-        rr2[(g8 * TT + col) * 2 + 1] = d[2 + h];
+        for (int q = 0; q < TT; ++q) {
+          float g1[1], u1[1];
+          if (q < n) {
+            group_dot_e2m1<1>(pg, xv0 + tok[q] * KI * 128, 0, 1, g1);
+            group_dot_e2m1<1>(pu, xv0 + tok[q] * KI * 128, 0, 1, u1);
+          } else {
+            g1[0] = 0.f; u1[0] = 0.f;
+          }
+          gg[q] = g1[0];
+          gu[q] = u1[0];
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < TT; ++q) {
+        ag[q] = __fmaf_rn(gg[q], s_g, ag[q]);
+        au[q] = __fmaf_rn(gu[q], s_u, au[q]);
+      }
+    };
+    if (ok && regs) {
+#pragma unroll
+      for (int i = 0; i < kRegGroups; ++i)
+        if (i < KI && lane + 32 * i < G) group(pgr[i], pur[i], sgr[i], sur[i], i);
+    } else if (ok) {
+#pragma unroll 2
+      for (int i = 0; i < KI; ++i) {
+        const int c = lane + 32 * i;
+        if (c < G)
+          group(*reinterpret_cast<const uint4*>(gp + 16 * c), *reinterpret_cast<const uint4*>(up + 16 * c), gs[c],
+                us[c], i);
       }
     }
-    named_sync(1 + grp, kConsumerThreads);
-    if (ok && gt < 8 * n) {
-      const int row = gt / n, col = gt - row * n;
-      const float* base = red_r + (grp * 2 + (rti & 1)) * kConsumerWarps * 8 * TT * 2;
-      float g = 0.f, u = 0.f;
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        g = __fadd_rn(g, base[(w * 8 * TT + row * TT + col) * 2 + 0]);
-        u = __fadd_rn(u, base[(w * 8 * TT + row * TT + col) * 2 + 1]);
+    if (!early) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+      for (int q = 0; q < TT; ++q) {
+        ag[q] = __fadd_rn(ag[q], __shfl_xor_sync(0xffffffffu, ag[q], off));
+        au[q] = __fadd_rn(au[q], __shfl_xor_sync(0xffffffffu, au[q], off));
       }
-      const int tj = s_perm[p0 + col] / a.k;
+    if (ok && lane < TT && lane < n) {
+      float g = ag[0], uu = au[0];
+      int tj = tok[0];
+#pragma unroll
+      for (int q = 1; q < TT; ++q)
+        if (lane == q) { g = ag[q]; uu = au[q]; tj = tok[q]; }
       const float m = tok_mult[tj];
-      a.act[static_cast<size_t>(p0 + col) * F + f0 + row] =
-          swiglu_bf16(round_bf16(__fmul_rn(g, m)), round_bf16(__fmul_rn(u, m)), a.limit);
+      a.act[static_cast<size_t>(p0 + lane) * F + f] =
+          swiglu_bf16(round_bf16(__fmul_rn(g, m)), round_bf16(__fmul_rn(uu, m)), a.limit);
     }
   }
 }
+
+// One 32-column MXFP4 group of a down row against the staged activations of
+// the expert's routes: acc[q] += scale * sum of 32 products for route q.
+template <int TT>
+__device__ __forceinline__ void down_group(const uint4& pkv, uint32_t sbyte, const uint4* xv0, int G, int n,
+                                           float (&acc)[TT]) {
+  const float scl = e8m0_to_f32(sbyte);
+  const uint32_t w4v[4] = {pkv.x, pkv.y, pkv.z, pkv.w};
+  float c[4][TT];
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int q = 0; q < TT; ++q) c[w][q] = 0.f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int q = 0; q < TT; ++q)
+      if (q < n) c[w][q] = dot8_e2m1_f16(w4v[w], xv0[(q * 4 + w) * G], c[w][q]);
+#pragma unroll
+  for (int q = 0; q < TT; ++q)
+    acc[q] = __fmaf_rn(__fadd_rn(__fadd_rn(c[0][q], c[1][q]), __fadd_rn(c[2][q], c[3][q])), scl, acc[q]);
+}
+
+// What a routed down consumer lane works on within one stage.
+template <int TT>
+struct DnRouted {
+  const unsigned char* st;  // stage: packed rows then scale rows
+  size_t pk;                // bytes of packed rows
+  int F, G, d, LPR, slots, slot, sub, per_lane, warp, p0, n, r0;
+  const uint4* xv;          // staged activations of route p0 (word w of route q: + (q*4+w)*G)
+  const float* rscale;      // per-route activation scale, from route p0
+  uint16_t* y;
+  int slot_of[TT];          // route slot of route p0+q
+
+  // reduce a row's partial sums over its LPR lanes and write the routes' outputs
+  __device__ __forceinline__ void finish_row(float (&acc)[TT], int rl) const {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1)
+      if (off < LPR)
+#pragma unroll
+        for (int q = 0; q < TT; ++q) acc[q] = __fadd_rn(acc[q], __shfl_xor_sync(0xffffffffu, acc[q], off));
+    if (rl < kDnRowsRouted && sub < TT && sub < n) {
+      float v = acc[0];
+      int sl = slot_of[0];
+#pragma unroll
+      for (int q = 1; q < TT; ++q)
+        if (sub == q) { v = acc[q]; sl = slot_of[q]; }
+      y[static_cast<size_t>(sl) * d + r0 + rl] = f32_to_bf16(__fmul_rn(v, rscale[sub]));
+    }
+  }
+};
 
 // ---------------------------------------------------------------------------
 template <int TT>
@@ -449,22 +473,25 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages];
   __shared__ __align__(8) uint64_t empty[kMaxStages];
-  __shared__ __align__(8) uint64_t tbl;
   const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int M = a.M, k = a.k, d = a.d, F = a.F, Fs = a.Fs;
   const int G = F >> 5;
   const int S = sc.stages;
+  const int LPR = a.lpr_down;
+  const int slots = 32 / LPR;
+  const int sub = lane & (LPR - 1), slot = lane / LPR;
+  const int per_lane = (G + LPR - 1) / LPR;
   const int WS = (Fs / 8 + 31) / 32;  // 8-element words per lane of a shared row
   const int n_sh = Fs > 0 ? d / kDnRowsShared : 0;
   const int nrb = d / kDnRowsRouted;
   const int R = M * k;
-  uint16_t* xr = reinterpret_cast<uint16_t*>(smem + sc.x_off);  // f16 [p][F]
-  uint4* xsb = reinterpret_cast<uint4*>(xr + static_cast<size_t>(R) * F);  // bf16 [t][w4][lane]
+  uint4* xr = reinterpret_cast<uint4*>(smem + sc.x_off);  // f16 [p][q4][grp]
+  uint4* xsb = xr + R * G * 4;                            // bf16 [t][w4][lane]
   float* rscale = reinterpret_cast<float*>(smem + sc.aux_off);
-  float* red_r = rscale + ((R + 3) & ~3);  // [group][2][8 warps][32 rows][TT]
-  int* s_active = reinterpret_cast<int*>(red_r + kGroups * 2 * kConsumerWarps * kDnRowsRouted * TT);
+  int* s_active = reinterpret_cast<int*>(rscale + ((R + 3) & ~3));
   int* s_offsets = s_active + (((a.E + 1) + 3) & ~3);
   int* s_perm = s_offsets + (((a.E + 1) + 3) & ~3);
+  __shared__ __align__(8) uint64_t tbl;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumerWarps); }
     mbar_init(&tbl, 1);
@@ -476,43 +503,35 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
     // Weights depend on nothing earlier and the routing tables are complete
     // (the gate/up kernel waited on the router before letting this kernel
     // launch), so streaming starts before griddepcontrol.wait.
-    bool ok = true;
     if (lane == 0) {
       copy_tables(a, s_active, s_offsets, s_perm, &tbl);
-      ok = mbar_wait(&tbl, 0, a.status, kSiteDnEmpty);
-    }
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    int it = 0;
-    const int n_r = ok ? s_active[0] * nrb : 0;
-    const unsigned shb = kDnRowsShared * Fs * 2;
-    const int rb = F >> 1;
-    const unsigned rbytes = kDnRowsRouted * (rb + G);
-    for (int j = blockIdx.x; j < n_sh + n_r; j += gridDim.x, ++it) {
-      const int s = it % S;
-      const unsigned round = it / S;
-      if (lane == 0) {
+      bool ok = mbar_wait(&tbl, 0, a.status, kSiteDnEmpty);
+      int it = 0;
+      const int n_r = ok ? s_active[0] * nrb : 0;
+      const unsigned shb = kDnRowsShared * Fs * 2;
+      const unsigned pk = kDnRowsRouted * (F >> 1), sk = kDnRowsRouted * G;
+      for (int j = blockIdx.x; j < n_sh + n_r; j += gridDim.x, ++it) {
+        const int s = it % S;
+        const unsigned round = it / S;
         if (ok && round > 0) ok = mbar_wait(&empty[s], (round - 1) & 1, a.status, kSiteDnEmpty);
-        if (ok) mbar_arrive_expect_tx(&full[s], j < n_sh ? shb : rbytes);
+        if (!ok) continue;
+        unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
+        if (j < n_sh) {
+          mbar_arrive_expect_tx(&full[s], shb);
+          bulk_g2s(st, a.sh_down + static_cast<size_t>(j) * kDnRowsShared * Fs, shb, &full[s]);
+        } else {
+          const int jr = j - n_sh;
+          const int e = s_active[1 + jr / nrb];
+          const size_t r0 = static_cast<size_t>(jr % nrb) * kDnRowsRouted;
+          mbar_arrive_expect_tx(&full[s], pk + sk);
+          bulk_g2s(st, a.down_p + e * a.down_ps + r0 * (F >> 1), pk, &full[s]);
+          bulk_g2s(st + pk, a.down_s + e * a.down_ss + r0 * G, sk, &full[s]);
+        }
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) continue;
-      unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
-      if (j < n_sh) {
-        if (lane == 0) bulk_g2s(st, a.sh_down + static_cast<size_t>(j) * kDnRowsShared * Fs, shb, &full[s]);
-      } else {
-        const int jr = j - n_sh;
-        const int e = s_active[1 + jr / nrb];
-        const size_t r0 = static_cast<size_t>(jr % nrb) * kDnRowsRouted;
-        // 8 blocks of 4 consecutive rows at padded stride sc.rs, then the
-        // chunk's scale rows as one block [32][G]
-        issue_rows(st, a.down_p + e * a.down_ps + r0 * rb, kDnRowsRouted / 4, 4 * rb, sc.rs, lane, &full[s]);
-        if (lane == 31)
-          bulk_g2s(st + (kDnRowsRouted / 4) * sc.rs, a.down_s + e * a.down_ss + r0 * G, kDnRowsRouted * G, &full[s]);
+      if (!ok) {
+        for (int q = (it > S ? it - S : 0); q < it; ++q)
+          mbar_wait(&full[q % S], (q / S) & 1, a.status, kSiteDnDrain);
       }
-    }
-    if (!ok && lane == 0) {
-      for (int q = (it > S ? it - S : 0); q < it; ++q)
-        mbar_wait(&full[q % S], (q / S) & 1, a.status, kSiteDnDrain);
     }
     pdl_wait();
     pdl_trigger();
@@ -523,15 +542,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   const int grp = warp_id / kConsumerWarps;
   const int warp = warp_id % kConsumerWarps;
   const int ct = threadIdx.x;
-  const int gt = ct - grp * kConsumerThreads;
   constexpr int kAll = kGroups * kConsumerThreads;
   pdl_wait();  // activations from the gate/up kernel
   pdl_trigger();
-  bool ok = mbar_wait(&tbl, 0, a.status, kSiteDnFull);
+  bool ok = mbar_wait_warp(&tbl, 0, a.status, kSiteDnFull);
   const int n_active = ok ? s_active[0] : 0;
   const int n_r = n_active * nrb;
   // routed activations as f16 with a per-route power-of-two prescale; a warp
-  // holds its row in registers (F/8 <= 32*kRowRegs uint4) across the max
+  // holds its row in registers (G*4 <= 32*kRowRegs uint4) across the max
   constexpr int kRowRegs = 8;
   for (int r = warp_id; r < R; r += kGroups * kConsumerWarps) {
     const uint16_t* src = a.act + static_cast<size_t>(r) * F;
@@ -540,12 +558,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
 #pragma unroll
     for (int q = 0; q < kRowRegs; ++q) {
       const int v = lane + 32 * q;
-      if (v < F / 8) v8[q] = __ldcg(reinterpret_cast<const uint4*>(src + 8 * v));
+      if (v < G * 4) v8[q] = __ldcg(reinterpret_cast<const uint4*>(src + 8 * v));
     }
 #pragma unroll
     for (int q = 0; q < kRowRegs; ++q) {
       const int v = lane + 32 * q;
-      if (v < F / 8) {
+      if (v < G * 4) {
         const uint4 u = v8[q];
         m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.x)), fabsf(bf16hi(u.x))), fmaxf(fabsf(bf16lo(u.y)), fabsf(bf16hi(u.y)))));
         m = fmaxf(m, fmaxf(fmaxf(fabsf(bf16lo(u.z)), fabsf(bf16hi(u.z))), fmaxf(fabsf(bf16lo(u.w)), fabsf(bf16hi(u.w)))));
@@ -559,9 +577,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
 #pragma unroll
     for (int q = 0; q < kRowRegs; ++q) {
       const int v = lane + 32 * q;
-      if (v < F / 8) {
+      if (v < G * 4) {
         const uint4 u = v8[q];
-        reinterpret_cast<uint4*>(xr + static_cast<size_t>(r) * F)[v] =
+        xr[(r * 4 + (v & 3)) * G + (v >> 2)] =
             make_uint4(bf16x2_to_f16x2_scaled(u.x, sc2), bf16x2_to_f16x2_scaled(u.y, sc2),
                        bf16x2_to_f16x2_scaled(u.z, sc2), bf16x2_to_f16x2_scaled(u.w, sc2));
       }
@@ -577,12 +595,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
   }
   named_sync(kBarAllConsumers, kAll);
 
-  const int g8 = lane >> 2, q4 = lane & 3;
-  const int gpw = (G + kConsumerWarps - 1) / kConsumerWarps;
-  int rti = 0;
-  for (int it = grp, j = blockIdx.x + grp * gridDim.x; j < n_sh + n_r; it += kGroups, j += kGroups * gridDim.x) {
+  for (int it = grp, j = blockIdx.x + grp * gridDim.x; j < n_sh + n_r;
+       it += kGroups, j += kGroups * gridDim.x) {
     const int s = it % S;
-    if (ok) ok = mbar_wait(&full[s], (it / S) & 1, a.status, kSiteDnFull);
+    if (ok) ok = mbar_wait_warp(&full[s], (it / S) & 1, a.status, kSiteDnFull);
     const unsigned char* st = smem + static_cast<size_t>(s) * sc.stage_bytes;
     if (j < n_sh) {  // shared: warp -> row j*8 + warp, whole Fs
       const int row = j * kDnRowsShared + warp;
@@ -591,8 +607,30 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
       for (int w = 0; w < 4; ++w)
 #pragma unroll
         for (int t = 0; t < TT; ++t) acc[w][t] = 0.f;
-      if (ok) {
-        const unsigned char* wr = st + static_cast<size_t>(warp) * Fs * 2;
+      const unsigned char* wr = st + static_cast<size_t>(warp) * Fs * 2;
+      const bool regs = WS <= 8;  // copy this lane's slice out and release the stage first
+      uint4 wrg[8];
+      if (ok && regs) {
+#pragma unroll
+        for (int w4 = 0; w4 < 8; ++w4) {
+          const int el = 8 * (lane + 32 * w4);
+          if (w4 < WS && el < Fs) wrg[w4] = *reinterpret_cast<const uint4*>(wr + 2 * el);
+        }
+      }
+      __syncwarp();
+      const bool early = regs || !ok;
+      if (early && lane == 0) mbar_arrive(&empty[s]);
+      if (ok && regs) {
+#pragma unroll
+        for (int w4 = 0; w4 < 8; ++w4) {
+          const int el = 8 * (lane + 32 * w4);
+          if (w4 < WS && el < Fs) {
+#pragma unroll
+            for (int t = 0; t < TT; ++t)
+              if (t < M) acc[w4 & 3][t] = dot8_bf16(wrg[w4], xsb[t * WS * 32 + w4 * 32 + lane], acc[w4 & 3][t]);
+          }
+        }
+      } else if (ok) {
         for (int w0 = 0; w0 < WS; w0 += 4) {
 #pragma unroll
           for (int u4 = 0; u4 < 4; ++u4) {
@@ -607,8 +645,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
           }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if (!early) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
       float v[TT];
 #pragma unroll
       for (int t = 0; t < TT; ++t) v[t] = __fadd_rn(__fadd_rn(acc[0][t], acc[1][t]), __fadd_rn(acc[2][t], acc[3][t]));
@@ -623,71 +663,43 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_stream_kernel(DecodeAr
           if (lane == t) o = v[t];
         a.ys[static_cast<size_t>(lane) * d + row] = f32_to_bf16(o);
       }
-    } else {  // routed: rows r0 .. r0+31 (two 16-row tiles) of expert e, K split over warps
+    } else {  // routed: rows r0 .. r0+31 of expert e; a warp iteration covers `slots` rows
       const int jr = j - n_sh;
       const int e = s_active[1 + jr / nrb];
       const int r0 = (jr % nrb) * kDnRowsRouted;
       const int p0 = s_offsets[e];
       const int n = s_offsets[e + 1] - p0;
-      // tile t (0, 1): MMA row m < 8 is row 4m + 2t, row m + 8 is row 4m + 2t + 1;
-      // the 8 rows of one fragment load sit in 8 differently padded blocks
-      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+      int slot_of[TT];
+#pragma unroll
+      for (int q = 0; q < TT; ++q) slot_of[q] = q < n ? s_perm[p0 + q] : 0;
+      const size_t pk = static_cast<size_t>(kDnRowsRouted) * (F >> 1);
+      DnRouted<TT> dr{st, pk, F, G, d, LPR, slots, slot, sub, per_lane, warp, p0, n, r0,
+                      xr + p0 * 4 * G, rscale + p0, a.y};
+#pragma unroll
+      for (int q = 0; q < TT; ++q) dr.slot_of[q] = slot_of[q];
+      // A lane's rows are rl = warp*slots + slot + it*8*slots and its groups
+      // gi = sub + LPR*qg.  The warp computes from the stage and releases it
+      // afterwards: a register copy of the slice spills at this CTA size.
+      const int row_iters = (kDnRowsRouted + kConsumerWarps * slots - 1) / (kConsumerWarps * slots);
       if (ok) {
-        const uint16_t* xrow = xr + static_cast<size_t>(p0 + (g8 < n ? g8 : 0)) * F + 8 * q4;
-        const int rb = F >> 1;
-        const unsigned char* blkp = st + static_cast<size_t>(g8) * sc.rs + 4 * q4;
-        const unsigned char* w0r = blkp;           // row 4g
-        const unsigned char* w1r = blkp + rb;      // row 4g + 1
-        const unsigned char* w2r = blkp + 2 * rb;  // row 4g + 2
-        const unsigned char* w3r = blkp + 3 * rb;  // row 4g + 3
-        const unsigned char* s0 = st + (kDnRowsRouted / 4) * sc.rs + (4 * g8) * G;
-        const int c0 = warp * gpw, c1 = min(G, c0 + gpw);
-#pragma unroll 2
-        for (int c = c0; c < c1; ++c) {
-          const uint4 xv = *reinterpret_cast<const uint4*>(xrow + 32 * c);
-          const uint32_t wa = *reinterpret_cast<const uint32_t*>(w0r + 16 * c);
-          const uint32_t wb = *reinterpret_cast<const uint32_t*>(w1r + 16 * c);
-          const uint32_t wc = *reinterpret_cast<const uint32_t*>(w2r + 16 * c);
-          const uint32_t wd = *reinterpret_cast<const uint32_t*>(w3r + 16 * c);
-          const float sa = e8m0_to_f32(s0[c]), sb = e8m0_to_f32(s0[G + c]);
-          const float sc_ = e8m0_to_f32(s0[2 * G + c]), sd = e8m0_to_f32(s0[3 * G + c]);
-          float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
-          group_mma(t0, wa, wb, xv);  // rows 4g (m = g) and 4g+1 (m = g+8)
-          group_mma(t1, wc, wd, xv);  // rows 4g+2 and 4g+3
-          d0[0] = __fmaf_rn(t0[0], sa, d0[0]);
-          d0[1] = __fmaf_rn(t0[1], sa, d0[1]);
-          d0[2] = __fmaf_rn(t0[2], sb, d0[2]);
-          d0[3] = __fmaf_rn(t0[3], sb, d0[3]);
-          d1[0] = __fmaf_rn(t1[0], sc_, d1[0]);
-          d1[1] = __fmaf_rn(t1[1], sc_, d1[1]);
-          d1[2] = __fmaf_rn(t1[2], sd, d1[2]);
-          d1[3] = __fmaf_rn(t1[3], sd, d1[3]);
+        for (int it2 = 0; it2 < row_iters; ++it2) {
+          float acc[TT];
+#pragma unroll
+          for (int q = 0; q < TT; ++q) acc[q] = 0.f;
+          const int rl = warp * slots + slot + it2 * kConsumerWarps * slots;
+          if (rl < kDnRowsRouted) {
+            const unsigned char* wp = st + static_cast<size_t>(rl) * (F >> 1);
+            const unsigned char* ws = st + pk + rl * G;
+            for (int qg = 0; qg < per_lane; ++qg) {
+              const int gi = sub + LPR * qg;
+              if (gi < G) down_group<TT>(*reinterpret_cast<const uint4*>(wp + 16 * gi), ws[gi], dr.xv + gi, G, n, acc);
+            }
+          }
+          dr.finish_row(acc, rl);
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-      float* rr2 = red_r + ((grp * 2 + (rti & 1)) * kConsumerWarps + warp) * kDnRowsRouted * TT;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int col = 2 * q4 + h;
-        if (col < n && col < TT) {
-          rr2[(4 * g8 + 0) * TT + col] = d0[h];
-          rr2[(4 * g8 + 1) * TT + col] = d0[2 + h];
-          rr2[(4 * g8 + 2) * TT + col] = d1[h];
-          rr2[(4 * g8 + 3) * TT + col] = d1[2 + h];
-        }
-      }
-      named_sync(1 + grp, kConsumerThreads);
-      if (ok) {
-        const float* base = red_r + (grp * 2 + (rti & 1)) * kConsumerWarps * kDnRowsRouted * TT;
-        for (int o = gt; o < kDnRowsRouted * n; o += kConsumerThreads) {
-          const int row = o / n, col = o - row * n;
-          float v = 0.f;
-          for (int w = 0; w < kConsumerWarps; ++w) v = __fadd_rn(v, base[(w * kDnRowsRouted + row) * TT + col]);
-          a.y[static_cast<size_t>(s_perm[p0 + col]) * d + r0 + row] = f32_to_bf16(__fmul_rn(v, rscale[p0 + col]));
-        }
-      }
-      ++rti;
     }
   }
 }

