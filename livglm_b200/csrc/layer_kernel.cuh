@@ -64,15 +64,13 @@ constexpr int kDnRowsMax = 32;  // routed down rows per chunk (16 row sets x 2)
 constexpr int kMaxRoutes = 32;  // M * k
 constexpr int kMaxExperts = 256;
 constexpr int kMaxGroups = 32;
-constexpr int kXRegs = 4;       // uint4 per consumer thread when staging x
-constexpr int kActRegs = 12;    // uint4 per consumer thread when staging act
-constexpr int kActSRegs = 2;    // uint4 per consumer thread when staging act_s
 
 // status sites (LG_ERR_TIMEOUT | site << 8)
 constexpr int kSiteFull = 7 << 8, kSiteEmpty = 8 << 8, kSiteDrain = 9 << 8;
 constexpr int kSiteLogits = 10 << 8, kSiteAct = 11 << 8, kSiteTable = 12 << 8;
-constexpr int kSiteSync = 13 << 8;
-constexpr int kSiteRed = 14 << 8;  // with LG_ERR_WORKSPACE: grid counters were not zero on entry
+constexpr int kSiteSync = 13 << 8;   // with LG_ERR_WORKSPACE: grid counters were not zero on entry
+constexpr int kSiteRed = 14 << 8;
+constexpr int kSiteRoute = 15 << 8;  // with LG_ERR_INVALID_ARG: a routed expert id outside [0, E)
 
 struct Args {
   int M, d, F, Fs, E, k, G, g, norm;
@@ -323,99 +321,111 @@ struct Tables {
   float w[kMaxRoutes];   // slot -> route weight
   int n_active;
   float bias[kMaxExperts];
-  float sc[kMaxExperts];
-  float ch[kMaxExperts];
+  float sc[kDecodeMaxTokens][kMaxExperts];  // sigmoid scores, per token
+  float ch[kDecodeMaxTokens][kMaxExperts];  // choice scores (masked), per token
+  int ix[kDecodeMaxTokens][kMaxExperts];    // candidate indices, per token
 };
 
-// Segmented (value, index) argmax over aligned groups of `seg` lanes
-// (seg a power of two <= 32): every lane ends with its segment's best.
-__device__ __forceinline__ void seg_best(float& v, int& i, int seg) {
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    if (off < seg) {
-      const float ov = __shfl_xor_sync(0xffffffffu, v, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, i, off);
-      if (after(ov, oi, v, i)) { v = ov; i = oi; }
-    }
+// Top two (value, index) pairs under the stable order: merge (w1, j1, w2, j2)
+// into (v1, i1, v2, i2).
+__device__ __forceinline__ void top2_merge(float& v1, int& i1, float& v2, int& i2, float w1, int j1, float w2, int j2) {
+  if (after(w1, j1, v1, i1)) {
+    if (after(v1, i1, w2, j2)) { v2 = v1; i2 = i1; } else { v2 = w2; i2 = j2; }
+    v1 = w1; i1 = j1;
+  } else if (after(w1, j1, v2, i2)) {
+    v2 = w1; i2 = j1;
   }
 }
 
-// Routing of token t by one warp, every score in registers: lane l holds
-// experts l + 32q.  Same results as the sequential scans of the checker for
-// the stable (value, index) order: group top-2 by two segmented argmaxes
-// (groups of `per` lanes, per | 32), kept groups by rank, top-k by k warp
-// argmaxes.  Writes T.sel[t*k + j] and T.w[t*k + j].  Returns false (and does
-// nothing) for group sizes that are not a divisor of 32.
-__device__ __forceinline__ bool route_token_warp(const Args& a, Tables& T, int t, int lane, bool write_out) {
-  constexpr int V = kMaxExperts / 32;
-  const int E = a.E, G = a.G, k = a.k, per = E / G;
-  if (a.g < G && (per > 32 || (32 % per) != 0)) return false;
+// Routing of token t by one warp.  Lane l owns the contiguous experts
+// l*V .. l*V+V-1 (V = E/32); per-expert values live in shared memory and every
+// loop is rolled, so the code stays small (this runs once per call while the
+// memory system is saturated, where each instruction-cache miss is slow).
+// Same results as the checker's sequential scans for the stable (value,
+// index) order: group top-2 by a merge over the group's lanes, kept groups by
+// rank, top-k by k warp argmaxes over per-lane sorted candidate lists.
+// Returns false (doing nothing) for E % 32 != 0, E > 256, or groups that do
+// not span a power-of-two number of whole lanes.
+__device__ __forceinline__ bool warp_routing_ok(const Args& a) {
+  const int E = a.E, per = E / a.G, V = E >> 5;
+  if ((E & 31) || V < 1 || V > kMaxExperts / 32) return false;
+  const int L = per / V;  // lanes per group
+  return a.g >= a.G || (per % V == 0 && L >= 1 && (L & (L - 1)) == 0);
+}
+
+__device__ __noinline__ bool route_token_warp(const Args& a, Tables& T, int t, int lane, bool write_out) {
+  if (!warp_routing_ok(a)) return false;
+  const int E = a.E, G = a.G, k = a.k, per = E / G, V = E >> 5;
+  const bool grouped = a.g < G;
+  const int L = per / V;  // lanes per group
+  float* sc = T.sc[t];
+  float* ch = T.ch[t];
+  int* ix = T.ix[t];
   const float ninf = __uint_as_float(0xff800000u);
-  float lg[V], sc[V], ch[V];
+  const int e0 = lane * V;
+  {  // logits of this lane's experts in one batch of loads
+    float lg[kMaxExperts / 32];
 #pragma unroll
-  for (int q = 0; q < V; ++q) {
-    const int e = lane + 32 * q;
-    lg[q] = e < E ? __ldcg(a.logits + static_cast<size_t>(t) * E + e) : 0.f;
+    for (int q = 0; q < kMaxExperts / 32; ++q) lg[q] = q < V ? __ldcg(a.logits + static_cast<size_t>(t) * E + e0 + q) : 0.f;
+#pragma unroll
+    for (int q = 0; q < kMaxExperts / 32; ++q)
+      if (q < V) sc[e0 + q] = lg[q];
   }
-#pragma unroll
+#pragma unroll 1
   for (int q = 0; q < V; ++q) {
-    const int e = lane + 32 * q;
-    sc[q] = e < E ? own_sigmoidf(lg[q]) : 0.f;
-    ch[q] = e < E ? __fadd_rn(sc[q], T.bias[e]) : ninf;
+    const float s = own_sigmoidf(sc[e0 + q]);
+    sc[e0 + q] = s;
+    ch[e0 + q] = __fadd_rn(s, T.bias[e0 + q]);
   }
-  if (a.g < G) {
-    // group score = second best + best of the group, in the group's lanes
-    float gsc[V];
-#pragma unroll
-    for (int q = 0; q < V; ++q) {
-      const int e = lane + 32 * q;
-      float v1 = ch[q];
-      int i1 = e < E ? e : -1;
-      seg_best(v1, i1, per);
-      float v2 = ch[q];
-      int i2 = (e < E && e != i1) ? e : -1;
-      seg_best(v2, i2, per);
-      gsc[q] = __fadd_rn(v2, v1);
+  if (grouped) {
+    // group score: the two best of the group's experts, summed (second + best)
+    float v1 = 0.f, v2 = 0.f;
+    int i1 = -1, i2 = -1;
+#pragma unroll 1
+    for (int q = 0; q < V; ++q) top2_merge(v1, i1, v2, i2, ch[e0 + q], e0 + q, 0.f, -1);
+#pragma unroll 1
+    for (int off = 1; off < L; off <<= 1) {
+      const float w1 = __shfl_xor_sync(0xffffffffu, v1, off), w2 = __shfl_xor_sync(0xffffffffu, v2, off);
+      const int j1 = __shfl_xor_sync(0xffffffffu, i1, off), j2 = __shfl_xor_sync(0xffffffffu, i2, off);
+      top2_merge(v1, i1, v2, i2, w1, j1, w2, j2);
     }
-    // lane gi < G takes the score of group gi, then its rank among the groups
-    float mine = ninf;
-    const int src = (lane * per) & 31, qs = (lane * per) >> 5;
-#pragma unroll
-    for (int q = 0; q < V; ++q) {
-      const float sv = __shfl_sync(0xffffffffu, gsc[q], src);
-      if (q == qs) mine = sv;
-    }
+    const float gsc = __fadd_rn(v2, v1);
+    const int gi = lane / L;
     int rank = 0;
+#pragma unroll 1
     for (int gj = 0; gj < G; ++gj) {
-      const float sj = __shfl_sync(0xffffffffu, mine, gj);
-      rank += after(sj, gj, mine, lane) ? 1 : 0;
+      const float sj = __shfl_sync(0xffffffffu, gsc, gj * L);
+      rank += after(sj, gj, gsc, gi) ? 1 : 0;
     }
-    const unsigned keep = __ballot_sync(0xffffffffu, lane < G && rank < a.g);
-#pragma unroll
-    for (int q = 0; q < V; ++q) {
-      const int e = lane + 32 * q;
-      if (e < E && !((keep >> (e / per)) & 1u)) ch[q] = ninf;
+    if (rank >= a.g) {
+#pragma unroll 1
+      for (int q = 0; q < V; ++q) ch[e0 + q] = ninf;
     }
   }
-  // top-k, best first; slot k-1-s gets the s-th best
-  unsigned taken = 0u;
-  float wj = 0.f;
-  for (int s = 0; s < k; ++s) {
-    float v = 0.f;
-    int i = -1;
-#pragma unroll
-    for (int q = 0; q < V; ++q) {
-      const int e = lane + 32 * q;
-      if (e < E && !((taken >> q) & 1u) && (i < 0 || after(ch[q], e, v, i))) { v = ch[q]; i = e; }
+  // this lane's candidates sorted best first (insertion sort)
+#pragma unroll 1
+  for (int q = 0; q < V; ++q) {
+    const float v = ch[e0 + q];
+    const int e = e0 + q;
+    int p = q;
+    while (p > 0 && after(v, e, ch[e0 + p - 1], ix[e0 + p - 1])) {
+      ch[e0 + p] = ch[e0 + p - 1];
+      ix[e0 + p] = ix[e0 + p - 1];
+      --p;
     }
+    ch[e0 + p] = v;
+    ix[e0 + p] = e;
+  }
+  // top-k: k warp argmaxes over the lanes' next candidates
+  int head = 0;
+  float wj = 0.f;
+#pragma unroll 1
+  for (int s = 0; s < k; ++s) {
+    float v = head < V ? ch[e0 + head] : 0.f;
+    int i = head < V ? ix[e0 + head] : -1;
     warp_best(v, i);
-    const int qo = i >> 5;
-    float c = 0.f;
-#pragma unroll
-    for (int q = 0; q < V; ++q)
-      if (q == qo) c = sc[q];
-    const float sw = __shfl_sync(0xffffffffu, c, i & 31);
-    if ((i & 31) == lane) taken |= 1u << qo;
+    if (i / V == lane) ++head;
+    const float sw = sc[i];
     if (lane == k - 1 - s) wj = sw;
     if (lane == 0) T.sel[t * k + (k - 1 - s)] = i;
   }
@@ -423,6 +433,7 @@ __device__ __forceinline__ bool route_token_warp(const Args& a, Tables& T, int t
   float denom = 1.f;
   if (a.norm) {
     float sum = __shfl_sync(0xffffffffu, wj, 0);
+#pragma unroll 1
     for (int j = 1; j < k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, wj, j));
     denom = __fadd_rn(sum, 0x1.79ca1p-67f);
   }
@@ -439,14 +450,14 @@ __device__ __forceinline__ bool route_token_warp(const Args& a, Tables& T, int t
 
 // Same routing by one warp for all tokens, scanning shared memory: the path
 // for group sizes that do not divide 32.
-__device__ __forceinline__ void route_tokens_scan(const Args& a, Tables& T, int lane, bool write_out) {
+__device__ __noinline__ void route_tokens_scan(const Args& a, Tables& T, int lane, bool write_out) {
   const int E = a.E, G = a.G, k = a.k, per = E / G;
   const float ninf = __uint_as_float(0xff800000u);
   for (int t = 0; t < a.M; ++t) {
     for (int e = lane; e < E; e += 32) {
       const float s = own_sigmoidf(__ldcg(a.logits + static_cast<size_t>(t) * E + e));
-      T.sc[e] = s;
-      T.ch[e] = __fadd_rn(s, T.bias[e]);
+      T.sc[0][e] = s;
+      T.ch[0][e] = __fadd_rn(s, T.bias[e]);
     }
     __syncwarp();
     if (a.g < G) {
@@ -455,10 +466,10 @@ __device__ __forceinline__ void route_tokens_scan(const Args& a, Tables& T, int 
         int b1 = -1, b2 = -1;
         for (int j = 0; j < per; ++j) {
           const int e = lane * per + j;
-          if (b1 < 0 || after(T.ch[e], e, T.ch[b1], b1)) { b2 = b1; b1 = e; }
-          else if (b2 < 0 || after(T.ch[e], e, T.ch[b2], b2)) { b2 = e; }
+          if (b1 < 0 || after(T.ch[0][e], e, T.ch[0][b1], b1)) { b2 = b1; b1 = e; }
+          else if (b2 < 0 || after(T.ch[0][e], e, T.ch[0][b2], b2)) { b2 = e; }
         }
-        gsc = __fadd_rn(T.ch[b2], T.ch[b1]);
+        gsc = __fadd_rn(T.ch[0][b2], T.ch[0][b1]);
       }
       bool kept = false;
       for (int s = 0; s < a.g; ++s) {
@@ -470,7 +481,7 @@ __device__ __forceinline__ void route_tokens_scan(const Args& a, Tables& T, int 
       const unsigned keep = __ballot_sync(0xffffffffu, kept);
       __syncwarp();
       for (int e = lane; e < E; e += 32)
-        if (!((keep >> (e / per)) & 1u)) T.ch[e] = ninf;
+        if (!((keep >> (e / per)) & 1u)) T.ch[0][e] = ninf;
       __syncwarp();
     }
     unsigned taken = 0u;
@@ -479,14 +490,14 @@ __device__ __forceinline__ void route_tokens_scan(const Args& a, Tables& T, int 
       int i = -1;
       for (int q = 0; lane + 32 * q < E; ++q) {
         const int e = lane + 32 * q;
-        if (!((taken >> q) & 1u) && (i < 0 || after(T.ch[e], e, v, i))) { v = T.ch[e]; i = e; }
+        if (!((taken >> q) & 1u) && (i < 0 || after(T.ch[0][e], e, v, i))) { v = T.ch[0][e]; i = e; }
       }
       warp_best(v, i);
       if (i >= 0 && (i & 31) == lane) taken |= 1u << (i >> 5);
       if (lane == 0) T.sel[t * k + (k - 1 - s)] = i;
     }
     __syncwarp();
-    const float wj = lane < k ? T.sc[T.sel[t * k + lane]] : 0.f;
+    const float wj = lane < k ? T.sc[0][T.sel[t * k + lane]] : 0.f;
     float denom = 1.f;
     if (a.norm) {
       float sum = __shfl_sync(0xffffffffu, wj, 0);
@@ -508,6 +519,16 @@ __device__ __forceinline__ void route_tokens_scan(const Args& a, Tables& T, int 
 // position and route count.
 __device__ __forceinline__ void dispatch_routes(const Args& a, Tables& T, int lane) {
   const int S = a.M * a.k;
+  // every selected expert must be a real one before any copy uses it
+  const bool bad = __any_sync(0xffffffffu, lane < S && (T.sel[lane] < 0 || T.sel[lane] >= a.E));
+  if (bad) {
+    if (lane == 0) {
+      atomicExch(a.status, 1 | kSiteRoute);
+      T.n_active = 0;
+    }
+    __syncwarp();
+    return;
+  }
   const bool valid = lane < S;
   const int e = valid ? T.sel[lane] : 0x40000000 + lane;
   const unsigned peers = __match_any_sync(0xffffffffu, e);
@@ -553,15 +574,15 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
   __shared__ __align__(8) uint64_t empty[kMaxStages];
   __shared__ __align__(8) uint64_t tbl;     // routing tables ready
   __shared__ __align__(8) uint64_t lgdone;  // this CTA's logits written
+  __shared__ __align__(8) uint64_t xbar;    // x copied in
+  __shared__ __align__(8) uint64_t abar;    // act / act_s copied in
   __shared__ Tables T;
   __shared__ float red[kNRed][kWarps][32];
   __shared__ int red_cnt[kNRed], red_gen[kNRed];
   __shared__ int s_go;
   __shared__ unsigned rel_sink[kConsumers];
-  __shared__ unsigned amax_x[TT];
-  __shared__ float tok_mult[TT];
-  __shared__ unsigned amax_r[kMaxRoutes];
-  __shared__ float rscale[kMaxRoutes];
+  __shared__ float tok_mult[TT], tok_inv[TT];
+  __shared__ float rscale[kMaxRoutes], rinv[kMaxRoutes];
   __shared__ int s_nact, s_fail;
 
   const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -579,11 +600,11 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kWarps); }
     mbar_init(&tbl, 1);
     mbar_init(&lgdone, kWarps * (n_rt > 0 ? n_rt : 1));
+    mbar_init(&xbar, 1);
+    mbar_init(&abar, 1);
     mbar_fence_init();
     T.n_active = 0;
   }
-  if (threadIdx.x < TT) amax_x[threadIdx.x] = 0u;
-  if (threadIdx.x < kMaxRoutes) amax_r[threadIdx.x] = 0u;
   if (threadIdx.x < kNRed) { red_cnt[threadIdx.x] = 0; red_gen[threadIdx.x] = 0; }
   __syncthreads();
 
@@ -621,6 +642,9 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
       return true;
     };
     if (cw == 0 && lane == 0) {
+      // the tokens' hidden states first (bf16 rows, contiguous)
+      mbar_arrive_expect_tx(&xbar, static_cast<unsigned>(M) * d * 2u);
+      bulk_g2s(smem + pl.x_off + static_cast<size_t>(TT) * d * 2, a.x, static_cast<unsigned>(M) * d * 2u, &xbar);
       const unsigned rrow = static_cast<unsigned>(d) * 4u;
       for (int rc = 0; rc < n_rt; ++rc, ++it) {
         if (!stage_free()) continue;
@@ -654,8 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
     }
     named_sync(kBarCtl, kCtl * 32);
     const bool go = s_go != 0;
-    const int per = E / a.G;
-    const bool scan = a.g < a.G && (per > 32 || (32 % per) != 0);
+    const bool scan = !warp_routing_ok(a);
     if (go) {
       __threadfence();
       if (!scan) {
@@ -723,52 +746,30 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
   // =============================== consumers ==============================
   const int wg = warp_id, ct = threadIdx.x;
   uint4* xh = reinterpret_cast<uint4*>(smem + pl.x_off);  // f16 [t][wq][c], scaled
-  uint4* xb = xh + TT * 4 * G;                             // bf16 [t][wq][c]
+  uint4* xb = xh + TT * 4 * G;                             // bf16 [t][d], as copied
   float* ysm = reinterpret_cast<float*>(smem + pl.y_off);  // [R + TT][rows_max]
+  const int d8 = d >> 3;
 
-  // ---- stage x: bf16 copy, then f16 scaled so max|x| < 2^8 ----
-  {
-    const int n4 = M * (d >> 3);
-    uint4 xr[kXRegs];
-#pragma unroll
-    for (int q = 0; q < kXRegs; ++q) {
-      const int i4 = ct + q * kConsumers;
-      if (i4 < n4) {
-        const int t = i4 / (d >> 3);
-        xr[q] = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(t) * d + 8 * (i4 - t * (d >> 3)));
-      }
+  // ---- stage x: f16 copy scaled so max|x| < 2^8, in the [t][wq][c] order ----
+  bool ok = wait_warp(&xbar, 0, a.status, kSiteFull, lane);
+  if (wg < M) {
+    unsigned m = 0u;
+#pragma unroll 1
+    for (int u = lane; u < d8; u += 32) m = max(m, __float_as_uint(absmax8_bf16(xb[wg * d8 + u])));
+    m = __reduce_max_sync(0xffffffffu, m);
+    if (lane == 0) {
+      tok_mult[wg] = pow2i(act_shift(__uint_as_float(m)));
+      tok_inv[wg] = __fdiv_rn(1.0f, tok_mult[wg]);
     }
-    // per-token max |x|: one shared atomic per warp when a warp's 32 lanes
-    // cover one token (d/8 a multiple of 32), else one per lane
-    const bool warp_rows = ((d >> 3) & 31) == 0;
-#pragma unroll
-    for (int q = 0; q < kXRegs; ++q) {
-      const int i4 = ct + q * kConsumers;
-      const int t = i4 / (d >> 3), i8 = i4 - t * (d >> 3);
-      const unsigned m = i4 < n4 ? __float_as_uint(absmax8_bf16(xr[q])) : 0u;
-      if (i4 < n4) xb[(t * 4 + (i8 & 3)) * G + (i8 >> 2)] = xr[q];
-      if (warp_rows) {
-        const unsigned wm = __reduce_max_sync(0xffffffffu, m);
-        if (lane == 0 && i4 < n4) atomicMax(amax_x + t, wm);
-      } else if (i4 < n4) {
-        atomicMax(amax_x + t, m);
-      }
-    }
-    named_sync(kBarCons, kConsumers);
-    if (ct < M) tok_mult[ct] = pow2i(act_shift(__uint_as_float(amax_x[ct])));
-    named_sync(kBarCons, kConsumers);
-#pragma unroll
-    for (int q = 0; q < kXRegs; ++q) {
-      const int i4 = ct + q * kConsumers;
-      if (i4 < n4) {
-        const int t = i4 / (d >> 3), i8 = i4 - t * (d >> 3);
-        xh[(t * 4 + (i8 & 3)) * G + (i8 >> 2)] = bf16x8_to_f16x8_scaled(xr[q], __fdiv_rn(1.0f, tok_mult[t]));
-      }
-    }
-    named_sync(kBarCons, kConsumers);
   }
+  named_sync(kBarCons, kConsumers);
+#pragma unroll 1
+  for (int i4 = ct; i4 < M * d8; i4 += kConsumers) {
+    const int t = i4 / d8, i8 = i4 - t * d8;
+    xh[(t * 4 + (i8 & 3)) * G + (i8 >> 2)] = bf16x8_to_f16x8_scaled(xb[i4], tok_inv[t]);
+  }
+  named_sync(kBarCons, kConsumers);
 
-  bool ok = true;
   int it = 0;
   // Cross-warp reductions without a CTA barrier: use u of buffer rb waits
   // until the previous use was finished, every warp adds its partials, and
@@ -840,7 +841,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
 #pragma unroll
         for (int t = 0; t < TT; ++t) {
           if (t < M) {
-            const uint4 u = xb[(t * 4 + (c8 & 3)) * G + (c8 >> 2)];
+            const uint4 u = xb[t * d8 + c8];
             const float xv[8] = {bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y),
                                  bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w)};
 #pragma unroll
@@ -907,9 +908,9 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
         }
         const uint4* xp[TT];
 #pragma unroll
-        for (int t = 0; t < TT; ++t) xp[t] = xb + (min(t, M - 1) * 4) * G + c;
+        for (int t = 0; t < TT; ++t) xp[t] = xb + min(t, M - 1) * d8 + c * 4;
         float part[2][TT];
-        bf_dot<2, TT>(wv, xp, G, part);
+        bf_dot<2, TT>(wv, xp, 1, part);
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -1063,62 +1064,33 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
   }
   named_sync(kBarCons, kConsumers);
   if (s_fail) ok = false;
-  // stage act (f16, scaled per route) and act_s (bf16) into the union area
-  uint4* xa = reinterpret_cast<uint4*>(smem + pl.x_off);  // f16 [p][wq][c]
-  uint4* xs = xa + R * 4 * G2;                             // bf16 [t][wq][c]
-  {
-    const int n4 = ok ? R * (F >> 3) : 0;
-    const int n4s = ok ? M * (Fs >> 3) : 0;
-    uint4 ar[kActRegs], sr[kActSRegs];
-#pragma unroll
-    for (int q = 0; q < kActRegs; ++q) {
-      const int i4 = ct + q * kConsumers;
-      if (i4 < n4) {
-        const int p = i4 / (F >> 3);
-        ar[q] = __ldcg(reinterpret_cast<const uint4*>(a.act + static_cast<size_t>(p) * F + 8 * (i4 - p * (F >> 3))));
-      }
-    }
-#pragma unroll
-    for (int q = 0; q < kActSRegs; ++q) {
-      const int i4 = ct + q * kConsumers;
-      if (i4 < n4s) {
-        const int t = i4 / (Fs >> 3);
-        sr[q] = __ldcg(reinterpret_cast<const uint4*>(a.act_s + static_cast<size_t>(t) * Fs + 8 * (i4 - t * (Fs >> 3))));
-      }
-    }
-    const bool warp_rows = ((F >> 3) & 31) == 0;
-#pragma unroll
-    for (int q = 0; q < kActRegs; ++q) {
-      const int i4 = ct + q * kConsumers;
-      const unsigned m = i4 < n4 ? __float_as_uint(absmax8_bf16(ar[q])) : 0u;
-      if (warp_rows) {
-        const unsigned wm = __reduce_max_sync(0xffffffffu, m);
-        if (lane == 0 && i4 < n4) atomicMax(amax_r + i4 / (F >> 3), wm);
-      } else if (i4 < n4) {
-        atomicMax(amax_r + i4 / (F >> 3), m);
-      }
-    }
-#pragma unroll
-    for (int q = 0; q < kActSRegs; ++q) {
-      const int i4 = ct + q * kConsumers;
-      if (i4 < n4s) {
-        const int t = i4 / (Fs >> 3), i8 = i4 - t * (Fs >> 3);
-        xs[(t * 4 + (i8 & 3)) * G2s + (i8 >> 2)] = sr[q];
-      }
-    }
-    named_sync(kBarCons, kConsumers);
-    if (ct < R) rscale[ct] = pow2i(act_shift(__uint_as_float(amax_r[ct])));
-    named_sync(kBarCons, kConsumers);
-#pragma unroll
-    for (int q = 0; q < kActRegs; ++q) {
-      const int i4 = ct + q * kConsumers;
-      if (i4 < n4) {
-        const int p = i4 / (F >> 3), i8 = i4 - p * (F >> 3);
-        xa[(p * 4 + (i8 & 3)) * G2 + (i8 >> 2)] = bf16x8_to_f16x8_scaled(ar[q], __fdiv_rn(1.0f, rscale[p]));
-      }
-    }
-    named_sync(kBarCons, kConsumers);
+  // act (f16 in place, scaled per route so max|v| < 2^8) and act_s (bf16),
+  // both row-major as written, copied into the union area in one batch
+  uint4* xa = reinterpret_cast<uint4*>(smem + pl.x_off);  // f16 [p][F]
+  uint4* xs = xa + R * (F >> 3);                           // bf16 [t][Fs]
+  const int f8 = F >> 3, fs8 = Fs >> 3;
+  if (ct == 0 && ok) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");  // generic writes of other CTAs -> async-proxy reads
+    mbar_arrive_expect_tx(&abar, static_cast<unsigned>(R) * F * 2u + static_cast<unsigned>(M) * Fs * 2u);
+    bulk_g2s(xa, a.act, static_cast<unsigned>(R) * F * 2u, &abar);
+    if (Fs > 0) bulk_g2s(xs, a.act_s, static_cast<unsigned>(M) * Fs * 2u, &abar);
   }
+  if (ok) ok = wait_warp(&abar, 0, a.status, kSiteAct, lane);
+#pragma unroll 1
+  for (int p = wg; p < R; p += kWarps) {
+    unsigned m = 0u;
+#pragma unroll 1
+    for (int u = lane; u < f8; u += 32) m = max(m, __float_as_uint(absmax8_bf16(xa[p * f8 + u])));
+    m = __reduce_max_sync(0xffffffffu, m);
+    if (lane == 0) {
+      rscale[p] = pow2i(act_shift(__uint_as_float(m)));
+      rinv[p] = __fdiv_rn(1.0f, rscale[p]);
+    }
+  }
+  named_sync(kBarCons, kConsumers);
+#pragma unroll 1
+  for (int i4 = ct; i4 < R * f8; i4 += kConsumers) xa[i4] = bf16x8_to_f16x8_scaled(xa[i4], rinv[i4 / f8]);
+  named_sync(kBarCons, kConsumers);
 
   // ---------------------------- phase 2 ----------------------------
   const DownRange dr(a, pl, b, P);
@@ -1143,9 +1115,9 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
           for (int wq = 0; wq < 4; ++wq) wv[0][wq] = lds128(wrow + c * 64 + 16 * wq);
           const uint4* xp[TT];
 #pragma unroll
-          for (int t = 0; t < TT; ++t) xp[t] = xs + (min(t, M - 1) * 4) * G2s + c;
+          for (int t = 0; t < TT; ++t) xp[t] = xs + min(t, M - 1) * fs8 + c * 4;
           float part[1][TT];
-          bf_dot<1, TT>(wv, xp, G2s, part);
+          bf_dot<1, TT>(wv, xp, 1, part);
 #pragma unroll
           for (int t = 0; t < TT; ++t) acc[t] = __fadd_rn(acc[t], part[0][t]);
         }
@@ -1214,10 +1186,10 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
               for (int cc = 0; cc < 3; ++cc) {
                 const int c = min(cd + 16 * (cb * 3 + cc), G2 - 1);
 #pragma unroll
-                for (int tq = 0; tq < TP; ++tq) xp[cc][tq] = xa + ((p0 + min(q0 + tq, n - 1)) * 4) * G2 + c;
+                for (int tq = 0; tq < TP; ++tq) xp[cc][tq] = xa + (p0 + min(q0 + tq, n - 1)) * f8 + c * 4;
               }
               float part[2][3][TP];
-              mx_dot<2, 3, TP>(w, xp, G2, part);
+              mx_dot<2, 3, TP>(w, xp, 1, part);
 #pragma unroll
               for (int h = 0; h < 2; ++h)
 #pragma unroll

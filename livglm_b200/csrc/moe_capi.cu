@@ -505,17 +505,14 @@ bool layer_fits_t(const lg_moe_config* c, int M) {
 }
 
 // The fused kernel needs: 1..4 tokens, M*k <= 32 routes, E <= 256 router
-// experts in <= 32 groups, d % 64 == 0, register-staged activations
-// (M*d <= 16384, M*k*F <= 49152), 16-byte aligned scale banks (every bulk copy
-// starts and ends on 16 bytes) and a shared-memory plan.
+// experts in <= 32 groups, d % 64 == 0, 16-byte aligned scale banks (every
+// bulk copy starts and ends on 16 bytes) and a shared-memory plan.
 bool layer_fits(const lg_moe_config* c, const lg_moe_weights* w, int64_t M) {
   using namespace lg::layer;
   if (M < 1 || M > lg::kDecodeMaxTokens) return false;
   const long long R = M * c->num_experts_per_tok;
   if (R > kMaxRoutes || c->n_routed_experts > kMaxExperts || c->n_group > kMaxGroups) return false;
   if (c->hidden_size % 64) return false;
-  if (static_cast<long long>(c->hidden_size) * M > 8LL * kConsumers * kXRegs) return false;
-  if (R * c->moe_intermediate_size > 8LL * kConsumers * kActRegs) return false;
   if (!aligned(w->gate_scale, 16) || !aligned(w->up_scale, 16) || !aligned(w->down_scale, 16)) return false;
   if (w->gate_scale_stride % 16 || w->up_scale_stride % 16 || w->down_scale_stride % 16) return false;
   const int m = static_cast<int>(M);
