@@ -57,7 +57,9 @@ constexpr int kBarCons = 1;                // named barrier over the consumer wa
 constexpr int kBarCtl = 2;                 // named barrier over the control warps
 constexpr int kNRed = 4;                   // cross-warp reduction buffers
 constexpr int kMaxStages = 8;
-constexpr int kGuRows = 8;      // routed gate/up rows per chunk
+constexpr int kGuRows = 8;      // routed gate/up rows per chunk (one token: one row pair per warp)
+constexpr int kXcg = 4;         // one token: column groups per lane (d <= 32 * 32 * kXcg)
+static_assert(kGuRows == kWarps, "one token: each consumer warp owns one row pair of a chunk");
 constexpr int kShGuRows = 2;    // shared gate/up rows per chunk
 constexpr int kShDnRows = 8;    // shared down rows per chunk (warp per row)
 constexpr int kDnRowsMax = 32;  // routed down rows per chunk (16 row sets x 2)
@@ -71,6 +73,24 @@ constexpr int kSiteLogits = 10 << 8, kSiteAct = 11 << 8, kSiteTable = 12 << 8;
 constexpr int kSiteSync = 13 << 8;   // with LG_ERR_WORKSPACE: grid counters were not zero on entry
 constexpr int kSiteRed = 14 << 8;
 constexpr int kSiteRoute = 15 << 8;  // with LG_ERR_INVALID_ARG: a routed expert id outside [0, E)
+constexpr int kSiteActS = 16 << 8;
+
+// grid counters in the workspace (zero between calls)
+constexpr int kSyncLogits = 0;  // router rows written
+constexpr int kSyncGu = 1;      // CTAs done with the routed gate/up rows
+constexpr int kSyncExit = 2;    // CTAs done
+constexpr int kSyncShGu = 3;    // CTAs done with the shared gate/up rows
+constexpr int kSyncComb = 8;    // one token: per output block, down rows finished
+constexpr int kMaxGrid = 1024;
+constexpr int kSyncWords = kSyncComb + kMaxGrid;
+
+// one token, phase 2: the CTA owns output block b (rows [b*d/P, (b+1)*d/P))
+// of the shared down rows and an even slice of the routed down rows, routes
+// concatenated; the last CTA to finish a block's rows combines it
+constexpr int kDn1Rows = 32;  // routed down rows per chunk (two per half-warp)
+constexpr int kDcg = 3;       // routed down column groups per half-warp lane (F <= 1536)
+constexpr int kScg = 6;       // shared down 8-column words per lane (Fs <= 1536)
+constexpr int kMaxComb = 64;  // output blocks one CTA may complete
 
 struct Args {
   int M, d, F, Fs, E, k, G, g, norm;
@@ -85,9 +105,11 @@ struct Args {
   uint32_t* i_out;  // [M, k] or NULL
   uint16_t* act;    // [M*k, F] workspace, route-position order
   uint16_t* act_s;  // [M, Fs] workspace
+  uint16_t* y;      // [M*k, d] workspace, slot order (one token: routed down rows)
+  uint16_t* ys;     // [M, d] workspace (one token: shared down rows)
   float* out;       // [M, d]
   int* status;
-  unsigned* sync;   // [0] logits rows done, [1] CTAs past phase 1, [2] CTAs done
+  unsigned* sync;   // grid counters, kSync* below
 };
 
 // Host-computed shared-memory plan (all offsets in bytes from the dynamic base).
@@ -100,6 +122,10 @@ struct Plan {
   int sub_rows;  // routed down rows per chunk
   int sh_rows;   // shared down rows per chunk
   int rows_max;  // most down rows of one CTA
+  int act_off;   // one token: staged act_s [Fs] then act [rr_max][F], bf16
+  int rr_max;    // one token: most routes in one CTA's routed down slice
+  int yb_off;    // one token: this CTA's routed then shared down rows, bf16
+  int yb_rows;   // one token: most routed down rows of one CTA
 };
 
 // ---------------------------------------------------------------------------
@@ -108,6 +134,9 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Every CTA polls the same counter word: poll slowly, or the waiters' loads
+// on that one L2 line slow the weight stream sharing its L2 slice.
+constexpr unsigned kPollNs = 512;
 // bounded wait until *p >= target
 __device__ __forceinline__ bool spin_geq(const unsigned* p, unsigned target, int* status, int site) {
   if (ld_acquire(p) >= target) return true;
@@ -117,14 +146,16 @@ __device__ __forceinline__ bool spin_geq(const unsigned* p, unsigned target, int
       atomicExch(status, 6 | site);
       return false;
     }
-    __nanosleep(64);
+    __nanosleep(kPollNs);
   }
   return true;
 }
 
 // try_wait that may suspend the thread in the barrier for up to `hint_ns`
 // (instead of a busy poll that takes issue slots and shared-memory bandwidth
-// from the warps doing work)
+// from the warps doing work).  Keep the hint short: a waiter suspended with a
+// long hint was observed to resume microseconds after the phase completed.
+constexpr unsigned kSleepHintNs = 200;
 __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* b, unsigned parity, unsigned hint_ns) {
   uint32_t ok;
   asm volatile(
@@ -140,9 +171,9 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* b, unsigned parity
 // phase itself (each gets the acquire).  Returns the same result in all lanes.
 __device__ __forceinline__ bool wait_warp(uint64_t* b, unsigned parity, int* status, int site, int lane) {
   unsigned good = 1u;
-  if (lane == 0 && !mbar_try_wait_sleep(b, parity, 20000u)) {
+  if (lane == 0 && !mbar_try_wait_sleep(b, parity, kSleepHintNs)) {
     const unsigned long long t0 = globaltimer_ns();
-    while (!mbar_try_wait_sleep(b, parity, 20000u)) {
+    while (!mbar_try_wait_sleep(b, parity, kSleepHintNs)) {
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
         atomicExch(status, 6 | site);
         good = 0u;
@@ -156,8 +187,15 @@ __device__ __forceinline__ bool wait_warp(uint64_t* b, unsigned parity, int* sta
   }
   return good != 0u;
 }
+// Every lane tests the phase itself (one instruction when it is already
+// complete, the usual case in a deep ring); otherwise the bounded wait_warp.
+__device__ __forceinline__ bool wait_all(uint64_t* b, unsigned parity, int* status, int site, int lane) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(b, parity))) return true;
+  return wait_warp(b, parity, status, site, lane);
+}
 
 __device__ __forceinline__ uint4 lds128(const unsigned char* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint32_t lds32(const unsigned char* p) { return *reinterpret_cast<const uint32_t*>(p); }
 __device__ __forceinline__ unsigned fold4(const uint4& v) { return v.x ^ v.y ^ v.z ^ v.w; }
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
   return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
@@ -177,6 +215,16 @@ __device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
                "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
                : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
                : "r"(w));
+}
+// Same conversion, free for the scheduler to interleave with the FMA pipe
+// (used where the working set is small enough not to spill).
+__device__ __forceinline__ void e2m1x8_to_f16x2_nv(uint32_t w, uint32_t (&h)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(w));
 }
 __device__ __forceinline__ float f16x2_sum(uint32_t h) {
   const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
@@ -260,6 +308,36 @@ __device__ __forceinline__ void bf_dot(const uint4 (&w)[NV][4], const uint4* con
 #pragma unroll
     for (int q = 0; q < TP; ++q)
       part[v][q] = __fadd_rn(__fadd_rn(ch[v][0][q], ch[v][1][q]), __fadd_rn(ch[v][2][q], ch[v][3][q]));
+}
+
+// mx_dot with the activation words in registers: groups w[r][C0 + c] against
+// xv[C0 + c][wq] (one activation row), same chains and order as mx_dot.
+template <int NR, int C0, int NC, int NW>
+__device__ __forceinline__ void mx_dot_reg(const uint4 (&w)[NR][NW], const uint4 (&xv)[NW][4], float (&part)[NR][NC]) {
+  uint32_t ch[NR][NC][2];
+#pragma unroll
+  for (int r = 0; r < NR; ++r)
+#pragma unroll
+    for (int c = 0; c < NC; ++c) { ch[r][c][0] = 0u; ch[r][c][1] = 0u; }
+#pragma unroll
+  for (int wq = 0; wq < 4; ++wq) {
+    uint32_t h[NR][NC][4];
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+#pragma unroll
+      for (int c = 0; c < NC; ++c) e2m1x8_to_f16x2_nv(word_of(w[r][C0 + c], wq), h[r][c]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+#pragma unroll
+      for (int r = 0; r < NR; ++r)
+#pragma unroll
+        for (int c = 0; c < NC; ++c)
+          ch[r][c][wq >> 1] = hfma2(h[r][c][e], word_of(xv[C0 + c][wq], e), ch[r][c][wq >> 1]);
+  }
+#pragma unroll
+  for (int r = 0; r < NR; ++r)
+#pragma unroll
+    for (int c = 0; c < NC; ++c) part[r][c] = __fadd_rn(f16x2_sum(ch[r][c][0]), f16x2_sum(ch[r][c][1]));
 }
 
 // Reduce V values over SEG lanes (aligned segments of a warp) by halving:
@@ -566,6 +644,29 @@ struct DownRange {
   }
 };
 
+// One token: CTA b's shared down rows [sr_lo, sr_hi) (its output block) and
+// routed down rows [u_lo, u_hi) of the routes concatenated (route p has rows
+// [p*d, (p+1)*d)), split evenly in units of pl.unit rows.
+// (32-bit arithmetic: d <= 4096, P <= kMaxGrid, M*k*d/unit <= 2^17, so every
+// product stays below 2^31.)
+struct Down1 {
+  int sr_lo, sr_hi, u_lo, u_hi;
+  __device__ __forceinline__ Down1(const Args& a, const Plan& pl, int b, int P) {
+    const unsigned d = a.d, p = P, nu = static_cast<unsigned>(a.M * a.k) * d / pl.unit;
+    sr_lo = static_cast<int>(b * d / p);
+    sr_hi = static_cast<int>((b + 1) * d / p);
+    u_lo = pl.unit * static_cast<int>(b * nu / p);
+    u_hi = pl.unit * static_cast<int>((b + 1) * nu / p);
+  }
+};
+// output block holding row r: the largest c with c*d/P <= r
+__device__ __forceinline__ int out_block(int r, int d, int P) {
+  return static_cast<int>((static_cast<unsigned>(r + 1) * P - 1u) / static_cast<unsigned>(d));
+}
+__device__ __forceinline__ int block_lo(int c, int d, int P) {
+  return static_cast<int>(static_cast<unsigned>(c) * d / static_cast<unsigned>(P));
+}
+
 // ---------------------------------------------------------------------------
 template <int TT>
 __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
@@ -575,7 +676,8 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
   __shared__ __align__(8) uint64_t tbl;     // routing tables ready
   __shared__ __align__(8) uint64_t lgdone;  // this CTA's logits written
   __shared__ __align__(8) uint64_t xbar;    // x copied in
-  __shared__ __align__(8) uint64_t abar;    // act / act_s copied in
+  __shared__ __align__(8) uint64_t abar;    // act / act_s copied in (one token: act)
+  __shared__ __align__(8) uint64_t sbar;    // one token: act_s copied in
   __shared__ Tables T;
   __shared__ float red[kNRed][kWarps][32];
   __shared__ int red_cnt[kNRed], red_gen[kNRed];
@@ -583,7 +685,8 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
   __shared__ unsigned rel_sink[kConsumers];
   __shared__ float tok_mult[TT], tok_inv[TT];
   __shared__ float rscale[kMaxRoutes], rinv[kMaxRoutes];
-  __shared__ int s_nact, s_fail;
+  __shared__ int s_nact, s_fail, s_afail;
+  __shared__ int s_ncomb, s_comb[kMaxComb], s_ncb, s_cb[kMaxComb], s_cr[kMaxComb];
 
   const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int P = gridDim.x, b = blockIdx.x;
@@ -602,8 +705,10 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
     mbar_init(&lgdone, kWarps * (n_rt > 0 ? n_rt : 1));
     mbar_init(&xbar, 1);
     mbar_init(&abar, 1);
+    mbar_init(&sbar, 1);
     mbar_fence_init();
     T.n_active = 0;
+    s_afail = 0;
   }
   if (threadIdx.x < kNRed) { red_cnt[threadIdx.x] = 0; red_gen[threadIdx.x] = 0; }
   __syncthreads();
@@ -619,7 +724,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
     // this CTA's logits are written: publish them to the grid
     auto signal_logits = [&]() {
       __threadfence();
-      atomicAdd(a.sync + 0, static_cast<unsigned>(nrr));
+      atomicAdd(a.sync + kSyncLogits, static_cast<unsigned>(nrr));
       signaled = true;
     };
     // lane 0: bounded wait until stage `it` is free (its previous chunk
@@ -629,7 +734,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
       if (it < S) return true;
       const unsigned par = ((it / S) - 1) & 1;
       unsigned long long t0 = 0;
-      while (!mbar_try_wait_sleep(&empty[it % S], par, signaled ? 20000u : 500u)) {
+      while (!mbar_try_wait_sleep(&empty[it % S], par, kSleepHintNs)) {
         if (!signaled && mbar_try_wait(&lgdone, 0)) signal_logits();
         const unsigned long long t = globaltimer_ns();
         if (!t0) t0 = t;
@@ -667,7 +772,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
         if (mbar_wait(&lgdone, 0, a.status, kSiteLogits)) signal_logits();
         else ok = false;
       }
-      s_go = (ok && spin_geq(a.sync + 0, static_cast<unsigned>(E), a.status, kSiteLogits)) ? 1 : 0;
+      s_go = (ok && spin_geq(a.sync + kSyncLogits, static_cast<unsigned>(E), a.status, kSiteLogits)) ? 1 : 0;
     }
     if (cw == 1) {  // score-correction bias, one batch of loads
       float bv[kMaxExperts / 32];
@@ -688,6 +793,39 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
       }
     }
     named_sync(kBarCtl, kCtl * 32);
+    if constexpr (TT == 1) {
+      // one token: control warp 1 stages act_s and this CTA's act rows once
+      // every CTA has written them (plain arrive on failure, with s_afail set)
+      if (cw == 1 && lane == 0) {
+        const Down1 dn(a, pl, b, P);
+        unsigned char* as = smem + pl.act_off;
+        if (Fs > 0) {
+          if (go && spin_geq(a.sync + kSyncShGu, static_cast<unsigned>(P), a.status, kSiteActS)) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            mbar_arrive_expect_tx(&sbar, static_cast<unsigned>(Fs) * 2u);
+            bulk_g2s(as, a.act_s, static_cast<unsigned>(Fs) * 2u, &sbar);
+          } else {
+            s_afail = 1;
+            mbar_arrive(&sbar);
+          }
+        }
+        if (dn.u_hi > dn.u_lo) {
+          const int p_lo = dn.u_lo / d, np = (dn.u_hi - 1) / d - p_lo + 1;
+          const unsigned bytes = static_cast<unsigned>(np) * F * 2u;
+          if (go && spin_geq(a.sync + kSyncGu, static_cast<unsigned>(P), a.status, kSiteAct)) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            mbar_arrive_expect_tx(&abar, bytes);
+            bulk_g2s(as + static_cast<size_t>(Fs) * 2, a.act + static_cast<size_t>(p_lo) * F, bytes, &abar);
+          } else {
+            s_afail = 1;
+            mbar_arrive(&abar);
+          }
+        }
+        // the copies land before this warp (and so the CTA) can leave
+        if (Fs > 0) mbar_wait(&sbar, 0, a.status, kSiteDrain);
+        if (dn.u_hi > dn.u_lo) mbar_wait(&abar, 0, a.status, kSiteDrain);
+      }
+    }
     if (cw != 0) return;
     if (go) dispatch_routes(a, T, lane);
     else ok = false;
@@ -713,6 +851,32 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
         bulk_g2s(st + 2 * pk + sk, a.up_s + e * a.up_ss + f0 * G, sk, fb);
       }
       // down weights need nothing from the gate/up phase
+      if constexpr (TT == 1) {
+        const Down1 dn(a, pl, b, P);
+        if (Fs > 0) {
+          for (int r0 = dn.sr_lo; r0 < dn.sr_hi; r0 += kShDnRows, ++it) {
+            if (!stage_free()) continue;
+            const int nr = min(kShDnRows, dn.sr_hi - r0);
+            const unsigned bytes = static_cast<unsigned>(nr) * Fs * 2u;
+            unsigned char* st = smem + static_cast<size_t>(it % S) * pl.stage_bytes;
+            mbar_arrive_expect_tx(&full[it % S], bytes);
+            bulk_g2s(st, a.sh_down + static_cast<size_t>(r0) * Fs, bytes, &full[it % S]);
+          }
+        }
+        // one token: route p is active expert p (none if the routing failed)
+        for (int u = T.n_active == R ? dn.u_lo : dn.u_hi; u < dn.u_hi; ++it) {
+          const int p = u / d, r0 = u - p * d, nr = min(kDn1Rows, min(dn.u_hi, (p + 1) * d) - u);
+          u += nr;
+          if (!stage_free()) continue;
+          const long long e = T.ae[p];
+          const unsigned pb = static_cast<unsigned>(nr) * (F / 2), sb = static_cast<unsigned>(nr) * G2;
+          unsigned char* st = smem + static_cast<size_t>(it % S) * pl.stage_bytes;
+          uint64_t* fb = &full[it % S];
+          mbar_arrive_expect_tx(fb, pb + sb);
+          bulk_g2s(st, a.down_p + e * a.down_ps + static_cast<size_t>(r0) * (F / 2), pb, fb);
+          bulk_g2s(st + pb, a.down_s + e * a.down_ss + static_cast<size_t>(r0) * G2, sb, fb);
+        }
+      } else {
       const DownRange dr(a, pl, b, P);
       for (int pc = 0; pc < dr.n_sdp; ++pc, ++it) {
         if (!stage_free()) continue;
@@ -734,6 +898,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
           bulk_g2s(st, a.down_p + e * a.down_ps + static_cast<size_t>(r0) * (F / 2), pb, fb);
           bulk_g2s(st + pb, a.down_s + e * a.down_ss + static_cast<size_t>(r0) * G2, sb, fb);
         }
+      }
       }
       if (!ok) {  // copies already issued land before the CTA leaves
         for (int q = (it > S ? it - S : 0); q < it; ++q)
@@ -946,6 +1111,10 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
     }
   }
 
+  // this CTA's act_s rows are written: publish them
+  __threadfence();
+  named_sync(kBarCons, kConsumers);
+  if (ct == 0) atomicAdd(a.sync + kSyncShGu, 1u);
   // routing tables from the producer warp; one agreed active-expert count
   if (ok) ok = wait_warp(&tbl, 0, a.status, kSiteTable, lane);
   named_sync(kBarCons, kConsumers);
@@ -953,6 +1122,111 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
   named_sync(kBarCons, kConsumers);
   const int n_act = s_nact;
 
+  if constexpr (TT == 1) {
+    // One token: warp wg owns gate row and up row f0 + wg of every chunk, so
+    // each row's sum stays inside the warp, and the token's activation words
+    // stay in registers for the whole loop.  Lane l covers the column groups
+    // 4*q(l) + ((i + l) & 3), i = 0..3: every 16-byte weight load is
+    // conflict-free and the lane's four scale bytes are one 32-bit word.
+    // The next chunk's loads are in flight while this chunk's sums are
+    // reduced; finished (gate, up) sums wait in lane (n % 32) and become
+    // activations 32 at a time.
+    const int ql = (lane & ~7) | ((lane & 3) << 1) | ((lane >> 2) & 1);
+    int cg[kXcg];
+#pragma unroll
+    for (int i = 0; i < kXcg; ++i) cg[i] = 4 * ql + ((i + lane) & 3);
+    uint4 xr[kXcg][4];
+#pragma unroll
+    for (int i = 0; i < kXcg; ++i)
+#pragma unroll
+      for (int wq = 0; wq < 4; ++wq) xr[i][wq] = cg[i] < G ? xh[wq * G + cg[i]] : make_uint4(0u, 0u, 0u, 0u);
+    const int nend = n_sh + n_act * nrb;
+    const size_t pk = static_cast<size_t>(kGuRows) * (d >> 1);
+    const size_t rowb = static_cast<size_t>(wg) * (d >> 1);
+    const bool has_sc = 4 * ql < G;
+    int s = it % S, ph = (it / S) & 1;
+    int ai = 0, fc = 0;
+    if (j < nend) {
+      ai = (j - n_sh) / nrb;
+      fc = (j - n_sh) - ai * nrb;
+    }
+    uint4 w[2][kXcg];
+    uint32_t sw[2];
+    // wait for stage s and issue this lane's loads (not waited for here)
+    auto fetch = [&]() {
+      if (ok) ok = wait_all(&full[s], ph, a.status, kSiteFull, lane);
+      const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int i = 0; i < kXcg; ++i)
+          w[h][i] = ok && cg[i] < G ? lds128(st + h * pk + rowb + 16 * cg[i]) : make_uint4(0u, 0u, 0u, 0u);
+        sw[h] = ok && has_sc ? lds32(st + 2 * pk + (h * kGuRows + wg) * G + 4 * ql) : 0u;
+      }
+    };
+    auto loaded = [&]() {
+      unsigned dep = sw[0] ^ sw[1];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int i = 0; i < kXcg; ++i) dep ^= fold4(w[h][i]);
+      return dep;
+    };
+    float pg = 0.f, pu = 0.f;
+    int pidx = 0, npend = 0;
+    const float m = tok_mult[0];
+    auto flush = [&]() {
+      if (ok && lane < npend) a.act[pidx] = swiglu_bf16(round_bf16(__fmul_rn(pg, m)), round_bf16(__fmul_rn(pu, m)), a.limit);
+      npend = 0;
+    };
+    if (j < nend) {
+      fetch();
+      release_after(s, loaded());
+    }
+    // warps wg and wg + 4 share a scheduler: start the second half later so
+    // one warp's conversions overlap the other's waits and reductions
+    if (wg >= kWarps / 2) __nanosleep(300);
+    while (j < nend) {
+      float v[2] = {0.f, 0.f};
+      {
+        float scl[2][kXcg];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int i = 0; i < kXcg; ++i) scl[h][i] = e8m0_to_f32((sw[h] >> (8 * ((i + lane) & 3))) & 0xffu);
+        float part[2][2];
+        mx_dot_reg<2, 0, 2, kXcg>(w, xr, part);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) v[h] = __fmaf_rn(part[h][c], scl[h][c], v[h]);
+        mx_dot_reg<2, 2, 2, kXcg>(w, xr, part);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) v[h] = __fmaf_rn(part[h][c], scl[h][2 + c], v[h]);
+      }
+      const int idx = T.ap0[ai] * F + fc * kGuRows + wg;
+      // next chunk: stage, expert and row block without divisions
+      j += P;
+      ++it;
+      if (++s == S) { s = 0; ph ^= 1; }
+      fc += P;
+      while (fc >= nrb) { fc -= nrb; ++ai; }
+      const bool more = j < nend;
+      if (more) fetch();
+      reduce_scatter<2, 32>(v, lane);  // lanes 0-15: gate sum, 16-31: up sum
+      const float gs = __shfl_sync(0xffffffffu, v[0], 0), us = __shfl_sync(0xffffffffu, v[0], 16);
+      if (more) release_after(s, loaded());
+      if (lane == npend) {
+        pg = gs;
+        pu = us;
+        pidx = idx;
+      }
+      if (++npend == 32) flush();
+    }
+    flush();
+  } else {
   // routed gate/up: thread -> rows rs*4 .. rs*4+3 of the chunk's 8, gate and up
   {
     const int n_r = n_act * nrb;
@@ -1053,13 +1327,221 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
       }
     }
   }
+  }
 
+  if constexpr (TT == 1) {
+    // ---------------------- one token, phase 2 ----------------------
+    // this CTA's act rows are written: publish them (control warp 1 stages
+    // the rows this CTA needs once every CTA has)
+    __threadfence();
+    named_sync(kBarCons, kConsumers);
+    if (ct == 0) atomicAdd(a.sync + kSyncGu, 1u);
+    const Down1 dn(a, pl, b, P);
+    const unsigned char* as = smem + pl.act_off;
+    // finished rows wait here (routed, then shared) until the end of phase 2:
+    // a global store before a stage release would hold the release up
+    uint16_t* yb = reinterpret_cast<uint16_t*>(smem + pl.yb_off);
+    uint16_t* ysb = yb + pl.yb_rows;
+    // shared down: warp wg owns row r0 + wg of each chunk, act_s in registers
+    if (Fs > 0 && dn.sr_hi > dn.sr_lo) {
+      if (ok) ok = wait_warp(&sbar, 0, a.status, kSiteActS, lane) && *reinterpret_cast<volatile int*>(&s_afail) == 0;
+      const int fs8 = Fs >> 3;
+      uint4 xs[kScg];
+#pragma unroll
+      for (int i = 0; i < kScg; ++i)
+        xs[i] = lane + 32 * i < fs8 ? reinterpret_cast<const uint4*>(as)[lane + 32 * i] : make_uint4(0u, 0u, 0u, 0u);
+      for (int r0 = dn.sr_lo; r0 < dn.sr_hi; r0 += kShDnRows, ++it) {
+        const int s = it % S;
+        if (ok) ok = wait_all(&full[s], (it / S) & 1, a.status, kSiteFull, lane);
+        const int nr = min(kShDnRows, dn.sr_hi - r0);
+        const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes + static_cast<size_t>(wg) * Fs * 2;
+        uint4 wv[kScg];
+        unsigned dep = 0u;
+#pragma unroll
+        for (int i = 0; i < kScg; ++i) {
+          wv[i] = ok && wg < nr && lane + 32 * i < fs8 ? lds128(st + 16 * (lane + 32 * i)) : make_uint4(0u, 0u, 0u, 0u);
+          dep ^= fold4(wv[i]);
+        }
+        release_after(s, dep);
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < kScg; ++i) {
+          acc = fma_bf16(wv[i].x, xs[i].x, acc);
+          acc = fma_bf16(wv[i].y, xs[i].y, acc);
+          acc = fma_bf16(wv[i].z, xs[i].z, acc);
+          acc = fma_bf16(wv[i].w, xs[i].w, acc);
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+        if (lane == 0 && wg < nr) ysb[r0 - dn.sr_lo + wg] = f32_to_bf16(acc);
+      }
+    }
+    // routed down: chunks of up to kDn1Rows rows of one route; half-warp hh of
+    // warp wg owns rows 4*wg + 2*hh + {0, 1}, lane hl the column groups
+    // hl + 16*cc with the route's activations in registers
+    if (dn.u_hi > dn.u_lo && n_act == R) {
+      if (ok) ok = wait_warp(&abar, 0, a.status, kSiteAct, lane) && *reinterpret_cast<volatile int*>(&s_afail) == 0;
+      const uint4* av = reinterpret_cast<const uint4*>(as + static_cast<size_t>(Fs) * 2);  // bf16 [route][F]
+      const int p_lo = dn.u_lo / d;
+      const int hl = lane & 15, hh = lane >> 4, f8 = F >> 3;
+      int cgd[kDcg];
+#pragma unroll
+      for (int cc = 0; cc < kDcg; ++cc) cgd[cc] = hl + 16 * cc;
+      uint4 xr[kDcg][4];
+      float rsc = 1.f;
+      // the route's act row: power-of-two scale from its max, f16 copy of
+      // this lane's column groups (both half-warps hold the same row)
+      auto load_route = [&](int p) {
+        const uint4* row = av + static_cast<size_t>(p - p_lo) * f8;
+        unsigned m = 0u;
+#pragma unroll
+        for (int cc = 0; cc < kDcg; ++cc)
+#pragma unroll
+          for (int wq = 0; wq < 4; ++wq)
+            if (cgd[cc] < G2) m = max(m, __float_as_uint(absmax8_bf16(row[cgd[cc] * 4 + wq])));
+#pragma unroll
+        for (int off = 8; off >= 1; off >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, off));
+        rsc = pow2i(act_shift(__uint_as_float(m)));
+        const float inv = __fdiv_rn(1.0f, rsc);
+#pragma unroll
+        for (int cc = 0; cc < kDcg; ++cc)
+#pragma unroll
+          for (int wq = 0; wq < 4; ++wq)
+            xr[cc][wq] = cgd[cc] < G2 ? bf16x8_to_f16x8_scaled(row[cgd[cc] * 4 + wq], inv) : make_uint4(0u, 0u, 0u, 0u);
+      };
+      uint4 w[2][kDcg];
+      uint32_t sw[2][kDcg];
+      int s = it % S, ph = (it / S) & 1;
+      auto fetch = [&](int nrr) {
+        if (ok) ok = wait_all(&full[s], ph, a.status, kSiteFull, lane);
+        const unsigned char* st = smem + static_cast<size_t>(s) * pl.stage_bytes;
+        const size_t pb = static_cast<size_t>(nrr) * (F >> 1);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = 4 * wg + 2 * hh + h;
+#pragma unroll
+          for (int cc = 0; cc < kDcg; ++cc) {
+            const bool in = ok && row < nrr && cgd[cc] < G2;
+            w[h][cc] = in ? lds128(st + static_cast<size_t>(row) * (F >> 1) + 16 * cgd[cc]) : make_uint4(0u, 0u, 0u, 0u);
+            sw[h][cc] = in ? lds32(st + pb + static_cast<size_t>(row) * G2 + 4 * ((hl >> 2) + 4 * cc)) : 0u;
+          }
+        }
+      };
+      auto loaded = [&]() {
+        unsigned dep = 0u;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int cc = 0; cc < kDcg; ++cc) dep ^= fold4(w[h][cc]) ^ sw[h][cc];
+        return dep;
+      };
+      int u = dn.u_lo;
+      int p = u / d, r0 = u - p * d, nr = min(kDn1Rows, min(dn.u_hi, (p + 1) * d) - u);
+      fetch(nr);
+      release_after(s, loaded());
+      int pcur = -1;
+      while (u < dn.u_hi) {
+        if (p != pcur) {
+          load_route(p);
+          pcur = p;
+        }
+        float v[2] = {0.f, 0.f};
+        {
+          float part[2][kDcg];
+          mx_dot_reg<2, 0, kDcg, kDcg>(w, xr, part);
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int cc = 0; cc < kDcg; ++cc)
+              v[h] = __fmaf_rn(part[h][cc], e8m0_to_f32((sw[h][cc] >> (8 * (hl & 3))) & 0xffu), v[h]);
+        }
+        const int cu = u - dn.u_lo, cnr = nr;
+        const float crs = rsc;
+        u += nr;
+        ++it;
+        if (++s == S) { s = 0; ph ^= 1; }
+        const bool more = u < dn.u_hi;
+        if (more) {
+          p = u / d;
+          r0 = u - p * d;
+          nr = min(kDn1Rows, min(dn.u_hi, (p + 1) * d) - u);
+          fetch(nr);
+        }
+        reduce_scatter<2, 16>(v, lane);  // half-warp lanes 0-7: row 0, 8-15: row 1
+        if (more) release_after(s, loaded());
+        if ((hl & 7) == 0) {
+          const int row = 4 * wg + 2 * hh + (hl >> 3);
+          if (row < cnr) yb[cu + row] = f32_to_bf16(__fmul_rn(v[0], crs));
+        }
+      }
+    }
+    // publish this CTA's rows, then count them per output block (one atomic
+    // per block, in parallel); the CTA completing a block merges it: routes
+    // in slot order, then the shared row
+    named_sync(kBarCons, kConsumers);
+    if (ok && n_act == R)
+      for (int i = ct; i < dn.u_hi - dn.u_lo; i += kConsumers) {
+        const int u = dn.u_lo + i, pp = u / d;
+        a.y[static_cast<size_t>(T.perm[pp]) * d + (u - pp * d)] = yb[i];
+      }
+    if (ok && Fs > 0)
+      for (int i = ct; i < dn.sr_hi - dn.sr_lo; i += kConsumers) a.ys[dn.sr_lo + i] = ysb[i];
+    __threadfence();
+    if (ct == 0) {
+      int nc = 0;
+      auto add = [&](int c, int rows) {
+        if (nc < kMaxComb) {
+          s_cb[nc] = c;
+          s_cr[nc] = rows;
+        }
+        ++nc;
+      };
+      if (Fs > 0 && dn.sr_hi > dn.sr_lo) add(b, dn.sr_hi - dn.sr_lo);
+      for (int uu = dn.u_lo; uu < dn.u_hi;) {
+        const int pp = uu / d, end = min(dn.u_hi, (pp + 1) * d) - pp * d;
+        for (int rr = uu - pp * d; rr < end;) {
+          const int c = out_block(rr, d, P), chi = min(end, block_lo(c + 1, d, P));
+          add(c, chi - rr);
+          rr = chi;
+        }
+        uu = pp * d + end;
+      }
+      if (nc > kMaxComb) {
+        atomicExch(a.status, 2 | kSiteSync);
+        nc = kMaxComb;
+      }
+      s_ncb = nc;
+      s_ncomb = 0;
+    }
+    named_sync(kBarCons, kConsumers);
+    if (ct < s_ncb) {
+      const int c = s_cb[ct], rows = s_cr[ct];
+      const unsigned target =
+          static_cast<unsigned>(R + (Fs > 0 ? 1 : 0)) * static_cast<unsigned>(block_lo(c + 1, d, P) - block_lo(c, d, P));
+      if (atomicAdd(a.sync + kSyncComb + c, static_cast<unsigned>(rows)) + rows == target) {
+        __threadfence();
+        s_comb[atomicAdd(&s_ncomb, 1)] = c;
+      }
+    }
+    named_sync(kBarCons, kConsumers);
+    for (int q = 0; q < s_ncomb; ++q) {
+      const int c = s_comb[q], lo = block_lo(c, d, P), hi = block_lo(c + 1, d, P);
+      for (int r = lo + ct; r < hi; r += kConsumers) {
+        float sacc = 0.f;
+        for (int jj = 0; jj < k; ++jj)
+          sacc = __fadd_rn(sacc, __fmul_rn(bf16_to_f32(__ldcg(a.y + static_cast<size_t>(jj) * d + r)), T.w[jj]));
+        if (Fs > 0) sacc = __fadd_rn(sacc, bf16_to_f32(__ldcg(a.ys + r)));
+        if (ok) a.out[r] = sacc;
+      }
+      if (ct == 0) atomicExch(a.sync + kSyncComb + c, 0u);
+    }
+  } else {
   // ------------------------- phase 1 -> phase 2 -------------------------
   named_sync(kBarCons, kConsumers);
   if (ct == 0) {
     __threadfence();
-    atomicAdd(a.sync + 1, 1u);
-    s_fail = (ok && spin_geq(a.sync + 1, static_cast<unsigned>(P), a.status, kSiteAct)) ? 0 : 1;
+    atomicAdd(a.sync + kSyncGu, 1u);
+    s_fail = (ok && spin_geq(a.sync + kSyncGu, static_cast<unsigned>(P), a.status, kSiteAct)) ? 0 : 1;
     __threadfence();
   }
   named_sync(kBarCons, kConsumers);
@@ -1233,15 +1715,18 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
       a.out[static_cast<size_t>(t) * d + r_lo + rl] = sacc;
     }
   }
+  }
   // The last CTA out checks that the counters saw exactly this call (a
   // workspace that was not zeroed before its first use fails here, once) and
   // resets them for the next call.
   if (ct == 0) {
     __threadfence();
-    if (atomicAdd(a.sync + 2, 1u) == static_cast<unsigned>(P) - 1u) {
-      const unsigned nl = atomicExch(a.sync + 0, 0u), na = atomicExch(a.sync + 1, 0u);
-      atomicExch(a.sync + 2, 0u);
-      if (nl != static_cast<unsigned>(E) || na != static_cast<unsigned>(P)) atomicExch(a.status, 3 | kSiteSync);
+    if (atomicAdd(a.sync + kSyncExit, 1u) == static_cast<unsigned>(P) - 1u) {
+      const unsigned nl = atomicExch(a.sync + kSyncLogits, 0u), na = atomicExch(a.sync + kSyncGu, 0u);
+      const unsigned ns = atomicExch(a.sync + kSyncShGu, 0u);
+      atomicExch(a.sync + kSyncExit, 0u);
+      if (nl != static_cast<unsigned>(E) || na != static_cast<unsigned>(P) || ns != static_cast<unsigned>(P))
+        atomicExch(a.status, 3 | kSiteSync);
     }
   }
 }

@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstring>
 #include <algorithm>
+#include <cstdlib>
 #include <utility>
 
 #include "livglm_moe.h"
@@ -88,7 +89,7 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   L.y = o;       o += up(m * k * d * 2);
   L.ys = o;      o += up(m * d * 2);
   L.tickets = o; o += up(d * 4);
-  L.sync = o;    o += up(4 * 4);
+  L.sync = o;    o += up(lg::layer::kSyncWords * 4);
   L.total = o;
   return L;
 }
@@ -462,6 +463,34 @@ size_t layer_static_smem() {
 
 size_t round128(size_t v) { return (v + 127) / 128 * 128; }
 
+// One token, phase 2: the most routes one CTA's routed down slice spans and
+// the most output blocks one CTA can complete (same split as lg::layer::Down1).
+void one_token_split(int d, int R, int grid, int unit, bool shared, int* rr_max, int* blocks_max, int* rows_max) {
+  *rr_max = 0;
+  *blocks_max = 0;
+  *rows_max = 0;
+  auto lo = [&](long long c) { return static_cast<int>(c * d / grid); };
+  auto blk = [&](int r) { return static_cast<int>((static_cast<long long>(r + 1) * grid - 1) / d); };
+  const long long nu = static_cast<long long>(R) * d / unit;
+  for (int b = 0; b < grid; ++b) {
+    const int u_lo = unit * static_cast<int>(b * nu / grid), u_hi = unit * static_cast<int>((b + 1) * nu / grid);
+    int nb = shared ? 1 : 0, nr = 0;
+    for (int u = u_lo; u < u_hi;) {
+      const int p = u / d, end = std::min(u_hi, (p + 1) * d) - p * d;
+      ++nr;
+      for (int r = u - p * d; r < end;) {
+        const int c = blk(r);
+        r = std::min(end, lo(c + 1));
+        ++nb;
+      }
+      u = p * d + end;
+    }
+    *rr_max = std::max(*rr_max, nr);
+    *blocks_max = std::max(*blocks_max, nb);
+    *rows_max = std::max(*rows_max, u_hi - u_lo);
+  }
+}
+
 // Shared-memory plan: ring stages of the largest chunk, the union of the
 // phase-1 activations and the phase-2 activations, the per-CTA y rows.
 bool plan_layer(const lg_moe_config* c, int M, int TT, size_t static_smem, int grid, lg::layer::Plan* P,
@@ -471,12 +500,30 @@ bool plan_layer(const lg_moe_config* c, int M, int TT, size_t static_smem, int g
   const size_t G = d / 32, G2 = F / 32, R = static_cast<size_t>(M) * c->num_experts_per_tok;
   size_t stage = std::max<size_t>(d * 4, 2 * kGuRows * (d / 2) + 2 * kGuRows * G);
   if (Fs > 0) stage = std::max<size_t>(stage, 2 * kShGuRows * d * 2);
-  stage = round128(stage);
-  const size_t x_bytes = round128(std::max<size_t>(2 * static_cast<size_t>(TT) * d * 2, R * F * 2 + M * Fs * 2));
   const int unit = 16 / gcd_int(static_cast<int>(G2), 16);
   const int nunits = static_cast<int>(d) / unit;
   const int rows_max = unit * ((nunits + grid - 1) / grid);
-  const size_t y_bytes = round128((R + TT) * static_cast<size_t>(rows_max) * 4);
+  size_t x_bytes, y_bytes;
+  int rr_max = 0, yb_rows = 0;
+  size_t yb_off = 0;
+  if (TT == 1) {
+    // one token: routed down chunks of kDn1Rows rows, shared down chunks of
+    // kShDnRows rows; x, then act_s and this CTA's act rows
+    int blocks_max = 0;
+    if (grid > kMaxGrid) return false;
+    one_token_split(static_cast<int>(d), static_cast<int>(R), grid, unit, Fs > 0, &rr_max, &blocks_max, &yb_rows);
+    if (blocks_max > kMaxComb) return false;
+    stage = std::max<size_t>(stage, kDn1Rows * (F / 2 + G2));
+    if (Fs > 0) stage = std::max<size_t>(stage, kShDnRows * Fs * 2);
+    yb_off = round128(2 * d * 2 + Fs * 2 + static_cast<size_t>(rr_max) * F * 2);
+    const size_t sh_rows = (d + grid - 1) / grid;
+    x_bytes = round128(yb_off + (static_cast<size_t>(yb_rows) + sh_rows) * 2);
+    y_bytes = 0;
+  } else {
+    x_bytes = round128(std::max<size_t>(2 * static_cast<size_t>(TT) * d * 2, R * F * 2 + M * Fs * 2));
+    y_bytes = round128((R + TT) * static_cast<size_t>(rows_max) * 4);
+  }
+  stage = round128(stage);
   const size_t budget = 227 * 1024 - static_smem;
   if (x_bytes + y_bytes + 2 * stage > budget) return false;
   const int stages = static_cast<int>(std::min<size_t>(kMaxStages, (budget - x_bytes - y_bytes) / stage));
@@ -493,6 +540,10 @@ bool plan_layer(const lg_moe_config* c, int M, int TT, size_t static_smem, int g
   P->sub_rows = sub;
   P->sh_rows = sh;
   P->rows_max = rows_max;
+  P->act_off = P->x_off + static_cast<int>(2 * d * 2);
+  P->rr_max = rr_max;
+  P->yb_off = P->x_off + static_cast<int>(yb_off);
+  P->yb_rows = yb_rows;
   *dyn = P->y_off + y_bytes;
   return true;
 }
@@ -504,6 +555,16 @@ bool layer_fits_t(const lg_moe_config* c, int M) {
   return plan_layer(c, M, TT, layer_static_smem<TT>(), num_sms(), &P, &dyn);
 }
 
+// Decode path choice: the chain of stream kernels (default) or the fused
+// one-kernel layer, LIVGLM_FUSED_LAYER=1 (read once per process).
+bool fused_layer_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LIVGLM_FUSED_LAYER");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
 // The fused kernel needs: 1..4 tokens, M*k <= 32 routes, E <= 256 router
 // experts in <= 32 groups, d % 64 == 0, 16-byte aligned scale banks (every
 // bulk copy starts and ends on 16 bytes) and a shared-memory plan.
@@ -513,6 +574,12 @@ bool layer_fits(const lg_moe_config* c, const lg_moe_weights* w, int64_t M) {
   const long long R = M * c->num_experts_per_tok;
   if (R > kMaxRoutes || c->n_routed_experts > kMaxExperts || c->n_group > kMaxGroups) return false;
   if (c->hidden_size % 64) return false;
+  // one token: activation words in registers, scale bytes read as words
+  if (M == 1) {
+    const int F = c->moe_intermediate_size, Fs = F * c->n_shared_experts;
+    if (c->hidden_size > 32 * 32 * kXcg || c->hidden_size % 128) return false;
+    if (F > 16 * 32 * kDcg || F % 128 || Fs > 32 * 8 * kScg) return false;
+  }
   if (!aligned(w->gate_scale, 16) || !aligned(w->up_scale, 16) || !aligned(w->down_scale, 16)) return false;
   if (w->gate_scale_stride % 16 || w->up_scale_stride % 16 || w->down_scale_stride % 16) return false;
   const int m = static_cast<int>(M);
@@ -541,6 +608,7 @@ int launch_layer_t(const lg_moe_config* c, const lg_moe_weights* w, const uint16
   a.sh_gate = w->shared_gate; a.sh_up = w->shared_up; a.sh_down = w->shared_down;
   a.logits = at<float>(ws, L.logits); a.w_out = wts; a.i_out = idx;
   a.act = at<uint16_t>(ws, L.act); a.act_s = at<uint16_t>(ws, L.act_s);
+  a.y = at<uint16_t>(ws, L.y); a.ys = at<uint16_t>(ws, L.ys);
   a.out = out; a.status = at<int>(ws, L.status); a.sync = at<unsigned>(ws, L.sync);
   cudaError_t e = cudaFuncSetAttribute(layer_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(dyn));
@@ -776,7 +844,8 @@ int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint
   int* active = at<int>(workspace, L.active);
   const int slot = trace_slot();
   trace_mark(slot, 0, s);
-  if (layer_fits(cfg, w, M)) return launch_layer(cfg, w, x, m, out, weights_out, indices_out, workspace, L, slot, s);
+  if (fused_layer_enabled() && layer_fits(cfg, w, M))
+    return launch_layer(cfg, w, x, m, out, weights_out, indices_out, workspace, L, slot, s);
   if (decode_fits(cfg, w, M)) {
     rc = launch_decode(cfg, w, x, m, out, wts, idx, workspace, L, slot, s);
     return rc;
