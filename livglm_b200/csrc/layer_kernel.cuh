@@ -390,7 +390,7 @@ __device__ __forceinline__ uint4 bf16x8_to_f16x8_scaled(const uint4& u, float s)
 // Routing of one CTA, computed by the producer warp from the global logits.
 // Restates TopKRouter.__call__ (moe.py:39-62) with the stable (value, index)
 // order of the CPU checker; results go to shared memory.
-struct Tables {
+struct alignas(16) Tables {
   int ae[kMaxRoutes];    // active experts, ascending id
   int ap0[kMaxRoutes];   // first route position of active expert
   int an[kMaxRoutes];    // routes of active expert
@@ -400,7 +400,7 @@ struct Tables {
   int n_active;
   float bias[kMaxExperts];
   float sc[kDecodeMaxTokens][kMaxExperts];  // sigmoid scores, per token
-  float ch[kDecodeMaxTokens][kMaxExperts];  // choice scores (masked), per token
+  alignas(16) float ch[kDecodeMaxTokens][kMaxExperts];  // choice scores (masked), per token (16-byte rows)
   int ix[kDecodeMaxTokens][kMaxExperts];    // candidate indices, per token
 };
 
@@ -416,12 +416,11 @@ __device__ __forceinline__ void top2_merge(float& v1, int& i1, float& v2, int& i
 }
 
 // Routing of token t by one warp.  Lane l owns the contiguous experts
-// l*V .. l*V+V-1 (V = E/32); per-expert values live in shared memory and every
-// loop is rolled, so the code stays small (this runs once per call while the
-// memory system is saturated, where each instruction-cache miss is slow).
-// Same results as the checker's sequential scans for the stable (value,
-// index) order: group top-2 by a merge over the group's lanes, kept groups by
-// rank, top-k by k warp argmaxes over per-lane sorted candidate lists.
+// l*V .. l*V+V-1 (V = E/32) in registers.  Same results as the checker's
+// sequential scans for the stable (value, index) order (for non-NaN scores):
+// group top-2 by a merge over the group's lanes, kept groups by rank, then k
+// rounds of a warp argmax done with two redux.sync reductions (largest score
+// key, then largest index among equal keys).
 // Returns false (doing nothing) for E % 32 != 0, E > 256, or groups that do
 // not span a power-of-two number of whole lanes.
 __device__ __forceinline__ bool warp_routing_ok(const Args& a) {
@@ -431,36 +430,44 @@ __device__ __forceinline__ bool warp_routing_ok(const Args& a) {
   return a.g >= a.G || (per % V == 0 && L >= 1 && (L & (L - 1)) == 0);
 }
 
+// order-preserving key of a choice score (0 = no candidate, NaN lowest)
+__device__ __forceinline__ unsigned score_key(float v) {
+  const unsigned u = __float_as_uint(v);
+  if (v != v) return 1u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 __device__ __noinline__ bool route_token_warp(const Args& a, Tables& T, int t, int lane, bool write_out) {
   if (!warp_routing_ok(a)) return false;
+  constexpr int VM = kMaxExperts / 32;
   const int E = a.E, G = a.G, k = a.k, per = E / G, V = E >> 5;
   const bool grouped = a.g < G;
   const int L = per / V;  // lanes per group
   float* sc = T.sc[t];
-  float* ch = T.ch[t];
-  int* ix = T.ix[t];
   const float ninf = __uint_as_float(0xff800000u);
   const int e0 = lane * V;
-  {  // logits of this lane's experts in one batch of loads
-    float lg[kMaxExperts / 32];
+  float cv[VM];
+  {
+    float lg[VM];
 #pragma unroll
-    for (int q = 0; q < kMaxExperts / 32; ++q) lg[q] = q < V ? __ldcg(a.logits + static_cast<size_t>(t) * E + e0 + q) : 0.f;
+    for (int q = 0; q < VM; ++q) lg[q] = q < V ? __ldcg(a.logits + static_cast<size_t>(t) * E + e0 + q) : 0.f;
 #pragma unroll
-    for (int q = 0; q < kMaxExperts / 32; ++q)
-      if (q < V) sc[e0 + q] = lg[q];
-  }
-#pragma unroll 1
-  for (int q = 0; q < V; ++q) {
-    const float s = own_sigmoidf(sc[e0 + q]);
-    sc[e0 + q] = s;
-    ch[e0 + q] = __fadd_rn(s, T.bias[e0 + q]);
+    for (int q = 0; q < VM; ++q) {
+      cv[q] = ninf;
+      if (q < V) {
+        const float sg = own_sigmoidf(lg[q]);
+        sc[e0 + q] = sg;
+        cv[q] = __fadd_rn(sg, T.bias[e0 + q]);
+      }
+    }
   }
   if (grouped) {
     // group score: the two best of the group's experts, summed (second + best)
     float v1 = 0.f, v2 = 0.f;
     int i1 = -1, i2 = -1;
-#pragma unroll 1
-    for (int q = 0; q < V; ++q) top2_merge(v1, i1, v2, i2, ch[e0 + q], e0 + q, 0.f, -1);
+#pragma unroll
+    for (int q = 0; q < VM; ++q)
+      if (q < V) top2_merge(v1, i1, v2, i2, cv[q], e0 + q, 0.f, -1);
 #pragma unroll 1
     for (int off = 1; off < L; off <<= 1) {
       const float w1 = __shfl_xor_sync(0xffffffffu, v1, off), w2 = __shfl_xor_sync(0xffffffffu, v2, off);
@@ -476,35 +483,30 @@ __device__ __noinline__ bool route_token_warp(const Args& a, Tables& T, int t, i
       rank += after(sj, gj, gsc, gi) ? 1 : 0;
     }
     if (rank >= a.g) {
-#pragma unroll 1
-      for (int q = 0; q < V; ++q) ch[e0 + q] = ninf;
+#pragma unroll
+      for (int q = 0; q < VM; ++q) cv[q] = ninf;
     }
   }
-  // this lane's candidates sorted best first (insertion sort)
-#pragma unroll 1
-  for (int q = 0; q < V; ++q) {
-    const float v = ch[e0 + q];
-    const int e = e0 + q;
-    int p = q;
-    while (p > 0 && after(v, e, ch[e0 + p - 1], ix[e0 + p - 1])) {
-      ch[e0 + p] = ch[e0 + p - 1];
-      ix[e0 + p] = ix[e0 + p - 1];
-      --p;
-    }
-    ch[e0 + p] = v;
-    ix[e0 + p] = e;
-  }
-  // top-k: k warp argmaxes over the lanes' next candidates
-  int head = 0;
+  __syncwarp();  // sigmoid scores in shared memory for the weight lookup
+  // top-k: round s takes the best remaining candidate of the warp
+  unsigned taken = 0u;
   float wj = 0.f;
 #pragma unroll 1
   for (int s = 0; s < k; ++s) {
-    float v = head < V ? ch[e0 + head] : 0.f;
-    int i = head < V ? ix[e0 + head] : -1;
-    warp_best(v, i);
-    if (i / V == lane) ++head;
-    const float sw = sc[i];
-    if (lane == k - 1 - s) wj = sw;
+    float bv = 0.f;
+    int bi = -1;
+#pragma unroll
+    for (int q = 0; q < VM; ++q)
+      if (q < V && !((taken >> q) & 1u) && after(cv[q], e0 + q, bv, bi)) {
+        bv = cv[q];
+        bi = e0 + q;
+      }
+    const unsigned key = bi < 0 ? 0u : score_key(bv);
+    const unsigned m = __reduce_max_sync(0xffffffffu, key);
+    const unsigned wi = __reduce_max_sync(0xffffffffu, key == m && bi >= 0 ? static_cast<unsigned>(bi) + 1u : 0u);
+    const int i = static_cast<int>(wi) - 1;
+    if (i >= 0 && i - e0 >= 0 && i - e0 < V) taken |= 1u << (i - e0);
+    if (lane == k - 1 - s) wj = i >= 0 ? sc[i] : 0.f;
     if (lane == 0) T.sel[t * k + (k - 1 - s)] = i;
   }
   // weights: sequential sum over the k routes in output order
@@ -524,6 +526,92 @@ __device__ __noinline__ bool route_token_warp(const Args& a, Tables& T, int t, i
   }
   __syncwarp();
   return true;
+}
+
+// Routing of token t by the kCtl control warps, one thread per expert
+// (E <= kCtl*32, groups of a power-of-two size <= 32 experts).  Same results
+// as the checker's sequential scans for the stable (value, index) order:
+// group score = second + best of the group (a merge over the group's lanes),
+// a group is kept when fewer than topk_group groups come after it, and expert
+// e is chosen in place k-1-r when r < k candidates come after it.  Named
+// barrier kBarCtl separates the steps; every control thread must call this.
+__device__ __forceinline__ bool block_routing_ok(const Args& a) {
+  const int per = a.E / a.G;
+  return a.E <= kCtl * 32 && a.E % a.G == 0 && per <= 32 && (per & (per - 1)) == 0 && a.k <= kMaxRoutes;
+}
+__device__ __forceinline__ void route_token_block(const Args& a, Tables& T, int t, int tid, bool write_out) {
+  const int E = a.E, G = a.G, k = a.k, per = E / G;
+  const bool grouped = a.g < G;
+  const bool live = tid < E;
+  const float ninf = __uint_as_float(0xff800000u);
+  float* sc = T.sc[t];
+  float* cm = T.ch[t];                          // masked choice scores
+  float* gs = reinterpret_cast<float*>(T.ix[t]);  // group scores
+  const int e = tid;
+  float c = ninf;
+  if (live) {
+    const float sg = own_sigmoidf(__ldcg(a.logits + static_cast<size_t>(t) * E + e));
+    sc[e] = sg;
+    c = __fadd_rn(sg, T.bias[e]);
+  }
+  if (grouped) {
+    // best two of the group: merge over the group's `per` lanes
+    float v1 = live ? c : 0.f, v2 = 0.f;
+    int i1 = live ? e : -1, i2 = -1;
+#pragma unroll 1
+    for (int off = 1; off < per; off <<= 1) {
+      const float w1 = __shfl_xor_sync(0xffffffffu, v1, off), w2 = __shfl_xor_sync(0xffffffffu, v2, off);
+      const int j1 = __shfl_xor_sync(0xffffffffu, i1, off), j2 = __shfl_xor_sync(0xffffffffu, i2, off);
+      top2_merge(v1, i1, v2, i2, w1, j1, w2, j2);
+    }
+    if (live && (e % per) == 0) gs[e / per] = __fadd_rn(v2, v1);
+    named_sync(kBarCtl, kCtl * 32);
+    if (live) {
+      const int gi = e / per;
+      const float mine = gs[gi];
+      int rank = 0;
+#pragma unroll 4
+      for (int gj = 0; gj < G; ++gj) {
+        const float v = gs[gj];
+        rank += (v > mine) | ((v == mine) & (gj > gi));  // after(v, gj, mine, gi)
+      }
+      if (rank >= a.g) c = ninf;
+    }
+  }
+  if (live) cm[e] = c;
+  named_sync(kBarCtl, kCtl * 32);
+  if (live) {
+    // candidates after this one, four per 16-byte broadcast load
+    int rank = 0;
+    const float4* cm4 = reinterpret_cast<const float4*>(cm);
+#pragma unroll 8
+    for (int q = 0; q < (E >> 2); ++q) {
+      const float4 v = cm4[q];
+      const int ej = 4 * q;
+      rank += (v.x > c) | ((v.x == c) & (ej > e));
+      rank += (v.y > c) | ((v.y == c) & (ej + 1 > e));
+      rank += (v.z > c) | ((v.z == c) & (ej + 2 > e));
+      rank += (v.w > c) | ((v.w == c) & (ej + 3 > e));
+    }
+    for (int ej = E & ~3; ej < E; ++ej) rank += (cm[ej] > c) | ((cm[ej] == c) & (ej > e));
+    if (rank < k) T.sel[t * k + (k - 1 - rank)] = e;
+  }
+  named_sync(kBarCtl, kCtl * 32);
+  // weights: sequential sum over the k routes in output order
+  if (tid < k) {
+    const float wj = sc[T.sel[t * k + tid]];
+    float denom = 1.f;
+    if (a.norm) {
+      float sum = sc[T.sel[t * k]];
+      for (int j = 1; j < k; ++j) sum = __fadd_rn(sum, sc[T.sel[t * k + j]]);
+      denom = __fadd_rn(sum, 0x1.79ca1p-67f);
+    }
+    const float w = __fmul_rn(a.norm ? __fdiv_rn(wj, denom) : wj, a.scale);
+    T.w[t * k + tid] = w;
+    if (write_out && a.w_out) a.w_out[static_cast<size_t>(t) * k + tid] = w;
+    if (write_out && a.i_out) a.i_out[static_cast<size_t>(t) * k + tid] = static_cast<uint32_t>(T.sel[t * k + tid]);
+  }
+  named_sync(kBarCtl, kCtl * 32);
 }
 
 // Same routing by one warp for all tokens, scanning shared memory: the path
@@ -693,7 +781,8 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
   const int M = a.M, d = a.d, F = a.F, Fs = a.Fs, E = a.E, k = a.k;
   const int G = d >> 5, G2 = F >> 5, G2s = Fs >> 5;
   const int S = pl.stages, R = M * k;
-  const int nrb = F / kGuRows, n_sh = Fs / kShGuRows;
+  constexpr int GR = kGuRows;
+  const int nrb = F / GR, n_sh = Fs / kShGuRows;
   // chunk sequence: router rows, shared gate/up, routed gate/up, shared down,
   // routed down (expert-major); the routed parts follow the routing tables
   const int nrr = b < E ? (E - b + P - 1) / P : 0;
@@ -783,10 +872,13 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
     }
     named_sync(kBarCtl, kCtl * 32);
     const bool go = s_go != 0;
-    const bool scan = !warp_routing_ok(a);
+    const bool blk = block_routing_ok(a), scan = !blk && !warp_routing_ok(a);
     if (go) {
-      __threadfence();
-      if (!scan) {
+      // the logits were acquired by the counter poll before the barrier and
+      // are read through L2 (ld.global.cg)
+      if (blk) {
+        for (int t = 0; t < M; ++t) route_token_block(a, T, t, cw * 32 + lane, b == 0);
+      } else if (!scan) {
         if (cw < M) route_token_warp(a, T, cw, lane, b == 0);
       } else if (cw == 0) {
         route_tokens_scan(a, T, lane, b == 0);
@@ -833,7 +925,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
     if (lane == 0) mbar_arrive(&tbl);
     if (lane == 0) {
       const int n_r = T.n_active * nrb;
-      const unsigned pk = kGuRows * static_cast<unsigned>(d) / 2u, sk = kGuRows * static_cast<unsigned>(G);
+      const unsigned pk = GR * static_cast<unsigned>(d) / 2u, sk = GR * static_cast<unsigned>(G);
       int j = b;
       while (j < n_sh) j += P;
       for (; j < n_sh + n_r; j += P, ++it) {
@@ -841,7 +933,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
         const int jr = j - n_sh;
         const int ai = jr / nrb;
         const long long e = T.ae[ai];
-        const size_t f0 = static_cast<size_t>(jr - ai * nrb) * kGuRows;
+        const size_t f0 = static_cast<size_t>(jr - ai * nrb) * GR;
         unsigned char* st = smem + static_cast<size_t>(it % S) * pl.stage_bytes;
         uint64_t* fb = &full[it % S];
         mbar_arrive_expect_tx(fb, 2 * pk + 2 * sk);
@@ -1141,7 +1233,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
 #pragma unroll
       for (int wq = 0; wq < 4; ++wq) xr[i][wq] = cg[i] < G ? xh[wq * G + cg[i]] : make_uint4(0u, 0u, 0u, 0u);
     const int nend = n_sh + n_act * nrb;
-    const size_t pk = static_cast<size_t>(kGuRows) * (d >> 1);
+    const size_t pk = static_cast<size_t>(GR) * (d >> 1);
     const size_t rowb = static_cast<size_t>(wg) * (d >> 1);
     const bool has_sc = 4 * ql < G;
     int s = it % S, ph = (it / S) & 1;
@@ -1161,7 +1253,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
 #pragma unroll
         for (int i = 0; i < kXcg; ++i)
           w[h][i] = ok && cg[i] < G ? lds128(st + h * pk + rowb + 16 * cg[i]) : make_uint4(0u, 0u, 0u, 0u);
-        sw[h] = ok && has_sc ? lds32(st + 2 * pk + (h * kGuRows + wg) * G + 4 * ql) : 0u;
+        sw[h] = ok && has_sc ? lds32(st + 2 * pk + (h * GR + wg) * G + 4 * ql) : 0u;
       }
     };
     auto loaded = [&]() {
@@ -1206,7 +1298,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(Args a, Plan pl) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) v[h] = __fmaf_rn(part[h][c], scl[h][2 + c], v[h]);
       }
-      const int idx = T.ap0[ai] * F + fc * kGuRows + wg;
+      const int idx = T.ap0[ai] * F + fc * GR + wg;
       // next chunk: stage, expert and row block without divisions
       j += P;
       ++it;
