@@ -38,6 +38,13 @@ CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.a
                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
+# kernel, from an ncu capture of this bench (workload, stage, fused layer).
+MEASURED_TRAFFIC = {
+    ("decode1", "gate_up", False): 80.53e6,  # profiles/stream_chain_cfg1_decode_M1.md
+}
+
+
 def parse_args(argv=None):
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
@@ -336,10 +343,13 @@ def run_ours(args) -> None:
 
     peaks = measured_peaks()
     by = layer_bytes(cfg, M, U)
+    # decode calls take the fused one-kernel layer when the library was told to
+    fused = M <= 4 and os.environ.get("LIVGLM_FUSED_LAYER", "") == "1"
     mean = {k: statistics.fmean(s[k] for s in stages) for k in _native.TRACE_STAGES} if stages else {}
     dominant = max(mean, key=mean.get) if mean else "gate_up"
     dom_ms = mean.get(dominant, float("nan"))
-    achieved = by[dominant] / (dom_ms * 1e-3) / 1e9 if dom_ms and dom_ms > 0 else None
+    dom_bytes = by["layer"] if fused else by[dominant]  # the fused kernel's time is all in one stage
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9 if dom_ms and dom_ms > 0 else None
     ms_step = ms / args.steps
     value = world * M * args.steps / (ms * 1e-3)
     layer_gbs = by["layer"] / (ms_step * 1e-3) / 1e9
@@ -355,14 +365,14 @@ def run_ours(args) -> None:
                    "l2": f"inputs larger than L2: {L} distinct layers cycled ({L * 1.33:.1f} GB of weights)",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "operands": "x bf16, routed w MXFP4 (E2M1+E8M0), shared w bf16, f32 accumulate, f32 out"},
-        "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peaks["hbm_gbs"],
+        "roofline": {"bound": "hbm", "kernel": "layer_kernel" if fused else dominant, "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": (achieved / peaks["hbm_gbs"]) if achieved else None,
-                     "traffic": None, "peak_source": peaks["source"],
-                     "algorithmic_bytes_per_launch": by[dominant], "launch_ms": dom_ms},
+                     "traffic": MEASURED_TRAFFIC.get((args.workload, dominant, fused)), "peak_source": peaks["source"],
+                     "algorithmic_bytes_per_launch": dom_bytes, "launch_ms": dom_ms},
         "e2e": {"value": world * M * K_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": M * cfg.hidden_size * 2, "d2h_bytes_per_step": M * cfg.hidden_size * 4,
                 "steps": K_e2e, "path": "ExpertSSDMoE.__call__ eager (ctypes -> C ABI), pinned host buffers"},
-        "gpu_launches": (4 if M <= 4 else 6) * args.steps,
+        "gpu_launches": (1 if fused else 5 if M <= 4 else 6) * args.steps,
         "clocks": sampler.summary(),
         "extra": {"layer_hbm_gbs": layer_gbs, "layer_hbm_frac": layer_gbs / peaks["hbm_gbs"],
                   "layer_bytes": by["layer"], "unique_experts_per_call": U,
