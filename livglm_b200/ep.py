@@ -1,0 +1,177 @@
+"""Expert-parallel MoE block: routed experts sharded over ranks, NCCL exchange.
+
+No counterpart in the reference (its experts stream from SSD on one device);
+this is the multi-GPU form of ExpertSSDMoE.__call__ (moe.py:96-201) for
+batched work.  Rank r of a W-rank process group holds the routed experts
+[r*E/W, (r+1)*E/W) and a replica of the router and the shared expert; tokens
+are data-parallel (each rank brings its own rows).  One call:
+
+1. route the local rows (lg_moe_router) and sort the route slots t*k + j by
+   expert id (lg_moe_dispatch, a stable counting sort); because expert ranges
+   are contiguous per rank, that order also groups the slots by destination;
+2. exchange the per-destination route counts (all-to-all of W integers; the
+   split sizes go to the host once per call);
+3. send one bf16 row per route slot, with its expert id local to the
+   destination, by all-to-all;
+4. run the received rows through the local experts (lg_moe_experts with
+   top-k 1 over the E/W local experts);
+5. send the bf16 outputs back by the reverse all-to-all, put them back in
+   slot order and merge them with the local shared expert (lg_moe_combine).
+
+The per-route arithmetic is the single-GPU kernels' own, so the result equals
+ExpertSSDMoE on the same rows up to the batched kernels' rounding order.
+Collectives run on the caller's process group (NCCL for CUDA tensors).
+"""
+
+from __future__ import annotations
+
+from dataclasses import replace
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+from . import _native
+from .config import ContractError, MoEConfig
+from .moe import (DenseMLP, ResidentExperts, TopKRouter, Workspace, _rows_bf16, _stream_ptr,
+                  require_weight)
+
+LocalCompute = Callable[[torch.Tensor, torch.Tensor], torch.Tensor]
+
+
+def expert_owner(expert: torch.Tensor, n_experts: int, world: int) -> torch.Tensor:
+    """Rank that holds each expert id (contiguous ranges of E/W experts)."""
+    return torch.div(expert, n_experts // world, rounding_mode="floor")
+
+
+def exchange_routes(rows: torch.Tensor, slot_expert: torch.Tensor, perm: torch.Tensor,
+                    send_counts: torch.Tensor, n_experts: int, compute_local: LocalCompute,
+                    group=None) -> torch.Tensor:
+    """Steps 2-5 above: ship route rows to the experts' owners and back.
+
+    rows [M, d] (one row per token); slot_expert [M*k] int64 expert id of each
+    route slot; perm [M*k] int64 route slots sorted by expert id (stable);
+    send_counts [W] int64 slots bound for each rank, in perm order.
+    compute_local(x [N, d], local_expert [N] int64) -> [N, d] runs on the
+    received rows.  Returns [M*k, d]: the output of every route slot.
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    per_rank = n_experts // world
+    k = slot_expert.numel() // max(1, rows.shape[0])
+    d = rows.shape[1]
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    counts = torch.stack([send_counts, recv_counts]).cpu()  # the split sizes, one host copy
+    send_split, recv_split = counts[0].tolist(), counts[1].tolist()
+    n_send, n_recv = sum(send_split), sum(recv_split)
+    if n_send != slot_expert.numel():
+        raise ContractError("route counts do not cover every route slot")
+    token = torch.div(perm, max(1, k), rounding_mode="floor")
+    x_send = rows.index_select(0, token)
+    e_send = (slot_expert.index_select(0, perm) % per_rank).to(torch.int32)
+    x_recv = rows.new_empty((n_recv, d))
+    e_recv = torch.empty(n_recv, dtype=torch.int32, device=rows.device)
+    dist.all_to_all_single(x_recv, x_send, recv_split, send_split, group=group)
+    dist.all_to_all_single(e_recv, e_send, recv_split, send_split, group=group)
+    if n_recv:
+        y_recv = compute_local(x_recv, e_recv.to(torch.int64)).reshape(n_recv, d).to(rows.dtype)
+    else:
+        y_recv = rows.new_empty((0, d))
+    del rank
+    y_back = rows.new_empty((n_send, d))
+    dist.all_to_all_single(y_back, y_recv.contiguous(), send_split, recv_split, group=group)
+    y_slots = rows.new_empty((n_send, d))
+    y_slots.index_copy_(0, perm, y_back)
+    return y_slots
+
+
+class ExpertParallelMoE:
+    """ExpertSSDMoE with its routed experts sharded over a process group.
+
+    tensors: the layer's stacked tensors as built by synthetic.layer_weights
+    (router_weight, router_bias, shared_*, and either the full expert banks,
+    of which this rank keeps its own slice, or banks already holding only the
+    E/W local experts).
+    """
+
+    def __init__(self, config: MoEConfig, layer_idx: int, tensors: dict, *, group=None):
+        if not dist.is_initialized():
+            raise ContractError("expert parallelism needs an initialised torch.distributed group")
+        self.config = config
+        self.layer_idx = layer_idx
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        E = config.n_routed_experts
+        if E % self.world:
+            raise ContractError(f"{E} routed experts do not split evenly over {self.world} ranks")
+        self.per_rank = E // self.world
+        lo = self.rank * self.per_rank
+        self.gate = TopKRouter(config)
+        self.gate.weight = require_weight(tensors.get("router_weight"), "router.weight")
+        self.gate.e_score_correction_bias = require_weight(tensors.get("router_bias"),
+                                                           "router.e_score_correction_bias")
+        self.shared_experts = DenseMLP(config.hidden_size, config.shared_intermediate_size,
+                                       config.swiglu_limit, config)
+        if config.n_shared_experts > 0:
+            self.shared_experts.gate_proj.weight = tensors["shared_gate"]
+            self.shared_experts.up_proj.weight = tensors["shared_up"]
+            self.shared_experts.down_proj.weight = tensors["shared_down"]
+        # local experts: top-1 over E/W experts, no routing or shared part of their own
+        self.local_config = replace(config, n_routed_experts=self.per_rank, num_experts_per_tok=1,
+                                    n_group=1, topk_group=1, n_shared_experts=0)
+        self.experts = ResidentExperts(self.local_config, layer=layer_idx)
+        banks = []
+        for name in ("gate_packed", "gate_scale", "up_packed", "up_scale", "down_packed", "down_scale"):
+            t = tensors[name]
+            if t.shape[0] == E:
+                t = t[lo:lo + self.per_rank]
+            if t.shape[0] != self.per_rank:
+                raise ContractError(f"{name} holds {t.shape[0]} experts, expected {E} or {self.per_rank}")
+            banks.append(t.contiguous())
+        self.experts.set_banks(*banks)
+        self._cfg = _native.LgConfig.from_config(config)
+        self._ws = Workspace()
+
+    def _local(self, x: torch.Tensor, local_expert: torch.Tensor) -> torch.Tensor:
+        idx = local_expert.to(torch.int32).view(torch.uint32).reshape(-1, 1)
+        return self.experts(x, idx).reshape(x.shape[0], self.config.hidden_size)
+
+    def __call__(self, hidden_states: torch.Tensor, *, return_route: bool = False):
+        """Local bf16 rows [..., d] -> f32 [..., d], as ExpertSSDMoE.__call__."""
+        c = self.config
+        rows = _rows_bf16(hidden_states, c.hidden_size)
+        M, dev, k, E = rows.shape[0], rows.device, c.num_experts_per_tok, c.n_routed_experts
+        lib = _native.load()
+        stream = _stream_ptr(dev)
+        if M:
+            _, weights, indices = self.gate(rows)
+            counts = torch.empty(E, dtype=torch.int32, device=dev)
+            offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+            perm = torch.empty(M * k, dtype=torch.int32, device=dev)
+            ws, nbytes = self._ws.get(self._cfg, M, dev)
+            _native.check(lib.lg_moe_dispatch(self._cfg, indices.data_ptr(), M, counts.data_ptr(),
+                                              offsets.data_ptr(), perm.data_ptr(), ws, nbytes, stream),
+                          "lg_moe_dispatch")
+            bounds = offsets[::self.per_rank].to(torch.int64)  # [W + 1] slot ranges per owner
+            send_counts = bounds[1:] - bounds[:-1]
+            slot_expert = indices.reshape(-1).view(torch.int32).to(torch.int64)
+            perm64 = perm.to(torch.int64)
+        else:
+            weights = torch.empty(0, k, dtype=torch.float32, device=dev)
+            indices = torch.empty(0, k, dtype=torch.uint32, device=dev)
+            send_counts = torch.zeros(self.world, dtype=torch.int64, device=dev)
+            slot_expert = torch.empty(0, dtype=torch.int64, device=dev)
+            perm64 = torch.empty(0, dtype=torch.int64, device=dev)
+        y_slots = exchange_routes(rows, slot_expert, perm64, send_counts, E, self._local, self.group)
+        out = torch.empty(M, c.hidden_size, dtype=torch.float32, device=dev)
+        if M:
+            shared = self.shared_experts(rows) if c.n_shared_experts > 0 else None
+            _native.check(lib.lg_moe_combine(self._cfg, y_slots.data_ptr(), weights.data_ptr(),
+                                             shared.data_ptr() if shared is not None else None, M,
+                                             out.data_ptr(), stream), "lg_moe_combine")
+        result = out.reshape(*hidden_states.shape[:-1], c.hidden_size)
+        if return_route:
+            return result, weights, indices
+        return result
