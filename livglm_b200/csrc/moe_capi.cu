@@ -77,6 +77,10 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   Layout L{};
   size_t o = 0;
   L.status = o;  o += up(4);
+  // grid counters right after the status word: the same offset for every M,
+  // so a workspace (or the static scratch) reused with another token count
+  // still finds the counters the previous call left at zero
+  L.sync = o;    o += up(lg::layer::kSyncWords * 4);
   L.logits = o;  o += up(m * E * 4);
   L.weights = o; o += up(m * k * 4);
   L.indices = o; o += up(m * k * 4);
@@ -89,7 +93,6 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   L.y = o;       o += up(m * k * d * 2);
   L.ys = o;      o += up(m * d * 2);
   L.tickets = o; o += up(d * 4);
-  L.sync = o;    o += up(lg::layer::kSyncWords * 4);
   L.total = o;
   return L;
 }

@@ -3,7 +3,9 @@
 The library reads the switch once per process, so the decode-shaped parity
 tests of test_gpu_parity.py run again in a child pytest with the switch on:
 every M <= 4 call there then goes through the fused cooperative kernel
-instead of the chain of stream kernels.
+instead of the chain of stream kernels (the allocation-free entry point's
+check included: its fixed scratch is shared by calls of different token
+counts, whose grid counters must line up).
 """
 
 import os
@@ -25,6 +27,7 @@ DECODE_TESTS = " or ".join([
     "test_forward_large_activations",
     "test_golden_cfg0_forward",
     "test_checkpoint_names_drop_in",
+    "test_static_scratch_forward_matches_workspace_forward",
 ])
 
 
@@ -32,7 +35,8 @@ def test_decode_parity_through_fused_layer(cuda, native_lib):
     env = dict(os.environ, LIVGLM_FUSED_LAYER="1")
     r = subprocess.run(
         [sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
-         str(ROOT / "tests" / "test_gpu_parity.py"), "-k", DECODE_TESTS],
+         str(ROOT / "tests" / "test_gpu_parity.py"), str(ROOT / "tests" / "test_zz_no_alloc.py"),
+         "-k", DECODE_TESTS],
         cwd=ROOT, env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
     assert " passed" in r.stdout
