@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(kRouterExperts * 32) router_logits_decode_kern
 // Then the dispatch tables for all M*k slots, and zeroed combine tickets.
 // Shared memory: sc[E] ch[E] gtop1[G] gtop2[G] gs[G] keep[G] + small arrays.
 __global__ void __launch_bounds__(256) router_select_dispatch_kernel(DecodeArgs a, int n_tickets) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   const int E = a.E, G = a.G, k = a.k, M = a.M;
   float* sc = sm;
   float* ch = sc + E;
@@ -206,7 +206,10 @@ __global__ void __launch_bounds__(256) router_select_dispatch_kernel(DecodeArgs 
         const float v = ch[e];
         int r = 0;
 #pragma unroll 8
-        for (int j = 0; j < per; ++j) r += after(ch[g0 + j], g0 + j, v, e);
+        for (int j = 0; j < per; ++j) {
+          const float u = ch[g0 + j];
+          r += (u > v) | ((u == v) & (g0 + j > e));  // after(u, g0 + j, v, e), both indices valid
+        }
         if (r == 0) gt1[e / per] = v;
         if (r == 1) gt2[e / per] = v;
       }
@@ -224,10 +227,25 @@ __global__ void __launch_bounds__(256) router_select_dispatch_kernel(DecodeArgs 
       __syncthreads();
     }
     for (int e = tid; e < E; e += blockDim.x) {
+      // candidates after this one (after(u, j, v, e) with both indices valid),
+      // four per 16-byte broadcast load when the row allows it
       const float v = ch[e];
       int r = 0;
+      int j0 = 0;
+      if ((E & 3) == 0) {
+        const float4* ch4 = reinterpret_cast<const float4*>(ch);
 #pragma unroll 8
-      for (int j = 0; j < E; ++j) r += after(ch[j], j, v, e);
+        for (int q = 0; q < (E >> 2); ++q) {
+          const float4 u = ch4[q];
+          const int j = 4 * q;
+          r += (u.x > v) | ((u.x == v) & (j > e));
+          r += (u.y > v) | ((u.y == v) & (j + 1 > e));
+          r += (u.z > v) | ((u.z == v) & (j + 2 > e));
+          r += (u.w > v) | ((u.w == v) & (j + 3 > e));
+        }
+        j0 = E;
+      }
+      for (int j = j0; j < E; ++j) r += (ch[j] > v) | ((ch[j] == v) & (j > e));
       if (r < k) {
         sel_e[t * k + (k - 1 - r)] = e;
         sel_w[k - 1 - r] = sc[e];
