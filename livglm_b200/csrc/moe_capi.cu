@@ -14,6 +14,7 @@
 #include "layer_kernel.cuh"
 #include "stream_kernels.cuh"
 #include "moe_kernels.cuh"
+#include "down1_kernel.cuh"
 
 namespace {
 
@@ -361,6 +362,39 @@ bool plan_stream(const lg_moe_config* c, int M, int TT, StreamPlan* P) {
   return true;
 }
 
+// One-token down kernel plan: routed chunks of kRows rows (scale copies start
+// on 16 bytes: rows in units of 16/gcd(F/32, 16)), shared chunks of kShRows
+// rows; activations in registers need F <= 1536 with F % 128 == 0 (scale
+// words) and Fs <= 1536.
+bool plan_down1(const lg_moe_config* c, lg::down1::Cfg* D, size_t* smem) {
+  using namespace lg::down1;
+  const size_t F = c->moe_intermediate_size, Fs = F * c->n_shared_experts, G2 = F / 32;
+  if (F % 128 || F > 16 * 32 * kDcg || Fs > 32 * 8 * kScg || Fs % 8) return false;
+  size_t stage = kRows * (F / 2 + G2);
+  if (Fs > 0) stage = std::max<size_t>(stage, kShRows * Fs * 2);
+  stage = (stage + 127) / 128 * 128;
+  int g = static_cast<int>(G2), h = 16;
+  while (h) { const int t = g % h; g = h; h = t; }
+  D->unit = 16 / g;
+  if (c->hidden_size % D->unit) return false;
+  // routes one CTA's routed slice can span: ceil((slice + unit - 1) / d) + 1
+  const size_t d = c->hidden_size, R = c->num_experts_per_tok;
+  const size_t slice = (R * d + num_sms() - 1) / num_sms() + D->unit;
+  const size_t span = (slice + d - 1) / d + 1;  // routes one slice can touch
+  if (span > 4) return false;                    // down1 kernel's kMaxSpan
+  const size_t act = span * F * 2;
+  const size_t tail = (act + 127) / 128 * 128 + (slice + (d + num_sms() - 1) / num_sms()) * 2;
+  const int stages = static_cast<int>(std::min<size_t>(kMaxStages, (kSmemBudget - tail) / stage));
+  if (stages < 2) return false;
+  D->stages = stages;
+  D->stage_bytes = static_cast<int>(stage);
+  D->act_off = static_cast<int>(static_cast<size_t>(stages) * stage);
+  D->yb_off = D->act_off + static_cast<int>((act + 127) / 128 * 128);
+  D->yb_rows = static_cast<int>(slice);
+  *smem = D->yb_off + (slice + (d + num_sms() - 1) / num_sms()) * 2;
+  return true;
+}
+
 // The decode chain needs bulk-copyable chunks: 16-byte aligned bases and
 // expert strides (scales included), d % 64 == 0.
 bool decode_fits(const lg_moe_config* c, const lg_moe_weights* w, int64_t M) {
@@ -426,8 +460,15 @@ int launch_decode_t(const lg_moe_config* c, const lg_moe_weights* w, const uint1
   if (e != cudaSuccess) return cuda_check(e, "gate/up launch");
   trace_mark(slot, 3, s);
   // 4. down + combine
-  occupancy(down_stream_kernel<TT>, kStreamThreads, P.dn_smem);
-  e = launch_ex(down_stream_kernel<TT>, dim3(sms), dim3(kStreamThreads), P.dn_smem, s, pdl, a, P.dn);
+  lg::down1::Cfg D1;
+  size_t d1_smem = 0;
+  if (TT == 1 && M == 1 && plan_down1(c, &D1, &d1_smem)) {
+    occupancy(lg::down1::down1_stream_kernel, lg::down1::kThreads, d1_smem);
+    e = launch_ex(lg::down1::down1_stream_kernel, dim3(sms), dim3(lg::down1::kThreads), d1_smem, s, pdl, a, D1);
+  } else {
+    occupancy(down_stream_kernel<TT>, kStreamThreads, P.dn_smem);
+    e = launch_ex(down_stream_kernel<TT>, dim3(sms), dim3(kStreamThreads), P.dn_smem, s, pdl, a, P.dn);
+  }
   if (e != cudaSuccess) return cuda_check(e, "down launch");
   trace_mark(slot, 4, s);
   // 5. combine
