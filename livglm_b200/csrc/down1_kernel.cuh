@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(kThreads, 1) down1_stream_kernel(DecodeArgs a,
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages];
   __shared__ __align__(8) uint64_t empty[kMaxStages];
-  __shared__ unsigned rel_sink[kConsumers];
+  __shared__ volatile unsigned rel_sink[kConsumers];
   const int warp_id = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int d = a.d, F = a.F, Fs = a.Fs, G2 = F >> 5, E = a.E;
   const int P = gridDim.x, b = blockIdx.x, S = c.stages;
@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1) down1_stream_kernel(DecodeArgs a,
   int it = 0;
   auto release_after = [&](int s, unsigned dep) {
     // every copied word is in registers before the stage goes back
-    *reinterpret_cast<volatile unsigned*>(&rel_sink[ct]) = dep;
+    rel_sink[ct] = dep;
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   };
@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1) down1_stream_kernel(DecodeArgs a,
       return dep;
     };
     int u = sp.u_lo;
-    int p = u / d, r0 = u - p * d, nr = min(kRows, min(sp.u_hi, (p + 1) * d) - u);
+    int p = u / d, nr = min(kRows, min(sp.u_hi, (p + 1) * d) - u);
     fetch(nr);
     release_after(s, loaded());
     int pcur = -1;
@@ -287,7 +287,6 @@ __global__ void __launch_bounds__(kThreads, 1) down1_stream_kernel(DecodeArgs a,
       const bool more = u < sp.u_hi;
       if (more) {
         p = u / d;
-        r0 = u - p * d;
         nr = min(kRows, min(sp.u_hi, (p + 1) * d) - u);
         fetch(nr);
       }
