@@ -95,7 +95,7 @@ struct DecodeArgs {
 // shared memory before griddepcontrol.wait, so they stream while the previous
 // kernel on the stream finishes; only x is read after the wait.  Lane l forms
 // the canonical partial over chunks l, l+32, ... then the xor butterfly.
-constexpr int kRouterExperts = 4;
+constexpr int kRouterExperts = 1;
 template <int TT>
 __global__ void __launch_bounds__(kRouterExperts * 32) router_logits_decode_kernel(DecodeArgs a) {
   extern __shared__ __align__(128) unsigned char rsm[];
