@@ -307,24 +307,35 @@ def run_ours(args) -> None:
     x_host.copy_(xs[0].cpu())
     out_host = torch.empty(M, cfg.hidden_size, dtype=torch.float32, pin_memory=True)
     x_dev = torch.empty_like(xs[0])
-    for s in range(max(args.warmup, 3) if args.warmup < 50 else 50):
-        x_dev.copy_(x_host, non_blocking=True)
-        out_host.copy_(layers[s % L](x_dev), non_blocking=True)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for s in range(K_e2e):
-        x_dev.copy_(x_host, non_blocking=True)
-        out_host.copy_(layers[s % L](x_dev), non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    ms_e2e = e0.elapsed_time(e1)
-    if world > 1:
-        tt = torch.tensor([ms_e2e], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms_e2e = float(tt.item())
+
+    def e2e_step(s: int, host_api: bool) -> None:
+        if host_api:  # tokens and result in page-locked host memory, handed to the module
+            layers[s % L](x_host, out=out_host)
+        else:         # device tensors, with the caller's own copies
+            x_dev.copy_(x_host, non_blocking=True)
+            out_host.copy_(layers[s % L](x_dev), non_blocking=True)
+
+    def e2e_ms(host_api: bool) -> float:
+        for s in range(max(args.warmup, 3) if args.warmup < 50 else 50):
+            e2e_step(s, host_api)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for s in range(K_e2e):
+            e2e_step(s, host_api)
+        e1.record()
+        torch.cuda.synchronize()
+        ms_ = e0.elapsed_time(e1)
+        if world > 1:
+            tt = torch.tensor([ms_], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms_ = float(tt.item())
+        return ms_
+
+    ms_e2e = e2e_ms(True)
+    ms_e2e_copies = e2e_ms(False)
 
     # ---- CPU baseline (rank 0, N=1 only) -------------------------------------
     cpu = None
@@ -371,7 +382,12 @@ def run_ours(args) -> None:
                      "algorithmic_bytes_per_launch": dom_bytes, "launch_ms": dom_ms},
         "e2e": {"value": world * M * K_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": M * cfg.hidden_size * 2, "d2h_bytes_per_step": M * cfg.hidden_size * 4,
-                "steps": K_e2e, "path": "ExpertSSDMoE.__call__ eager (ctypes -> C ABI), pinned host buffers"},
+                "steps": K_e2e,
+                "path": "ExpertSSDMoE.__call__(x_host, out=out_host) eager (ctypes -> C ABI): bf16 tokens and "
+                        "f32 result in page-locked host memory, read and written by the kernels over the host link",
+                "with_caller_copies": {"value": world * M * K_e2e / (ms_e2e_copies * 1e-3),
+                                       "path": "device tensors; the caller copies x in and the result out "
+                                               "with non-blocking copies around each call"}},
         "gpu_launches": (1 if fused else 5 if M <= 4 else 6) * args.steps,
         "clocks": sampler.summary(),
         "extra": {"layer_hbm_gbs": layer_gbs, "layer_hbm_frac": layer_gbs / peaks["hbm_gbs"],

@@ -161,6 +161,14 @@ int lg_moe_combine(const lg_moe_config *cfg, const uint16_t *y,
  *   x bf16 [M, d]; out f32 [M, d]
  *   weights_out f32 [M, k] and indices_out u32 [M, k] may be NULL; when given
  *   they receive the router's outputs (the reference's last_route record).
+ *   x, out, weights_out and indices_out may each be device memory of the
+ *   current device, managed memory, or page-locked host memory
+ *   (cudaHostAlloc / cudaHostRegister) mapped for the current device: the
+ *   reference's hidden states live in unified memory, and a caller whose
+ *   tokens sit on the host passes them as they are.  Host tokens are read
+ *   once over the host link into the workspace; host outputs are written in
+ *   place by the kernels.  Pageable host memory or another device's memory
+ *   returns LG_ERR_INVALID_ARG.
  */
 int lg_moe_forward(const lg_moe_config *cfg, const lg_moe_weights *w,
                    const uint16_t *x, int64_t M, float *out,
@@ -177,7 +185,7 @@ int lg_moe_forward(const lg_moe_config *cfg, const lg_moe_weights *w,
  * inside the library, so this call performs no cudaMalloc/cudaFree and no
  * other allocation.
  *  - Limit: M must fit in 4 MiB of scratch (lg_moe_workspace_size(cfg, M)
- *    <= 4194304; about 40 tokens at d=4096, E=128, k=8, F=1536); larger M
+ *    <= 4194304; about 37 tokens at d=4096, E=128, k=8, F=1536); larger M
  *    returns LG_ERR_UNSUPPORTED with a message saying so.
  *  - The first call on a device resolves the array's device address for the
  *    current device (cudaGetSymbolAddress); make that first call before any

@@ -90,6 +90,20 @@ struct DecodeArgs {
 };
 
 // ---------------------------------------------------------------------------
+// Token staging for hidden states the caller keeps in page-locked host memory:
+// copies n 16-byte words from the host mapping into the workspace, so the
+// chain's kernels read the tokens from HBM and the host read happens once, in
+// a kernel that joins the PDL chain (a copy-engine memcpy in front of the chain
+// would wait for the previous layer to drain and leave the chain cold).  The
+// source is read after griddepcontrol.wait: work before it on the stream may
+// still be writing the host buffer.
+__global__ void __launch_bounds__(256) stage_tokens_kernel(const uint4* src, uint4* dst, int n) {
+  pdl_wait();
+  pdl_trigger();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) dst[i] = src[i];
+}
+
+// ---------------------------------------------------------------------------
 // Router logits for decode: CTA = kRouterExperts warps = kRouterExperts
 // experts.  The CTA's router-weight rows (contiguous) are bulk-copied into
 // shared memory before griddepcontrol.wait, so they stream while the previous

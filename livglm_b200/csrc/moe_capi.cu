@@ -35,6 +35,41 @@ int cuda_check(cudaError_t e, const char* what) {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// The address kernels on the current device use for a caller pointer: device
+// memory of this device and managed memory as given, page-locked host memory
+// (cudaHostAlloc / cudaHostRegister) through its device mapping, with *host
+// set.  Pageable host memory and another device's memory are refused here
+// rather than faulting in a kernel.
+int resolve(const void* p, const char* what, const void** dp, bool* host) {
+  cudaPointerAttributes at{};
+  const cudaError_t e = cudaPointerGetAttributes(&at, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LG_ERR_INVALID_ARG, "%s: pointer attributes: %s", what, cudaGetErrorString(e));
+  }
+  *host = false;
+  *dp = p;
+  switch (at.type) {
+    case cudaMemoryTypeDevice: {
+      int dev = -1;
+      cudaGetDevice(&dev);
+      if (at.device != dev)
+        return fail(LG_ERR_INVALID_ARG, "%s: memory of device %d, but the current device is %d", what, at.device, dev);
+      return LG_OK;
+    }
+    case cudaMemoryTypeManaged:
+      return LG_OK;
+    case cudaMemoryTypeHost:
+      if (!at.devicePointer)
+        return fail(LG_ERR_INVALID_ARG, "%s: page-locked host memory not mapped for the current device", what);
+      *dp = at.devicePointer;
+      *host = true;
+      return LG_OK;
+    default:
+      return fail(LG_ERR_INVALID_ARG, "%s: pageable host memory; pass device or page-locked host memory", what);
+  }
+}
+
 constexpr size_t kAlign = 256;
 size_t up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
@@ -68,7 +103,7 @@ int validate_tokens(int64_t M, const lg_moe_config* c) {
 }
 
 struct Layout {
-  size_t status, logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, sync, total;
+  size_t status, logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, xs, sync, total;
 };
 
 Layout layout(const lg_moe_config* c, int64_t M) {
@@ -94,6 +129,7 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   L.y = o;       o += up(m * k * d * 2);
   L.ys = o;      o += up(m * d * 2);
   L.tickets = o; o += up(d * 4);
+  L.xs = o;      o += up(m * d * 2);  // tokens staged from page-locked host memory
   L.total = o;
   return L;
 }
@@ -413,7 +449,7 @@ bool decode_fits(const lg_moe_config* c, const lg_moe_weights* w, int64_t M) {
 
 template <int TT>
 int launch_decode_t(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M, float* out,
-                    float* wts, uint32_t* idx, void* ws, const Layout& L, int slot, cudaStream_t s) {
+                    float* wts, uint32_t* idx, void* ws, const Layout& L, bool x_host, int slot, cudaStream_t s) {
   using namespace lg;
   const int d = c->hidden_size, F = c->moe_intermediate_size, E = c->n_routed_experts, k = c->num_experts_per_tok;
   const int Fs = F * c->n_shared_experts;
@@ -441,6 +477,16 @@ int launch_decode_t(const lg_moe_config* c, const lg_moe_weights* w, const uint1
   const int sms = num_sms();
   const bool pdl = slot < 0;
   cudaError_t e;
+  // 0. tokens in page-locked host memory: one read over the host link, into HBM
+  if (x_host) {
+    uint16_t* xs = at<uint16_t>(ws, L.xs);
+    const int n16 = M * d / 8;
+    const int blocks = std::min((n16 + 255) / 256, sms);
+    e = launch_ex(stage_tokens_kernel, dim3(blocks), dim3(256), 0, s, pdl, reinterpret_cast<const uint4*>(x),
+                  reinterpret_cast<uint4*>(xs), n16);
+    if (e != cudaSuccess) return cuda_check(e, "token staging launch");
+    a.x = xs;
+  }
   // 1. router logits
   const size_t smem_rl = static_cast<size_t>(kRouterExperts) * d * 4;
   occupancy(router_logits_decode_kernel<TT>, kRouterExperts * 32, smem_rl);
@@ -481,10 +527,10 @@ int launch_decode_t(const lg_moe_config* c, const lg_moe_weights* w, const uint1
 }
 
 int launch_decode(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M, float* out,
-                  float* wts, uint32_t* idx, void* ws, const Layout& L, int slot, cudaStream_t s) {
-  if (M <= 1) return launch_decode_t<1>(c, w, x, M, out, wts, idx, ws, L, slot, s);
-  if (M <= 2) return launch_decode_t<2>(c, w, x, M, out, wts, idx, ws, L, slot, s);
-  return launch_decode_t<4>(c, w, x, M, out, wts, idx, ws, L, slot, s);
+                  float* wts, uint32_t* idx, void* ws, const Layout& L, bool x_host, int slot, cudaStream_t s) {
+  if (M <= 1) return launch_decode_t<1>(c, w, x, M, out, wts, idx, ws, L, x_host, slot, s);
+  if (M <= 2) return launch_decode_t<2>(c, w, x, M, out, wts, idx, ws, L, x_host, slot, s);
+  return launch_decode_t<4>(c, w, x, M, out, wts, idx, ws, L, x_host, slot, s);
 }
 
 // ---- fused decode layer (M <= 4): one cooperative kernel ----------------------
@@ -877,6 +923,24 @@ int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint
   if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w->router_weight, 16))
     return fail(LG_ERR_INVALID_ARG, "forward: x, out and router_weight must be 16-byte aligned");
   if ((rc = check_ws(cfg, M, workspace, workspace_bytes))) return rc;
+  // x and the outputs may be device memory or page-locked host memory (read
+  // and written through the device mapping; host tokens are staged into HBM)
+  bool x_host = false, host = false;
+  {
+    const void* p = nullptr;
+    if ((rc = resolve(x, "forward: x", &p, &x_host))) return rc;
+    x = static_cast<const uint16_t*>(p);
+    if ((rc = resolve(out, "forward: out", &p, &host))) return rc;
+    out = static_cast<float*>(const_cast<void*>(p));
+    if (weights_out) {
+      if ((rc = resolve(weights_out, "forward: weights_out", &p, &host))) return rc;
+      weights_out = static_cast<float*>(const_cast<void*>(p));
+    }
+    if (indices_out) {
+      if ((rc = resolve(indices_out, "forward: indices_out", &p, &host))) return rc;
+      indices_out = static_cast<uint32_t*>(const_cast<void*>(p));
+    }
+  }
   const Layout L = layout(cfg, M);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int m = static_cast<int>(M);
@@ -888,12 +952,17 @@ int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint
   int* active = at<int>(workspace, L.active);
   const int slot = trace_slot();
   trace_mark(slot, 0, s);
+  if (decode_fits(cfg, w, M) && !(fused_layer_enabled() && layer_fits(cfg, w, M)))
+    return launch_decode(cfg, w, x, m, out, wts, idx, workspace, L, x_host, slot, s);
+  if (x_host) {  // the other paths read x many times: one copy into HBM first
+    uint16_t* xs = at<uint16_t>(workspace, L.xs);
+    if ((rc = cuda_check(cudaMemcpyAsync(xs, x, static_cast<size_t>(M) * cfg->hidden_size * 2,
+                                         cudaMemcpyDefault, s), "token staging copy")))
+      return rc;
+    x = xs;
+  }
   if (fused_layer_enabled() && layer_fits(cfg, w, M))
     return launch_layer(cfg, w, x, m, out, weights_out, indices_out, workspace, L, slot, s);
-  if (decode_fits(cfg, w, M)) {
-    rc = launch_decode(cfg, w, x, m, out, wts, idx, workspace, L, slot, s);
-    return rc;
-  }
   if ((rc = cuda_check(cudaMemsetAsync(counts, 0, cfg->n_routed_experts * sizeof(int), s), "memset"))) return rc;
   if ((rc = launch_router(cfg, x, m, w->router_weight, w->router_bias, at<float>(workspace, L.logits), wts, idx,
                           counts, s)))

@@ -34,23 +34,39 @@ ROUTED_EXPERT_RE = re.compile(
 
 
 def _stream_ptr(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """Raw handle of the current stream of `device` (an int; no Stream object)."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    return torch._C._cuda_getCurrentRawStream(index)
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
-def _rows_bf16(hidden_states: torch.Tensor, hidden: int) -> torch.Tensor:
+def _rows_bf16(hidden_states: torch.Tensor, hidden: int, *, allow_host: bool = False) -> torch.Tensor:
+    """[..., d] bf16 -> contiguous [M, d].  With allow_host, a contiguous
+    tensor in page-locked host memory is accepted as it is."""
     if not isinstance(hidden_states, torch.Tensor):
         raise ContractError("hidden states must be a torch tensor")
     if hidden_states.dtype != torch.bfloat16:
         raise ContractError(f"hidden states must be bf16, got {hidden_states.dtype}")
-    if not hidden_states.is_cuda:
-        raise ContractError("hidden states must be on a CUDA device")
     if hidden_states.shape[-1] != hidden:
         raise ContractError(f"hidden size {hidden_states.shape[-1]} != {hidden}")
-    return hidden_states.reshape(-1, hidden).contiguous()
+    if hidden_states.is_cuda:
+        return hidden_states.reshape(-1, hidden).contiguous()
+    if not allow_host:
+        raise ContractError("hidden states must be on a CUDA device")
+    if not hidden_states.is_pinned() or not hidden_states.is_contiguous():
+        raise ContractError("host hidden states must be a contiguous tensor in page-locked memory")
+    return hidden_states.reshape(-1, hidden)
+
+
+def _out_f32(out: torch.Tensor, M: int, hidden: int) -> torch.Tensor:
+    if (not isinstance(out, torch.Tensor) or out.dtype != torch.float32 or out.numel() != M * hidden
+            or not out.is_contiguous() or not (out.is_cuda or out.is_pinned())):
+        raise ContractError(f"out must be a contiguous f32 tensor of {M}x{hidden} elements on the "
+                            "device or in page-locked host memory")
+    return out
 
 
 class Workspace:
@@ -61,14 +77,24 @@ class Workspace:
 
     def __init__(self) -> None:
         self.buf: torch.Tensor | None = None
+        self._ptr = 0
+        self._device: torch.device | None = None
+        self._need: dict[tuple[int, int], tuple[_native.LgConfig, int]] = {}
 
     def get(self, cfg: _native.LgConfig, tokens: int, device: torch.device) -> tuple[int, int]:
-        need = _native.load().lg_moe_workspace_size(cfg, max(int(tokens), 1))
-        if need == 0:
-            _native.check(_native.LG_ERR_INVALID_ARG, "workspace size")
-        if self.buf is None or self.buf.numel() < need or self.buf.device != device:
+        tokens = max(int(tokens), 1)
+        hit = self._need.get((id(cfg), tokens))
+        if hit is not None and hit[0] is cfg:
+            need = hit[1]
+        else:
+            need = _native.load().lg_moe_workspace_size(cfg, tokens)
+            if need == 0:
+                _native.check(_native.LG_ERR_INVALID_ARG, "workspace size")
+            self._need[(id(cfg), tokens)] = (cfg, need)  # holds cfg, so its id stays unique
+        if self.buf is None or self.buf.numel() < need or self._device != device:
             self.buf = torch.zeros(need, dtype=torch.uint8, device=device)
-        return self.buf.data_ptr(), self.buf.numel()
+            self._ptr, self._device = self.buf.data_ptr(), device
+        return self._ptr, self.buf.numel()
 
     def status(self) -> int:
         """The device status word (synchronises with the device)."""
@@ -355,8 +381,27 @@ class ExpertSSDMoE:
         self._last_indices: torch.Tensor | None = None
         self._cfg = _native.LgConfig.from_config(config)
         self._ws = Workspace()
+        self._w_cache: tuple | None = None
+
+    def _weight_key(self) -> tuple:
+        """Identity and address of every tensor the native weight table points
+        at; the table is rebuilt (and re-validated) when any of them changes."""
+        g, s = self.gate, self.shared_experts
+        refs = (g.weight, g.e_score_correction_bias, s.gate_proj.weight, s.up_proj.weight,
+                s.down_proj.weight, self.experts.native_weights())
+        ptrs = tuple(_ptr(t) for t in refs[:5])
+        return refs, ptrs
 
     def native_weights(self) -> _native.LgWeights:
+        refs, ptrs = self._weight_key()
+        c = self._w_cache
+        if c is not None and c[1] == ptrs and all(a is b for a, b in zip(c[0], refs)):
+            return c[2]
+        w = self._build_native_weights()
+        self._w_cache = (refs, ptrs, w)
+        return w
+
+    def _build_native_weights(self) -> _native.LgWeights:
         w = _native.LgWeights()
         ctypes_copy = self.experts.native_weights()
         for name, _ in _native.LgWeights._fields_:
@@ -368,16 +413,28 @@ class ExpertSSDMoE:
             self.shared_experts.native_into(w)
         return w
 
-    def __call__(self, hidden_states: torch.Tensor, *, return_route: bool = False):
-        """bf16 hidden states [..., d] -> f32 [..., d] (moe.py:96-201)."""
-        rows = _rows_bf16(hidden_states, self.hidden_size)
-        M, dev = rows.shape[0], rows.device
+    def __call__(self, hidden_states: torch.Tensor, *, return_route: bool = False,
+                 out: torch.Tensor | None = None):
+        """bf16 hidden states [..., d] -> f32 [..., d] (moe.py:96-201).
+
+        The hidden states may be on the device or, as the reference's unified
+        memory allows, in page-locked host memory (read once by the GPU).
+        `out`, when given, receives the result (device or page-locked host
+        memory) and is returned reshaped; like a non-blocking copy, a host
+        `out` holds the result once the current stream reaches this point."""
+        rows = _rows_bf16(hidden_states, self.hidden_size, allow_host=True)
+        w = self.native_weights()
+        M = rows.shape[0]
+        dev = rows.device if rows.is_cuda else self.gate.weight.device
         k = self.config.num_experts_per_tok
-        out = torch.empty(M, self.hidden_size, dtype=torch.float32, device=dev)
+        if out is None:
+            out = torch.empty(M, self.hidden_size, dtype=torch.float32, device=dev)
+        else:
+            out = _out_f32(out, M, self.hidden_size)
         weights = torch.empty(M, k, dtype=torch.float32, device=dev)
         indices = torch.empty(M, k, dtype=torch.uint32, device=dev)
         ws, nbytes = self._ws.get(self._cfg, M, dev)
-        rc = _native.load().lg_moe_forward(self._cfg, self.native_weights(), rows.data_ptr(), M,
+        rc = _native.load().lg_moe_forward(self._cfg, w, rows.data_ptr(), M,
                                            out.data_ptr(), weights.data_ptr(), indices.data_ptr(),
                                            ws, nbytes, _stream_ptr(dev))
         _native.check(rc, "lg_moe_forward")

@@ -28,6 +28,7 @@ DECODE_TESTS = " or ".join([
     "test_golden_cfg0_forward",
     "test_checkpoint_names_drop_in",
     "test_static_scratch_forward_matches_workspace_forward",
+    "test_forward_host_tokens_and_output",
 ])
 
 

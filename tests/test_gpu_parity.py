@@ -11,8 +11,8 @@ import numpy as np
 import pytest
 import torch
 
-from livglm_b200 import synthetic
-from livglm_b200.config import CONFIGS
+from livglm_b200 import _native, synthetic
+from livglm_b200.config import CONFIGS, ContractError
 from livglm_b200.moe import ExpertSSDMoE, ResidentExperts, TopKRouter, build_layer
 from oracle import moe_oracle as mo
 from tests.helpers import (assert_close, bank_to_device, bank_to_numpy, to_device, to_numpy)
@@ -184,6 +184,76 @@ def test_forward_deterministic_and_shape_preserving(cfg1_layer, cuda, M):
     assert torch.equal(a, b)
     empty = moe(x[:0])
     assert empty.shape == (0, 3, cfg.hidden_size)
+
+
+@pytest.mark.parametrize("M", [1, 3, 256])
+def test_forward_host_tokens_and_output(cfg1_layer, cuda, M):
+    """Tokens and result in page-locked host memory (the reference keeps hidden
+    states in unified memory) give the bits of the device-resident call: the
+    decode chain stages host tokens with a kernel (M=1, 3), the batched path
+    with one copy (M=256); the result is written in place."""
+    cfg, t, _ = cfg1_layer
+    moe = build_layer(cfg, t)
+    x = synthetic.hidden_states(cfg, M, seed=21 + M, device=cuda)
+    ref = moe(x)
+    x_host = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+    x_host.copy_(x)
+    out_host = torch.full((M, cfg.hidden_size), float("nan"), dtype=torch.float32, pin_memory=True)
+    got = moe(x_host, out=out_host)
+    got_dev = moe(x_host)
+    out_dev = torch.full_like(ref, float("nan"))
+    got_dev2 = moe(x, out=out_dev)
+    torch.cuda.synchronize()
+    assert got.data_ptr() == out_host.data_ptr() and not got.is_cuda
+    assert torch.equal(got, ref.cpu())
+    assert got_dev.is_cuda and torch.equal(got_dev, ref)
+    assert got_dev2.data_ptr() == out_dev.data_ptr() and torch.equal(got_dev2, ref)
+
+
+def test_forward_refuses_pageable_host_memory(cfg1_layer, cuda):
+    """Pageable host memory is refused by the module and, before anything is
+    launched, by the library itself."""
+    cfg, t, _ = cfg1_layer
+    moe = build_layer(cfg, t)
+    x = torch.zeros(1, cfg.hidden_size, dtype=torch.bfloat16)
+    with pytest.raises(ContractError, match="page-locked"):
+        moe(x)
+    with pytest.raises(ContractError, match="page-locked"):
+        moe(x.to(cuda), out=torch.empty(1, cfg.hidden_size, dtype=torch.float32))
+    lib = _native.load()
+    out = torch.empty(1, cfg.hidden_size, dtype=torch.float32, device=cuda)
+    ws = torch.zeros(lib.lg_moe_workspace_size(moe._cfg, 1), dtype=torch.uint8, device=cuda)
+    rc = lib.lg_moe_forward(moe._cfg, moe.native_weights(), x.data_ptr(), 1, out.data_ptr(), None, None,
+                            ws.data_ptr(), ws.numel(), torch.cuda.current_stream(cuda).cuda_stream)
+    assert rc == _native.LG_ERR_INVALID_ARG
+    assert "pageable" in _native.last_error()
+
+
+def test_rebinding_weights_after_a_call(cuda, native_lib, golden_cfg0):
+    """The module caches its native weight table between calls; rebinding a
+    router, shared-expert or routed-expert tensor (a new tensor, or new storage
+    under the same tensor) must reach the next call."""
+    z = golden_cfg0
+    cfg = CONFIGS["cfg0"]
+    t = bank_to_device(z, cuda)
+    x = to_device(z["x"], cuda, bf16=True)
+    moe = build_layer(cfg, t)
+    base = moe(x)
+    bias2 = t["router_bias"].flip(0).contiguous()
+    moe.gate.e_score_correction_bias = bias2
+    t2 = dict(t, router_bias=bias2)
+    assert torch.equal(moe(x), build_layer(cfg, t2)(x))
+    down2 = (t["shared_down"].float() * 0.5).to(torch.bfloat16)
+    moe.shared_experts.down_proj.weight.data = down2  # same tensor object, new storage
+    t2["shared_down"] = down2
+    assert torch.equal(moe(x), build_layer(cfg, t2)(x))
+    gate2 = t["gate_packed"].flip(0).contiguous()
+    moe.experts.set_banks(gate2, t["gate_scale"], t["up_packed"], t["up_scale"],
+                          t["down_packed"], t["down_scale"])
+    t2["gate_packed"] = gate2
+    got = moe(x)
+    assert torch.equal(got, build_layer(cfg, t2)(x))
+    assert not torch.equal(got, base)
 
 
 def test_checkpoint_names_drop_in(cuda, native_lib, golden_cfg0):
