@@ -20,6 +20,10 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OUT = PKG / "_lib" / "liblivglm_moe.so"
 SOURCES = ["moe_capi.cu", "moe_noalloc.cu"]
+# self-check of the tensor-core (tcgen05) building blocks, a separate library
+# so the MoE C ABI stays the reference-facing surface
+UMMA_OUT = PKG / "_lib" / "liblivglm_umma_selftest.so"
+UMMA_SOURCES = ["umma_selftest.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -30,25 +34,30 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
-def _stale() -> bool:
-    if not OUT.exists():
+def _stale(out: Path) -> bool:
+    if not out.exists():
         return True
     newest = max(p.stat().st_mtime for p in list(CSRC.glob("*.cu*")) + list((ROOT / "include").glob("*.h")))
-    return newest > OUT.stat().st_mtime
+    return newest > out.stat().st_mtime
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not _stale():
-        return OUT
-    OUT.parent.mkdir(parents=True, exist_ok=True)
-    tmp = OUT.with_suffix(f".{os.getpid()}.tmp")
+def _build_one(out: Path, sources: list[str], force: bool, verbose: bool) -> Path:
+    if not force and not _stale(out):
+        return out
+    out.parent.mkdir(parents=True, exist_ok=True)
+    tmp = out.with_suffix(f".{os.getpid()}.tmp")
     cmd = [nvcc(), "-O3", "-std=c++17", *ARCH, "-lineinfo", "-shared", "-Xcompiler", "-fPIC",
-           f"-I{ROOT / 'include'}", f"-I{CSRC}", *[str(CSRC / s) for s in SOURCES], "-o", str(tmp)]
+           f"-I{ROOT / 'include'}", f"-I{CSRC}", *[str(CSRC / s) for s in sources], "-o", str(tmp)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)
-    os.replace(tmp, OUT)
-    return OUT
+    os.replace(tmp, out)
+    return out
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    _build_one(UMMA_OUT, UMMA_SOURCES, force, verbose)
+    return _build_one(OUT, SOURCES, force, verbose)
 
 
 if __name__ == "__main__":
