@@ -15,6 +15,9 @@
 #include "stream_kernels.cuh"
 #include "moe_kernels.cuh"
 #include "down1_kernel.cuh"
+#include "down_tc.cuh"
+
+#include <cudaTypedefs.h>
 
 namespace {
 
@@ -431,6 +434,78 @@ bool plan_down1(const lg_moe_config* c, lg::down1::Cfg* D, size_t* smem) {
   return true;
 }
 
+// ---- tensor-core one-token down (LIVGLM_TC_DOWN=1) ------------------------------
+bool tc_down_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LIVGLM_TC_DOWN");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// 2-D byte tensor [rows][inner] (row stride = inner bytes), boxes of
+// box_inner bytes x 128 rows, 128-byte swizzle or none
+bool map_bytes(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_inner, bool sw128) {
+  const PFN_cuTensorMapEncodeTiled_v12000 fn = encode_tiled();
+  if (!fn || !aligned(base, 16) || inner % 16) return false;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {inner};
+  const cuuint32_t box[2] = {box_inner, static_cast<cuuint32_t>(lg::dtc::kTile)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Needs: one token, d % 128 == 0, F a multiple of 512 up to 1536 (whole
+// 256-value atom columns, 16-byte scale rows), Fs a multiple of 64 up to 1536,
+// contiguous banks, every CTA of the routed share with at most kMaxUnits tiles
+// over at most two routes.
+bool plan_down_tc(const lg_moe_config* c, const lg_moe_weights* w, lg::dtc::Cfg* D, size_t* smem) {
+  using namespace lg::dtc;
+  const int d = c->hidden_size, F = c->moe_intermediate_size, Fs = F * c->n_shared_experts, k = c->num_experts_per_tok;
+  if (d % kTile || F % 512 || F > 1536 || (Fs > 0 && (Fs % 64 || Fs > 1536))) return false;
+  if (w->down_packed_stride != static_cast<int64_t>(d) * F / 2 || w->down_scale_stride != static_cast<int64_t>(d) * F / 32)
+    return false;
+  const int blocks = d / kTile, P = num_sms();
+  D->n_sh = Fs > 0 ? blocks : 0;
+  D->n_units = k * blocks;
+  const int q = P - D->n_sh;
+  if (q < 1) return false;
+  for (int i = 0; i < q; ++i) {
+    const int lo = static_cast<int>(static_cast<long long>(i) * D->n_units / q);
+    const int hi = static_cast<int>(static_cast<long long>(i + 1) * D->n_units / q);
+    if (hi - lo > kMaxUnits || (hi > lo && (hi - 1) / blocks - lo / blocks > 1)) return false;
+  }
+  D->cols = F / 256;
+  D->sh_cols = Fs / 64;
+  D->sc_bytes = F / 32;
+  const size_t bsize = std::max<size_t>(2 * D->cols * kBRows * 128, static_cast<size_t>(D->sh_cols) * kShBRows * 128);
+  const size_t scale = 2 * kTile * static_cast<size_t>(D->sc_bytes);
+  const size_t budget = 227 * 1024 - 4096 - 1024;  // less static shared memory and the 1024-byte alignment slack
+  const size_t fixed = (scale + 1023) / 1024 * 1024 + bsize;
+  if (fixed + 2 * kBox > budget) return false;
+  D->stages = static_cast<int>(std::min<size_t>(kMaxStages, (budget - fixed) / kBox));
+  D->ring_off = 0;
+  D->scale_off = D->stages * kBox;
+  D->b_off = D->scale_off + static_cast<int>((scale + 1023) / 1024 * 1024);
+  *smem = 1024 + D->b_off + bsize;
+  return true;
+}
+
 // The decode chain needs bulk-copyable chunks: 16-byte aligned bases and
 // expert strides (scales included), d % 64 == 0.
 bool decode_fits(const lg_moe_config* c, const lg_moe_weights* w, int64_t M) {
@@ -507,8 +582,18 @@ int launch_decode_t(const lg_moe_config* c, const lg_moe_weights* w, const uint1
   trace_mark(slot, 3, s);
   // 4. down + combine
   lg::down1::Cfg D1;
-  size_t d1_smem = 0;
-  if (TT == 1 && M == 1 && plan_down1(c, &D1, &d1_smem)) {
+  lg::dtc::Cfg DT;
+  size_t d1_smem = 0, dt_smem = 0;
+  CUtensorMap tm_w, tm_s, tm_sh;
+  if (TT == 1 && M == 1 && tc_down_enabled() && plan_down_tc(c, w, &DT, &dt_smem) &&
+      map_bytes(&tm_w, w->down_packed, F / 2, static_cast<uint64_t>(E) * d, 128, true) &&
+      map_bytes(&tm_s, w->down_scale, F / 32, static_cast<uint64_t>(E) * d, F / 32, false) &&
+      (Fs == 0 ? map_bytes(&tm_sh, w->down_packed, F / 2, static_cast<uint64_t>(E) * d, 128, true)
+               : map_bytes(&tm_sh, w->shared_down, static_cast<uint64_t>(Fs) * 2, d, 128, true))) {
+    occupancy(lg::dtc::down_tc_kernel, lg::dtc::kThreads, dt_smem);
+    e = launch_ex(lg::dtc::down_tc_kernel, dim3(sms), dim3(lg::dtc::kThreads), dt_smem, s, pdl, a, DT, tm_w, tm_s,
+                  tm_sh);
+  } else if (TT == 1 && M == 1 && plan_down1(c, &D1, &d1_smem)) {
     occupancy(lg::down1::down1_stream_kernel, lg::down1::kThreads, d1_smem);
     e = launch_ex(lg::down1::down1_stream_kernel, dim3(sms), dim3(lg::down1::kThreads), d1_smem, s, pdl, a, D1);
   } else {

@@ -15,16 +15,18 @@
 //
 // Activation split (kind::mxf4 needs E2M1 on both sides): a bf16 vector is
 // written as a sum of T terms, each term a row of E2M1 values with one UE8M0
-// scale per 32-value block, chosen so the block's largest residual maps into
-// [0, 6]; each term takes the round-to-nearest E2M1 of the residual and the
-// residual shrinks by a factor of at least 3 per term.  A bf16 value's
-// residual stays a multiple of its own ulp, so it reaches exactly zero after a
-// few terms more than it takes the block scale to come down to its
-// magnitude; with T = 16 a block whose values span 2^-18 of its max is exact.
+// scale per 32-value block: the first term's scale maps the block's largest
+// magnitude into [0, 6], each later term's scale is 4x smaller, and each term
+// takes the round-to-nearest E2M1 of the residual, so the residual after t
+// terms is at most 2^(s0 - 2(t-1)).  A bf16 value's residual stays a multiple
+// of its own ulp, so values down to about 2^-(2T-7) of the block max come out
+// exact (T = 16: the whole block for ordinary data).
 // The MMA then sums the terms as separate B rows (N = T columns of the
 // accumulator); products of E2M1 values and power-of-two scales are exact.
 #pragma once
 #include <cstdint>
+
+#include <cuda_fp16.h>
 
 namespace lg {
 namespace umma {
@@ -117,16 +119,32 @@ __device__ __forceinline__ void ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32])
 // ---- activation split --------------------------------------------------------
 
 // UE8M0 exponent e (biased byte e + 127) of the smallest power of two with
-// 6 * 2^e >= a, for a > 0 normal; residuals below 2^-100 count as zero.
+// 6 * 2^e >= a, for a normal a >= 2^-100.
 __device__ __forceinline__ int term_exponent(float a) {
   const uint32_t u = __float_as_uint(a);
   const int e0 = static_cast<int>((u >> 23) & 0xFFu) - 127;  // floor(log2 a)
   const bool low = (u & 0x7FFFFFu) <= 0x400000u;              // a / 2^e0 <= 1.5
-  return low ? e0 - 2 : e0 - 1;
+  const int e = low ? e0 - 2 : e0 - 1;
+  return e > 126 ? 126 : e;
 }
 
-// Round two f32 values to E2M1 (hardware round-to-nearest, saturating):
-// the byte's low nibble holds `lo`.
+// The split of a 32-value block held by a half-warp, two values per lane
+// (lane i of the half: values 2i, 2i+1).  split_base reduces the block's
+// largest magnitude once and returns the first term's exponent s0 (*live is
+// false for a block below 2^-100, whose terms are all zero with scale byte
+// 127); term t then uses the fixed exponent s0 - 2t: a residual is at most one
+// grid step of the previous term, 2^(s0 - 2(t-1)), which the next term's range
+// 6 * 2^(s0 - 2t) covers, so no term saturates and no further reduction is
+// needed.
+__device__ __forceinline__ int split_base(float r0, float r1, bool* live) {
+  float a = fmaxf(fabsf(r0), fabsf(r1));
+#pragma unroll
+  for (int off = 8; off >= 1; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
+  *live = a >= 0x1p-100f;
+  return *live ? term_exponent(a) : 0;
+}
+// Round two f32 values to E2M1 (hardware round-to-nearest-even, saturating
+// at 6): the byte's low nibble holds `lo`.
 __device__ __forceinline__ uint32_t e2m1x2_rn(float lo, float hi) {
   uint32_t r;
   asm("{\n\t.reg .b8 b;\n\tcvt.rn.satfinite.e2m1x2.f32 b, %1, %2;\n\tcvt.u32.u8 %0, b;\n\t}" : "=r"(r) : "f"(hi), "f"(lo));
@@ -140,28 +158,23 @@ __device__ __forceinline__ void e2m1x2_to_f32(uint32_t byte, float& lo, float& h
   hi = __half2float(__ushort_as_half(static_cast<unsigned short>(h >> 16)));
 }
 
-// One term of the split for a 32-value block held by a half-warp, two values
-// per lane (lane i of the half: values 2i, 2i+1).  Returns the E2M1 byte of
-// the lane's pair; *scale gets the block's UE8M0 byte; the residual pair is
-// updated in place.
-__device__ __forceinline__ uint32_t split_term(float& r0, float& r1, uint32_t* scale) {
-  float a = fmaxf(fabsf(r0), fabsf(r1));
-#pragma unroll
-  for (int off = 8; off >= 1; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
-  if (!(a >= 0x1p-100f)) {  // block residual is (effectively) zero
-    *scale = 127u;
-    return 0u;
-  }
-  int e = term_exponent(a);
-  e = e < -126 ? -126 : (e > 126 ? 126 : e);  // 2^e and 2^-e both normal
-  const float inv = __int_as_float((127 - e) << 23), sc = __int_as_float((127 + e) << 23);
+// One term at exponent s (|s| <= 126): the E2M1 byte of the lane's pair; the
+// residual pair loses the term's value.
+__device__ __forceinline__ uint32_t split_step(float& r0, float& r1, int s) {
+  const float inv = __int_as_float((127 - s) << 23), sc = __int_as_float((127 + s) << 23);
   const uint32_t byte = e2m1x2_rn(r0 * inv, r1 * inv);
   float q0, q1;
   e2m1x2_to_f32(byte, q0, q1);
   r0 = __fsub_rn(r0, q0 * sc);
   r1 = __fsub_rn(r1, q1 * sc);
-  *scale = static_cast<uint32_t>(127 + e);
   return byte;
+}
+
+// Exponent of term t, kept >= -126 (a live block reaches that only after
+// its residual is below 2^-120; E2M1 saturates at 6 there).
+__device__ __forceinline__ int term_scale(int s0, int t) {
+  const int s = s0 - 2 * t;
+  return s < -126 ? -126 : s;
 }
 
 }  // namespace umma

@@ -76,9 +76,11 @@ __global__ void __launch_bounds__(128, 1) tile_kernel(int kind, const uint8_t* w
       const int blk = warp * 2 + (lane >> 4), hl = lane & 15;
       const int k0 = c * 256 + blk * 32 + 2 * hl;
       float r0 = __uint_as_float(static_cast<uint32_t>(x[k0]) << 16), r1 = __uint_as_float(static_cast<uint32_t>(x[k0 + 1]) << 16);
+      bool live;
+      const int s0 = split_base(r0, r1, &live);
       for (int t = 0; t < T; ++t) {
-        uint32_t sc;
-        const uint32_t byte = split_term(r0, r1, &sc);
+        const uint32_t sc = live ? static_cast<uint32_t>(127 + term_scale(s0, t)) : 127u;
+        const uint32_t byte = live ? split_step(r0, r1, term_scale(s0, t)) : 0u;
         sb[sw128_offset(t, blk * 16 + hl)] = static_cast<uint8_t>(byte);
         terms[static_cast<size_t>(t) * (K / 2) + c * 128 + blk * 16 + hl] = static_cast<uint8_t>(byte);
         if (hl == 0) {

@@ -26,15 +26,19 @@ def test_sixteen_terms_reconstruct_bf16_vectors_exactly():
         np.testing.assert_array_equal(reconstruct(codes, scales), x.astype(np.float64))
 
 
-def test_residual_shrinks_by_at_least_three_per_term():
+def test_residual_bound_and_no_saturation():
+    """After t terms the block residual is at most 2^(s0 - 2(t-1)), inside the
+    next term's range, so no code saturates."""
     rng = np.random.default_rng(1)
     x = bf16_values(rng, 1024)
-    prev = np.abs(x).reshape(-1, 32).max(axis=1)
-    for t in range(1, 6):
+    amax = np.abs(x).reshape(-1, 32).max(axis=1)
+    codes, scales, _ = split(x, 8)
+    s0 = scales[0].astype(np.int64) - 127
+    assert np.all(6.0 * np.ldexp(1.0, s0) >= amax) and np.all(3.0 * np.ldexp(1.0, s0) < amax)
+    for t in range(1, 8):
         _, _, r = split(x, t)
         cur = np.abs(r).reshape(-1, 32).max(axis=1)
-        assert np.all(cur <= prev / 3 + 1e-30)
-        prev = cur
+        assert np.all(cur <= np.ldexp(1.0, s0 - 2 * (t - 1)))
 
 
 def test_zero_and_tiny_blocks():

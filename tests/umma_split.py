@@ -2,11 +2,12 @@
 (the checker for the tensor-core building blocks; test infrastructure).
 
 A bf16 vector is written as T terms; term t holds, per 32-value block, one
-UE8M0 scale byte 127 + e (e the smallest integer with 6 * 2^e >= the block's
-largest residual, kept in [-126, 126]) and the round-to-nearest-even E2M1
-codes of residual / 2^e; the residual then loses the term's value.  Blocks
-whose largest residual is below 2^-100 get code 0 and scale 127.  All
-arithmetic in float32, as on the device.
+UE8M0 scale byte 127 + e_t, e_t = max(s0 - 2t, -126) with s0 the smallest
+integer such that 6 * 2^s0 >= the block's largest magnitude (at most 126),
+and the round-to-nearest-even E2M1 codes (saturating at 6) of
+residual / 2^e_t; the residual then loses the term's value.  Blocks whose
+largest magnitude is below 2^-100 get code 0 and scale 127.  All arithmetic
+in float32, as on the device.
 """
 
 from __future__ import annotations
@@ -17,8 +18,8 @@ GRID = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], np.float32)
 
 
 def e2m1_rn(v: np.ndarray) -> np.ndarray:
-    """float32 values with |v| <= 6 -> 4-bit codes (sign in bit 3), ties to even."""
-    a = np.abs(v).astype(np.float32)
+    """float32 values -> 4-bit codes (sign in bit 3), nearest with ties to even, saturating at 6."""
+    a = np.minimum(np.abs(v).astype(np.float32), np.float32(6))
     d = np.abs(a[..., None] - GRID)
     best = np.argmin(d, axis=-1)  # first of equal distances: the lower code
     nxt = np.minimum(best + 1, 7)
@@ -38,13 +39,13 @@ def split(x: np.ndarray, terms: int):
     r = x.astype(np.float32).reshape(K // 32, 32).copy()
     codes = np.zeros((terms, K // 32, 32), np.uint8)
     scales = np.full((terms, K // 32), 127, np.uint8)
+    a = np.max(np.abs(r), axis=1)
+    live = a >= np.float32(2.0 ** -100)
+    m, p = np.frexp(np.where(live, a, np.float32(1)))
+    e0 = p.astype(np.int64) - 1
+    s0 = np.minimum(np.where(2 * m <= 1.5, e0 - 2, e0 - 1), 126)
     for t in range(terms):
-        a = np.max(np.abs(r), axis=1)
-        live = a >= np.float32(2.0 ** -100)
-        m, p = np.frexp(np.where(live, a, np.float32(1)))
-        e0 = p.astype(np.int64) - 1
-        e = np.where(2 * m <= 1.5, e0 - 2, e0 - 1)
-        e = np.clip(e, -126, 126)
+        e = np.maximum(s0 - 2 * t, -126)
         inv = np.ldexp(np.float32(1), -e).astype(np.float32)
         sc = np.ldexp(np.float32(1), e).astype(np.float32)
         c = e2m1_rn((r * inv[:, None]).astype(np.float32))
