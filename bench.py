@@ -371,6 +371,11 @@ def run_ours(args) -> None:
             dist.destroy_process_group()
         return
 
+    # kernels per layer call: fused layer 1; decode chain 5 (router logits,
+    # select + dispatch, gate/up, down, combine), plus the activation split of
+    # the tensor-core down kernel for one token (on unless LIVGLM_TC_DOWN=0)
+    tc_down = M == 1 and os.environ.get("LIVGLM_TC_DOWN", "1") != "0"
+    launches_per_step = 1 if fused else (6 if tc_down else 5) if M <= 4 else 6
     peaks = measured_peaks()
     by = layer_bytes(cfg, M, U)
     # decode calls take the fused one-kernel layer when the library was told to
@@ -408,7 +413,7 @@ def run_ours(args) -> None:
                 "with_caller_copies": {"value": world * M * K_e2e / (ms_e2e_copies * 1e-3),
                                        "path": "device tensors; the caller copies x in and the result out "
                                                "with non-blocking copies around each call"}},
-        "gpu_launches": (1 if fused else 5 if M <= 4 else 6) * args.steps,
+        "gpu_launches": launches_per_step * args.steps,
         "clocks": sampler.summary(),
         "extra": {"layer_hbm_gbs": layer_gbs, "layer_hbm_frac": layer_gbs / peaks["hbm_gbs"],
                   "layer_bytes": by["layer"], "unique_experts_per_call": U,

@@ -65,7 +65,36 @@ struct Cfg {
   int sh_cols;     // bf16 atom columns per shared row (Fs / 64)
   int sc_bytes;    // scale bytes per routed row (F / 32)
   int ring_off, scale_off, b_off;  // shared-memory regions (from the 1024-aligned base)
+  uint8_t* bimg;   // split route activations: [route][col] 1 KB = term rows 0-7 of the swizzled B tile
+  uint8_t* bsc;    // their scales: [route][term][F / 32]
 };
+
+// Activation split of every route, once per call: half-warp h of the grid
+// takes 32-value block j of route p (h = p * blocks + j) and writes its
+// kTerms term bytes into the swizzled B image and the term scales.  Runs
+// between the gate/up kernel (act) and down_tc_kernel, chained by PDL.
+__global__ void __launch_bounds__(64) split_act_kernel(DecodeArgs a, Cfg c) {
+  // let down_tc_kernel launch (and start its weight loads) at once: its own
+  // dependency wait covers this kernel's completion, which follows the
+  // gate/up kernel's
+  pdl_trigger();
+  pdl_wait();  // act from the gate/up kernel
+  const int nblk = c.cols * 8, routes = a.M * a.k;
+  const int h = (blockIdx.x * blockDim.x + threadIdx.x) >> 4, hl = threadIdx.x & 15;
+  if (h >= routes * nblk) return;  // whole half-warps leave together (nblk * routes % 2 == 0)
+  const int p = h / nblk, j = h - p * nblk, col = j >> 3, jb = j & 7;
+  const uint32_t pair = __ldcg(reinterpret_cast<const uint32_t*>(a.act + static_cast<size_t>(p) * a.F + j * 32) + hl);
+  float r0 = __uint_as_float(pair << 16), r1 = __uint_as_float(pair & 0xFFFF0000u);
+  bool live;
+  const int s0 = umma::split_base(r0, r1, &live);
+  uint8_t* img = c.bimg + (static_cast<size_t>(p) * c.cols + col) * 1024;
+#pragma unroll
+  for (int t = 0; t < kTerms; ++t) {
+    const int e = umma::term_scale(s0, t);
+    img[umma::sw128_offset(t, jb * 16 + hl)] = static_cast<uint8_t>(live ? umma::split_step(r0, r1, e) : 0u);
+    if (hl == 0) c.bsc[(static_cast<size_t>(p) * kTerms + t) * c.sc_bytes + j] = static_cast<uint8_t>(live ? 127 + e : 127);
+  }
+}
 
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -242,56 +271,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   else {
     const int ct = threadIdx.x;  // 0..127
     const uint32_t lanes = tbase + (static_cast<uint32_t>(warp * 32) << 16);
-    pdl_wait();  // act / act_s from the gate/up kernel
-    pdl_trigger();
     bool ok = nu > 0;
-    if (shared_cta && ok) {
-      // B: act_s as row 0 of each 16-row column tile, other rows zero
-      const int n16 = c.sh_cols * kShBRows * 128 / 16;
+    const int nr = shared_cta || !ok ? 0 : (u_hi - 1) / blocks - p_first + 1;  // routes of this CTA
+    // zero B rows and the constant scales of the zero term rows: no dependence
+    // on the gate/up kernel, so before the dependency wait
+    if (ok) {
+      const int n16 = shared_cta ? c.sh_cols * kShBRows * 128 / 16 : nr * c.cols * kBRows * 128 / 16;
       for (int i = ct; i < n16; i += kCompute) reinterpret_cast<uint4*>(bop)[i] = make_uint4(0u, 0u, 0u, 0u);
-      named_sync(1, kCompute);
+      for (int i = ct; i < nr * (kBRows - kTerms) * c.sc_bytes; i += kCompute) {
+        const int r = i / ((kBRows - kTerms) * c.sc_bytes), rem = i - r * ((kBRows - kTerms) * c.sc_bytes);
+        sfb_s[r][kTerms + rem / c.sc_bytes][rem % c.sc_bytes] = 127;
+      }
+    }
+    named_sync(1, kCompute);
+    pdl_wait();  // act / act_s from the gate/up kernel, the split from split_act_kernel
+    pdl_trigger();
+    if (shared_cta && ok) {
+      // B: act_s as row 0 of each 16-row column tile
       for (int i = ct; i < c.sh_cols * 8; i += kCompute) {
         const int col = i >> 3, ch = i & 7;
         *reinterpret_cast<uint4*>(bop + col * (kShBRows * 128) + umma::sw128_offset(0, ch * 16)) =
             __ldcg(reinterpret_cast<const uint4*>(a.act_s) + i);
       }
     } else if (ok) {
-      // B: the split of each route's activations (at most two routes)
-      const int p_last = (u_hi - 1) / blocks, nr = p_last - p_first + 1;
-      const int n16 = nr * c.cols * kBRows * 128 / 16;
-      for (int i = ct; i < n16; i += kCompute) reinterpret_cast<uint4*>(bop)[i] = make_uint4(0u, 0u, 0u, 0u);
-      named_sync(1, kCompute);
-      // half-warp hw splits block hw of every atom column (block j = 8 col + hw),
-      // all its blocks at once so the per-term reductions overlap
-      const int hw = ct >> 4, hl = ct & 15;
-      for (int r = 0; r < nr; ++r) {
-        const uint16_t* act = a.act + static_cast<size_t>(p_first + r) * a.F;
-        float r0[kMaxCols], r1[kMaxCols];
-#pragma unroll
-        for (int q = 0; q < kMaxCols; ++q) {
-          const uint32_t pair = q < c.cols ? __ldcg(reinterpret_cast<const uint32_t*>(act + (8 * q + hw) * 32) + hl) : 0u;
-          r0[q] = __uint_as_float(pair << 16);
-          r1[q] = __uint_as_float(pair & 0xFFFF0000u);
-        }
-        int s0[kMaxCols];
-        bool live[kMaxCols];
-#pragma unroll
-        for (int q = 0; q < kMaxCols; ++q) s0[q] = q < c.cols ? umma::split_base(r0[q], r1[q], &live[q]) : 0;
-#pragma unroll
-        for (int t = 0; t < kTerms; ++t) {
-#pragma unroll
-          for (int q = 0; q < kMaxCols; ++q) {
-            if (q < c.cols) {
-              const int e = umma::term_scale(s0[q], t);
-              const uint32_t byte = live[q] ? umma::split_step(r0[q], r1[q], e) : 0u;
-              bop[(r * c.cols + q) * (kBRows * 128) + umma::sw128_offset(t, hw * 16 + hl)] = static_cast<uint8_t>(byte);
-              if (hl == 0) sfb_s[r][t][8 * q + hw] = static_cast<uint8_t>(live[q] ? 127 + e : 127);
-            }
-          }
-        }
-        if (hl == 0)
-          for (int q = 0; q < c.cols; ++q)
-            for (int t = kTerms; t < kBRows; ++t) sfb_s[r][t][8 * q + hw] = 127;
+      // B: the routes' split activations (split_act_kernel), term rows 0-7 of each column tile
+      for (int i = ct; i < nr * c.cols * 64; i += kCompute) {
+        const int rc = i >> 6, w16 = i & 63;  // (route, column) image, 16-byte word
+        *reinterpret_cast<uint4*>(bop + rc * (kBRows * 128) + w16 * 16) =
+            __ldcg(reinterpret_cast<const uint4*>(c.bimg + (static_cast<size_t>(p_first) * c.cols + rc) * 1024) + w16);
+      }
+      for (int i = ct; i < nr * kTerms * c.sc_bytes; i += kCompute) {
+        const int r = i / (kTerms * c.sc_bytes), rem = i - r * (kTerms * c.sc_bytes);
+        sfb_s[r][rem / c.sc_bytes][rem % c.sc_bytes] =
+            __ldcg(c.bsc + (static_cast<size_t>(p_first + r) * kTerms) * c.sc_bytes + rem);
       }
       named_sync(1, kCompute);
       // term scales into tensor memory: lane l = B row l, byte s = block 2m + s

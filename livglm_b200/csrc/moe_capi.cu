@@ -106,7 +106,8 @@ int validate_tokens(int64_t M, const lg_moe_config* c) {
 }
 
 struct Layout {
-  size_t status, logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, xs, sync, total;
+  size_t status, logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, xs, bimg, bsc, sync,
+      total;
 };
 
 Layout layout(const lg_moe_config* c, int64_t M) {
@@ -133,6 +134,10 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   L.ys = o;      o += up(m * d * 2);
   L.tickets = o; o += up(d * 4);
   L.xs = o;      o += up(m * d * 2);  // tokens staged from page-locked host memory
+  // one-token tensor-core down: split route activations (a swizzled 1 KB image
+  // per 256-value column and route) and their scales
+  L.bimg = o;    o += m == 1 ? up(k * (F / 256) * 1024) : 0;
+  L.bsc = o;     o += m == 1 ? up(k * lg::dtc::kTerms * (F / 32)) : 0;
   L.total = o;
   return L;
 }
@@ -434,11 +439,13 @@ bool plan_down1(const lg_moe_config* c, lg::down1::Cfg* D, size_t* smem) {
   return true;
 }
 
-// ---- tensor-core one-token down (LIVGLM_TC_DOWN=1) ------------------------------
+// ---- tensor-core one-token down ------------------------------------------------
+// Default for one-token calls whose geometry fits plan_down_tc; LIVGLM_TC_DOWN=0
+// (read once per process) selects the CUDA-core down1 kernel instead.
 bool tc_down_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("LIVGLM_TC_DOWN");
-    return v && v[0] == '1';
+    return !(v && v[0] == '0');
   }();
   return on;
 }
@@ -590,6 +597,11 @@ int launch_decode_t(const lg_moe_config* c, const lg_moe_weights* w, const uint1
       map_bytes(&tm_s, w->down_scale, F / 32, static_cast<uint64_t>(E) * d, F / 32, false) &&
       (Fs == 0 ? map_bytes(&tm_sh, w->down_packed, F / 2, static_cast<uint64_t>(E) * d, 128, true)
                : map_bytes(&tm_sh, w->shared_down, static_cast<uint64_t>(Fs) * 2, d, 128, true))) {
+    DT.bimg = at<uint8_t>(ws, L.bimg);
+    DT.bsc = at<uint8_t>(ws, L.bsc);
+    const int halves = M * k * DT.cols * 8;  // one half-warp per 32-value block
+    e = launch_ex(lg::dtc::split_act_kernel, dim3((halves * 16 + 63) / 64), dim3(64), 0, s, pdl, a, DT);
+    if (e != cudaSuccess) return cuda_check(e, "activation split launch");
     occupancy(lg::dtc::down_tc_kernel, lg::dtc::kThreads, dt_smem);
     e = launch_ex(lg::dtc::down_tc_kernel, dim3(sms), dim3(lg::dtc::kThreads), dt_smem, s, pdl, a, DT, tm_w, tm_s,
                   tm_sh);

@@ -1,9 +1,10 @@
-"""The tensor-core one-token down kernel (LIVGLM_TC_DOWN=1) against the oracle.
+"""The CUDA-core one-token down kernel (LIVGLM_TC_DOWN=0) against the oracle.
 
-The library reads the switch once per process, so the one-token parity tests
-of test_gpu_parity.py run again in a child pytest with the switch on: every
-M = 1 call then computes the routed and shared down projections with tcgen05
-MMAs (livglm_b200/csrc/down_tc.cuh) instead of the CUDA-core kernel.
+One-token calls use the tensor-core down kernel (livglm_b200/csrc/down_tc.cuh)
+by default, which test_gpu_parity.py covers.  The library reads the switch
+once per process, so the one-token parity tests run again in a child pytest
+with the switch off: every M = 1 call then takes down1_stream_kernel, the
+fallback for geometries the tensor-core plan does not cover.
 """
 
 import os
@@ -25,8 +26,8 @@ ONE_TOKEN_TESTS = " or ".join([
 ])
 
 
-def test_one_token_parity_through_tensor_core_down(cuda, native_lib):
-    env = dict(os.environ, LIVGLM_TC_DOWN="1")
+def test_one_token_parity_through_cuda_core_down(cuda, native_lib):
+    env = dict(os.environ, LIVGLM_TC_DOWN="0")
     r = subprocess.run(
         [sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
          str(ROOT / "tests" / "test_gpu_parity.py"), "-k", ONE_TOKEN_TESTS],
