@@ -371,15 +371,15 @@ def run_ours(args) -> None:
             dist.destroy_process_group()
         return
 
+    peaks = measured_peaks()
+    by = layer_bytes(cfg, M, U)
+    # decode calls take the fused one-kernel layer when the library was told to
+    fused = M <= 4 and os.environ.get("LIVGLM_FUSED_LAYER", "") == "1"
     # kernels per layer call: fused layer 1; decode chain 5 (router logits,
     # select + dispatch, gate/up, down, combine), plus the activation split of
     # the tensor-core down kernel for one token (on unless LIVGLM_TC_DOWN=0)
     tc_down = M == 1 and os.environ.get("LIVGLM_TC_DOWN", "1") != "0"
     launches_per_step = 1 if fused else (6 if tc_down else 5) if M <= 4 else 6
-    peaks = measured_peaks()
-    by = layer_bytes(cfg, M, U)
-    # decode calls take the fused one-kernel layer when the library was told to
-    fused = M <= 4 and os.environ.get("LIVGLM_FUSED_LAYER", "") == "1"
     mean = {k: statistics.fmean(s[k] for s in stages) for k in _native.TRACE_STAGES} if stages else {}
     dominant = max(mean, key=mean.get) if mean else "gate_up"
     dom_ms = mean.get(dominant, float("nan"))
