@@ -129,11 +129,6 @@ __device__ __forceinline__ bool wait_warp1(uint64_t* b, unsigned parity, int* st
   return __all_sync(0xffffffffu, wait1(b, parity, status, site));
 }
 
-__device__ __forceinline__ void st_32x32b_x4(uint32_t taddr, uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v0), "r"(v1), "r"(v2),
-               "r"(v3));
-}
-
 // routed tiles [lo, hi) of CTA b (b >= n_sh)
 __device__ __forceinline__ void unit_range(const Cfg& c, int b, int P, int& lo, int& hi) {
   const int q = P - c.n_sh, i = b - c.n_sh;
@@ -318,13 +313,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto stage_scales = [&](int li) -> bool {  // routed tile li: SFA into tensor memory
       const int sb = li & 1;
       if (!wait_warp1(&sfull[sb], (li >> 1) & 1, a.status, kSiteScale)) return false;
+      // MMA m's scales sit in columns 4m + q (q = row quarter), so a chunk of
+      // eight MMAs is 32 consecutive columns: bytes 16g..16g+15 of this
+      // lane's row in each quarter, one 16-byte load per quarter
       const unsigned char* sc = sslot + sb * kTile * c.sc_bytes;
-      for (int m = 0; m < c.cols * 4; ++m) {
-        uint32_t v[4];
+      for (int g = 0; g < c.cols / 2; ++g) {
+        uint4 rq[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          v[q] = *reinterpret_cast<const uint16_t*>(sc + (32 * q + lane) * c.sc_bytes + 2 * m);
-        st_32x32b_x4(lanes + kColSfa + 96u * (li & 1) + 4u * m, v[0], v[1], v[2], v[3]);
+        for (int q = 0; q < 4; ++q) rq[q] = *reinterpret_cast<const uint4*>(sc + (32 * q + lane) * c.sc_bytes + 16 * g);
+        uint32_t v[32];
+#pragma unroll
+        for (int m = 0; m < 8; ++m)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t word = m < 2 ? rq[q].x : (m < 4 ? rq[q].y : (m < 6 ? rq[q].z : rq[q].w));
+            v[4 * m + q] = (word >> (16 * (m & 1))) & 0xFFFFu;
+          }
+        umma::st_32x32b_x32(lanes + kColSfa + 96u * (li & 1) + 32u * g, v);
       }
       umma::wait_st();
       __syncwarp();
