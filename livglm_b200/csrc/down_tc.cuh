@@ -14,9 +14,10 @@
 // ranges of the routed tiles (route-major), at most kMaxUnits tiles and two
 // routes each (checked on the host).
 //
-// Warps: 0-3 split the route activations, stage scale factors into tensor
+// Warps: 0-3 copy the split route activations, stage scale factors into tensor
 // memory and read the accumulators; warps 4 and 6 issue the MMAs of the even
-// and odd atom columns (one lane each, into their own accumulators); warp 5
+// and odd atom columns (one lane each, into their own accumulators), with
+// warps 7 and 8 joining for the 24-column shared tile (columns mod 4); warp 5
 // issues the TMA loads (one lane; 128-byte-swizzled 128 B x 128-row boxes
 // into a stage ring, no multicast) from the start, before the dependency
 // wait, since weights and routes are ready when this kernel launches.
@@ -44,10 +45,11 @@ constexpr int kTile = 128;         // output rows per tile (M of the MMA)
 constexpr int kBox = 16384;        // one 128 B x 128-row weight box
 constexpr int kMaxUnits = 3;       // routed tiles per CTA
 constexpr int kMaxStages = 10;
-constexpr int kThreads = 224;
+constexpr int kThreads = 288;
 constexpr int kCompute = 128;      // threads of warps 0-3
-constexpr int kMmaWarp = 4, kTmaWarp = 5, kMmaWarp1 = 6;  // two MMA issuers: one issuing thread
-                                                          // keeps at most one MMA per ~47 ns
+// MMA issuers: warps 4, 6 (and 7, 8 for the shared tile); one issuing thread
+// keeps at most one MMA per ~47 ns
+constexpr int kMmaWarp = 4, kTmaWarp = 5, kMmaWarp1 = 6;
 // tensor memory columns
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColD = 0;      // routed: 2 buffers x 2 accumulators x 32; shared: 8 x 16
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sfull[i], 1);
       mbar_init(&sfree[i], kCompute / 32);
       mbar_init(&sf_ready[i], kCompute / 32);
-      mbar_init(&dfull[i], 2);  // one commit per MMA issuer
+      mbar_init(&dfull[i], shared_cta ? 4 : 2);  // one commit per MMA issuer
     }
     mbar_fence_init();
   }
@@ -221,11 +223,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_trigger();
   }
   // ------------------------------- MMA issuer ---------------------------------
-  else if (warp == kMmaWarp || warp == kMmaWarp1) {
+  else if (warp == kMmaWarp || warp >= kMmaWarp1) {
     pdl_wait();
     pdl_trigger();
-    const int w = warp == kMmaWarp ? 0 : 1;  // this issuer's atom columns: w, w + 2, ...
-    if (lane == 0 && nu > 0) {
+    const int n_iss = shared_cta ? 4 : 2;
+    const int w = warp == kMmaWarp ? 0 : warp - kMmaWarp1 + 1;  // this issuer's atom columns: w, w + n_iss, ...
+    if (lane == 0 && nu > 0 && w < n_iss) {
       bool ok = true;
       const uint32_t id_mx = umma::idesc_mxf4(kTile, kBRows), id_bf = umma::idesc_bf16(kTile, kShBRows);
       for (int li = 0; li < nu && ok; ++li) {
@@ -236,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t dcol = tbase + kColD + 64u * db;
         const int ncols = shared_cta ? c.sh_cols : c.cols;
         const int rbuf = shared_cta ? 0 : (u_lo + li) / blocks - p_first;
-        for (int col = w; col < ncols; col += 2) {
+        for (int col = w; col < ncols; col += n_iss) {
           const int it = li * ncols + col, s = it % S;  // the producer's stage count
           ok = wait1(&full[s], (it / S) & 1, a.status, kSiteFull);
           if (!ok) break;
@@ -245,8 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (shared_cta) {
             const uint64_t dbd = umma::desc_sw128(smem_u32(bop + col * (kShBRows * 128)));
 #pragma unroll
-            for (int i = 0; i < 4; ++i)  // accumulator 4 w + i, first written at column w
-              umma::mma_bf16(tbase + kColD + 16u * (4 * w + i), da + 2 * i, dbd + 2 * i, id_bf, col >= 2);
+            for (int i = 0; i < 4; ++i)  // accumulator 2 w + (i & 1), first written at column w
+              umma::mma_bf16(tbase + kColD + 16u * (2 * w + (i & 1)), da + 2 * i, dbd + 2 * i, id_bf, col >= 4 || i >= 2);
           } else {
             const uint64_t dbd = umma::desc_sw128(smem_u32(bop + (rbuf * c.cols + col) * (kBRows * 128)));
 #pragma unroll
