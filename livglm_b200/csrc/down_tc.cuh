@@ -5,9 +5,10 @@
 //   ys[r]         = bf16( act_s . Wsd[r] )             shared, bf16 weights
 // computed as 128-row tiles with tcgen05 MMAs:
 //  - routed tile: A = 128 rows of the expert's MXFP4 down weights (E2M1 +
-//    UE8M0), B = the route's activations split into kTerms E2M1 terms (B rows
-//    0..kTerms-1 of a 32-row operand, umma.cuh), kind::mxf4 block-scaled
-//    MMAs over K = F, y = sum of the accumulator's kTerms columns;
+//    UE8M0), B = the route's activations split into kTerms E2M1 terms by
+//    split_act_kernel (B rows 0..kTerms-1 of a 32-row operand, umma.cuh),
+//    kind::mxf4 block-scaled MMAs over K = F, y = sum of the accumulator's
+//    kTerms columns;
 //  - shared tile: A = 128 bf16 rows, B = act_s as row 0 of a 16-row operand,
 //    kind::f16 MMAs.
 // Work split: CTA b < n_sh owns shared tile b; the other CTAs own contiguous
@@ -21,12 +22,11 @@
 // issues the TMA loads (one lane; 128-byte-swizzled 128 B x 128-row boxes
 // into a stage ring, no multicast) from the start, before the dependency
 // wait, since weights and routes are ready when this kernel launches.
-// Accumulators, scale-factor columns and activation operands are double
-// buffered so the MMAs of one tile overlap the epilogue of the previous one.
-// The MMAs of a tile are small (N = 32 or 16), so their time is the tensor
-// pipe's latency when they all accumulate into one place; they go round-robin
-// over several accumulators (2 per routed tile buffer, 8 for the shared tile)
-// that the epilogue adds up.
+// Accumulators and scale-factor columns are double buffered (two route
+// operands per CTA) so the MMAs of one tile overlap the epilogue of the
+// previous one.  One thread issues at most one tcgen05.mma per ~47 ns
+// (measured), so a tile's MMAs are spread over two issuing warps (four for
+// the shared tile), each into its own accumulators, which the epilogue adds.
 // Every wait is bounded; a timeout records a status word and ends the CTA.
 #pragma once
 #include <cuda.h>
@@ -55,7 +55,6 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColD = 0;      // routed: 2 buffers x 2 accumulators x 32; shared: 8 x 16
 constexpr uint32_t kColSfa = 128;  // 2 x 96 (24 MMAs x 4 row quarters)
 constexpr uint32_t kColSfb = 320;  // 2 routes x 96 (24 MMAs, 4-column aligned)
-constexpr int kMaxCols = 6;        // MXFP4 atom columns per routed row (F <= 1536)
 constexpr int kSiteFull = 21 << 8, kSiteEmpty = 22 << 8, kSiteScale = 23 << 8, kSiteSf = 24 << 8,
               kSiteD = 25 << 8, kSiteRoute = 26 << 8;
 
