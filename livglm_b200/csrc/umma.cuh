@@ -53,6 +53,13 @@ __host__ __device__ constexpr uint32_t idesc_mxf4(int M, int N) {
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Scale-factor ids of a block-scaled instruction descriptor (A: bits 29-30,
+// B: bits 4-5): the byte of the tensor-memory column where the MMA's first
+// scale sits, 0 or 2 for two block-32 scales per row.
+__host__ __device__ constexpr uint32_t idesc_sf_ids(int id) {
+  return (static_cast<uint32_t>(id) << 29) | (static_cast<uint32_t>(id) << 4);
+}
+
 // Instruction descriptor, kind::f16 with bf16 A and B (format 1), f32 D.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |

@@ -47,7 +47,8 @@ __global__ void __launch_bounds__(128, 1) tile_kernel(int kind, const uint8_t* w
   unsigned char* sa = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
   unsigned char* sb = sa + kRows * kAtom;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const bool mx = kind == 0;
+  const bool mx = kind == 0 || kind == 2;
+  const bool packed = kind == 2;  // two MMAs per scale column, told apart by the scale-factor ids
   const int brows = mx ? kBRowsMx : kBRowsBf;
   const int per_col = mx ? 256 : 64;  // K values per atom column
   const int ncol = K / per_col;
@@ -97,15 +98,23 @@ __global__ void __launch_bounds__(128, 1) tile_kernel(int kind, const uint8_t* w
     fence_async_smem();
     __syncthreads();
     if (mx) {
-      // scale factors of MMA i (blocks 2i, 2i+1 of this column) into tensor memory
+      // scale factors of MMA i (blocks 2i, 2i+1 of this column) into tensor memory:
+      // one column group per MMA, or (packed) MMAs 2j and 2j+1 in the low and
+      // high halves of column group j
       for (int i = 0; i < 4; ++i) {
+        const int col = packed ? 4 * (i >> 1) : 4 * i, shift = packed ? 16 * (i & 1) : 0;
+        if (packed && (i & 1)) continue;  // written together with MMA i - 1
         for (int q = 0; q < 4; ++q) {
           const int r = 32 * q + lane;
           const uint8_t* s = wscale + static_cast<size_t>(r) * (K / 32) + c * 8 + 2 * i;
-          st_32x32b_x1(lanes + kColSfa + 4 * i + q, static_cast<uint32_t>(s[0]) | (static_cast<uint32_t>(s[1]) << 8));
+          uint32_t v = static_cast<uint32_t>(s[0]) | (static_cast<uint32_t>(s[1]) << 8);
+          if (packed) v |= (static_cast<uint32_t>(s[2]) | (static_cast<uint32_t>(s[3]) << 8)) << 16;
+          st_32x32b_x1(lanes + kColSfa + col + q, v << shift);
         }
-        st_32x32b_x1(lanes + kColSfb + 4 * i,
-                     static_cast<uint32_t>(sfb[lane][2 * i]) | (static_cast<uint32_t>(sfb[lane][2 * i + 1]) << 8));
+        uint32_t vb = static_cast<uint32_t>(sfb[lane][2 * i]) | (static_cast<uint32_t>(sfb[lane][2 * i + 1]) << 8);
+        if (packed)
+          vb |= (static_cast<uint32_t>(sfb[lane][2 * i + 2]) | (static_cast<uint32_t>(sfb[lane][2 * i + 3]) << 8)) << 16;
+        st_32x32b_x1(lanes + kColSfb + col, vb << shift);
       }
       wait_st();
     }
@@ -116,7 +125,10 @@ __global__ void __launch_bounds__(128, 1) tile_kernel(int kind, const uint8_t* w
       const uint64_t da = desc_sw128(smem_addr(sa)), db = desc_sw128(smem_addr(sb));
       for (int i = 0; i < 4; ++i) {
         const bool acc = c > 0 || i > 0;
-        if (mx)
+        if (packed)  // scale-factor ids 0 / 2 pick the low / high half of the column
+          mma_mxf4(tbase + kColD, da + 2 * i, db + 2 * i, idesc | idesc_sf_ids(2 * (i & 1)),
+                   tbase + kColSfa + 4 * (i >> 1), tbase + kColSfb + 4 * (i >> 1), acc);
+        else if (mx)
           mma_mxf4(tbase + kColD, da + 2 * i, db + 2 * i, idesc, tbase + kColSfa + 4 * i, tbase + kColSfb + 4 * i, acc);
         else
           mma_bf16(tbase + kColD, da + 2 * i, db + 2 * i, idesc, acc);
@@ -150,8 +162,8 @@ __global__ void __launch_bounds__(128, 1) tile_kernel(int kind, const uint8_t* w
 extern "C" int lg_umma_selftest_tile(int kind, const uint8_t* w, const uint8_t* wscale, const uint16_t* x, int K,
                                      int terms, float* y, uint8_t* terms_out, uint8_t* term_scales_out, int* status,
                                      void* stream) {
-  if (kind != 0 && kind != 1) return 1;
-  if (kind == 0 && (K < 256 || K > 4096 || K % 256 || terms < 1 || terms > 32 || !wscale || !terms_out || !term_scales_out))
+  if (kind < 0 || kind > 2) return 1;
+  if (kind != 1 && (K < 256 || K > 4096 || K % 256 || terms < 1 || terms > 32 || !wscale || !terms_out || !term_scales_out))
     return 1;
   if (kind == 1 && (K < 64 || K > 4096 || K % 64)) return 1;
   if (!w || !x || !y || !status) return 1;

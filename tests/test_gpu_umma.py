@@ -78,6 +78,22 @@ def test_mxf4_tile_over_split_activations(umma_lib, cuda, K, T, xscale):
         np.testing.assert_array_equal(xt, x.astype(np.float64))
 
 
+def test_mxf4_tile_two_mmas_per_scale_column(umma_lib, cuda):
+    """Scales of MMAs 2j and 2j+1 packed into one tensor-memory column and told
+    apart by the instruction's scale-factor ids give the same bits as one
+    column group per MMA."""
+    K, T = 1024, 12
+    rng = np.random.default_rng(7)
+    w = rng.integers(0, 256, size=(128, K // 2), dtype=np.uint8)
+    ws = rng.integers(118, 128, size=(128, K // 32), dtype=np.uint8)
+    xb = bf16_vector(rng, K)
+    y0, t0, s0 = run(umma_lib, cuda, 0, w, ws, xb, K, T)
+    y2, t2, s2 = run(umma_lib, cuda, 2, w, ws, xb, K, T)
+    np.testing.assert_array_equal(t2, t0)
+    np.testing.assert_array_equal(s2, s0)
+    np.testing.assert_array_equal(y2.view(np.uint32), y0.view(np.uint32))
+
+
 @pytest.mark.parametrize("K", [64, 1536, 4096])
 def test_bf16_tile(umma_lib, cuda, K):
     rng = np.random.default_rng(K)
