@@ -33,10 +33,16 @@ ROUTED_EXPERT_RE = re.compile(
 )
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream_ptr(device: torch.device) -> int:
-    """Raw handle of the current stream of `device` (an int; no Stream object)."""
+    """Raw handle of the current stream of `device` (an int; no Stream object
+    where the torch build offers the raw query)."""
     index = device.index if device.index is not None else torch.cuda.current_device()
-    return torch._C._cuda_getCurrentRawStream(index)
+    if _raw_stream is not None:
+        return _raw_stream(index)
+    return torch.cuda.current_stream(index).cuda_stream
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -193,6 +199,8 @@ class ResidentExperts:
         self._cfg = _native.LgConfig.from_config(config)
         self._ws = Workspace()
         self._w: _native.LgWeights | None = None
+        self._w_key: tuple = ()
+        self._w_refs: tuple = ()
 
     # -- loading -----------------------------------------------------------
     def set_banks(self, gate_packed, gate_scale, up_packed, up_scale, down_packed, down_scale) -> None:
@@ -245,8 +253,16 @@ class ResidentExperts:
                        banks[("down_proj", "weight_packed")], banks[("down_proj", "weight_scale")])
 
     # -- native view -------------------------------------------------------
+    def _bank_key(self) -> tuple:
+        """Identity and address of the six bank tensors: the cached native table
+        is rebuilt when a bank is rebound or its storage replaced."""
+        banks = (self.gate_proj.weight_packed, self.gate_proj.weight_scale, self.up_proj.weight_packed,
+                 self.up_proj.weight_scale, self.down_proj.weight_packed, self.down_proj.weight_scale)
+        return tuple(id(t) for t in banks) + tuple(_ptr(t) for t in banks), banks
+
     def native_weights(self) -> _native.LgWeights:
-        if self._w is None:
+        key, banks = self._bank_key()
+        if self._w is None or self._w_key != key:
             g, u, dn = self.gate_proj, self.up_proj, self.down_proj
             for name, t in (("gate_proj", g.weight_packed), ("up_proj", u.weight_packed),
                             ("down_proj", dn.weight_packed)):
@@ -261,7 +277,7 @@ class ResidentExperts:
             w.up_scale_stride = u.weight_scale[0].numel()
             w.down_packed_stride = dn.weight_packed[0].numel()
             w.down_scale_stride = dn.weight_scale[0].numel()
-            self._w = w
+            self._w, self._w_key, self._w_refs = w, key, banks  # refs keep the ids unique
         return self._w
 
     # -- reference interface -------------------------------------------------

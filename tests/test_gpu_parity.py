@@ -254,6 +254,10 @@ def test_rebinding_weights_after_a_call(cuda, native_lib, golden_cfg0):
     got = moe(x)
     assert torch.equal(got, build_layer(cfg, t2)(x))
     assert not torch.equal(got, base)
+    up2 = t["up_packed"].flip(0).contiguous()
+    moe.experts.up_proj.weight_packed.data = up2  # same tensor object, new storage
+    t2["up_packed"] = up2
+    assert torch.equal(moe(x), build_layer(cfg, t2)(x))
 
 
 def test_checkpoint_names_drop_in(cuda, native_lib, golden_cfg0):
