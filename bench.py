@@ -39,9 +39,9 @@ CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.a
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
-# kernel, from an ncu capture of this bench (workload, stage, fused layer).
+# kernel, from an ncu capture of this bench's command (workload, stage)
 MEASURED_TRAFFIC = {
-    ("decode1", "gate_up", False): 80.53e6,  # profiles/stream_chain_cfg1_decode_M1.md
+    ("decode1", "gate_up"): 80.53e6,
 }
 
 
@@ -373,17 +373,15 @@ def run_ours(args) -> None:
 
     peaks = measured_peaks()
     by = layer_bytes(cfg, M, U)
-    # decode calls take the fused one-kernel layer when the library was told to
-    fused = M <= 4 and os.environ.get("LIVGLM_FUSED_LAYER", "") == "1"
-    # kernels per layer call: fused layer 1; decode chain 5 (router logits,
-    # select + dispatch, gate/up, down, combine), plus the activation split of
-    # the tensor-core down kernel for one token (on unless LIVGLM_TC_DOWN=0)
+    # kernels per layer call: decode chain 5 (router logits, select + dispatch,
+    # gate/up, down, combine), plus the activation split of the tensor-core
+    # down kernel for one token (on unless LIVGLM_TC_DOWN=0)
     tc_down = M == 1 and os.environ.get("LIVGLM_TC_DOWN", "1") != "0"
-    launches_per_step = 1 if fused else (6 if tc_down else 5) if M <= 4 else 6
+    launches_per_step = (6 if tc_down else 5) if M <= 4 else 6
     mean = {k: statistics.fmean(s[k] for s in stages) for k in _native.TRACE_STAGES} if stages else {}
     dominant = max(mean, key=mean.get) if mean else "gate_up"
     dom_ms = mean.get(dominant, float("nan"))
-    dom_bytes = by["layer"] if fused else by[dominant]  # the fused kernel's time is all in one stage
+    dom_bytes = by[dominant]
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9 if dom_ms and dom_ms > 0 else None
     ms_step = ms / args.steps
     value = world * M * args.steps / (ms * 1e-3)
@@ -401,9 +399,9 @@ def run_ours(args) -> None:
                    "l2": f"inputs larger than L2: {L} distinct layers cycled ({L * 1.33:.1f} GB of weights)",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "operands": "x bf16, routed w MXFP4 (E2M1+E8M0), shared w bf16, f32 accumulate, f32 out"},
-        "roofline": {"bound": "hbm", "kernel": "layer_kernel" if fused else dominant, "achieved": achieved, "peak": peaks["hbm_gbs"],
+        "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": (achieved / peaks["hbm_gbs"]) if achieved else None,
-                     "traffic": MEASURED_TRAFFIC.get((args.workload, dominant, fused)), "peak_source": peaks["source"],
+                     "traffic": MEASURED_TRAFFIC.get((args.workload, dominant)), "peak_source": peaks["source"],
                      "algorithmic_bytes_per_launch": dom_bytes, "launch_ms": dom_ms},
         "e2e": {"value": world * M * K_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": M * cfg.hidden_size * 2, "d2h_bytes_per_step": M * cfg.hidden_size * 4,

@@ -20,12 +20,10 @@
  *  - Device-side failures cannot be returned from a stream-ordered call: the
  *    first 4 bytes of the workspace are a status word that kernels set when a
  *    bounded wait gives up (LG_ERR_TIMEOUT in the low byte, the waiting site
- *    above it).  Zero the workspace once after allocating it: besides the
- *    status word it holds the grid counters of the fused decode kernel, which
- *    every call leaves at zero for the next one (a call that finds them
- *    nonzero computes garbage and sets LG_ERR_WORKSPACE in the status word).
- *    The library never clears the status word; it stays set until the caller
- *    clears it.
+ *    above it) or when a routing table holds an expert id outside [0, E)
+ *    (LG_ERR_INVALID_ARG in the low byte).  Zero it once after allocating the
+ *    workspace.  The library never clears it: it stays set until the caller
+ *    clears it, so one read after a batch of calls reports any of them.
  *  - Routed expert tensors are banks: expert e's tensor starts at
  *    base + e * stride (bytes) and is byte-identical to the checkpoint's
  *      model.language_model.layers.{L}.mlp.experts.{e}.{gate,up}_proj.weight_packed  U8 [F, d/2]
@@ -193,14 +191,41 @@ int lg_moe_forward(const lg_moe_config *cfg, const lg_moe_weights *w,
  *  - Every call on a device shares the one array and it keeps the last
  *    call's contents; calls that overlap on the GPU (different streams, or
  *    threads without ordering) race on it.  Each call zeroes what must start
- *    at zero itself.
+ *    at zero for that call itself.  The array's first 4 bytes are the status
+ *    word of the workspace convention above: no call clears it, and since the
+ *    array is private, read and clear it with lg_moe_static_scratch_status.
  *  - The array occupies 4 MiB on every GPU where the library's device code
- *    is loaded, until the process exits.
+ *    is loaded, until the process exits.  The resolved address is cached per
+ *    device for the life of the process, so a cudaDeviceReset between calls
+ *    is not supported.
  */
 int lg_moe_forward_static_scratch(const lg_moe_config *cfg, const lg_moe_weights *w,
                                   const uint16_t *x, int64_t M, float *out,
                                   float *weights_out, uint32_t *indices_out,
                                   void *stream);
+
+/*
+ * Status word of the fixed scratch used by lg_moe_forward_static_scratch on
+ * the current device.  No counterpart in the reference.  Waits for `stream`,
+ * copies the word into *status_out (host) and, if `clear` is nonzero, zeroes
+ * it.  0 means no device-side failure since the last clear.  Allocates
+ * nothing.
+ */
+int lg_moe_static_scratch_status(int clear, int32_t *status_out, void *stream);
+
+/*
+ * Check of the device-side failure reporting.  No counterpart in the
+ * reference (its waits are host-side MLX evaluations).  Launches one kernel
+ * whose bounded waits (the same wait routines the MoE kernels use, with a
+ * limit of `limit_ns`, 1 us .. 2 s) wait on an mbarrier that never completes
+ * and on a flag that nothing sets: they give up after the limit and the
+ * kernel returns, the context staying usable.  status: device, 16-byte
+ * aligned, four int32 words, zeroed here first; afterwards status[0] (the
+ * warp-wide wait of the streaming kernels) and status[1] (the hinted wait of
+ * the tensor-core kernels) hold LG_ERR_TIMEOUT | 30 << 8, status[2] (a flag
+ * wait) LG_ERR_TIMEOUT | 31 << 8, and status[3] is the flag, still 0.
+ */
+int lg_moe_check_wait_timeout(int64_t limit_ns, int32_t *status, void *stream);
 
 /*
  * Stage tracing.  Counterpart of the reference's per-layer trace spans

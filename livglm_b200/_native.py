@@ -93,6 +93,8 @@ SIGNATURES = {
     "lg_moe_combine": (ctypes.c_int, [_CFG, _P, _P, _P, _I64, _P, _P]),
     "lg_moe_forward": (ctypes.c_int, [_CFG, _W, _P, _I64, _P, _P, _P, _P, ctypes.c_size_t, _P]),
     "lg_moe_forward_static_scratch": (ctypes.c_int, [_CFG, _W, _P, _I64, _P, _P, _P, _P]),
+    "lg_moe_static_scratch_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int32), _P]),
+    "lg_moe_check_wait_timeout": (ctypes.c_int, [_I64, _P, _P]),
     "lg_moe_trace_enable": (ctypes.c_int, [ctypes.c_int]),
     "lg_moe_trace_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_float), ctypes.c_int]),
 }

@@ -20,10 +20,6 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OUT = PKG / "_lib" / "liblivglm_moe.so"
 SOURCES = ["moe_capi.cu", "moe_noalloc.cu"]
-# self-check of the tensor-core (tcgen05) building blocks, a separate library
-# so the MoE C ABI stays the reference-facing surface
-UMMA_OUT = PKG / "_lib" / "liblivglm_umma_selftest.so"
-UMMA_SOURCES = ["umma_selftest.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -34,20 +30,21 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
-def _stale(out: Path) -> bool:
+def _stale(out: Path, sources: list[Path]) -> bool:
     if not out.exists():
         return True
-    newest = max(p.stat().st_mtime for p in list(CSRC.glob("*.cu*")) + list((ROOT / "include").glob("*.h")))
-    return newest > out.stat().st_mtime
+    deps = list(CSRC.glob("*.cu*")) + list((ROOT / "include").glob("*.h")) + list(sources)
+    return max(p.stat().st_mtime for p in deps) > out.stat().st_mtime
 
 
-def _build_one(out: Path, sources: list[str], force: bool, verbose: bool) -> Path:
-    if not force and not _stale(out):
+def build_library(out: Path, sources: list[Path], force: bool = False, verbose: bool = False) -> Path:
+    """nvcc -shared for sm_100a with the package's headers on the include path."""
+    if not force and not _stale(out, sources):
         return out
     out.parent.mkdir(parents=True, exist_ok=True)
     tmp = out.with_suffix(f".{os.getpid()}.tmp")
     cmd = [nvcc(), "-O3", "-std=c++17", *ARCH, "-lineinfo", "-shared", "-Xcompiler", "-fPIC",
-           f"-I{ROOT / 'include'}", f"-I{CSRC}", *[str(CSRC / s) for s in sources], "-o", str(tmp)]
+           f"-I{ROOT / 'include'}", f"-I{CSRC}", *[str(s) for s in sources], "-o", str(tmp)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)
@@ -56,8 +53,7 @@ def _build_one(out: Path, sources: list[str], force: bool, verbose: bool) -> Pat
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
-    _build_one(UMMA_OUT, UMMA_SOURCES, force, verbose)
-    return _build_one(OUT, SOURCES, force, verbose)
+    return build_library(OUT, [CSRC / s for s in SOURCES], force, verbose)
 
 
 if __name__ == "__main__":

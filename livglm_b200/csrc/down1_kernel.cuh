@@ -22,20 +22,20 @@
 //    no byte loads.
 // The next chunk's loads are issued while the current sums are reduced.
 #pragma once
-#include "layer_kernel.cuh"
+#include "decode_helpers.cuh"
 
 namespace lg {
 namespace down1 {
 
-using layer::bf16x8_to_f16x8_scaled;
-using layer::absmax8_bf16;
-using layer::act_shift;
-using layer::fold4;
-using layer::lds128;
-using layer::lds32;
-using layer::mx_dot_reg;
-using layer::reduce_scatter;
-using layer::wait_all;
+using dh::bf16x8_to_f16x8_scaled;
+using dh::absmax8_bf16;
+using dh::act_shift;
+using dh::fold4;
+using dh::lds128;
+using dh::lds32;
+using dh::mx_dot_reg;
+using dh::reduce_scatter;
+using dh::wait_all;
 
 constexpr int kWarps = 8;
 constexpr int kConsumers = kWarps * 32;

@@ -109,7 +109,8 @@ __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x,
 // one (or with a long one) was seen to resume microseconds after the phase
 // completed, which every stage handoff of this kernel would pay.
 constexpr unsigned kHintNs = 100;
-__device__ __forceinline__ bool wait1(uint64_t* b, unsigned parity, int* status, int site) {
+__device__ __forceinline__ bool wait1(uint64_t* b, unsigned parity, int* status, int site,
+                                      unsigned long long limit_ns = kWaitLimitNs) {
   const unsigned long long t0 = globaltimer_ns();
   for (;;) {
     uint32_t done;
@@ -119,7 +120,7 @@ __device__ __forceinline__ bool wait1(uint64_t* b, unsigned parity, int* status,
         : "r"(smem_u32(b)), "r"(parity), "r"(kHintNs)
         : "memory");
     if (done) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       if (status) atomicExch(status, 6 | site);
       return false;
     }

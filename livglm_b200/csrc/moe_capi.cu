@@ -11,7 +11,7 @@
 #include <utility>
 
 #include "livglm_moe.h"
-#include "layer_kernel.cuh"
+#include "decode_kernels.cuh"
 #include "stream_kernels.cuh"
 #include "moe_kernels.cuh"
 #include "down1_kernel.cuh"
@@ -106,7 +106,7 @@ int validate_tokens(int64_t M, const lg_moe_config* c) {
 }
 
 struct Layout {
-  size_t status, logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, xs, bimg, bsc, sync,
+  size_t status, logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, xs, bimg, bsc,
       total;
 };
 
@@ -117,10 +117,6 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   Layout L{};
   size_t o = 0;
   L.status = o;  o += up(4);
-  // grid counters right after the status word: the same offset for every M,
-  // so a workspace (or the static scratch) reused with another token count
-  // still finds the counters the previous call left at zero
-  L.sync = o;    o += up(lg::layer::kSyncWords * 4);
   L.logits = o;  o += up(m * E * 4);
   L.weights = o; o += up(m * k * 4);
   L.indices = o; o += up(m * k * 4);
@@ -630,205 +626,27 @@ int launch_decode(const lg_moe_config* c, const lg_moe_weights* w, const uint16_
   return launch_decode_t<4>(c, w, x, M, out, wts, idx, ws, L, x_host, slot, s);
 }
 
-// ---- fused decode layer (M <= 4): one cooperative kernel ----------------------
-int gcd_int(int x, int y) {
-  while (y) { const int t = x % y; x = y; y = t; }
-  return x;
-}
-
-template <int TT>
-size_t layer_static_smem() {
-  static size_t v = 0;
-  static bool done = false;
-  if (!done) {
-    cudaFuncAttributes fa{};
-    if (cudaFuncGetAttributes(&fa, lg::layer::layer_kernel<TT>) == cudaSuccess) v = fa.sharedSizeBytes;
-    done = true;
+// ---- bounded-wait check ---------------------------------------------------------
+// Runs the library's bounded waits, each with the given limit, against an
+// mbarrier that never completes (initialised for one arrival that nobody
+// makes) and a global flag that nothing sets: every wait must give up, record
+// 6 | site in its status word and let the kernel return, leaving the context
+// usable.  status[0]: the warp-wide wait of the streaming kernels (warp 0);
+// status[1]: the hinted wait of the tensor-core kernels (warp 1, one lane);
+// status[2]: the flag wait (warp 1, one lane); status[3]: the flag, zero.
+__global__ void wait_timeout_kernel(unsigned long long limit_ns, int* status) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    lg::mbar_init(&bar, 1);
+    lg::mbar_fence_init();
   }
-  return v;
-}
-
-size_t round128(size_t v) { return (v + 127) / 128 * 128; }
-
-// One token, phase 2: the most routes one CTA's routed down slice spans and
-// the most output blocks one CTA can complete (same split as lg::layer::Down1).
-void one_token_split(int d, int R, int grid, int unit, bool shared, int* rr_max, int* blocks_max, int* rows_max) {
-  *rr_max = 0;
-  *blocks_max = 0;
-  *rows_max = 0;
-  auto lo = [&](long long c) { return static_cast<int>(c * d / grid); };
-  auto blk = [&](int r) { return static_cast<int>((static_cast<long long>(r + 1) * grid - 1) / d); };
-  const long long nu = static_cast<long long>(R) * d / unit;
-  for (int b = 0; b < grid; ++b) {
-    const int u_lo = unit * static_cast<int>(b * nu / grid), u_hi = unit * static_cast<int>((b + 1) * nu / grid);
-    int nb = shared ? 1 : 0, nr = 0;
-    for (int u = u_lo; u < u_hi;) {
-      const int p = u / d, end = std::min(u_hi, (p + 1) * d) - p * d;
-      ++nr;
-      for (int r = u - p * d; r < end;) {
-        const int c = blk(r);
-        r = std::min(end, lo(c + 1));
-        ++nb;
-      }
-      u = p * d + end;
-    }
-    *rr_max = std::max(*rr_max, nr);
-    *blocks_max = std::max(*blocks_max, nb);
-    *rows_max = std::max(*rows_max, u_hi - u_lo);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    lg::mbar_wait_warp(&bar, 0, status, lg::kSiteSelfTestBar, limit_ns);
+  } else if (threadIdx.x == 32) {
+    lg::dtc::wait1(&bar, 0, status + 1, lg::kSiteSelfTestBar, limit_ns);
+    lg::flag_wait(reinterpret_cast<const unsigned*>(status + 3), status + 2, lg::kSiteSelfTestFlag, limit_ns);
   }
-}
-
-// Shared-memory plan: ring stages of the largest chunk, the union of the
-// phase-1 activations and the phase-2 activations, the per-CTA y rows.
-bool plan_layer(const lg_moe_config* c, int M, int TT, size_t static_smem, int grid, lg::layer::Plan* P,
-                size_t* dyn) {
-  using namespace lg::layer;
-  const size_t d = c->hidden_size, F = c->moe_intermediate_size, Fs = F * c->n_shared_experts;
-  const size_t G = d / 32, G2 = F / 32, R = static_cast<size_t>(M) * c->num_experts_per_tok;
-  size_t stage = std::max<size_t>(d * 4, 2 * kGuRows * (d / 2) + 2 * kGuRows * G);
-  if (Fs > 0) stage = std::max<size_t>(stage, 2 * kShGuRows * d * 2);
-  const int unit = 16 / gcd_int(static_cast<int>(G2), 16);
-  const int nunits = static_cast<int>(d) / unit;
-  const int rows_max = unit * ((nunits + grid - 1) / grid);
-  size_t x_bytes, y_bytes;
-  int rr_max = 0, yb_rows = 0;
-  size_t yb_off = 0;
-  if (TT == 1) {
-    // one token: routed down chunks of kDn1Rows rows, shared down chunks of
-    // kShDnRows rows; x, then act_s and this CTA's act rows
-    int blocks_max = 0;
-    if (grid > kMaxGrid) return false;
-    one_token_split(static_cast<int>(d), static_cast<int>(R), grid, unit, Fs > 0, &rr_max, &blocks_max, &yb_rows);
-    if (blocks_max > kMaxComb) return false;
-    stage = std::max<size_t>(stage, kDn1Rows * (F / 2 + G2));
-    if (Fs > 0) stage = std::max<size_t>(stage, kShDnRows * Fs * 2);
-    yb_off = round128(2 * d * 2 + Fs * 2 + static_cast<size_t>(rr_max) * F * 2);
-    const size_t sh_rows = (d + grid - 1) / grid;
-    x_bytes = round128(yb_off + (static_cast<size_t>(yb_rows) + sh_rows) * 2);
-    y_bytes = 0;
-  } else {
-    x_bytes = round128(std::max<size_t>(2 * static_cast<size_t>(TT) * d * 2, R * F * 2 + M * Fs * 2));
-    y_bytes = round128((R + TT) * static_cast<size_t>(rows_max) * 4);
-  }
-  stage = round128(stage);
-  const size_t budget = 227 * 1024 - static_smem;
-  if (x_bytes + y_bytes + 2 * stage > budget) return false;
-  const int stages = static_cast<int>(std::min<size_t>(kMaxStages, (budget - x_bytes - y_bytes) / stage));
-  const int sub = static_cast<int>(std::min<size_t>(kDnRowsMax, stage / (F / 2 + G2))) / unit * unit;
-  if (sub < unit) return false;
-  const int sh = Fs > 0 ? static_cast<int>(std::min<size_t>(kShDnRows, stage / (Fs * 2))) : 1;
-  if (sh < 1) return false;
-  P->stages = stages;
-  P->stage_bytes = static_cast<int>(stage);
-  P->x_off = static_cast<int>(stages * stage);
-  P->y_off = static_cast<int>(P->x_off + x_bytes);
-  P->rpr = static_cast<int>(stage / (d * 4));
-  P->unit = unit;
-  P->sub_rows = sub;
-  P->sh_rows = sh;
-  P->rows_max = rows_max;
-  P->act_off = P->x_off + static_cast<int>(2 * d * 2);
-  P->rr_max = rr_max;
-  P->yb_off = P->x_off + static_cast<int>(yb_off);
-  P->yb_rows = yb_rows;
-  *dyn = P->y_off + y_bytes;
-  return true;
-}
-
-template <int TT>
-bool layer_fits_t(const lg_moe_config* c, int M) {
-  lg::layer::Plan P;
-  size_t dyn = 0;
-  return plan_layer(c, M, TT, layer_static_smem<TT>(), num_sms(), &P, &dyn);
-}
-
-// Decode path choice: the chain of stream kernels (default) or the fused
-// one-kernel layer, LIVGLM_FUSED_LAYER=1 (read once per process).
-bool fused_layer_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("LIVGLM_FUSED_LAYER");
-    return v && v[0] == '1';
-  }();
-  return on;
-}
-
-// The fused kernel needs: 1..4 tokens, M*k <= 32 routes, E <= 256 router
-// experts in <= 32 groups, d % 64 == 0, 16-byte aligned scale banks (every
-// bulk copy starts and ends on 16 bytes) and a shared-memory plan.
-bool layer_fits(const lg_moe_config* c, const lg_moe_weights* w, int64_t M) {
-  using namespace lg::layer;
-  if (M < 1 || M > lg::kDecodeMaxTokens) return false;
-  const long long R = M * c->num_experts_per_tok;
-  if (R > kMaxRoutes || c->n_routed_experts > kMaxExperts || c->n_group > kMaxGroups) return false;
-  if (c->hidden_size % 64) return false;
-  // one token: activation words in registers, scale bytes read as words
-  if (M == 1) {
-    const int F = c->moe_intermediate_size, Fs = F * c->n_shared_experts;
-    if (c->hidden_size > 32 * 32 * kXcg || c->hidden_size % 128) return false;
-    if (F > 16 * 32 * kDcg || F % 128 || Fs > 32 * 8 * kScg) return false;
-  }
-  if (!aligned(w->gate_scale, 16) || !aligned(w->up_scale, 16) || !aligned(w->down_scale, 16)) return false;
-  if (w->gate_scale_stride % 16 || w->up_scale_stride % 16 || w->down_scale_stride % 16) return false;
-  const int m = static_cast<int>(M);
-  return m <= 1 ? layer_fits_t<1>(c, m) : m <= 2 ? layer_fits_t<2>(c, m) : layer_fits_t<4>(c, m);
-}
-
-template <int TT>
-int launch_layer_t(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M, float* out,
-                   float* wts, uint32_t* idx, void* ws, const Layout& L, int slot, cudaStream_t s) {
-  using namespace lg::layer;
-  const int grid = num_sms();
-  Plan pl;
-  size_t dyn = 0;
-  if (!plan_layer(c, M, TT, layer_static_smem<TT>(), grid, &pl, &dyn))
-    return fail(LG_ERR_UNSUPPORTED, "fused decode layer does not fit in shared memory");
-  Args a{};
-  a.M = M; a.d = c->hidden_size; a.F = c->moe_intermediate_size; a.Fs = a.F * c->n_shared_experts;
-  a.E = c->n_routed_experts; a.k = c->num_experts_per_tok; a.G = c->n_group; a.g = c->topk_group;
-  a.norm = c->norm_topk_prob; a.scale = c->routed_scaling_factor; a.limit = c->swiglu_limit;
-  a.x = x; a.Wr = w->router_weight; a.bias = w->router_bias;
-  a.gate_p = w->gate_packed; a.gate_s = w->gate_scale; a.up_p = w->up_packed; a.up_s = w->up_scale;
-  a.down_p = w->down_packed; a.down_s = w->down_scale;
-  a.gate_ps = w->gate_packed_stride; a.gate_ss = w->gate_scale_stride;
-  a.up_ps = w->up_packed_stride; a.up_ss = w->up_scale_stride;
-  a.down_ps = w->down_packed_stride; a.down_ss = w->down_scale_stride;
-  a.sh_gate = w->shared_gate; a.sh_up = w->shared_up; a.sh_down = w->shared_down;
-  a.logits = at<float>(ws, L.logits); a.w_out = wts; a.i_out = idx;
-  a.act = at<uint16_t>(ws, L.act); a.act_s = at<uint16_t>(ws, L.act_s);
-  a.y = at<uint16_t>(ws, L.y); a.ys = at<uint16_t>(ws, L.ys);
-  a.out = out; a.status = at<int>(ws, L.status); a.sync = at<unsigned>(ws, L.sync);
-  cudaError_t e = cudaFuncSetAttribute(layer_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(dyn));
-  if (e != cudaSuccess) return cuda_check(e, "fused layer smem attribute");
-  int occ = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, layer_kernel<TT>, kThreads, dyn);
-  if (e != cudaSuccess) return cuda_check(e, "fused layer occupancy");
-  if (occ < 1) return fail(LG_ERR_UNSUPPORTED, "fused decode layer: no CTA fits on an SM");
-  trace_mark(slot, 1, s);
-  trace_mark(slot, 2, s);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = dyn;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, layer_kernel<TT>, a, pl);
-  if (e != cudaSuccess) return cuda_check(e, "fused layer launch");
-  trace_mark(slot, 3, s);
-  trace_mark(slot, 4, s);
-  trace_mark(slot, 5, s);
-  return LG_OK;
-}
-
-int launch_layer(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M, float* out,
-                 float* wts, uint32_t* idx, void* ws, const Layout& L, int slot, cudaStream_t s) {
-  if (M <= 1) return launch_layer_t<1>(c, w, x, M, out, wts, idx, ws, L, slot, s);
-  if (M <= 2) return launch_layer_t<2>(c, w, x, M, out, wts, idx, ws, L, slot, s);
-  return launch_layer_t<4>(c, w, x, M, out, wts, idx, ws, L, slot, s);
 }
 
 // ---- stage tracing ------------------------------------------------------------
@@ -911,6 +729,17 @@ int lg_moe_trace_read(float* stage_ms, int max_calls) {
 
 
 int lg_moe_abi_version(void) { return LG_MOE_ABI_VERSION; }
+
+int lg_moe_check_wait_timeout(int64_t limit_ns, int32_t* status, void* stream) {
+  if (!status || !aligned(status, 16)) return fail(LG_ERR_INVALID_ARG, "wait check: status must be 16-byte aligned");
+  if (limit_ns < 1000 || limit_ns > 2000000000LL)
+    return fail(LG_ERR_INVALID_ARG, "wait check: limit %lld ns outside 1 us .. 2 s", static_cast<long long>(limit_ns));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(status, 0, 16, s);
+  if (e != cudaSuccess) return cuda_check(e, "wait check memset");
+  wait_timeout_kernel<<<1, 64, 0, s>>>(static_cast<unsigned long long>(limit_ns), status);
+  return cuda_check(cudaGetLastError(), "wait check launch");
+}
 
 const char* lg_moe_last_error(void) { return g_err; }
 
@@ -1049,7 +878,7 @@ int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint
   int* active = at<int>(workspace, L.active);
   const int slot = trace_slot();
   trace_mark(slot, 0, s);
-  if (decode_fits(cfg, w, M) && !(fused_layer_enabled() && layer_fits(cfg, w, M)))
+  if (decode_fits(cfg, w, M))
     return launch_decode(cfg, w, x, m, out, wts, idx, workspace, L, x_host, slot, s);
   if (x_host) {  // the other paths read x many times: one copy into HBM first
     uint16_t* xs = at<uint16_t>(workspace, L.xs);
@@ -1058,8 +887,6 @@ int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint
       return rc;
     x = xs;
   }
-  if (fused_layer_enabled() && layer_fits(cfg, w, M))
-    return launch_layer(cfg, w, x, m, out, weights_out, indices_out, workspace, L, slot, s);
   if ((rc = cuda_check(cudaMemsetAsync(counts, 0, cfg->n_routed_experts * sizeof(int), s), "memset"))) return rc;
   if ((rc = launch_router(cfg, x, m, w->router_weight, w->router_bias, at<float>(workspace, L.logits), wts, idx,
                           counts, s)))

@@ -57,6 +57,25 @@ int scratch_for_current_device(void** out) {
 
 }  // namespace
 
+extern "C" int lg_moe_static_scratch_status(int clear, int32_t* status_out, void* stream) {
+  if (!status_out) return lg_internal_set_error(LG_ERR_INVALID_ARG, "static-scratch status: NULL status_out");
+  void* scratch = nullptr;
+  const int rc = scratch_for_current_device(&scratch);
+  if (rc != LG_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t word = 0;
+  cudaError_t e = cudaMemcpyAsync(&word, scratch, sizeof word, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess && clear) e = cudaMemsetAsync(scratch, 0, sizeof word, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    char msg[256];
+    snprintf(msg, sizeof msg, "static-scratch status: %s", cudaGetErrorString(e));
+    return lg_internal_set_error(LG_ERR_CUDA, msg);
+  }
+  *status_out = word;
+  return LG_OK;
+}
+
 extern "C" int lg_moe_forward_static_scratch(const lg_moe_config* cfg, const lg_moe_weights* w,
                                              const uint16_t* x, int64_t M, float* out,
                                              float* weights_out, uint32_t* indices_out, void* stream) {

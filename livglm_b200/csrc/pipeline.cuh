@@ -15,6 +15,7 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 enum WaitSite : int {
   kSiteGuFull = 1 << 8, kSiteGuEmpty = 2 << 8, kSiteGuDrain = 3 << 8,
   kSiteDnFull = 4 << 8, kSiteDnEmpty = 5 << 8, kSiteDnDrain = 6 << 8,
+  kSiteSelfTestBar = 30 << 8, kSiteSelfTestFlag = 31 << 8,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -49,21 +50,43 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, int* status, int site) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, int* status, int site,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(b, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (!mbar_try_wait(b, parity)) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       if (status) atomicExch(status, 6 | site);
       return false;
     }
   }
   return true;
 }
+// Bounded wait until the global word *flag is nonzero (acquire loads, polls
+// backed off by poll_ns); on timeout the status word records 6 | site.
+__device__ __forceinline__ bool flag_wait(const unsigned* flag, int* status, int site,
+                                          unsigned long long limit_ns = kWaitLimitNs, unsigned poll_ns = 256) {
+  auto load = [&] {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    return v;
+  };
+  if (load()) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (!load()) {
+    if (globaltimer_ns() - t0 > limit_ns) {
+      if (status) atomicExch(status, 6 | site);
+      return false;
+    }
+    __nanosleep(poll_ns);
+  }
+  return true;
+}
 // mbar_wait by every lane of a warp with a warp-uniform result, so the
 // shuffles that follow never see lanes that disagree about a timeout
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* b, unsigned parity, int* status, int site) {
-  return __all_sync(0xffffffffu, mbar_wait(b, parity, status, site));
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* b, unsigned parity, int* status, int site,
+                                               unsigned long long limit_ns = kWaitLimitNs) {
+  return __all_sync(0xffffffffu, mbar_wait(b, parity, status, site, limit_ns));
 }
 // contiguous global -> shared copy completing `bytes` of transactions on `bar`;
 // dst, src and bytes must be multiples of 16

@@ -1,5 +1,6 @@
 """Tensor-core (tcgen05) building blocks against their checkers, on one
-128-row tile (livglm_b200/csrc/umma_selftest.cu):
+128-row tile (tests/csrc/umma_selftest.cu, built by tests/build_selftest.py
+over the product's livglm_b200/csrc/umma.cuh):
 
 * the E2M1 activation split equals its numpy restatement (tests/umma_split.py)
   byte for byte;
@@ -16,8 +17,8 @@ import numpy as np
 import pytest
 import torch
 
-from livglm_b200 import build
 from oracle import moe_oracle as mo
+from tests import build_selftest
 from tests.umma_split import pack, reconstruct, split
 
 pytestmark = pytest.mark.gpu
@@ -27,9 +28,7 @@ _P = ctypes.c_void_p
 
 @pytest.fixture(scope="module")
 def umma_lib(cuda):
-    if not build.UMMA_OUT.exists():
-        build.build()
-    lib = ctypes.CDLL(str(build.UMMA_OUT))
+    lib = ctypes.CDLL(str(build_selftest.build()))
     fn = lib.lg_umma_selftest_tile
     fn.restype = ctypes.c_int
     fn.argtypes = [ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P, _P, _P]

@@ -62,12 +62,19 @@ def test_static_scratch_forward_matches_workspace_forward(cuda, native_lib, M):
     w = moe.native_weights()
     x = synthetic.hidden_states(cfg, M, seed=11 + M, device=cuda)
     ref_out, ref_w, ref_idx = _forward_with_workspace(lib, c, w, x, M, cuda)
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    st = ctypes.c_int32(-1)
+    _native.check(lib.lg_moe_static_scratch_status(1, ctypes.byref(st), stream), "status")  # start clean
     for _ in range(2):  # two calls in a row share (and reuse) the fixed scratch
         out, wts, idx = _forward_static(lib, c, w, x, M, cuda)
         torch.cuda.synchronize()
         np.testing.assert_array_equal(to_numpy(idx), to_numpy(ref_idx))
         np.testing.assert_array_equal(to_numpy(wts), to_numpy(ref_w))
         assert_close(to_numpy(out), to_numpy(ref_out))
+        # the status word inside the fixed array: no device-side failure
+        st.value = -1
+        _native.check(lib.lg_moe_static_scratch_status(0, ctypes.byref(st), stream), "status")
+        assert st.value == 0
 
 
 def test_static_scratch_rejects_too_many_tokens(native_lib):
