@@ -16,6 +16,7 @@
 #include "moe_kernels.cuh"
 #include "down1_kernel.cuh"
 #include "down_tc.cuh"
+#include "grouped_tc.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -107,8 +108,33 @@ int validate_tokens(int64_t M, const lg_moe_config* c) {
 
 struct Layout {
   size_t status, logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, xs, bimg, bsc,
-      total;
+      xterm, xtsc, aterm, atsc, tiles, inv, total;
+  bool tc;  // batched tensor-core buffers reserved
 };
+
+// Batched calls of at least this many tokens run the tensor-core grouped GEMMs
+// (grouped_tc.cuh) when the geometry allows; smaller ones the CUDA-core
+// grouped GEMV.  kTcTerms E2M1 terms carry each bf16 activation.
+constexpr int kTcMinTokens = 64;
+constexpr int kTcTerms = lg::gtc::kTerms;
+
+// Geometry the batched tensor-core kernels take: whole 256-value atoms and
+// 16-byte scale rows along F (F a multiple of 512), scale rows of at most 256
+// bytes (d, F <= 8192), shared width in 64-value atoms, and d a multiple of
+// 1024: the gate/up kernel gathers the token-term scale rows (d/32 bytes) four
+// at a time, and a tensor copy's shared-memory destination must sit on 128
+// bytes, so 4 * d/32 must be a multiple of 128.
+bool tc_geometry(const lg_moe_config* c) {
+  const int d = c->hidden_size, F = c->moe_intermediate_size, Fs = F * c->n_shared_experts;
+  return d % 1024 == 0 && d <= 8192 && F % 512 == 0 && F <= 8192 && Fs % 64 == 0 && c->n_routed_experts <= 1024;
+}
+bool tc_batched_env() {
+  static const bool on = [] {
+    const char* v = std::getenv("LIVGLM_BATCHED_TC");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 Layout layout(const lg_moe_config* c, int64_t M) {
   const size_t E = c->n_routed_experts, k = c->num_experts_per_tok, d = c->hidden_size;
@@ -124,7 +150,13 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   L.offsets = o; o += up((E + 1) * 4);
   L.perm = o;    o += up(m * k * 4);
   L.active = o;  o += up((E + 1) * 4);
-  L.act = o;     o += up(m * k * F * 2);
+  // the batched tensor-core path writes act as T E2M1 terms + scales into the
+  // same region (route-major [M*k][T][F/2], then [M*k][T][F/32])
+  L.tc = M >= kTcMinTokens && tc_geometry(c);
+  const size_t aterm = kTcTerms * m * k * (F / 2), atsc = kTcTerms * m * k * (F / 32);
+  L.act = o;     o += up(std::max(m * k * F * 2, L.tc ? up(aterm) + atsc : size_t(0)));
+  L.aterm = L.act;
+  L.atsc = L.act + up(aterm);
   L.act_s = o;   o += up(m * Fs * 2);
   L.y = o;       o += up(m * k * d * 2);
   L.ys = o;      o += up(m * d * 2);
@@ -134,6 +166,12 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   // per 256-value column and route) and their scales
   L.bimg = o;    o += m == 1 ? up(k * (F / 256) * 1024) : 0;
   L.bsc = o;     o += m == 1 ? up(k * lg::dtc::kTerms * (F / 32)) : 0;
+  // batched tensor core: token terms at every dispatch position [M*k][T][d/2]
+  // + scales [M*k][T][d/32], route tiles, inverse dispatch permutation
+  L.xterm = o;   o += L.tc ? up(kTcTerms * m * k * (d / 2)) : 0;
+  L.xtsc = o;    o += L.tc ? up(kTcTerms * m * k * (d / 32)) : 0;
+  L.tiles = o;   o += L.tc ? up((E + 1) * 4) : 0;
+  L.inv = o;     o += L.tc ? up(m * k * 4) : 0;
   L.total = o;
   return L;
 }
@@ -282,6 +320,157 @@ int launch_gemv(const lg::GemvArgs& a, int M, int max_routes_per_expert, int E, 
     case 8: return launch_gemv_tt<8>(a, tt, max_items, s);
     default: return launch_gemv_tt<4>(a, tt, max_items, s);
   }
+}
+
+// ---- batched tensor-core path (grouped_tc.cuh) ----------------------------------
+void trace_mark(int slot, int i, cudaStream_t s);
+bool map_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_inner, uint32_t box_rows,
+            bool sw128);
+bool map_3d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t n, uint64_t n_stride,
+            uint32_t box_inner, uint32_t box_rows, bool sw128);
+bool map_scales_chunked(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint64_t n,
+                        uint64_t n_stride, uint32_t box_rows);
+// Weight banks and scale tensors the TMA reads: 16-byte aligned bases and
+// expert strides (checked for the packed banks by validate_weights).
+bool tc_weights_fit(const lg_moe_config* c, const lg_moe_weights* w, bool routed, bool shared) {
+  if (routed) {
+    if (!aligned(w->gate_scale, 16) || !aligned(w->up_scale, 16) || !aligned(w->down_scale, 16)) return false;
+    if (w->gate_scale_stride % 16 || w->up_scale_stride % 16 || w->down_scale_stride % 16) return false;
+  }
+  (void)c;
+  (void)shared;
+  return true;
+}
+
+struct GgMaps {
+  CUtensorMap A0, A1, B, B80, SA0, SA1, SB, SB80;
+};
+
+template <bool kRouted, bool kGateUp>
+int launch_grouped(const lg::gtc::Args& a0, int items_max, const GgMaps& m, cudaStream_t s) {
+  using namespace lg::gtc;
+  Args a = a0;
+  const int b_rows = kRouted ? kTerms * kNtMax : kNtShared;
+  a.stage_bytes = kABytes + b_rows * 128;
+  a.b_off = kABytes;
+  size_t fixed = 0;
+  size_t sfa = 0, sfb = 0, xch = 0, tab = 0;
+  if (kRouted) {
+    sfa = static_cast<size_t>(128) * a.sc_bytes;
+    sfb = static_cast<size_t>(b_rows) * a.sc_bytes;
+    tab = (static_cast<size_t>(a.E) + 1) * 4;
+  }
+  if (kGateUp) xch = static_cast<size_t>(4) * (kRouted ? kNtMax : kNtShared) * 32 * 2;
+  auto r1k = [](size_t v) { return (v + 1023) / 1024 * 1024; };
+  fixed = r1k(2 * sfa) + r1k(2 * sfb) + r1k(xch) + r1k(tab);
+  const size_t budget = 227 * 1024 - 1024 - 1024;  // dynamic limit less alignment slack and static barriers
+  if (fixed + 2 * static_cast<size_t>(a.stage_bytes) > budget)
+    return fail(LG_ERR_UNSUPPORTED, "batched tensor-core plan does not fit in shared memory");
+  a.stages = static_cast<int>(std::min<size_t>(kMaxStages, (budget - fixed) / a.stage_bytes));
+  a.ring_off = 0;
+  a.sfa_off = a.stages * a.stage_bytes;
+  a.sfa_bytes = static_cast<int>(sfa);
+  a.sfb_off = a.sfa_off + static_cast<int>(r1k(2 * sfa));
+  a.sfb_bytes = static_cast<int>(sfb);
+  a.xch_off = a.sfb_off + static_cast<int>(r1k(2 * sfb));
+  a.tab_off = a.xch_off + static_cast<int>(r1k(xch));
+  const size_t smem = 1024 + a.tab_off + r1k(tab);
+  auto kern = grouped_kernel<kRouted, kGateUp>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return cuda_check(e, "grouped kernel smem attribute");
+  int grid = num_sms();
+  if (items_max < grid) grid = items_max;
+  if (grid < 1) return LG_OK;
+  kern<<<grid, kThreads, smem, s>>>(a, m.A0, m.A1, m.B, m.B80, m.SA0, m.SA1, m.SB, m.SB80);
+  return cuda_check(cudaGetLastError(), "grouped kernel launch");
+}
+
+// The batched expert passes on the tensor core: token split, route tiles,
+// routed and/or shared gate/up, then routed and/or shared down.  Routing
+// tables (offsets, perm) must be ready; y gets the routed outputs in slot
+// order, ys the shared output.
+int launch_experts_tc(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M, const int* offsets,
+                      const int* perm, void* ws, const Layout& L, uint16_t* y, uint16_t* ys, bool with_routed,
+                      bool with_shared, cudaStream_t s, int slot = -1) {
+  using namespace lg::gtc;
+  const int d = c->hidden_size, F = c->moe_intermediate_size, E = c->n_routed_experts, k = c->num_experts_per_tok;
+  const int Fs = F * c->n_shared_experts, T = kTcTerms, R = M * k;
+  const bool sh = with_shared && Fs > 0;
+  Args a{};
+  a.M = M; a.d = d; a.F = F; a.Fs = Fs; a.E = E; a.k = k; a.R = R;
+  a.limit = c->swiglu_limit;
+  a.offsets = offsets; a.perm = perm; a.tile_start = at<int>(ws, L.tiles);
+  a.act_terms = at<uint8_t>(ws, L.aterm); a.act_tsc = at<uint8_t>(ws, L.atsc);
+  a.act_s = at<uint16_t>(ws, L.act_s); a.y = y; a.ys = ys;
+  a.status = at<int>(ws, L.status);
+  uint8_t* xterm = at<uint8_t>(ws, L.xterm);
+  uint8_t* xtsc = at<uint8_t>(ws, L.xtsc);
+  int* inv = at<int>(ws, L.inv);
+  const int tok_tiles = (M + kNtShared - 1) / kNtShared;
+  // routed tiles: at most one partial tile per expert beyond R / kNtMax full ones
+  const long long tiles_max = static_cast<long long>(R) / kNtMax + std::min(E, R);
+  const uint64_t rt = static_cast<uint64_t>(R) * T;  // term rows
+  GgMaps m;
+  int rc;
+  cudaError_t e;
+  if (with_routed) {
+    tile_table_kernel<<<1, 1024, 0, s>>>(offsets, E, at<int>(ws, L.tiles));
+    cudaMemsetAsync(inv, 0xFF, static_cast<size_t>(R) * 4, s);
+    inverse_perm_kernel<<<std::min((R + 255) / 256, 4 * num_sms()), 256, 0, s>>>(perm, offsets, E, inv);
+    const long long halves = static_cast<long long>(M) * (d / 32);
+    split_routes_kernel<<<static_cast<int>((halves * 16 + 255) / 256), 256, 0, s>>>(x, M, d, k, inv, xterm, xtsc);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_check(e, "route split launch");
+    Args g = a;
+    g.kb_count = d / 256; g.rb_count = F / 64; g.sc_bytes = d / 32; g.sc_swz = d / 32 == 128;
+    if (!map_3d(&m.A0, w->gate_packed, d / 2, F, E, w->gate_packed_stride, 128, 64, true) ||
+        !map_3d(&m.A1, w->up_packed, d / 2, F, E, w->up_packed_stride, 128, 64, true) ||
+        !map_2d(&m.B, xterm, d / 2, rt, 128, kTerms * kNtMax, true) ||
+        !map_2d(&m.B80, xterm, d / 2, rt, 128, kTerms * kNtMax / 2, true) ||
+        !map_3d(&m.SA0, w->gate_scale, d / 32, F, E, w->gate_scale_stride, d / 32, 64, g.sc_swz) ||
+        !map_3d(&m.SA1, w->up_scale, d / 32, F, E, w->up_scale_stride, d / 32, 64, g.sc_swz) ||
+        !map_2d(&m.SB, xtsc, d / 32, rt, d / 32, kTerms * kNtMax, g.sc_swz) ||
+        !map_2d(&m.SB80, xtsc, d / 32, rt, d / 32, kTerms * kNtMax / 2, g.sc_swz))
+      return fail(LG_ERR_CUDA, "batched gate/up: tensor map encoding failed");
+    const long long items = tiles_max * g.rb_count;
+    if ((rc = launch_grouped<true, true>(g, static_cast<int>(std::min<long long>(items, 1 << 30)), m, s))) return rc;
+  }
+  if (sh) {
+    Args g = a;
+    g.kb_count = d / 64; g.rb_count = Fs / 64; g.n_tok_tiles = tok_tiles;
+    if (!map_2d(&m.A0, w->shared_gate, static_cast<uint64_t>(d) * 2, Fs, 128, 64, true) ||
+        !map_2d(&m.A1, w->shared_up, static_cast<uint64_t>(d) * 2, Fs, 128, 64, true) ||
+        !map_2d(&m.B, x, static_cast<uint64_t>(d) * 2, M, 128, kNtShared, true))
+      return fail(LG_ERR_CUDA, "batched shared gate/up: tensor map encoding failed");
+    m.B80 = m.SA0 = m.SA1 = m.SB = m.SB80 = m.A0;  // unused by the shared kernels
+    if ((rc = launch_grouped<false, true>(g, g.rb_count * tok_tiles, m, s))) return rc;
+  }
+  trace_mark(slot, 3, s);
+  if (with_routed) {
+    Args g = a;
+    g.kb_count = F / 256; g.rb_count = d / 128; g.sc_bytes = F / 32; g.sc_swz = F / 32 == 128;
+    if (!map_3d(&m.A0, w->down_packed, F / 2, d, E, w->down_packed_stride, 128, 128, true) ||
+        !map_2d(&m.B, a.act_terms, F / 2, rt, 128, kTerms * kNtMax, true) ||
+        !map_2d(&m.B80, a.act_terms, F / 2, rt, 128, kTerms * kNtMax / 2, true) ||
+        !map_3d(&m.SA0, w->down_scale, F / 32, d, E, w->down_scale_stride, F / 32, 128, g.sc_swz) ||
+        !map_2d(&m.SB, a.act_tsc, F / 32, rt, F / 32, kTerms * kNtMax, g.sc_swz) ||
+        !map_2d(&m.SB80, a.act_tsc, F / 32, rt, F / 32, kTerms * kNtMax / 2, g.sc_swz))
+      return fail(LG_ERR_CUDA, "batched down: tensor map encoding failed");
+    m.A1 = m.SA1 = m.A0;
+    const long long items = tiles_max * g.rb_count;
+    if ((rc = launch_grouped<true, false>(g, static_cast<int>(std::min<long long>(items, 1 << 30)), m, s))) return rc;
+  }
+  if (sh) {
+    Args g = a;
+    g.kb_count = Fs / 64; g.rb_count = d / 128; g.n_tok_tiles = tok_tiles;
+    if (!map_2d(&m.A0, w->shared_down, static_cast<uint64_t>(Fs) * 2, d, 128, 128, true) ||
+        !map_2d(&m.B, a.act_s, static_cast<uint64_t>(Fs) * 2, M, 128, kNtShared, true))
+      return fail(LG_ERR_CUDA, "batched shared down: tensor map encoding failed");
+    m.A1 = m.B80 = m.SA0 = m.SA1 = m.SB = m.SB80 = m.A0;
+    if ((rc = launch_grouped<false, false>(g, g.rb_count * tok_tiles, m, s))) return rc;
+  }
+  trace_mark(slot, 4, s);
+  return LG_OK;
 }
 
 // Gate/up (+ SwiGLU) pass over routed experts and, when `with_shared`, the
@@ -469,6 +658,49 @@ bool map_bytes(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, 
   const cuuint32_t box[2] = {box_inner, static_cast<cuuint32_t>(lg::dtc::kTile)};
   const cuuint32_t estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Byte tensor maps of the batched tensor-core kernels: 2-D [rows][inner] or
+// 3-D [n][rows][inner] (expert banks, n_stride bytes between experts), boxes of
+// box_inner bytes x box_rows rows (x 1 expert), 128-byte swizzle or none.
+bool map_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_inner, uint32_t box_rows,
+            bool sw128) {
+  const PFN_cuTensorMapEncodeTiled_v12000 fn = encode_tiled();
+  if (!fn || !aligned(base, 16) || inner % 16) return false;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {inner};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// Scale bank [n][rows][row_bytes] walked in 16-byte chunks, chunk-major: dims
+// {16, rows, row_bytes / 16, n}, strides {row_bytes, 16, n_stride}; a box of
+// box_rows rows x all chunks lands as [chunk][row][16 B].
+bool map_scales_chunked(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint64_t n,
+                        uint64_t n_stride, uint32_t box_rows) {
+  const PFN_cuTensorMapEncodeTiled_v12000 fn = encode_tiled();
+  if (!fn || !aligned(base, 16) || row_bytes % 16 || n_stride % 16 || row_bytes / 16 > 256) return false;
+  const cuuint64_t dims[4] = {16, rows, row_bytes / 16, n};
+  const cuuint64_t strides[3] = {row_bytes, 16, n_stride};
+  const cuuint32_t box[4] = {16, box_rows, static_cast<cuuint32_t>(row_bytes / 16), 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+bool map_3d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t n, uint64_t n_stride,
+            uint32_t box_inner, uint32_t box_rows, bool sw128) {
+  const PFN_cuTensorMapEncodeTiled_v12000 fn = encode_tiled();
+  if (!fn || !aligned(base, 16) || inner % 16 || n_stride % 16) return false;
+  const cuuint64_t dims[3] = {inner, rows, n};
+  const cuuint64_t strides[2] = {inner, n_stride};
+  const cuuint32_t box[3] = {box_inner, box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -800,6 +1032,8 @@ int lg_moe_experts(const lg_moe_config* cfg, const lg_moe_weights* w, const uint
   int* perm = at<int>(workspace, L.perm);
   int* active = at<int>(workspace, L.active);
   if ((rc = launch_dispatch(cfg, indices, static_cast<int>(M), counts, offsets, perm, active, true, s))) return rc;
+  if (L.tc && tc_batched_env() && tc_weights_fit(cfg, w, true, false))
+    return launch_experts_tc(cfg, w, x, static_cast<int>(M), offsets, perm, workspace, L, y, nullptr, true, false, s);
   return launch_experts(cfg, w, x, static_cast<int>(M), offsets, perm, active, at<uint16_t>(workspace, L.act),
                         nullptr, y, nullptr, true, false, s);
 }
@@ -817,6 +1051,9 @@ int lg_moe_shared(const lg_moe_config* cfg, const lg_moe_weights* w, const uint1
   const Layout L = layout(cfg, M);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* active = at<int>(workspace, L.active);
+  if (L.tc && tc_batched_env())
+    return launch_experts_tc(cfg, w, x, static_cast<int>(M), nullptr, nullptr, workspace, L, nullptr, out, false,
+                             true, s);
   cudaMemsetAsync(active, 0, sizeof(int), s);
   return launch_experts(cfg, w, x, static_cast<int>(M), at<int>(workspace, L.offsets), at<int>(workspace, L.perm),
                         active, nullptr, at<uint16_t>(workspace, L.act_s), nullptr, out, false, true, s);
@@ -898,10 +1135,14 @@ int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint
   uint16_t* act_s = at<uint16_t>(workspace, L.act_s);
   uint16_t* y = at<uint16_t>(workspace, L.y);
   uint16_t* ys = cfg->n_shared_experts > 0 ? at<uint16_t>(workspace, L.ys) : nullptr;
-  if ((rc = launch_gate_up(cfg, w, x, m, offsets, perm, active, act, act_s, true, true, s))) return rc;
-  trace_mark(slot, 3, s);
-  if ((rc = launch_down(cfg, w, m, offsets, perm, active, act, act_s, y, ys, true, true, s))) return rc;
-  trace_mark(slot, 4, s);
+  if (L.tc && tc_batched_env() && tc_weights_fit(cfg, w, true, true)) {
+    if ((rc = launch_experts_tc(cfg, w, x, m, offsets, perm, workspace, L, y, ys, true, true, s, slot))) return rc;
+  } else {
+    if ((rc = launch_gate_up(cfg, w, x, m, offsets, perm, active, act, act_s, true, true, s))) return rc;
+    trace_mark(slot, 3, s);
+    if ((rc = launch_down(cfg, w, m, offsets, perm, active, act, act_s, y, ys, true, true, s))) return rc;
+    trace_mark(slot, 4, s);
+  }
   rc = lg_moe_combine(cfg, y, wts, ys, M, out, stream);
   trace_mark(slot, 5, s);
   return rc;

@@ -97,6 +97,20 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Named barrier `id` over `nthreads` threads that also ANDs a flag over them:
+// every participant gets the same verdict, so a group of warps leaves a loop
+// together (a warp that left alone would strand the others at the group's
+// next named barrier).
+__device__ __forceinline__ bool named_and(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbarrier.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
 // named barrier `id` (1..15) over `nthreads` threads of the CTA.  The
 // non-.aligned form: threads arrive one by one, so it is correct right after
 // code where one lane of a warp took a different path (bar.sync, the .aligned

@@ -466,6 +466,11 @@ class ExpertSSDMoE:
         if a bounded device wait gave up."""
         return self._ws.status()
 
+    def use_workspace(self, ws: Workspace) -> None:
+        """Run on a workspace shared with other layers.  Calls that share one
+        must not overlap on the GPU: layers called in order on one stream."""
+        self._ws = ws
+
     @property
     def last_route_ids(self) -> tuple[int, ...]:
         """The reference's last_route (moe.py:179,200); synchronises."""
