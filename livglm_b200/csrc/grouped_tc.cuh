@@ -41,7 +41,8 @@
 // Warps: 0 TMA producer, 1 MMA issuer (one lane), 2-5 scale-factor staging
 // (routed: per k-block, A and B scale words from shared memory into a ring of
 // tensor-memory slots with tcgen05.st), 6-9 epilogue (tcgen05.ld of the
-// double-buffered accumulator).  Every wait is bounded: a timeout records
+// double-buffered accumulator), 10-13 help 6-9 with the gate/up epilogue's
+// SwiGLU and activation split, the longest per-item work.  Every wait is bounded: a timeout records
 // 6 | site in the status word and the CTA leaves after its copies and MMAs in
 // flight have landed.
 #pragma once
@@ -55,13 +56,14 @@
 namespace lg {
 namespace gtc {
 
-constexpr int kThreads = 320;
-constexpr int kProdWarp = 0, kMmaWarp = 1, kSfWarp0 = 2, kEpiWarp0 = 6;
+constexpr int kThreads = 448;
+constexpr int kProdWarp = 0, kMmaWarp = 1, kSfWarp0 = 2, kEpiWarp0 = 6, kMathWarp0 = 10;
+constexpr int kMathWarps = 8;     // gate/up epilogue: warps 6-13 share the SwiGLU and split
 constexpr int kTerms = 5;         // E2M1 terms per bf16 activation
 constexpr int kNtMax = 32;        // routes per routed tile
 constexpr int kNtShared = 128;    // tokens per shared tile
 constexpr int kMaxStages = 8;
-constexpr int kSfSlots = 8;       // tensor-memory scale-factor ring (routed): 2 * 160 + 8 * 24 = 512 columns
+constexpr int kSfSlots = kMaxStages;  // tensor-memory scale-factor slots, one per ring stage: 2 * 160 + 8 * 24 = 512
 constexpr int kSfaCols = 8;       // A: 2 MMA pairs x 4 row quarters
 constexpr int kSfbCols = 16;      // B: 2 MMA pairs x 8 row groups (N <= 256)
 constexpr int kSfSlotCols = kSfaCols + kSfbCols;
@@ -112,35 +114,51 @@ __global__ void __launch_bounds__(256) inverse_perm_kernel(const int* __restrict
 }
 
 // Split every token row into kTerms E2M1 terms (umma.cuh) once and write them
-// to each of its k dispatch positions: half-warp h takes 32-value block j of
-// token t (h = t * (d/32) + j); lane i of the half holds values 2i, 2i+1.
+// to each of its k dispatch positions.  Thread q of a 4-thread group holds
+// values 8q .. 8q + 7 of one 32-value block (16 bytes of x); a warp covers 8
+// consecutive blocks (one 256-value k-block) of one token, so each term row
+// is written as one 128-byte line per store instruction.  d % 256 == 0.
 __global__ void __launch_bounds__(256) split_routes_kernel(const uint16_t* __restrict__ x, int M, int d, int k,
                                                            const int* __restrict__ inv, uint8_t* __restrict__ terms,
                                                            uint8_t* __restrict__ tsc) {
-  const int nblk = d / 32;
-  const long long h = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
-  const int hl = threadIdx.x & 15;
-  if (h >= static_cast<long long>(M) * nblk) return;  // whole half-warps leave together (nblk is even)
-  const int t = static_cast<int>(h / nblk), j = static_cast<int>(h - static_cast<long long>(t) * nblk);
-  const uint32_t pair = *(reinterpret_cast<const uint32_t*>(x + static_cast<size_t>(t) * d + j * 32) + hl);
-  float r0 = __uint_as_float(pair << 16), r1 = __uint_as_float(pair & 0xFFFF0000u);
-  bool live;
-  const int s0 = umma::split_base(r0, r1, &live);
-  uint8_t byte[kTerms], scale[kTerms];
+  const int nkb = d / 256;  // warps per token
+  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= static_cast<long long>(M) * nkb) return;  // whole warps leave together
+  const int t = static_cast<int>(w / nkb), kb = static_cast<int>(w - static_cast<long long>(t) * nkb);
+  const int col = kb * 256 + 8 * lane;  // first of this thread's 8 values
+  const uint4 u = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * d + col);
+  float r[8] = {bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y), bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w)};
+  float a = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(r[i]));
+  a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+  a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));  // the 32-value block's largest magnitude
+  const bool live = a >= 0x1p-100f;
+  const int s0 = live ? umma::term_exponent(a) : 0;
+  uint32_t word[kTerms];
+  uint8_t scale[kTerms];
 #pragma unroll
   for (int q = 0; q < kTerms; ++q) {
     const int e = umma::term_scale(s0, q);
-    byte[q] = static_cast<uint8_t>(live ? umma::split_step(r0, r1, e) : 0u);
+    uint32_t v = 0u;
+    if (live) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v |= umma::split_step(r[2 * i], r[2 * i + 1], e) << (8 * i);
+    }
+    word[q] = v;
     scale[q] = static_cast<uint8_t>(live ? 127 + e : 127);
   }
+  // the token's dispatch positions (k <= 32), loaded once per warp
+  const int pl = lane < k ? __ldg(inv + static_cast<size_t>(t) * k + lane) : -1;
   for (int jj = 0; jj < k; ++jj) {
-    const int p = __ldg(inv + static_cast<size_t>(t) * k + jj);
+    const int p = __shfl_sync(0xffffffffu, pl, jj);
     if (p < 0) continue;
 #pragma unroll
     for (int q = 0; q < kTerms; ++q) {
       const size_t row = static_cast<size_t>(p) * kTerms + q;
-      terms[row * (d / 2) + j * 16 + hl] = byte[q];
-      if (hl == 0) tsc[row * nblk + j] = scale[q];
+      reinterpret_cast<uint32_t*>(terms + row * (d / 2))[col / 8] = word[q];
+      if ((lane & 3) == 0) tsc[row * (d / 32) + col / 32] = scale[q];
     }
   }
 }
@@ -267,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap mSB, const __grid_constant__ CUtensorMap mSB80) {
   extern __shared__ __align__(1024) unsigned char smraw[];
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
-  __shared__ __align__(8) uint64_t sf_full[kSfSlots], sf_empty[kSfSlots];
+  __shared__ __align__(8) uint64_t sf_full[kSfSlots];
   __shared__ __align__(8) uint64_t sc_full[2], sc_free[2], acc_full[2], acc_empty[2], drain;
   __shared__ uint32_t tslot;
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
@@ -284,10 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int s = 0; s < kSfSlots; ++s) {
-      mbar_init(&sf_full[s], 4);
-      mbar_init(&sf_empty[s], 1);
-    }
+    for (int s = 0; s < S; ++s) mbar_init(&sf_full[s], 4);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sc_full[i], 1);
       mbar_init(&sc_free[i], 4);
@@ -314,25 +329,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       bool ok = true;
       int it_k = 0;  // stages issued
-      Item item;
-      for (int seq = 0; ok && next_item(seq, item); ++seq) {
+      // the scale tiles of item q (routed), one item ahead of its k-blocks so
+      // that their latency hides behind the previous item's MMAs
+      auto load_scales = [&](int q, const Item& it) -> bool {
+        const int sb = q & 1, n_rows = T * it.ntp;
+        if (q >= 2 && !dtc::wait1(&sc_free[sb], ((q >> 1) - 1) & 1, a.status, kSiteScFree)) return false;
+        unsigned char* sfa = base + a.sfa_off + sb * a.sfa_bytes;
+        unsigned char* sfb = base + a.sfb_off + sb * a.sfb_bytes;
+        mbar_arrive_expect_tx(&sc_full[sb], static_cast<unsigned>((128 + n_rows) * a.sc_bytes));
+        if (kGateUp) {
+          tma_3d(sfa, &mSA0, 0, it.rb * 64, it.e, &sc_full[sb]);
+          tma_3d(sfa + 64 * a.sc_bytes, &mSA1, 0, it.rb * 64, it.e, &sc_full[sb]);
+        } else {
+          tma_3d(sfa, &mSA0, 0, it.rb * 128, it.e, &sc_full[sb]);
+        }
+        dtc::tma_2d(sfb, it.ntp > 16 ? &mSB : &mSB80, 0, it.p0 * T, &sc_full[sb]);
+        return true;
+      };
+      Item item, nitem;
+      bool have = next_item(0, item);
+      if (kRouted && have) ok = load_scales(0, item);
+      for (int seq = 0; ok && have; ++seq) {
+        const bool have_next = next_item(seq + 1, nitem);
         const int n_rows = T * item.ntp;  // B rows (MMA N)
         const bool wide = item.ntp > 16;  // routed: 160-row boxes, else 80
-        if (kRouted) {  // this item's scale tiles
-          const int sb = seq & 1;
-          if (seq >= 2) ok = dtc::wait1(&sc_free[sb], ((seq >> 1) - 1) & 1, a.status, kSiteScFree);
-          if (!ok) break;
-          unsigned char* sfa = base + a.sfa_off + sb * a.sfa_bytes;
-          unsigned char* sfb = base + a.sfb_off + sb * a.sfb_bytes;
-          mbar_arrive_expect_tx(&sc_full[sb], static_cast<unsigned>((128 + n_rows) * a.sc_bytes));
-          if (kGateUp) {
-            tma_3d(sfa, &mSA0, 0, item.rb * 64, item.e, &sc_full[sb]);
-            tma_3d(sfa + 64 * a.sc_bytes, &mSA1, 0, item.rb * 64, item.e, &sc_full[sb]);
-          } else {
-            tma_3d(sfa, &mSA0, 0, item.rb * 128, item.e, &sc_full[sb]);
-          }
-          dtc::tma_2d(sfb, wide ? &mSB : &mSB80, 0, item.p0 * T, &sc_full[sb]);
-        }
         // bytes of B: the routed rows, or the shared expert's whole 128-row box
         // (rows past the last token are zero-filled and still counted)
         const unsigned bytes = static_cast<unsigned>(kABytes + (kRouted ? n_rows : kNtShared) * 128);
@@ -357,7 +377,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (kRouted) dtc::tma_2d(bt, wide ? &mB : &mB80, x, item.p0 * T, &full[s]);
           else dtc::tma_2d(bt, &mB, x, item.p0, &full[s]);
+          if (kRouted && have_next && kb == min(1, a.kb_count - 1)) ok = load_scales(seq + 1, nitem);
+          if (!ok) break;
         }
+        item = nitem;
+        have = have_next;
       }
       if (!ok) {  // let the copies in flight land before the CTA leaves
         for (int q = (it_k > S ? it_k - S : 0); q < it_k; ++q)
@@ -370,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   else if (warp == kMmaWarp) {
     if (lane == 0) {
       bool ok = true;
-      int it_k = 0, it_sf = 0;
+      int it_k = 0;
       Item item;
       for (int seq = 0; ok && next_item(seq, item); ++seq) {
         const int ab = seq & 1;
@@ -384,9 +408,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = it_k % S;
           ok = dtc::wait1(&full[s], (it_k / S) & 1, a.status, kSiteFull);
           if (!ok) break;
-          const int sl = it_sf % kSfSlots;
+          const int sl = s;  // the scale-factor slot of a k-block is its ring stage
           if (kRouted) {
-            ok = dtc::wait1(&sf_full[sl], (it_sf / kSfSlots) & 1, a.status, kSiteSfFull);
+            ok = dtc::wait1(&sf_full[sl], (it_k / S) & 1, a.status, kSiteSfFull);
             if (!ok) break;
           }
           umma::fence_after_sync();
@@ -402,11 +426,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             else
               umma::mma_bf16(acc, da + 2 * m, db + 2 * m, idesc, accum);
           }
+          // one commit frees the stage and (for the scale-factor warps, who
+          // wait on the same barrier) the scale-factor slot of this k-block
           umma::commit(&empty[s]);
-          if (kRouted) {
-            umma::commit(&sf_empty[sl]);
-            ++it_sf;
-          }
         }
         if (ok) umma::commit(&acc_full[ab]);
       }
@@ -430,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const unsigned char* sfa = base + a.sfa_off + sb * a.sfa_bytes;
         const unsigned char* sfb = base + a.sfb_off + sb * a.sfb_bytes;
         for (int kb = 0; kb < a.kb_count; ++kb, ++it_sf) {
-          const int sl = it_sf % kSfSlots;
+          const int sl = it_sf % S;  // slot = ring stage of this k-block
           // MMA pair j (MMAs 2j, 2j+1 of this k-block) reads scale word j of each
           // row: A row 32q + lane in column 4j + q, B row 32q + lane in column 8j + q.
           // The words are read from shared memory before waiting for the slot.
@@ -449,8 +471,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             vb[q] = w.x;
             vb[8 + q] = w.y;
           }
-          if (it_sf >= kSfSlots)
-            ok = dtc::wait_warp1(&sf_empty[sl], ((it_sf / kSfSlots) - 1) & 1, a.status, kSiteSfEmpty);
+          // slot sl was last used by k-block it_sf - S, whose MMAs' completion
+          // frees the ring stage too (empty[sl], the producer's wait); the
+          // barrier cannot pass that phase twice before this slot is refilled,
+          // since k-block it_sf needs this slot
+          if (it_sf >= S) ok = dtc::wait_warp1(&empty[sl], ((it_sf / S) - 1) & 1, a.status, kSiteSfEmpty);
           if (!ok) break;
           const uint32_t col = kColSf + sl * kSfSlotCols;
           umma::st_32x32b_x8(lanes + col, va);
@@ -467,8 +492,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   // ------------------------------ epilogue ----------------------------------
-  else {
-    const int sp = warp & 3;  // tensor-memory lanes 32 sp .. 32 sp + 31
+  else if (warp < kMathWarp0 || kGateUp) {
+    const bool tm = warp < kMathWarp0;  // reads the accumulator (else: SwiGLU / split helper)
+    const int sp = warp & 3;            // tensor-memory lanes 32 sp .. 32 sp + 31
+    const int mw = warp - kEpiWarp0;    // 0..7 among the gate/up epilogue warps
+    const int nbar = kGateUp ? 32 * kMathWarps : 128;
     const uint32_t lanes = tbase + (static_cast<uint32_t>(sp * 32) << 16);
     uint16_t* xch = reinterpret_cast<uint16_t*>(base + a.xch_off);  // [4][ntp max][32]
     const int xrows = kRouted ? kNtMax : kNtShared;
@@ -476,60 +504,63 @@ __global__ void __launch_bounds__(kThreads, 1)
     Item item;
     for (int seq = 0; ok && next_item(seq, item); ++seq) {
       const int ab = seq & 1;
-      ok = dtc::wait_warp1(&acc_full[ab], (seq >> 1) & 1, a.status, kSiteAccFull);
-      ok = named_and(kEpiBar, 128, ok);  // the four epilogue warps leave together
+      if (tm) ok = dtc::wait_warp1(&acc_full[ab], (seq >> 1) & 1, a.status, kSiteAccFull);
+      ok = named_and(kEpiBar, nbar, ok);  // the epilogue warps leave together
       if (!ok) break;
-      umma::fence_after_sync();
-      const uint32_t acc = lanes + ab * kAccStride;
-      // accumulator column of (route i, term t) = i * T + t: 16 routes are 16 T
-      // consecutive columns, read as T loads of 16 columns
-      for (int c0 = 0; c0 < item.ntp; c0 += 16) {
-        float s[16];
-        {
-          uint32_t v[16 * T];
-#pragma unroll
-          for (int q = 0; q < T; ++q) {
-            uint32_t (&vq)[16] = *reinterpret_cast<uint32_t(*)[16]>(v + 16 * q);
-            umma::ld_32x32b_x16_nowait(acc + c0 * T + 16 * q, vq);
+      if (tm) {
+        umma::fence_after_sync();
+        const uint32_t acc = lanes + ab * kAccStride;
+        // accumulator column of (route i, term t) = i * T + t: 16 routes are 16 T
+        // consecutive columns, read as T loads of 16 columns
+        for (int c0 = 0; c0 < item.ntp; c0 += 16) {
+          float s[16];
+          {
+            uint32_t v[16 * T];
+  #pragma unroll
+            for (int q = 0; q < T; ++q) {
+              uint32_t (&vq)[16] = *reinterpret_cast<uint32_t(*)[16]>(v + 16 * q);
+              umma::ld_32x32b_x16_nowait(acc + c0 * T + 16 * q, vq);
+            }
+            umma::wait_ld();
+  #pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float t0 = __uint_as_float(v[i * T]);
+  #pragma unroll
+              for (int t = 1; t < T; ++t) t0 = __fadd_rn(t0, __uint_as_float(v[i * T + t]));
+              s[i] = t0;
+            }
           }
-          umma::wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float t0 = __uint_as_float(v[i * T]);
-#pragma unroll
-            for (int t = 1; t < T; ++t) t0 = __fadd_rn(t0, __uint_as_float(v[i * T + t]));
-            s[i] = t0;
-          }
-        }
-        if (kGateUp) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) xch[(sp * xrows + c0 + i) * 32 + lane] = f32_to_bf16(s[i]);
-        } else {
-          // down: output rows d0 + 32 sp + lane of routes / tokens c0 .. c0 + 15
-          const int row = item.rb * 128 + sp * 32 + lane;
-          int my_slot = 0;  // lane i < 16: the route slot of route c0 + i
-          if (kRouted && lane < 16 && c0 + lane < item.nt) my_slot = __ldg(a.perm + item.p0 + c0 + lane);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int slot = __shfl_sync(0xffffffffu, my_slot, i);
-            if (c0 + i < item.nt) {
-              if (kRouted) {
-                a.y[static_cast<size_t>(slot) * a.d + row] = f32_to_bf16(s[i]);
-              } else {
-                a.ys[static_cast<size_t>(item.p0 + c0 + i) * a.d + row] = f32_to_bf16(s[i]);
+          if (kGateUp) {
+  #pragma unroll
+            for (int i = 0; i < 16; ++i) xch[(sp * xrows + c0 + i) * 32 + lane] = f32_to_bf16(s[i]);
+          } else {
+            // down: output rows d0 + 32 sp + lane of routes / tokens c0 .. c0 + 15
+            const int row = item.rb * 128 + sp * 32 + lane;
+            int my_slot = 0;  // lane i < 16: the route slot of route c0 + i
+            if (kRouted && lane < 16 && c0 + lane < item.nt) my_slot = __ldg(a.perm + item.p0 + c0 + lane);
+  #pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int slot = __shfl_sync(0xffffffffu, my_slot, i);
+              if (c0 + i < item.nt) {
+                if (kRouted) {
+                  a.y[static_cast<size_t>(slot) * a.d + row] = f32_to_bf16(s[i]);
+                } else {
+                  a.ys[static_cast<size_t>(item.p0 + c0 + i) * a.d + row] = f32_to_bf16(s[i]);
+                }
               }
             }
           }
         }
-      }
-      umma::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+        umma::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[ab]);
+      }  // tm
       if (kGateUp) {
-        named_sync(kEpiBar, 128);
-        // warp sp: columns f0 + 32 h + lane (h = sp & 1), routes / tokens of parity sp >> 1
-        const int h = sp & 1, f = item.rb * 64 + 32 * h + lane;
-        for (int i = sp >> 1; i < item.nt; i += 2) {
+        named_sync(kEpiBar, nbar);
+        // warp mw: columns f0 + 32 h + lane (h = mw & 1), routes / tokens i with
+        // i % 4 == mw >> 1
+        const int h = mw & 1, f = item.rb * 64 + 32 * h + lane;
+        for (int i = mw >> 1; i < item.nt; i += kMathWarps / 2) {
           const float g = bf16_to_f32(xch[(h * xrows + i) * 32 + lane]);
           const float u = bf16_to_f32(xch[((2 + h) * xrows + i) * 32 + lane]);
           const uint16_t act = swiglu_bf16(g, u, a.limit);
@@ -542,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             a.act_s[static_cast<size_t>(item.p0 + i) * a.Fs + f] = act;
           }
         }
-        named_sync(kEpiBar, 128);  // xch is rewritten by the next item
+        named_sync(kEpiBar, nbar);  // xch is rewritten by the next item
       }
     }
   }

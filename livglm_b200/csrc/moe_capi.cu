@@ -233,6 +233,12 @@ int launch_router(const lg_moe_config* c, const uint16_t* x, int M, const float*
   if (M <= 4) {
     dim3 grid((M + 0) / 1, (E + 7) / 8);
     router_logits_kernel<1, 1><<<grid, 256, 0, s>>>(x, Wr, M, d, E, logits);
+  } else if (d % 256 == 0 && M >= 1024) {
+    dim3 grid((M + 31) / 32, (E + kRlExperts - 1) / kRlExperts);
+    router_logits_tiled_kernel<4><<<grid, 256, 0, s>>>(x, Wr, M, d, E, logits);
+  } else if (d % 256 == 0 && M >= 64) {
+    dim3 grid((M + 15) / 16, (E + kRlExperts - 1) / kRlExperts);
+    router_logits_tiled_kernel<2><<<grid, 256, 0, s>>>(x, Wr, M, d, E, logits);
   } else {
     dim3 grid((M + 3) / 4, (E + 31) / 32);
     router_logits_kernel<4, 4><<<grid, 256, 0, s>>>(x, Wr, M, d, E, logits);
@@ -328,8 +334,6 @@ bool map_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uin
             bool sw128);
 bool map_3d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t n, uint64_t n_stride,
             uint32_t box_inner, uint32_t box_rows, bool sw128);
-bool map_scales_chunked(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint64_t n,
-                        uint64_t n_stride, uint32_t box_rows);
 // Weight banks and scale tensors the TMA reads: 16-byte aligned bases and
 // expert strides (checked for the packed banks by validate_weights).
 bool tc_weights_fit(const lg_moe_config* c, const lg_moe_weights* w, bool routed, bool shared) {
@@ -367,6 +371,7 @@ int launch_grouped(const lg::gtc::Args& a0, int items_max, const GgMaps& m, cuda
   if (fixed + 2 * static_cast<size_t>(a.stage_bytes) > budget)
     return fail(LG_ERR_UNSUPPORTED, "batched tensor-core plan does not fit in shared memory");
   a.stages = static_cast<int>(std::min<size_t>(kMaxStages, (budget - fixed) / a.stage_bytes));
+
   a.ring_off = 0;
   a.sfa_off = a.stages * a.stage_bytes;
   a.sfa_bytes = static_cast<int>(sfa);
@@ -417,8 +422,8 @@ int launch_experts_tc(const lg_moe_config* c, const lg_moe_weights* w, const uin
     tile_table_kernel<<<1, 1024, 0, s>>>(offsets, E, at<int>(ws, L.tiles));
     cudaMemsetAsync(inv, 0xFF, static_cast<size_t>(R) * 4, s);
     inverse_perm_kernel<<<std::min((R + 255) / 256, 4 * num_sms()), 256, 0, s>>>(perm, offsets, E, inv);
-    const long long halves = static_cast<long long>(M) * (d / 32);
-    split_routes_kernel<<<static_cast<int>((halves * 16 + 255) / 256), 256, 0, s>>>(x, M, d, k, inv, xterm, xtsc);
+    const long long warps = static_cast<long long>(M) * (d / 256);
+    split_routes_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 0, s>>>(x, M, d, k, inv, xterm, xtsc);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_check(e, "route split launch");
     Args g = a;
@@ -676,21 +681,6 @@ bool map_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uin
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-// Scale bank [n][rows][row_bytes] walked in 16-byte chunks, chunk-major: dims
-// {16, rows, row_bytes / 16, n}, strides {row_bytes, 16, n_stride}; a box of
-// box_rows rows x all chunks lands as [chunk][row][16 B].
-bool map_scales_chunked(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint64_t n,
-                        uint64_t n_stride, uint32_t box_rows) {
-  const PFN_cuTensorMapEncodeTiled_v12000 fn = encode_tiled();
-  if (!fn || !aligned(base, 16) || row_bytes % 16 || n_stride % 16 || row_bytes / 16 > 256) return false;
-  const cuuint64_t dims[4] = {16, rows, row_bytes / 16, n};
-  const cuuint64_t strides[3] = {row_bytes, 16, n_stride};
-  const cuuint32_t box[4] = {16, box_rows, static_cast<cuuint32_t>(row_bytes / 16), 1};
-  const cuuint32_t estr[4] = {1, 1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 bool map_3d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t n, uint64_t n_stride,
             uint32_t box_inner, uint32_t box_rows, bool sw128) {

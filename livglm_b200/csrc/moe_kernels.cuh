@@ -79,6 +79,97 @@ router_logits_kernel(const uint16_t* __restrict__ x, const float* __restrict__ W
 }
 
 // --------------------------------------------------------------------------
+// Router logits for many tokens, same arithmetic as router_logits_kernel
+// (lane l sums the 8-element chunks c = l, l + 32, ... in increasing order with
+// fma, then the 16/8/4/2/1 xor butterfly), with the operands staged through
+// shared memory: a block owns 8 * TW tokens x 16 experts and walks d in
+// k-blocks of 256 elements (32 chunks, one per lane), so every staged x and
+// W_r element serves all the block's pairs instead of being re-read from L2
+// per warp.  Warp w owns tokens t0 + TW w .. + TW - 1 and all 16 experts.
+// d must be a multiple of 256.
+constexpr int kRlExperts = 16;
+template <int TW>
+__global__ void __launch_bounds__(256)
+router_logits_tiled_kernel(const uint16_t* __restrict__ x, const float* __restrict__ W,
+                           int M, int d, int E, float* __restrict__ logits) {
+  constexpr int TB = 8 * TW;  // tokens per block
+  __shared__ __align__(16) uint16_t xs[TB * 256];
+  __shared__ __align__(16) float ws[kRlExperts * 256];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * TB, e0 = blockIdx.y * kRlExperts;
+  float acc[TW][kRlExperts];
+#pragma unroll
+  for (int a = 0; a < TW; ++a)
+#pragma unroll
+    for (int b = 0; b < kRlExperts; ++b) acc[a][b] = 0.0f;
+  // the next k-block's share of this thread, loaded while the current one is
+  // multiplied: TB * 32 uint4 of x and 16 * 64 float4 of W_r over 256 threads
+  constexpr int XV = TB * 32 / 256, WV = kRlExperts * 64 / 256;
+  uint4 xr[XV];
+  float4 wr[WV];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < XV; ++u) {
+      const int i = threadIdx.x + 256 * u, r = i >> 5, c = i & 31, t = t0 + r;
+      xr[u] = t < M ? *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * d + k0 + 8 * c)
+                    : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < WV; ++u) {
+      const int i = threadIdx.x + 256 * u, r = i >> 6, c = i & 63, e = e0 + r;
+      wr[u] = e < E ? *reinterpret_cast<const float4*>(W + static_cast<size_t>(e) * d + k0 + 4 * c)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  fetch(0);
+  for (int k0 = 0; k0 < d; k0 += 256) {
+    __syncthreads();  // the previous k-block's operands are consumed
+#pragma unroll
+    for (int u = 0; u < XV; ++u) reinterpret_cast<uint4*>(xs)[threadIdx.x + 256 * u] = xr[u];
+#pragma unroll
+    for (int u = 0; u < WV; ++u) reinterpret_cast<float4*>(ws)[threadIdx.x + 256 * u] = wr[u];
+    __syncthreads();
+    if (k0 + 256 < d) fetch(k0 + 256);
+    // lane l: chunk c = k0 / 8 + l (elements 8 l .. 8 l + 7 of this k-block)
+    float xv[TW][8];
+#pragma unroll
+    for (int a = 0; a < TW; ++a) {
+      const uint4 u = reinterpret_cast<const uint4*>(xs)[(warp * TW + a) * 32 + lane];
+      xv[a][0] = bf16lo(u.x); xv[a][1] = bf16hi(u.x);
+      xv[a][2] = bf16lo(u.y); xv[a][3] = bf16hi(u.y);
+      xv[a][4] = bf16lo(u.z); xv[a][5] = bf16hi(u.z);
+      xv[a][6] = bf16lo(u.w); xv[a][7] = bf16hi(u.w);
+    }
+#pragma unroll
+    for (int b = 0; b < kRlExperts; ++b) {
+      const float4 w0 = reinterpret_cast<const float4*>(ws)[b * 64 + 2 * lane];
+      const float4 w1 = reinterpret_cast<const float4*>(ws)[b * 64 + 2 * lane + 1];
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int a = 0; a < TW; ++a)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[a][b] = __fmaf_rn(xv[a][q], wv[q], acc[a][b]);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+    for (int a = 0; a < TW; ++a)
+#pragma unroll
+      for (int b = 0; b < kRlExperts; ++b)
+        acc[a][b] = __fadd_rn(acc[a][b], __shfl_xor_sync(0xffffffffu, acc[a][b], off));
+  // lane b < 16 writes expert e0 + b of the warp's tokens
+#pragma unroll
+  for (int a = 0; a < TW; ++a) {
+    const int t = t0 + warp * TW + a;
+    float v = 0.f;
+#pragma unroll
+    for (int b = 0; b < kRlExperts; ++b) v = lane == b ? acc[a][b] : v;
+    if (t < M && lane < kRlExperts && e0 + lane < E) logits[static_cast<size_t>(t) * E + e0 + lane] = v;
+  }
+}
+
+// --------------------------------------------------------------------------
 // Router selection: one warp per token.  E <= 1024 (32 experts per lane).
 // Shared memory per warp: scores[E], choice[E], gscore[G].
 constexpr int kSelectWarps = 4;

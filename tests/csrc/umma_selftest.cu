@@ -174,3 +174,76 @@ extern "C" int lg_umma_selftest_tile(int kind, const uint8_t* w, const uint8_t* 
                                                                      term_scales_out, status);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
+
+// ---- MMA issue rate ---------------------------------------------------------------
+// Throughput of back-to-back tcgen05.mma on resident shared-memory operands,
+// one CTA per SM, one issuing thread: kind 0 = kind::mxf4 block32 (M=128, K=64
+// per MMA, scale factors 1.0), kind 1 = kind::f16 bf16 (M=128, K=16).  Each
+// group of 64 MMAs is committed to an mbarrier and waited for (bounded), so at
+// most 64 are queued.  cycles_out[b] = clock64 cycles CTA b spent issuing.
+namespace {
+__global__ void __launch_bounds__(128, 1) mma_rate_kernel(int kind, int N, int groups, long long* cycles_out,
+                                                          int* status) {
+  extern __shared__ __align__(1024) unsigned char smraw[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t tslot;
+  unsigned char* sa = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sb = sa + kRows * kAtom;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  // operands: E2M1 bytes 0x22 (1.0, 1.0) or bf16 1/64; any finite values do
+  for (int i = tid; i < (kRows + 256) * kAtom / 4; i += 128)
+    reinterpret_cast<uint32_t*>(sa)[i] = kind == 0 ? 0x22222222u : 0x3C803C80u;
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&bar)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) tmem_alloc(&tslot, 512);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tbase = tslot, lanes = tbase + (static_cast<uint32_t>(warp * 32) << 16);
+  if (kind == 0) {  // scale factors 1.0 (127): A in columns 256..263, B in 264..279
+    for (int c = 0; c < 24; ++c) st_32x32b_x1(lanes + 256 + c, 0x7F7F7F7Fu);
+    wait_st();
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  if (tid == 0) {
+    fence_async_smem();
+    const uint64_t da = desc_sw128(smem_addr(sa)), db = desc_sw128(smem_addr(sb));
+    const uint32_t id = kind == 0 ? idesc_mxf4(kRows, N) : idesc_bf16(kRows, N);
+    bool ok = true;
+    const long long c0 = clock64();
+    for (int g = 0; g < groups && ok; ++g) {
+      for (int i = 0; i < 64; ++i) {
+        const int m = i & 3;
+        if (kind == 0)
+          mma_mxf4(tbase, da + 2 * m, db + 2 * m, id | idesc_sf_ids(2 * (m & 1)), tbase + 256 + 4 * (m >> 1),
+                   tbase + 264 + 8 * (m >> 1), i > 0 || g > 0);
+        else
+          mma_bf16(tbase, da + 2 * m, db + 2 * m, id, i > 0 || g > 0);
+      }
+      commit(&bar);
+      ok = wait_bar(&bar, static_cast<uint32_t>(g & 1));
+    }
+    cycles_out[blockIdx.x] = clock64() - c0;
+    if (!ok) atomicExch(status, 1);
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, 512);
+}
+}  // namespace
+
+extern "C" int lg_umma_mma_rate(int kind, int N, int groups, int ctas, long long* cycles_out, int* status,
+                                void* stream) {
+  if ((kind != 0 && kind != 1) || N < 16 || N > 256 || N % 16 || groups < 1 || groups > 100000 || ctas < 1 ||
+      ctas > 1024 || !cycles_out || !status)
+    return 1;
+  const int smem = (kRows + 256) * kAtom + 1024;
+  if (cudaFuncSetAttribute(mma_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return 2;
+  mma_rate_kernel<<<ctas, 128, smem, static_cast<cudaStream_t>(stream)>>>(kind, N, groups, cycles_out, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
