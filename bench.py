@@ -1,26 +1,34 @@
 #!/usr/bin/env python
 """Benchmark of the B200-native GLM MoE block.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode1|decode2|prefill256]
-    python bench.py --impl reference ...      # CPU restatement of the reference path
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg3|cfg4|prefill256|decode1|decode2]
+    python bench.py --impl reference ...      # the CPU restatement of the reference path
 
-Workload (default decode1): the full-size decode MoE layer (d=4096, 128
-experts, top-8, 8 groups / 4 kept, F=1536, one shared expert, scale 2.5) at
-M=1 token; decode2 is the width-two MTP verify (M=2); prefill256 is M=256.
-A step is one MoE-layer forward.  Steps cycle through `--layers` (default 8)
-independently generated layers so that no step finds its weights in L2
-(8 x 1.33 GB of weights > 126 MB L2).  Each layer's forward is a CUDA graph
-captured from the public module call; the timed region is K graph replays
-bracketed by CUDA events.  With N > 1 each rank runs its own replica
-(decode shards by independent token streams; no collective on the data
-path) and `value` is the sum over ranks.
+Workloads (the benchmark plan's configs; d=4096, 128 experts, top-8, 8 groups /
+4 kept, F=1536, one shared expert, routed scale 2.5; seeded synthetic data):
+  cfg3 (default)  42 stacked MoE layers at M=4096 tokens, an unweighted RMSNorm
+                  between layers (livglm_b200/stack.py); a step is one pass of
+                  the 4096 tokens through the 42 layers.  With N > 1 GPUs the
+                  routed experts are sharded expert-parallel (128/N per GPU,
+                  NCCL all-to-all dispatch and return, livglm_b200/ep.py), each
+                  rank bringing its own 4096 tokens (weak scaling).
+  cfg4            one layer at M=16384 with the Zipf(1.2) correction bias
+                  (livglm_b200/workloads.py); N > 1: expert-parallel, the 16384
+                  tokens split over the ranks (strong scaling).
+  prefill256      config 2: one layer at M=256.
+  decode1/2       config 1: one layer at M=1 / M=2 (MTP width-two verify);
+                  N > 1 runs N independent replicas.
+Single-layer workloads cycle through `--layers` independently generated
+layers (weights > L2).  Without expert parallelism every step is replayed
+from a CUDA graph captured from the public module call.  `value` is MoE-layer
+tokens/s (tokens x layers per step / time), summed over ranks.
 """
 
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -32,35 +40,49 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-WORKLOADS = {"decode1": 1, "decode2": 2, "prefill256": 256}
+WORKLOADS = {
+    "cfg3": {"cfg": "cfg3", "M": 4096, "layers": 42, "kind": "stack", "steps": 10},
+    "cfg4": {"cfg": "cfg4", "M": 16384, "layers": 2, "kind": "layer", "steps": 20, "zipf": True},
+    "prefill256": {"cfg": "cfg2", "M": 256, "layers": 8, "kind": "layer", "steps": 200},
+    "decode1": {"cfg": "cfg1", "M": 1, "layers": 8, "kind": "layer", "steps": 4000},
+    "decode2": {"cfg": "cfg1", "M": 2, "layers": 8, "kind": "layer", "steps": 4000},
+}
 CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
-# kernel, from an ncu capture of this bench's command (workload, stage)
+# kernel, from an ncu capture of this bench's command (workload -> bytes)
 MEASURED_TRAFFIC = {
-    ("decode1", "gate_up"): 80.53e6,
+    "decode1": 80.53e6,
 }
 
 
 def parse_args(argv=None):
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=4000)
-    p.add_argument("--warmup", type=int, default=200)
+    p.add_argument("--steps", type=int, default=None, help="timed steps (default per workload)")
+    p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=tuple(WORKLOADS), default="decode1")
-    p.add_argument("--layers", type=int, default=8)
+    p.add_argument("--workload", choices=tuple(WORKLOADS), default="cfg3")
+    p.add_argument("--layers", type=int, default=None, help="layers cycled (single-layer workloads)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline sample")
-    return p.parse_args(argv)
+    a = p.parse_args(argv)
+    wl = WORKLOADS[a.workload]
+    if a.steps is None:
+        a.steps = wl["steps"]
+    if a.layers is None:
+        a.layers = wl["layers"]
+    a.warmup = max(a.warmup, 3)
+    return a
 
 
 # ----------------------------------------------------------------- utils ---
 
 def measured_peaks() -> dict:
+    """HBM and bf16 peaks measured on this pool (MEASURED_PEAKS.json), else the
+    pool's recorded fallback."""
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         try:
@@ -69,6 +91,36 @@ def measured_peaks() -> dict:
         except (KeyError, ValueError):
             pass
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def fp4_peak_tflops() -> dict:
+    """Dense kind::mxf4 tcgen05 throughput measured on this GPU by the
+    self-test library's MMA-rate kernel (M=128, N=256, K=64 per MMA, one
+    issuing thread per SM), or the nominal 9 PFLOP/s when it is not built."""
+    try:
+        import torch
+
+        lib = ctypes.CDLL(str(ROOT / "tests" / "_build" / "liblivglm_umma_selftest.so"))
+        fn = lib.lg_umma_mma_rate
+        fn.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                       ctypes.c_void_p]
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        cyc = torch.zeros(sms, dtype=torch.int64, device="cuda")
+        st = torch.zeros(1, dtype=torch.int32, device="cuda")
+        fn(0, 256, 20, sms, cyc.data_ptr(), st.data_ptr(), None)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        groups = 200
+        e0.record()
+        rc = fn(0, 256, groups, sms, cyc.data_ptr(), st.data_ptr(), None)
+        e1.record()
+        torch.cuda.synchronize()
+        if rc == 0 and int(st.item()) == 0:
+            flop = 2 * 128 * 256 * 64 * 64 * groups * sms
+            return {"tflops": flop / e0.elapsed_time(e1) / 1e9, "source": "measured (tcgen05 kind::mxf4 MMA rate)"}
+    except (OSError, AttributeError, RuntimeError):
+        pass
+    return {"tflops": 9000.0, "source": "nominal (dense FP4, B200)"}
 
 
 class ClockSampler:
@@ -121,8 +173,9 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def layer_bytes(cfg, M: int, unique: float) -> dict:
-    """Algorithmic HBM bytes of one layer call and of its gate/up stage."""
+def layer_work(cfg, M: int, unique: float) -> dict:
+    """Algorithmic HBM bytes and FLOPs of one layer call and of its stages
+    (weights read once per call; activations once each way)."""
     d, F, E, k = cfg.hidden_size, cfg.moe_intermediate_size, cfg.n_routed_experts, cfg.num_experts_per_tok
     Fs = cfg.shared_intermediate_size
     per_proj = F * d // 2 + F * d // 32
@@ -131,34 +184,52 @@ def layer_bytes(cfg, M: int, unique: float) -> dict:
     router = E * d * 4 + E * 4 + M * d * 2 + M * E * 4
     combine = (M * k * d + M * d) * 2 + M * k * 4 + M * d * 4
     layer = unique * 3 * per_proj + 3 * Fs * d * 2 + E * d * 4 + E * 4 + M * d * 2 + M * d * 4
-    return {"gate_up": gate_up, "down": down, "router": router, "combine": combine, "layer": layer,
-            "per_expert": 3 * per_proj}
+    flops = {"gate_up": 2 * M * k * 2 * d * F, "gate_up_shared": 2 * M * 2 * d * Fs,
+             "down": 2 * M * k * d * F, "down_shared": 2 * M * d * Fs, "router": 2 * M * d * E}
+    flops["layer"] = sum(flops.values())
+    return {"bytes": {"gate_up": gate_up, "down": down, "router": router, "combine": combine, "layer": layer},
+            "flops": flops, "per_expert_bytes": 3 * per_proj}
+
+
+def kernels_per_layer(M: int, batched_tc: bool) -> int:
+    """Kernels of this library launched by one lg_moe_forward call."""
+    if M == 1:
+        return 6  # router logits, select+dispatch, gate/up, activation split, tensor-core down, combine
+    if M <= 4:
+        return 5
+    if batched_tc:
+        # router logits, select, dispatch, route tiles, inverse permutation,
+        # route split, routed / shared gate/up, routed / shared down, combine
+        return 11
+    return 6  # router logits, select, dispatch, gate/up GEMV, down GEMV, combine
 
 
 # -------------------------------------------------------------- CPU side ---
 
-def cpu_sample(cfg, tn: dict, x_bits, budget_s: float) -> dict:
-    """Time the oracle port of the layer on host cores, one token per call,
-    until the budget is spent (at least two tokens)."""
+def cpu_sample(cfg, tn: dict, x_bits, tokens_per_call: int, budget_s: float) -> dict:
+    """Layer-tokens/s of the CPU restatement of the reference path on the host
+    cores: calls of `tokens_per_call` tokens through one layer until the budget
+    is spent (at least two calls)."""
     from oracle import moe_oracle as mo
 
     n_threads = os.cpu_count() or 1
-    mo.moe_forward(x_bits[:1], tn, cfg)  # warm caches / build
+    n = max(1, tokens_per_call)
+    mo.moe_forward(x_bits[:n], tn, cfg)  # warm caches / build
     t0 = time.perf_counter()
-    n = 0
+    calls = 0
     while True:
-        mo.moe_forward(x_bits[n % len(x_bits):n % len(x_bits) + 1], tn, cfg)
-        n += 1
+        mo.moe_forward(x_bits[:n], tn, cfg)
+        calls += 1
         el = time.perf_counter() - t0
-        if (el >= budget_s and n >= 2) or n >= 10_000:
+        if (el >= budget_s and calls >= 2) or calls >= 10_000:
             break
-    return {"value": n / el, "unit": "tokens/s", "cores": n_threads, "kind": "port",
-            "sample": f"{n} single-token calls of the NumPy/C oracle (dequantise-then-matmul, BLAS threads="
-                      f"{n_threads}) on one cfg1 layer, {el:.1f} s"}
+    return {"value": calls * n / el, "unit": "tokens/s", "cores": n_threads, "kind": "port",
+            "sample": f"{calls} calls of {n} token(s) through one cfg1-shaped layer with the NumPy/C "
+                      f"restatement (BLAS threads={n_threads}), {el:.1f} s"}
 
 
 def run_reference(args) -> None:
-    """--impl reference: the CPU restatement of the reference path."""
+    """--impl reference: the CPU restatement of the reference path, rank 0."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -170,35 +241,38 @@ def run_reference(args) -> None:
     from oracle import moe_oracle as mo
     from oracle.torch_bridge import bank_to_numpy
 
+    wl = WORKLOADS[args.workload]
     torch.set_num_threads(os.cpu_count() or 1)
-    cfg = CONFIGS["cfg1"]
-    M = WORKLOADS[args.workload]
+    cfg = CONFIGS[wl["cfg"]]
+    M = wl["M"]
+    n = min(M, 32)  # tokens per CPU call: a bounded sample of the workload
     t = synthetic.layer_weights(cfg, seed=0, device="cpu")
     tn = bank_to_numpy(t)
-    x = mo.f32_to_bf16_bits(np.random.default_rng(0).standard_normal((max(M, 8), cfg.hidden_size)).astype(np.float32))
-    for _ in range(min(args.warmup, 1)):
-        mo.moe_forward(x[:M], tn, cfg)
+    x = mo.f32_to_bf16_bits(np.random.default_rng(0).standard_normal((n, cfg.hidden_size)).astype(np.float32))
+    mo.moe_forward(x, tn, cfg)
     budget = 60.0
-    t0 = time.perf_counter()
-    n = 0
-    while n < args.steps:
-        mo.moe_forward(x[:M], tn, cfg)
-        n += 1
-        if time.perf_counter() - t0 > budget:
+    times = []
+    t_all = time.perf_counter()
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        mo.moe_forward(x, tn, cfg)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > budget:
             break
-    el = time.perf_counter() - t0
-    value = n * M / el
+    el = sum(times)
+    value = len(times) * n / el
     cores = os.cpu_count() or 1
     line = {
         "impl": "reference", "metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s",
-        "n_gpus": args.gpus, "steps": n, "warmup": args.warmup, "ms_per_step": 1e3 * el / n,
+        "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup, "ms_per_step": 1e3 * el / len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"cfg1-{args.workload}", "M": M, "hidden_size": 4096, "n_routed_experts": 128,
-                   "num_experts_per_tok": 8, "moe_intermediate_size": 1536},
+        "config": {"workload": args.workload, "M": M, "hidden_size": cfg.hidden_size,
+                   "n_routed_experts": cfg.n_routed_experts, "num_experts_per_tok": cfg.num_experts_per_tok,
+                   "moe_intermediate_size": cfg.moe_intermediate_size},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{n} of {args.steps} requested steps (M={M}) of the NumPy/C restatement of "
-                                   f"kg36/livglm moe.py/expert_ssd.py in {el:.1f} s (MLX, the reference's own "
-                                   "runtime, is not installable here)"},
+                         "sample": f"{len(times)} calls of {n} tokens through one layer of the NumPy/C "
+                                   "restatement of kg36/livglm moe.py/expert_ssd.py/layers.py (MLX, the "
+                                   "reference's own runtime, is not installable here)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -206,13 +280,9 @@ def run_reference(args) -> None:
 
 # -------------------------------------------------------------- GPU side ---
 
-def run_ours(args) -> None:
+def setup_dist():
     import torch
     import torch.distributed as dist
-
-    from livglm_b200 import _native, synthetic
-    from livglm_b200.config import CONFIGS
-    from livglm_b200.moe import build_layer
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -223,138 +293,152 @@ def run_ours(args) -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    return world, rank, local, dev
 
-    cfg = CONFIGS["cfg1"]
-    M = WORKLOADS[args.workload]
-    L = max(1, args.layers)
-    _native.load()
-    layers, xs = [], []
-    for i in range(L):
-        t = synthetic.layer_weights(cfg, layer=i, seed=rank, device=dev)
-        layers.append(build_layer(cfg, t, layer_idx=i))
-        xs.append(synthetic.hidden_states(cfg, M, seed=1000 * rank + i, device=dev))
+
+def timed_region(run_steps, steps: int, warmup: int, world: int, sampler=None) -> float:
+    """Device time (ms, max over ranks) of exactly `steps` steps after
+    `warmup` untimed ones, bracketed by a barrier and synchronisation."""
+    import torch
+    import torch.distributed as dist
+
+    run_steps(warmup)
     torch.cuda.synchronize()
-
-    # routing statistics (distinct experts per call) for the byte count
-    uniq = []
-    for i in range(L):
-        _, _, idx = layers[i](xs[i], return_route=True)
-        uniq.append(len(set(idx.view(torch.int32).reshape(-1).tolist())))
-    U = sum(uniq) / len(uniq)
-
-    # warm every layer once outside capture (workspace allocation)
-    stream = torch.cuda.Stream(dev)
-    stream.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(stream):
-        for i in range(L):
-            layers[i](xs[i])
-    torch.cuda.current_stream(dev).wait_stream(stream)
-    torch.cuda.synchronize()
-
-    def capture(traced: bool):
-        if traced:
-            _native.trace_enable(L)  # one trace slot per captured layer
-        gs = []
-        for i in range(L):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                layers[i](xs[i])
-            gs.append(g)
-        torch.cuda.synchronize()
-        return gs
-
-    def capture_stack():
-        """One graph of all L layers in order, as a decode step through the
-        model's MoE layers is captured: consecutive layers chain by
-        programmatic dependent launch like the kernels inside a layer."""
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            for i in range(L):
-                layers[i](xs[i])
-        torch.cuda.synchronize()
-        return g
-
-    def timed(gs, steps: int, stack=None) -> float:
-        """Exactly `steps` layer forwards: whole replays of the L-layer graph,
-        then single-layer graphs for the remainder."""
-        def run(n: int) -> None:
-            full = n // L if stack is not None else 0
-            for _ in range(full):
-                stack.replay()
-            for s in range(n - full * L):
-                gs[s % L].replay()
-        run(max(args.warmup, 3))
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ev0.record()
-        run(steps)
-        ev1.record()
-        torch.cuda.synchronize()
-        return ev0.elapsed_time(ev1)
-
-    # (1) the timed region: plain graphs (kernels chained by programmatic
-    #     dependent launch, no trace events between them)
-    graphs = capture(traced=False)
-    stack = capture_stack()
-    sampler = ClockSampler(local)
-    with sampler:
-        time.sleep(0.25)
-        ms = timed(graphs, args.steps, stack)
-    del stack
-    # (2) per-stage device times: the same graphs with CUDA events between the
-    #     stages (which serialises the stages), replayed for the same steps
-    traced_graphs = capture(traced=True)
-    ms_traced = timed(traced_graphs, args.steps)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    stages = _native.trace_read(L)  # last replay of each layer's traced graph
-    del traced_graphs
-    _native.trace_enable(0)
-
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler is not None:
+        sampler.__enter__()
+        time.sleep(0.2)
+    ev0.record()
+    run_steps(steps)
+    ev1.record()
+    torch.cuda.synchronize()
+    if sampler is not None:
+        sampler.__exit__(None, None, None)
+    ms = ev0.elapsed_time(ev1)
     if world > 1:
-        tt = torch.tensor([ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
 
-    # ---- e2e: public module call with pinned host buffers (eager) ----------
-    K_e2e = min(args.steps, 2000)
+
+def build_layers(args, wl, cfg, world, rank, dev):
+    """The workload's layers on this rank: single-GPU ExpertSSDMoE layers, or
+    ExpertParallelMoE layers holding E / world local experts."""
+    from livglm_b200 import synthetic, workloads
+    from livglm_b200.moe import build_layer
+
+    bias = workloads.cfg4_bias(dev) if wl.get("zipf") else None
+    ep = world > 1 and (wl["kind"] == "stack" or bool(wl.get("zipf")))
+    layers = []
+    for i in range(args.layers):
+        if ep:
+            from livglm_b200.ep import ExpertParallelMoE
+
+            per = cfg.n_routed_experts // world
+            t = synthetic.layer_weights(cfg, layer=i, seed=0, device=dev, router_bias=bias, experts=per,
+                                        expert_seed=1 + rank)
+            layers.append(ExpertParallelMoE(cfg, i, t))
+        else:
+            t = synthetic.layer_weights(cfg, layer=i, seed=rank, device=dev, router_bias=bias)
+            layers.append(build_layer(cfg, t, layer_idx=i))
+        del t
+    return layers, ep
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from livglm_b200 import _native, synthetic, workloads
+    from livglm_b200.config import CONFIGS
+    from livglm_b200.stack import MoEStack
+
+    wl = WORKLOADS[args.workload]
+    world, rank, local, dev = setup_dist()
+    cfg = CONFIGS[wl["cfg"]]
+    _native.load()
+    stack_kind = wl["kind"] == "stack"
+    M = wl["M"]
+    if wl.get("zipf") and world > 1:
+        M = wl["M"] // world  # config 4: the 16384 tokens split over the ranks
+    layers, ep = build_layers(args, wl, cfg, world, rank, dev)
+    L = len(layers)
+    xs = [synthetic.hidden_states(cfg, M, seed=1000 * rank + i, device=dev) for i in range(1 if stack_kind else L)]
+    torch.cuda.synchronize()
+
+    # routing statistics of one call (distinct experts, load per expert)
+    idx = layers[0](xs[0], return_route=True)[2]
+    U = float(len(set(idx.view(torch.int32).reshape(-1).tolist())))
+    stats = workloads.load_stats(idx, cfg.n_routed_experts)
+
+    stack = MoEStack(layers) if stack_kind else None
+    use_graph = not ep
+
+    def forward(i: int):
+        return stack(xs[0]) if stack_kind else layers[i % L](xs[i % L])
+
+    # one CUDA graph per step shape (eager under expert parallelism: the
+    # exchange sizes reach the host every layer)
+    graphs = []
+    if use_graph:
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for i in range(1 if stack_kind else L):
+                forward(i)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize()
+        for i in range(1 if stack_kind else L):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                forward(i)
+            graphs.append(g)
+        torch.cuda.synchronize()
+
+    def run_steps(n: int) -> None:
+        for i in range(n):
+            if use_graph:
+                graphs[i % len(graphs)].replay()
+            else:
+                forward(i)
+
+    sampler = ClockSampler(local)
+    ms = timed_region(run_steps, args.steps, args.warmup, world, sampler)
+    ms_step = ms / args.steps
+    layers_per_step = L if stack_kind else 1
+    value = world * M * layers_per_step * args.steps / (ms * 1e-3)
+    del graphs
+
+    # per-stage device times of one layer (single GPU; the stages serialise
+    # under the trace events)
+    stage = {}
+    if world == 1:
+        _native.trace_enable(4)
+        for _ in range(4):
+            layers[0](xs[0])
+        torch.cuda.synchronize()
+        st = _native.trace_read(4)
+        _native.trace_enable(0)
+        stage = {k: statistics.fmean(s_[k] for s_ in st) for k in _native.TRACE_STAGES}
+
+    # ---- e2e: the public call with the tokens and the result on the host ----
     x_host = torch.empty(M, cfg.hidden_size, dtype=torch.bfloat16, pin_memory=True)
     x_host.copy_(xs[0].cpu())
     out_host = torch.empty(M, cfg.hidden_size, dtype=torch.float32, pin_memory=True)
     x_dev = torch.empty_like(xs[0])
+    K_e2e = max(1, min(args.steps, 2000))
 
-    def e2e_step(s: int, host_api: bool) -> None:
-        if host_api:  # tokens and result in page-locked host memory, handed to the module
-            layers[s % L](x_host, out=out_host)
-        else:         # device tensors, with the caller's own copies
+    def e2e_steps(n: int) -> None:
+        for i in range(n):
             x_dev.copy_(x_host, non_blocking=True)
-            out_host.copy_(layers[s % L](x_dev), non_blocking=True)
+            y = stack(x_dev) if stack_kind else layers[i % L](x_dev)
+            out_host.copy_(y, non_blocking=True)
 
-    def e2e_ms(host_api: bool) -> float:
-        for s in range(max(args.warmup, 3) if args.warmup < 50 else 50):
-            e2e_step(s, host_api)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for s in range(K_e2e):
-            e2e_step(s, host_api)
-        e1.record()
-        torch.cuda.synchronize()
-        ms_ = e0.elapsed_time(e1)
-        if world > 1:
-            tt = torch.tensor([ms_], device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            ms_ = float(tt.item())
-        return ms_
-
-    ms_e2e = e2e_ms(True)
-    ms_e2e_copies = e2e_ms(False)
+    ms_e2e = timed_region(e2e_steps, K_e2e, 1, world)
 
     # ---- CPU baseline (rank 0, N=1 only) -------------------------------------
     cpu = None
@@ -364,7 +448,9 @@ def run_ours(args) -> None:
         t0 = synthetic.layer_weights(cfg, layer=0, seed=0, device=dev)
         tn = bank_to_numpy(t0)
         del t0
-        cpu = cpu_sample(cfg, tn, to_numpy(synthetic.hidden_states(cfg, 8, seed=0, device=dev)), args.cpu_seconds)
+        n_cpu = min(M, 32)
+        cpu = cpu_sample(cfg, tn, to_numpy(synthetic.hidden_states(cfg, n_cpu, seed=0, device=dev)), n_cpu,
+                         args.cpu_seconds)
 
     if rank != 0:
         if world > 1:
@@ -372,50 +458,72 @@ def run_ours(args) -> None:
         return
 
     peaks = measured_peaks()
-    by = layer_bytes(cfg, M, U)
-    # kernels per layer call: decode chain 5 (router logits, select + dispatch,
-    # gate/up, down, combine), plus the activation split of the tensor-core
-    # down kernel for one token (on unless LIVGLM_TC_DOWN=0)
-    tc_down = M == 1 and os.environ.get("LIVGLM_TC_DOWN", "1") != "0"
-    launches_per_step = (6 if tc_down else 5) if M <= 4 else 6
-    mean = {k: statistics.fmean(s[k] for s in stages) for k in _native.TRACE_STAGES} if stages else {}
-    dominant = max(mean, key=mean.get) if mean else "gate_up"
-    dom_ms = mean.get(dominant, float("nan"))
-    dom_bytes = by[dominant]
-    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9 if dom_ms and dom_ms > 0 else None
-    ms_step = ms / args.steps
-    value = world * M * args.steps / (ms * 1e-3)
-    layer_gbs = by["layer"] / (ms_step * 1e-3) / 1e9
+    fp4 = fp4_peak_tflops()
+    work = layer_work(cfg, M, U)
+    batched_tc = M >= 64
+    # dominant stage and its roofline: the larger of its HBM and FP4-tensor times
+    if stage:
+        dominant = max(stage, key=stage.get)
+        dom_ms = stage[dominant]
+    else:
+        dominant, dom_ms = "layer", ms_step / layers_per_step
+    dom_bytes = work["bytes"].get(dominant, work["bytes"]["layer"])
+    dom_flops = {"gate_up": work["flops"]["gate_up"] + work["flops"]["gate_up_shared"],
+                 "down": work["flops"]["down"] + work["flops"]["down_shared"],
+                 "router": work["flops"]["router"]}.get(dominant, work["flops"]["layer"])
+    t_hbm = dom_bytes / (peaks["hbm_gbs"] * 1e9)
+    t_tc = dom_flops / (fp4["tflops"] * 1e12)
+    if t_tc > t_hbm:
+        bound, achieved, peak, unit = "tensor", dom_flops / (dom_ms * 1e-3) / 1e12, fp4["tflops"], "TFLOP/s"
+    else:
+        bound, achieved, peak, unit = "hbm", dom_bytes / (dom_ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s"
+    layer_ms = ms_step / layers_per_step
+    layer_t_hbm = work["bytes"]["layer"] / (peaks["hbm_gbs"] * 1e9)
+    layer_t_tc = work["flops"]["layer"] / (fp4["tflops"] * 1e12)
+    workload_name = {"cfg3": f"cfg3: {L} stacked layers, M={M} per rank",
+                     "cfg4": f"cfg4: Zipf(1.2) bias, M={M} per rank",
+                     "prefill256": "cfg2: M=256", "decode1": "cfg1: M=1", "decode2": "cfg1: M=2 (MTP verify)"}
+    routed_gb = L * work["per_expert_bytes"] * cfg.n_routed_experts / world / 1e9
     line = {
         "metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": "strong" if (wl.get("zipf") and world > 1) else "weak", "vs_baseline": None,
+        "dtype": ("mxf4 (E2M1 weights x E2M1-term activations), f32 accumulate" if batched_tc
+                  else "fp4 weights x f16/bf16 activations, f32 accumulate"),
         "data": "synthetic (seeded N(0,1) bf16 tokens; N(0,0.02) weights, routed MXFP4 g32, shared bf16)",
-        "config": {"workload": f"cfg1-{args.workload}", "M": M, "hidden_size": cfg.hidden_size,
-                   "n_routed_experts": cfg.n_routed_experts, "num_experts_per_tok": cfg.num_experts_per_tok,
-                   "n_group": cfg.n_group, "topk_group": cfg.topk_group,
-                   "moe_intermediate_size": cfg.moe_intermediate_size, "layers_rotated": L,
-                   "graph": f"one CUDA graph of the {L} layers, replayed",
-                   "l2": f"inputs larger than L2: {L} distinct layers cycled ({L * 1.33:.1f} GB of weights)",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "operands": "x bf16, routed w MXFP4 (E2M1+E8M0), shared w bf16, f32 accumulate, f32 out"},
-        "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peaks["hbm_gbs"],
-                     "unit": "GB/s", "frac": (achieved / peaks["hbm_gbs"]) if achieved else None,
-                     "traffic": MEASURED_TRAFFIC.get((args.workload, dominant)), "peak_source": peaks["source"],
-                     "algorithmic_bytes_per_launch": dom_bytes, "launch_ms": dom_ms},
-        "e2e": {"value": world * M * K_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
+        "config": {"workload": workload_name[args.workload], "M": M, "layers_per_step": layers_per_step,
+                   "hidden_size": cfg.hidden_size, "n_routed_experts": cfg.n_routed_experts,
+                   "num_experts_per_tok": cfg.num_experts_per_tok, "n_group": cfg.n_group,
+                   "topk_group": cfg.topk_group, "moe_intermediate_size": cfg.moe_intermediate_size,
+                   "graph": "one CUDA graph per step, replayed" if use_graph else "eager (expert-parallel)",
+                   "l2": f"inputs larger than L2: {L} distinct layers, {routed_gb:.1f} GB of routed weights per GPU",
+                   "parallelism": (f"expert-parallel x{world} ({cfg.n_routed_experts // world} experts/GPU, NCCL "
+                                   "all-to-all)") if ep else (f"replicas x{world}" if world > 1 else "single GPU")},
+        "roofline": {"bound": bound, "kernel": f"{dominant} stage", "achieved": achieved, "peak": peak, "unit": unit,
+                     "frac": achieved / peak if peak else None,
+                     "traffic": MEASURED_TRAFFIC.get(args.workload) if dominant == "gate_up" else None,
+                     "peak_source": peaks["source"] if unit == "GB/s" else fp4["source"],
+                     "algorithmic_bytes_per_launch": dom_bytes, "algorithmic_flops_per_launch": dom_flops,
+                     "launch_ms": dom_ms},
+        "e2e": {"value": world * M * layers_per_step * K_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": M * cfg.hidden_size * 2, "d2h_bytes_per_step": M * cfg.hidden_size * 4,
                 "steps": K_e2e,
-                "path": "ExpertSSDMoE.__call__(x_host, out=out_host) eager (ctypes -> C ABI): bf16 tokens and "
-                        "f32 result in page-locked host memory, read and written by the kernels over the host link",
-                "with_caller_copies": {"value": world * M * K_e2e / (ms_e2e_copies * 1e-3),
-                                       "path": "device tensors; the caller copies x in and the result out "
-                                               "with non-blocking copies around each call"}},
-        "gpu_launches": launches_per_step * args.steps,
+                "path": "pinned host tokens -> device copy -> public module call(s) -> f32 result copied to "
+                        "pinned host memory, every step"},
+        "gpu_launches": kernels_per_layer(M, batched_tc) * layers_per_step * args.steps,
         "clocks": sampler.summary(),
-        "extra": {"layer_hbm_gbs": layer_gbs, "layer_hbm_frac": layer_gbs / peaks["hbm_gbs"],
-                  "layer_bytes": by["layer"], "unique_experts_per_call": U,
-                  "stage_ms": mean, "ms_per_step_stages_serialised": ms_traced / args.steps},
+        "extra": {"layer_ms": layer_ms,
+                  "layer_roofline": {"hbm_us": layer_t_hbm * 1e6, "fp4_us": layer_t_tc * 1e6,
+                                     "frac": max(layer_t_hbm, layer_t_tc) / (layer_ms * 1e-3),
+                                     "hbm_frac": layer_t_hbm / (layer_ms * 1e-3),
+                                     "fp4_frac": layer_t_tc / (layer_ms * 1e-3)},
+                  "layer_bytes": work["bytes"]["layer"], "layer_flops": work["flops"]["layer"],
+                  "fp4_peak_tflops": fp4["tflops"], "fp4_peak_source": fp4["source"],
+                  "bf16_peak_tflops": peaks["bf16_tflops"],
+                  "unique_experts_per_call": U, "stage_ms": stage,
+                  "stack_tokens_per_s": world * M * args.steps / (ms * 1e-3) if stack_kind else None,
+                  "load": {k: v for k, v in stats.items() if k != "counts"},
+                  "expert_counts": stats["counts"] if wl.get("zipf") else None},
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu

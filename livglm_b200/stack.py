@@ -38,18 +38,22 @@ class MoEStack:
         self.layers = layers
         self.eps = eps
         self.workspace = Workspace()
-        for layer in layers:
-            layer.use_workspace(self.workspace)
+        for layer in layers:  # expert-parallel layers keep their own scratch
+            if hasattr(layer, "use_workspace"):
+                layer.use_workspace(self.workspace)
 
-    def __call__(self, x: torch.Tensor, *, inputs: list | None = None) -> torch.Tensor:
-        """x: bf16 [M, d].  With `inputs` (a list), the bf16 input of every
-        layer is appended to it (for layer-by-layer checks)."""
+    def __call__(self, x: torch.Tensor, *, inputs: list | None = None,
+                 outputs: list | None = None) -> torch.Tensor:
+        """x: bf16 [M, d].  With `inputs` / `outputs` (lists), the bf16 input
+        and the f32 output of every layer are appended (layer-by-layer checks)."""
         h = x
         out = None
         for i, layer in enumerate(self.layers):
             if inputs is not None:
                 inputs.append(h)
             out = layer(h)
+            if outputs is not None:
+                outputs.append(out)
             if i + 1 < len(self.layers):
                 h = unweighted_rmsnorm_bf16(out, self.eps)
         return out

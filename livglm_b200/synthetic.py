@@ -34,9 +34,16 @@ def hidden_states(cfg: MoEConfig, tokens: int, *, seed: int = 0, device="cuda") 
 
 
 def layer_weights(cfg: MoEConfig, *, layer: int = 0, seed: int = 0, device="cuda",
-                  expert_chunk: int = 16, router_bias: torch.Tensor | None = None) -> dict:
-    """One MoE layer's tensors, stacked per expert (the HBM bank layout)."""
+                  expert_chunk: int = 16, router_bias: torch.Tensor | None = None,
+                  experts: int | None = None, expert_seed: int | None = None) -> dict:
+    """One MoE layer's tensors, stacked per expert (the HBM bank layout).
+
+    experts / expert_seed: generate routed banks for only that many experts,
+    from their own seed (an expert-parallel rank's local slice; the router and
+    shared expert still follow `seed`, so every rank holds the same ones)."""
     d, F, E = cfg.hidden_size, cfg.moe_intermediate_size, cfg.n_routed_experts
+    n_banks = E if experts is None else experts
+    bank_seed = seed if expert_seed is None else expert_seed
     Fs = cfg.shared_intermediate_size
     out: dict[str, torch.Tensor] = {}
     g = _gen(device, seed, layer, "router_weight")
@@ -46,11 +53,11 @@ def layer_weights(cfg: MoEConfig, *, layer: int = 0, seed: int = 0, device="cuda
         router_bias = (torch.rand(E, generator=g, device=device) * 0.02 - 0.01)
     out["router_bias"] = router_bias.to(device=device, dtype=torch.float32).contiguous()
     for proj, rows, cols in (("gate", F, d), ("up", F, d), ("down", d, F)):
-        packed = torch.empty(E, rows, cols // 2, dtype=torch.uint8, device=device)
-        scale = torch.empty(E, rows, cols // 32, dtype=torch.uint8, device=device)
-        g = _gen(device, seed, layer, proj)
-        for e0 in range(0, E, expert_chunk):
-            e1 = min(E, e0 + expert_chunk)
+        packed = torch.empty(n_banks, rows, cols // 2, dtype=torch.uint8, device=device)
+        scale = torch.empty(n_banks, rows, cols // 32, dtype=torch.uint8, device=device)
+        g = _gen(device, bank_seed, layer, proj)
+        for e0 in range(0, n_banks, expert_chunk):
+            e1 = min(n_banks, e0 + expert_chunk)
             w = torch.randn(e1 - e0, rows, cols, generator=g, device=device) * 0.02
             packed[e0:e1], scale[e0:e1] = quantize_mxfp4(w)
             del w

@@ -2,7 +2,7 @@
 
 Compiles oracle/router_ref.c into oracle/_build/liboracle.so with gcc, with
 floating-point contraction off so every fmaf/add/mul rounds exactly where the
-source says.  The reference itself (kg36/livglm) is Python + MLX and has no
+source says, and OpenMP across tokens (each token's arithmetic is sequential).  The reference itself (kg36/livglm) is Python + MLX and has no
 C/C++ sources for this path, so there is nothing to build under oracle/_ref.
 """
 
@@ -24,7 +24,7 @@ def build(force: bool = False) -> Path:
     tmp = OUT.with_suffix(f".{os.getpid()}.tmp")
     cmd = [
         "gcc", "-O2", "-std=c11", "-shared", "-fPIC",
-        "-ffp-contract=off", "-fno-fast-math", "-fno-builtin",
+        "-ffp-contract=off", "-fno-fast-math", "-fno-builtin", "-fopenmp",
         str(SRC), "-o", str(tmp), "-lm",
     ]
     subprocess.run(cmd, check=True)

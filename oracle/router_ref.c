@@ -132,10 +132,12 @@ int oracle_router(const uint16_t *x, const float *w, const float *bias, int M,
   if (d % 8 || G < 1 || E % G || g < 1 || g > G || E / G < 2 || k < 1 ||
       k > E || E > 4096)
     return -1;
-  float scores[4096], choice[4096], gscore[4096];
-  int gsel[4096];
   int per = E / G;
+  /* tokens are independent; each (token, expert) sum keeps its own order */
+#pragma omp parallel for schedule(static)
   for (int t = 0; t < M; ++t) {
+    float scores[4096], choice[4096], gscore[4096];
+    int gsel[4096];
     const uint16_t *xt = x + (int64_t)t * d;
     for (int e = 0; e < E; ++e) {
       float lg = oracle_router_logit(xt, w + (int64_t)e * d, d);
