@@ -11,8 +11,9 @@ are data-parallel (each rank brings its own rows).  One call:
    are contiguous per rank, that order also groups the slots by destination;
 2. exchange the per-destination route counts (all-to-all of W integers; the
    split sizes go to the host once per call);
-3. send one bf16 row per route slot, with its expert id local to the
-   destination, by all-to-all;
+3. send one bf16 row per route slot and its expert id local to the
+   destination by all-to-all, and run the local tokens' shared expert while
+   the exchange is in flight;
 4. run the received rows through the local experts (lg_moe_experts with
    top-k 1 over the E/W local experts);
 5. send the bf16 outputs back by the reverse all-to-all, put them back in
@@ -46,17 +47,24 @@ def expert_owner(expert: torch.Tensor, n_experts: int, world: int) -> torch.Tens
 
 def exchange_routes(rows: torch.Tensor, slot_expert: torch.Tensor, perm: torch.Tensor,
                     send_counts: torch.Tensor, n_experts: int, compute_local: LocalCompute,
-                    group=None) -> torch.Tensor:
+                    group=None, overlap: Callable[[], None] | None = None) -> torch.Tensor:
     """Steps 2-5 above: ship route rows to the experts' owners and back.
 
     rows [M, d] (one row per token); slot_expert [M*k] int64 expert id of each
     route slot; perm [M*k] int64 route slots sorted by expert id (stable);
     send_counts [W] int64 slots bound for each rank, in perm order.
     compute_local(x [N, d], local_expert [N] int64) -> [N, d] runs on the
-    received rows.  Returns [M*k, d]: the output of every route slot.
+    received rows.  overlap(), if given, runs after the dispatch exchange is
+    issued and before it is waited for (the shared expert overlaps the
+    transfer that way).  Returns [M*k, d]: the output of every route slot.
+
+    One all-to-all of W counts (whose values reach the host once: NCCL's
+    variable-size exchange takes host split sizes), one of the route rows and
+    one of their expert ids (both issued before overlap() runs), and one of
+    the outputs, which are put back in slot order by a gather through the
+    inverse of perm.
     """
     world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
     per_rank = n_experts // world
     k = slot_expert.numel() // max(1, rows.shape[0])
     d = rows.shape[1]
@@ -72,18 +80,21 @@ def exchange_routes(rows: torch.Tensor, slot_expert: torch.Tensor, perm: torch.T
     e_send = (slot_expert.index_select(0, perm) % per_rank).to(torch.int32)
     x_recv = rows.new_empty((n_recv, d))
     e_recv = torch.empty(n_recv, dtype=torch.int32, device=rows.device)
-    dist.all_to_all_single(x_recv, x_send, recv_split, send_split, group=group)
-    dist.all_to_all_single(e_recv, e_send, recv_split, send_split, group=group)
+    w_x = dist.all_to_all_single(x_recv, x_send, recv_split, send_split, group=group, async_op=True)
+    w_e = dist.all_to_all_single(e_recv, e_send, recv_split, send_split, group=group, async_op=True)
+    if overlap is not None:
+        overlap()
+    w_x.wait()
+    w_e.wait()
     if n_recv:
         y_recv = compute_local(x_recv, e_recv.to(torch.int64)).reshape(n_recv, d).to(rows.dtype)
     else:
         y_recv = rows.new_empty((0, d))
-    del rank
     y_back = rows.new_empty((n_send, d))
     dist.all_to_all_single(y_back, y_recv.contiguous(), send_split, recv_split, group=group)
-    y_slots = rows.new_empty((n_send, d))
-    y_slots.index_copy_(0, perm, y_back)
-    return y_slots
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(n_send, dtype=perm.dtype, device=perm.device)
+    return y_back.index_select(0, inv)
 
 
 class ExpertParallelMoE:
@@ -134,6 +145,15 @@ class ExpertParallelMoE:
         self._cfg = _native.LgConfig.from_config(config)
         self._ws = Workspace()
 
+    def use_workspace(self, ws: Workspace) -> None:
+        """Share one scratch area with other layers run in order on one stream
+        (this layer's router, local experts, shared expert and dispatch all
+        use it, one call after another)."""
+        self._ws = ws
+        for part in (self.gate, self.experts, self.shared_experts):
+            if hasattr(part, "_ws"):
+                part._ws = ws
+
     def _local(self, x: torch.Tensor, local_expert: torch.Tensor) -> torch.Tensor:
         idx = local_expert.to(torch.int32).view(torch.uint32).reshape(-1, 1)
         return self.experts(x, idx).reshape(x.shape[0], self.config.hidden_size)
@@ -164,10 +184,17 @@ class ExpertParallelMoE:
             send_counts = torch.zeros(self.world, dtype=torch.int64, device=dev)
             slot_expert = torch.empty(0, dtype=torch.int64, device=dev)
             perm64 = torch.empty(0, dtype=torch.int64, device=dev)
-        y_slots = exchange_routes(rows, slot_expert, perm64, send_counts, E, self._local, self.group)
+        shared = None
+
+        def run_shared() -> None:  # overlaps the dispatch exchange
+            nonlocal shared
+            if M and c.n_shared_experts > 0:
+                shared = self.shared_experts(rows)
+
+        y_slots = exchange_routes(rows, slot_expert, perm64, send_counts, E, self._local, self.group,
+                                  overlap=run_shared)
         out = torch.empty(M, c.hidden_size, dtype=torch.float32, device=dev)
         if M:
-            shared = self.shared_experts(rows) if c.n_shared_experts > 0 else None
             _native.check(lib.lg_moe_combine(self._cfg, y_slots.data_ptr(), weights.data_ptr(),
                                              shared.data_ptr() if shared is not None else None, M,
                                              out.data_ptr(), stream), "lg_moe_combine")
