@@ -69,6 +69,20 @@ __device__ __forceinline__ uint16_t swiglu_bf16(float g, float u, float limit) {
   float a = round_bf16(__fmul_rn(g, s));
   return f32_to_bf16(__fmul_rn(a, u));
 }
+// bf16(g * bf16(sigmoid(g))) of a bf16 g, the first two roundings of
+// swiglu_bf16 after the clip; tabulated for all 65536 bf16 bit patterns.
+__device__ __forceinline__ uint16_t silu_bf16(float g) {
+  return f32_to_bf16(__fmul_rn(g, round_bf16(own_sigmoidf(g))));
+}
+// swiglu_bf16 with the silu factor read from such a table (same result).
+__device__ __forceinline__ uint16_t swiglu_bf16_tab(float g, float u, float limit, const uint16_t* __restrict__ silu) {
+  if (limit > 0.0f) {
+    g = fminf(g, limit);
+    u = fminf(fmaxf(u, -limit), limit);
+  }
+  const float a = bf16_to_f32(__ldg(silu + f32_to_bf16(g)));
+  return f32_to_bf16(__fmul_rn(a, u));
+}
 
 // ---- MXFP4 (OCP MX, group 32) -------------------------------------------
 // E8M0 scale byte s -> 2^(s-127); 255 is NaN; 0 is the subnormal 2^-127.

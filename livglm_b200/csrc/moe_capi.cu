@@ -17,6 +17,7 @@
 #include "down1_kernel.cuh"
 #include "down_tc.cuh"
 #include "grouped_tc.cuh"
+#include "grouped_dq.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -108,7 +109,7 @@ int validate_tokens(int64_t M, const lg_moe_config* c) {
 
 struct Layout {
   size_t status, logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, xs, bimg, bsc,
-      xterm, xtsc, aterm, atsc, tiles, inv, total;
+      xterm, xtsc, aterm, atsc, tiles, inv, silu, total;
   bool tc;  // batched tensor-core buffers reserved
 };
 
@@ -172,6 +173,7 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   L.xtsc = o;    o += L.tc ? up(kTcTerms * m * k * (d / 32)) : 0;
   L.tiles = o;   o += L.tc ? up((E + 1) * 4) : 0;
   L.inv = o;     o += L.tc ? up(m * k * 4) : 0;
+  L.silu = o;    o += L.tc ? up(65536 * 2) : 0;  // SwiGLU factor table of the bf16 grouped GEMMs
   L.total = o;
   return L;
 }
@@ -390,6 +392,85 @@ int launch_grouped(const lg::gtc::Args& a0, int items_max, const GgMaps& m, cuda
   return cuda_check(cudaGetLastError(), "grouped kernel launch");
 }
 
+bool map_3d_swz(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t n, uint64_t n_stride,
+                uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz);
+
+// Tensor-core calls whose experts average at least this many routes run the
+// routed products with the weights widened to bf16 (grouped_dq.cuh): four
+// K = 16 MMAs per 64 values instead of one K = 64 kind::mxf4 MMA per term,
+// but no activation terms and 256-route tiles.  LIVGLM_BATCHED_DQ=0 / 1
+// forces it off / on for every tensor-core call.
+constexpr int kDqMinRoutesPerExpert = 128;
+bool dq_mode(const lg_moe_config* c, int M) {
+  static const int env = [] {
+    const char* v = std::getenv("LIVGLM_BATCHED_DQ");
+    return v && v[0] == '0' ? 0 : (v && v[0] == '1' ? 1 : -1);
+  }();
+  if (env >= 0) return env == 1;
+  return static_cast<long long>(M) * c->num_experts_per_tok >=
+         static_cast<long long>(kDqMinRoutesPerExpert) * c->n_routed_experts;
+}
+
+template <bool kGateUp>
+int launch_dq(const lg::gdq::Args& a0, long long items_max, const CUtensorMap& A0, const CUtensorMap& A1,
+              const CUtensorMap& B, cudaStream_t s) {
+  using namespace lg::gdq;
+  Args a = a0;
+  const size_t smem = 1024 + kSmemBytes;  // 1024-byte alignment slack
+  auto kern = grouped_dq_kernel<kGateUp>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return cuda_check(e, "grouped bf16 kernel smem attribute");
+  long long grid = num_sms();
+  if (items_max < grid) grid = items_max;
+  if (grid < 1) return LG_OK;
+  kern<<<static_cast<int>(grid), kThreads, smem, s>>>(a, A0, A1, B);
+  return cuda_check(cudaGetLastError(), "grouped bf16 kernel launch");
+}
+
+// Routed gate/up (kGateUp) or down with the bf16-widened weights: route
+// chunks, the token rows gathered to dispatch order (gate/up), the kernel.
+int launch_routed_dq(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M, const int* offsets,
+                     const int* perm, void* ws, const Layout& L, uint16_t* y, bool gate_up, cudaStream_t s) {
+  const int d = c->hidden_size, F = c->moe_intermediate_size, E = c->n_routed_experts, k = c->num_experts_per_tok;
+  const int R = M * k;
+  lg::gdq::Args q{};
+  q.d = d; q.F = F; q.E = E; q.R = R;
+  q.limit = c->swiglu_limit;
+  q.offsets = offsets; q.perm = perm; q.chunk_start = at<int>(ws, L.tiles);
+  q.act = at<uint16_t>(ws, L.act); q.y = y;
+  q.silu = at<uint16_t>(ws, L.silu);
+  q.status = at<int>(ws, L.status);
+  uint16_t* xp = at<uint16_t>(ws, L.xterm);  // [R][d] bf16: fits the token-term region
+  const long long chunks_max = static_cast<long long>(R) / lg::gdq::kNMax + std::min(E, R);
+  CUtensorMap A0, A1, B;
+  if (gate_up) {
+    lg::gdq::chunk_table_kernel<<<1, 1024, 0, s>>>(offsets, E, at<int>(ws, L.tiles));
+    lg::gdq::silu_table_kernel<<<256, 256, 0, s>>>(at<uint16_t>(ws, L.silu));
+    const long long vec = static_cast<long long>(R) * (d / 8);
+    lg::gdq::gather_rows_kernel<<<static_cast<int>(std::min<long long>((vec + 255) / 256, 8LL * num_sms())), 256, 0,
+                                  s>>>(x, d, k, perm, offsets, E, xp);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_check(e, "route gather launch");
+    q.ks_count = d / 64; q.rb_count = F / 128; q.rb_rows = 128; q.acc1_rows = 0;
+    q.sc0 = w->gate_scale; q.sc1 = w->up_scale;
+    q.sc0_stride = static_cast<long long>(w->gate_scale_stride); q.sc1_stride = static_cast<long long>(w->up_scale_stride);
+    q.sc_row = d / 32;
+    if (!map_3d_swz(&A0, w->gate_packed, d / 2, F, E, w->gate_packed_stride, 32, 128, CU_TENSOR_MAP_SWIZZLE_32B) ||
+        !map_3d_swz(&A1, w->up_packed, d / 2, F, E, w->up_packed_stride, 32, 128, CU_TENSOR_MAP_SWIZZLE_32B) ||
+        !map_2d(&B, xp, static_cast<uint64_t>(d) * 2, R, 128, lg::gdq::kBoxRows, true))
+      return fail(LG_ERR_CUDA, "batched bf16 gate/up: tensor map encoding failed");
+    return launch_dq<true>(q, chunks_max * q.rb_count, A0, A1, B, s);
+  }
+  q.ks_count = F / 64; q.rb_count = d / 256; q.rb_rows = 256; q.acc1_rows = 128;
+  q.sc0 = q.sc1 = w->down_scale;
+  q.sc0_stride = q.sc1_stride = static_cast<long long>(w->down_scale_stride);
+  q.sc_row = F / 32;
+  if (!map_3d_swz(&A0, w->down_packed, F / 2, d, E, w->down_packed_stride, 32, 128, CU_TENSOR_MAP_SWIZZLE_32B) ||
+      !map_2d(&B, q.act, static_cast<uint64_t>(F) * 2, R, 128, lg::gdq::kBoxRows, true))
+    return fail(LG_ERR_CUDA, "batched bf16 down: tensor map encoding failed");
+  return launch_dq<false>(q, chunks_max * q.rb_count, A0, A0, B, s);
+}
+
 // The batched expert passes on the tensor core: token split, route tiles,
 // routed and/or shared gate/up, then routed and/or shared down.  Routing
 // tables (offsets, perm) must be ready; y gets the routed outputs in slot
@@ -418,7 +499,10 @@ int launch_experts_tc(const lg_moe_config* c, const lg_moe_weights* w, const uin
   GgMaps m;
   int rc;
   cudaError_t e;
-  if (with_routed) {
+  const bool dq = with_routed && dq_mode(c, M);
+  if (dq) {
+    if ((rc = launch_routed_dq(c, w, x, M, offsets, perm, ws, L, y, true, s))) return rc;
+  } else if (with_routed) {
     tile_table_kernel<<<1, 1024, 0, s>>>(offsets, E, at<int>(ws, L.tiles));
     cudaMemsetAsync(inv, 0xFF, static_cast<size_t>(R) * 4, s);
     inverse_perm_kernel<<<std::min((R + 255) / 256, 4 * num_sms()), 256, 0, s>>>(perm, offsets, E, inv);
@@ -451,7 +535,9 @@ int launch_experts_tc(const lg_moe_config* c, const lg_moe_weights* w, const uin
     if ((rc = launch_grouped<false, true>(g, g.rb_count * tok_tiles, m, s))) return rc;
   }
   trace_mark(slot, 3, s);
-  if (with_routed) {
+  if (dq) {
+    if ((rc = launch_routed_dq(c, w, x, M, offsets, perm, ws, L, y, false, s))) return rc;
+  } else if (with_routed) {
     Args g = a;
     g.kb_count = F / 256; g.rb_count = d / 128; g.sc_bytes = F / 32; g.sc_swz = F / 32 == 128;
     if (!map_3d(&m.A0, w->down_packed, F / 2, d, E, w->down_packed_stride, 128, 128, true) ||
@@ -682,8 +768,8 @@ bool map_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uin
             CU_TENSOR_MAP_INTERLEAVE_NONE, sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
-bool map_3d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t n, uint64_t n_stride,
-            uint32_t box_inner, uint32_t box_rows, bool sw128) {
+bool map_3d_swz(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t n, uint64_t n_stride,
+                uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
   const PFN_cuTensorMapEncodeTiled_v12000 fn = encode_tiled();
   if (!fn || !aligned(base, 16) || inner % 16 || n_stride % 16) return false;
   const cuuint64_t dims[3] = {inner, rows, n};
@@ -691,8 +777,13 @@ bool map_3d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uin
   const cuuint32_t box[3] = {box_inner, box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+bool map_3d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t n, uint64_t n_stride,
+            uint32_t box_inner, uint32_t box_rows, bool sw128) {
+  return map_3d_swz(m, base, inner, rows, n, n_stride, box_inner, box_rows,
+                    sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 // Needs: one token, d % 128 == 0, F a multiple of 512 up to 1536 (whole

@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include "umma.cuh"
+#include "grouped_dq.cuh"
 
 namespace {
 
@@ -245,5 +246,24 @@ extern "C" int lg_umma_mma_rate(int kind, int N, int groups, int ctas, long long
   if (cudaFuncSetAttribute(mma_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return 2;
   mma_rate_kernel<<<ctas, 128, smem, static_cast<cudaStream_t>(stream)>>>(kind, N, groups, cycles_out, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+// ---- E2M1 -> bf16 widening of the bf16 grouped GEMMs (grouped_dq.cuh) ------------
+// out[i] = the eight bf16 values of words[i] under scale byte scales[i], by the
+// same choice of table or f32 path as the converter warps.
+namespace {
+__global__ void widen_kernel(const uint32_t* words, const uint8_t* scales, int n, uint4* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t S = scales[i];
+  out[i] = lg::gdq::lut_exact(S) ? lg::gdq::widen8(words[i], lg::gdq::make_lut(S)) : lg::gdq::widen8_slow(words[i], S);
+}
+}  // namespace
+
+extern "C" int lg_dq_widen_selftest(const uint32_t* words, const uint8_t* scales, int n, void* out, void* stream) {
+  if (!words || !scales || !out || n < 1 || n > (1 << 24)) return 1;
+  widen_kernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(words, scales, n,
+                                                                               static_cast<uint4*>(out));
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
