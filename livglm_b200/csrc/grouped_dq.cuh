@@ -30,10 +30,11 @@
 // equal size.  Items are ordered (expert, row block, chunk), chunk fastest; one
 // persistent CTA per SM walks items b, b + P, ...
 //
-// Warps: 0 TMA producer of the B rows, 1 MMA issuer (one lane), 2 TMA
-// producer of the packed weights (also prefetches weight bytes into L2 a few
-// stages ahead), 3-18 workers.  Workers widen every stage
-// (thread u: half u / 256 of A row u % 256) and, between items, run the
+// Warps: 0 TMA producer of the B rows (also prefetches the weight bytes into
+// L2 a few stages ahead), 1 MMA issuer (one lane), 2-17 workers in two
+// groups that take alternate stages (thread u widens A row u % 256 of the
+// stages ks % 2 == u / 256, loading its 32 packed bytes a stage straight from
+// global memory a few stages ahead) and, between items, run the
 // epilogue of the previous item (tcgen05.ld of the two accumulators; 512
 // tensor-memory columns, single-buffered): after converting the first stages
 // of item i they wait for item i - 1's accumulators, write its outputs and
@@ -56,22 +57,21 @@
 namespace lg {
 namespace gdq {
 
-constexpr int kBProdWarp = 0, kMmaWarp = 1, kPkProdWarp = 2, kWorkWarp0 = 3, kWorkWarps = 16;
+constexpr int kBProdWarp = 0, kMmaWarp = 1, kWorkWarp0 = 2, kWorkWarps = 16;
 constexpr int kThreads = 32 * (kWorkWarp0 + kWorkWarps);
 constexpr int kWorkThreads = 32 * kWorkWarps;
+constexpr int kGroupWarps = kWorkWarps / 2;  // two worker groups take alternate stages
 constexpr int kNMax = 256;          // routes per item (MMA N)
 constexpr int kBoxRows = 32;        // B rows per TMA box; N is a multiple of it
 constexpr int kBBytes = kNMax * 128;
-constexpr int kPackedBytes = 8192;  // 2 x 128 rows x 32 bytes
 constexpr int kConvBytes = 32768;   // converted slot: 2 x 128 rows x 64 bf16 (two A operands)
-constexpr int kBStages = 3, kPkStages = 8, kConvSlots = 2;
-constexpr int kPkOff = kBStages * kBBytes, kConvOff = kPkOff + kPkStages * kPackedBytes;
+constexpr int kBStages = 4, kConvSlots = 3;
+constexpr int kConvOff = kBStages * kBBytes;
 constexpr int kSmemBytes = kConvOff + kConvSlots * kConvBytes;  // from the 1024-aligned base
 constexpr int kPrefetch = 16;       // stages between an L2 prefetch of weight bytes and their load
 constexpr int kWorkBar = 3;         // named barrier of the worker warps
 constexpr int kSiteBFull = 50 << 8, kSiteBEmpty = 51 << 8, kSiteConv = 52 << 8, kSiteAccFull = 53 << 8,
-              kSiteAccEmpty = 54 << 8, kSiteDrain = 55 << 8, kSiteConvEmpty = 56 << 8, kSitePkFull = 57 << 8,
-              kSitePkEmpty = 58 << 8;
+              kSiteAccEmpty = 54 << 8, kSiteDrain = 55 << 8, kSiteConvEmpty = 56 << 8;
 
 struct Args {
   int d, F, E, R;
@@ -83,6 +83,10 @@ struct Args {
   const int* offsets;      // [E + 1] dispatch offsets
   const int* perm;         // [R] route slot of dispatch position p
   const int* chunk_start;  // [E + 1] route chunks of experts before e
+  const uint8_t* pk0;      // packed bank of accumulator 0 rows (gate or down)
+  const uint8_t* pk1;      // of accumulator 1 rows (up or down)
+  long long pk0_stride, pk1_stride;  // bytes between experts
+  int pk_row;              // packed bytes per row: K / 2
   const uint8_t* sc0;      // scale bank of accumulator 0 rows (gate or down)
   const uint8_t* sc1;      // of accumulator 1 rows (up or down)
   long long sc0_stride, sc1_stride;  // bytes between experts
@@ -241,18 +245,19 @@ __device__ __forceinline__ void prefetch_3d(const CUtensorMap* map, int x, int y
                : "memory");
 }
 
-// mA0 / mA1: 3-D [E][rows][bytes] packed banks of the accumulator 0 / 1 rows,
-// 32 x 128-byte boxes with the 32-byte swizzle; mB: 2-D [R][K * 2 bytes] B rows,
-// 128-byte x 32-row boxes with the 128-byte swizzle.
-// Shared memory: a ring of kBStages B stages (freed by the MMAs' commit), a
-// deeper ring of kPkStages packed-weight stages (freed by the workers once
-// widened) and kConvSlots widened A slots (freed by the MMAs' commit).
+// mA0 / mA1: 3-D [E][rows][bytes] packed banks of the accumulator 0 / 1 rows
+// (L2 prefetches only); mB: 2-D [R][K * 2 bytes] B rows, 128-byte x 32-row
+// boxes with the 128-byte swizzle.
+// Shared memory: a ring of kBStages B stages and kConvSlots widened A slots,
+// both freed by the MMAs' commit.  The packed weight bytes never pass
+// through shared memory: each worker loads its row's 32 bytes of a stage
+// from global memory into registers one of its stages (two stages) early.
 template <bool kGateUp>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_dq_kernel(Args a, const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mA1,
                       const __grid_constant__ CUtensorMap mB) {
   extern __shared__ __align__(1024) unsigned char smraw[];
-  __shared__ __align__(8) uint64_t bfull[kBStages], bempty[kBStages], pfull[kPkStages], pempty[kPkStages];
+  __shared__ __align__(8) uint64_t bfull[kBStages], bempty[kBStages];
   __shared__ __align__(8) uint64_t conv_full[kConvSlots], conv_empty[kConvSlots];
   __shared__ __align__(8) uint64_t acc_full, acc_empty, drain;
   __shared__ uint32_t tslot;
@@ -267,12 +272,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bfull[s], 1);
       mbar_init(&bempty[s], 1);
     }
-    for (int s = 0; s < kPkStages; ++s) {
-      mbar_init(&pfull[s], 1);
-      mbar_init(&pempty[s], kWorkWarps);
-    }
     for (int c = 0; c < kConvSlots; ++c) {
-      mbar_init(&conv_full[c], kWorkWarps);
+      mbar_init(&conv_full[c], kGroupWarps);
       mbar_init(&conv_empty[c], 1);
     }
     mbar_init(&acc_full, 1);
@@ -288,11 +289,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto next_item = [&](int seq, Item& it) -> bool { return item_of(a, cs, blockIdx.x + seq * P, it); };
 
   // ------------------------------ B producer --------------------------------
+  // Also requests the weight bytes of stage i + kPrefetch into L2 when it
+  // issues the B rows of stage i.
   if (warp == kBProdWarp) {
     if (lane == 0) {
       bool ok = true;
       int it_k = 0;
-      Item item;
+      Item item, pitem;
+      int pseq = 0, pks = 0;
+      bool phave = next_item(0, pitem);
+      auto pf_step = [&]() {
+        if (!phave) return;
+        prefetch_3d(&mA0, pks * 32, pitem.rb * a.rb_rows, pitem.e);
+        prefetch_3d(&mA1, pks * 32, pitem.rb * a.rb_rows + a.acc1_rows, pitem.e);
+        if (++pks == a.ks_count) {
+          pks = 0;
+          phave = next_item(++pseq, pitem);
+        }
+      };
+      for (int q = 0; q < kPrefetch; ++q) pf_step();
       for (int seq = 0; ok && next_item(seq, item); ++seq) {
         const unsigned bytes = static_cast<unsigned>(item.n * 128);
         for (int ks = 0; ks < a.ks_count; ++ks, ++it_k) {
@@ -303,55 +318,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&bfull[s], bytes);
           for (int b = 0; b < item.n / kBoxRows; ++b)
             dtc::tma_2d(bt + b * (kBoxRows * 128), &mB, ks * 128, item.p0 + b * kBoxRows, &bfull[s]);
+          pf_step();
         }
       }
       if (!ok) {  // let the copies in flight land before the CTA leaves
         for (int q = (it_k > kBStages ? it_k - kBStages : 0); q < it_k; ++q)
           dtc::wait1(&bfull[q % kBStages], (q / kBStages) & 1, a.status, kSiteBFull);
-      }
-    }
-    __syncwarp();
-  }
-  // ------------------------- packed-weight producer -------------------------
-  else if (warp == kPkProdWarp) {
-    if (lane == 0) {
-      bool ok = true;
-      int it_k = 0;
-      Item item, nitem;
-      bool have = next_item(0, item);
-      bool have_next = have && next_item(1, nitem);
-      // weight bytes of the first stages, then kPrefetch stages ahead of every load
-      for (int ks = 0; have && ks < kPrefetch && ks < a.ks_count; ++ks) {
-        prefetch_3d(&mA0, ks * 32, item.rb * a.rb_rows, item.e);
-        prefetch_3d(&mA1, ks * 32, item.rb * a.rb_rows + a.acc1_rows, item.e);
-      }
-      for (int seq = 0; ok && have; ++seq) {
-        const int y0 = item.rb * a.rb_rows;
-        for (int ks = 0; ks < a.ks_count; ++ks, ++it_k) {
-          const int s = it_k % kPkStages;
-          if (it_k >= kPkStages) ok = dtc::wait1(&pempty[s], ((it_k / kPkStages) - 1) & 1, a.status, kSitePkEmpty);
-          if (!ok) break;
-          unsigned char* pt = base + kPkOff + s * kPackedBytes;
-          mbar_arrive_expect_tx(&pfull[s], kPackedBytes);
-          gtc::tma_3d(pt, &mA0, ks * 32, y0, item.e, &pfull[s]);
-          gtc::tma_3d(pt + kPackedBytes / 2, &mA1, ks * 32, y0 + a.acc1_rows, item.e, &pfull[s]);
-          const int kp = ks + kPrefetch;
-          if (kp < a.ks_count) {
-            prefetch_3d(&mA0, kp * 32, y0, item.e);
-            prefetch_3d(&mA1, kp * 32, y0 + a.acc1_rows, item.e);
-          } else if (have_next && kp - a.ks_count < a.ks_count) {
-            const int kq = kp - a.ks_count;
-            prefetch_3d(&mA0, kq * 32, nitem.rb * a.rb_rows, nitem.e);
-            prefetch_3d(&mA1, kq * 32, nitem.rb * a.rb_rows + a.acc1_rows, nitem.e);
-          }
-        }
-        item = nitem;
-        have = have_next;
-        if (have) have_next = next_item(seq + 2, nitem);
-      }
-      if (!ok) {
-        for (int q = (it_k > kPkStages ? it_k - kPkStages : 0); q < it_k; ++q)
-          dtc::wait1(&pfull[q % kPkStages], (q / kPkStages) & 1, a.status, kSitePkFull);
       }
     }
     __syncwarp();
@@ -396,13 +368,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ------------------------------ workers -----------------------------------
   else {
     const int u = threadIdx.x - kWorkWarp0 * 32;  // 0..511
-    const int row = u & 255, hv = u >> 8;          // A row of every stage, half of its 64 values
-    const int acc = row >> 7, r = row & 127;       // accumulator, row within it
+    const int grp = u >> 8;                        // stages ks % 2 == grp of every item
+    const int row = u & 255;                       // A row: accumulator row / 128, row % 128 within it
+    const int acc = row >> 7, r = row & 127;
     const int periods = a.ks_count / 8;           // 16 scale bytes (8 stages) per period
-    auto scale_row = [&](const Item& it) -> const uint8_t* {
-      const int br = it.rb * a.rb_rows + (acc ? a.acc1_rows : 0) + r;
+    auto row_of = [&](const Item it) { return it.rb * a.rb_rows + (acc ? a.acc1_rows : 0) + r; };
+    auto scale_row = [&](const Item it) -> const uint8_t* {
       const uint8_t* bank = acc ? a.sc1 + it.e * a.sc1_stride : a.sc0 + it.e * a.sc0_stride;
-      return bank + static_cast<size_t>(br) * a.sc_row;
+      return bank + static_cast<size_t>(row_of(it)) * a.sc_row;
+    };
+    auto packed_row = [&](const Item it) -> const uint8_t* {
+      const uint8_t* bank = acc ? a.pk1 + it.e * a.pk1_stride : a.pk0 + it.e * a.pk0_stride;
+      return bank + static_cast<size_t>(row_of(it)) * a.pk_row;
     };
     // epilogue of one item: warp w reads tensor-memory lanes 32 (w & 3) ..,
     // quarter q = (w - kWorkWarp0) / 4 of the work.  Every worker calls it at
@@ -410,7 +387,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sp = warp & 3, q = (warp - kWorkWarp0) >> 2;
     const uint32_t lanes = tbase + (static_cast<uint32_t>(sp * 32) << 16);
     const int er = sp * 32 + lane;
-    auto epilogue = [&](const Item& it, int seq, bool ok) -> bool {
+    auto epilogue = [&](const Item it, int seq, bool ok) -> bool {
+      // down: the route slots of this warp's columns, loaded before the wait
+      // (lane i holds the slots of columns c_lo + i, c_lo + 32 + i, ...)
+      int slots[4] = {0, 0, 0, 0};
+      const int dh = q >> 1, c_lo_d = (q & 1) * (it.n / 2);
+      if (!kGateUp) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int c = c_lo_d + 32 * k + lane;
+          if (32 * k < it.n / 2 && c < it.nt) slots[k] = __ldg(a.perm + it.p0 + c);
+        }
+      }
       if (ok) ok = dtc::wait_warp1(&acc_full, seq & 1, a.status, kSiteAccFull);
       ok = named_and(kWorkBar, kWorkThreads, ok);
       if (!ok) return false;
@@ -432,18 +420,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {  // accumulator q / 2, columns [(q % 2) n/2, (q % 2 + 1) n/2)
-        const int h = q >> 1, drow = it.rb * 256 + h * 128 + er;
-        const int c_lo = (q & 1) * (it.n / 2), c_hi = c_lo + it.n / 2;
-        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-          uint32_t v[16];
-          umma::ld_32x32b_x16_nowait(lanes + h * kNMax + c0, v);
-          int my_slot = 0;  // lane i < 16: the route slot of column c0 + i
-          if (lane < 16 && c0 + lane < it.nt) my_slot = __ldg(a.perm + it.p0 + c0 + lane);
-          umma::wait_ld();
+        const int drow = it.rb * 256 + dh * 128 + er;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int slot = __shfl_sync(0xffffffffu, my_slot, i);
-            if (c0 + i < it.nt) a.y[static_cast<size_t>(slot) * a.d + drow] = f32_to_bf16(__uint_as_float(v[i]));
+        for (int k = 0; k < 4; ++k) {
+          const int cb = c_lo_d + 32 * k;
+          if (32 * k >= it.n / 2) break;
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t v[16];
+            umma::ld_32x32b_x16_nowait(lanes + dh * kNMax + cb + 16 * hh, v);
+            umma::wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int slot = __shfl_sync(0xffffffffu, slots[k], 16 * hh + i);
+              if (cb + 16 * hh + i < it.nt)
+                a.y[static_cast<size_t>(slot) * a.d + drow] = f32_to_bf16(__uint_as_float(v[i]));
+            }
           }
         }
       }
@@ -452,73 +444,96 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&acc_empty);
       return true;
     };
-    // scales are prefetched one period ahead, across items
-    Item item, pf_item, prev;
-    bool have = next_item(0, item), have_prev = false;
-    uint4 sc_next = make_uint4(0, 0, 0, 0), sc_cur;
-    int pf_seq = 0, pf_per = 0;
-    bool pf_have = have;
-    if (have) {
-      pf_item = item;
-      sc_next = __ldg(reinterpret_cast<const uint4*>(scale_row(pf_item)));
-    }
-    const int pk = row * 32 + ((hv ^ ((row >> 2) & 1)) << 4);  // 32-byte swizzle of the packed tile
-    const uint32_t conv_row = static_cast<uint32_t>(acc * (kConvBytes / 2) + (r >> 3) * 1024 + (r & 7) * 128);
-    const int epi_at = min(kConvSlots, a.ks_count) - 1;  // stage after which the previous item's epilogue runs
-    bool ok = true, done = false;
-    int it_k = 0, seq = 0;
-    for (; have && !done; ++seq) {
-      for (int ks = 0; ks < a.ks_count; ++ks, ++it_k) {
-        if ((ks & 7) == 0) {
-          sc_cur = sc_next;
-          if (++pf_per == periods) {
-            pf_per = 0;
-            pf_have = next_item(++pf_seq, pf_item);
-          }
-          if (pf_have) sc_next = __ldg(reinterpret_cast<const uint4*>(scale_row(pf_item)) + pf_per);
+    // This group's stages: ks = grp, grp + 2, ... of every item.  Weight bytes
+    // and scales are loaded ahead along that sequence, across items; the
+    // iterators keep row pointers only (items are recomputed where needed).
+    Item tmp;
+    bool have = next_item(0, tmp);
+    const uint8_t* ld_row = have ? packed_row(tmp) : nullptr;
+    const uint8_t* sc_ptr = have ? scale_row(tmp) : nullptr;
+    int ld_seq = 0, ld_ks = grp, sc_seq = 0, sc_per = 0;
+    bool ld_have = have, sc_have = have;
+    uint4 wq[2];  // packed bytes of this group's next stage
+    auto ld_next = [&]() {
+      if (ld_have) {
+        const uint4* src = reinterpret_cast<const uint4*>(ld_row + ld_ks * 32);
+        wq[0] = __ldg(src);
+        wq[1] = __ldg(src + 1);
+        ld_ks += 2;
+        if (ld_ks >= a.ks_count) {
+          ld_ks = grp;
+          Item t;
+          ld_have = next_item(++ld_seq, t);
+          if (ld_have) ld_row = packed_row(t);
         }
-        const int p = it_k % kPkStages, c = it_k % kConvSlots;
-        if (ok) ok = dtc::wait_warp1(&pfull[p], (it_k / kPkStages) & 1, a.status, kSitePkFull);
+      }
+    };
+    ld_next();
+    uint4 sc_next = make_uint4(0, 0, 0, 0), sc_cur = sc_next;
+    if (have) sc_next = __ldg(reinterpret_cast<const uint4*>(sc_ptr));
+    const uint32_t conv_row = static_cast<uint32_t>(acc * (kConvBytes / 2) + (r >> 3) * 1024 + (r & 7) * 128);
+    bool ok = true, done = false;
+    int seq = 0;
+    for (; have && !done; ++seq) {
+      for (int ks = grp; ks < a.ks_count; ks += 2) {
+        const int it_k = seq * a.ks_count + ks;
+        if ((ks & 7) == grp) {  // this group's first stage of a period of 8
+          sc_cur = sc_next;
+          if (++sc_per == periods) {
+            sc_per = 0;
+            Item t;
+            sc_have = next_item(++sc_seq, t);
+            if (sc_have) sc_ptr = scale_row(t);
+          }
+          if (sc_have) sc_next = __ldg(reinterpret_cast<const uint4*>(sc_ptr) + sc_per);
+        }
+        // this stage's packed bytes, then the load of this group's next stage
+        const uint4 w0 = wq[0], w1 = wq[1];
+        ld_next();
+        const int c = it_k % kConvSlots;
         if (ok && it_k >= kConvSlots)
           ok = dtc::wait_warp1(&conv_empty[c], ((it_k / kConvSlots) - 1) & 1, a.status, kSiteConvEmpty);
         if (ok) {
           const int j = ks & 7;
           const uint32_t wsc = j < 4 ? (j < 2 ? sc_cur.x : sc_cur.y) : (j < 6 ? sc_cur.z : sc_cur.w);
-          const uint32_t S8 = (wsc >> ((j & 1) * 16 + 8 * hv)) & 0xFFu;
-          const uint4 qv = *reinterpret_cast<const uint4*>(base + kPkOff + p * kPackedBytes + pk);
-          const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
           unsigned char* cv = conv + c * kConvBytes + conv_row;
-          if (lut_exact(S8)) {
-            const Lut lut = make_lut(S8);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              *reinterpret_cast<uint4*>(cv + (((4 * hv + k) ^ (r & 7)) << 4)) = widen8(qw[k], lut);
-          } else {
+          for (int h = 0; h < 2; ++h) {  // 32 values (one scale) per half
+            const uint32_t S8 = (wsc >> ((j & 1) * 16 + 8 * h)) & 0xFFu;
+            const uint4 qv = h ? w1 : w0;
+            const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+            if (lut_exact(S8)) {
+              const Lut lut = make_lut(S8);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              *reinterpret_cast<uint4*>(cv + (((4 * hv + k) ^ (r & 7)) << 4)) = widen8_slow(qw[k], S8);
+              for (int k = 0; k < 4; ++k)
+                *reinterpret_cast<uint4*>(cv + (((4 * h + k) ^ (r & 7)) << 4)) = widen8(qw[k], lut);
+            } else {
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                *reinterpret_cast<uint4*>(cv + (((4 * h + k) ^ (r & 7)) << 4)) = widen8_slow(qw[k], S8);
+            }
           }
           umma::fence_async_smem();  // the generic-proxy writes, seen by the tensor core
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&conv_full[c]);
-            mbar_arrive(&pempty[p]);
-          }
+          if (lane == 0) mbar_arrive(&conv_full[c]);
         }
-        if (have_prev && ks == epi_at) {
-          have_prev = false;
-          if (!epilogue(prev, seq - 1, ok)) {
+        if (seq > 0 && ks == grp) {  // both groups have converted the item's first stage each
+          Item pv;
+          next_item(seq - 1, pv);
+          if (!epilogue(pv, seq - 1, ok)) {
             done = true;
             break;
           }
         }
       }
       if (done) break;
-      prev = item;
-      have_prev = true;
-      have = next_item(seq + 1, item);
+      have = next_item(seq + 1, tmp);
     }
-    if (!done && have_prev) epilogue(prev, seq - 1, ok);
+    if (!done && seq > 0) {
+      Item pv;
+      next_item(seq - 1, pv);
+      epilogue(pv, seq - 1, ok);
+    }
   }
   __syncwarp();
   umma::fence_before_sync();

@@ -452,6 +452,10 @@ int launch_routed_dq(const lg_moe_config* c, const lg_moe_weights* w, const uint
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_check(e, "route gather launch");
     q.ks_count = d / 64; q.rb_count = F / 128; q.rb_rows = 128; q.acc1_rows = 0;
+    q.pk0 = w->gate_packed; q.pk1 = w->up_packed;
+    q.pk0_stride = static_cast<long long>(w->gate_packed_stride);
+    q.pk1_stride = static_cast<long long>(w->up_packed_stride);
+    q.pk_row = d / 2;
     q.sc0 = w->gate_scale; q.sc1 = w->up_scale;
     q.sc0_stride = static_cast<long long>(w->gate_scale_stride); q.sc1_stride = static_cast<long long>(w->up_scale_stride);
     q.sc_row = d / 32;
@@ -462,6 +466,9 @@ int launch_routed_dq(const lg_moe_config* c, const lg_moe_weights* w, const uint
     return launch_dq<true>(q, chunks_max * q.rb_count, A0, A1, B, s);
   }
   q.ks_count = F / 64; q.rb_count = d / 256; q.rb_rows = 256; q.acc1_rows = 128;
+  q.pk0 = q.pk1 = w->down_packed;
+  q.pk0_stride = q.pk1_stride = static_cast<long long>(w->down_packed_stride);
+  q.pk_row = F / 2;
   q.sc0 = q.sc1 = w->down_scale;
   q.sc0_stride = q.sc1_stride = static_cast<long long>(w->down_scale_stride);
   q.sc_row = F / 32;
