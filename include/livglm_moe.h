@@ -153,6 +153,28 @@ int lg_moe_combine(const lg_moe_config *cfg, const uint16_t *y,
                    const float *weights, const uint16_t *shared, int64_t M,
                    float *out, void *stream);
 
+/* Expert parallelism (no counterpart in the reference, whose experts stream
+ * from SSD on one device; the multi-GPU form of ExpertSSDMoE.__call__,
+ * moe.py:96-201).  The exchange itself runs on the caller's NCCL group.
+ *
+ * lg_moe_ep_pack: for the route slots sorted by expert id (perm from
+ * lg_moe_dispatch; sorted by expert is also sorted by owning rank when rank
+ * r owns experts [r*E/n_ranks, (r+1)*E/n_ranks)), write the send buffers of
+ * the dispatch exchange: x_send[p] = x[perm[p] / k] (bf16 [M*k, d]),
+ * e_send[p] = indices[perm[p]] % (E / n_ranks) (int32 [M*k], the expert id
+ * local to its owner) and inv[perm[p]] = p (int32 [M*k]). */
+int lg_moe_ep_pack(const lg_moe_config *cfg, const uint16_t *x, int64_t M,
+                   const uint32_t *indices, const int32_t *perm, int32_t n_ranks,
+                   uint16_t *x_send, int32_t *e_send, int32_t *inv, void *stream);
+
+/* lg_moe_combine with the routed outputs in dispatch order (as the reverse
+ * exchange returns them): the output of route slot s is row inv[s] of
+ * y_disp.  Same arithmetic and order as lg_moe_combine. */
+int lg_moe_combine_gather(const lg_moe_config *cfg, const uint16_t *y_disp,
+                          const int32_t *inv, const float *weights,
+                          const uint16_t *shared, int64_t M, float *out,
+                          void *stream);
+
 /*
  * Whole block.  Replaces ExpertSSDMoE.__call__ (moe.py:96-201) for bf16
  * hidden states: returns the f32 merge the MLX graph produces.

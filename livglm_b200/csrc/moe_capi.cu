@@ -1163,6 +1163,41 @@ int lg_moe_combine(const lg_moe_config* cfg, const uint16_t* y, const float* wei
   return cuda_check(cudaGetLastError(), "combine launch");
 }
 
+int lg_moe_combine_gather(const lg_moe_config* cfg, const uint16_t* y_disp, const int32_t* inv, const float* weights,
+                          const uint16_t* shared, int64_t M, float* out, void* stream) {
+  int rc;
+  if ((rc = validate_cfg(cfg)) || (rc = validate_tokens(M, cfg))) return rc;
+  if (M == 0) return LG_OK;
+  if (!y_disp || !inv || !weights || !out) return fail(LG_ERR_INVALID_ARG, "combine_gather: NULL tensor pointer");
+  if (!aligned(y_disp, 8) || !aligned(out, 16) || (shared && !aligned(shared, 8)))
+    return fail(LG_ERR_INVALID_ARG, "combine_gather: misaligned tensor");
+  const int d = cfg->hidden_size;
+  const long long n4 = M * (d / 4);
+  const int grid = static_cast<int>(n4 / 256 + 1 < 4 * num_sms() ? n4 / 256 + 1 : 4 * num_sms());
+  lg::combine_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      y_disp, weights, shared, static_cast<int>(M), cfg->num_experts_per_tok, d, out, inv);
+  return cuda_check(cudaGetLastError(), "combine_gather launch");
+}
+
+int lg_moe_ep_pack(const lg_moe_config* cfg, const uint16_t* x, int64_t M, const uint32_t* indices,
+                   const int32_t* perm, int32_t n_ranks, uint16_t* x_send, int32_t* e_send, int32_t* inv,
+                   void* stream) {
+  int rc;
+  if ((rc = validate_cfg(cfg)) || (rc = validate_tokens(M, cfg))) return rc;
+  if (M == 0) return LG_OK;
+  if (n_ranks < 1 || cfg->n_routed_experts % n_ranks)
+    return fail(LG_ERR_INVALID_ARG, "ep_pack: %d experts do not split over %d ranks", cfg->n_routed_experts,
+                n_ranks);
+  if (!x || !indices || !perm || !x_send || !e_send || !inv) return fail(LG_ERR_INVALID_ARG, "ep_pack: NULL pointer");
+  if (!aligned(x, 16) || !aligned(x_send, 16)) return fail(LG_ERR_INVALID_ARG, "ep_pack: rows must be 16-byte aligned");
+  const int d = cfg->hidden_size, k = cfg->num_experts_per_tok;
+  const long long R = M * k, n = R * (d / 8);
+  const int grid = static_cast<int>(std::min<long long>((n + 255) / 256, 8LL * num_sms()));
+  lg::ep_pack_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, indices, perm, static_cast<int>(R), k, d, cfg->n_routed_experts / n_ranks, x_send, e_send, inv);
+  return cuda_check(cudaGetLastError(), "ep_pack launch");
+}
+
 int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint16_t* x, int64_t M, float* out,
                    float* weights_out, uint32_t* indices_out, void* workspace, size_t workspace_bytes,
                    void* stream) {

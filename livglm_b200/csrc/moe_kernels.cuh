@@ -503,8 +503,11 @@ grouped_gemv_kernel(GemvArgs a) {
 // Combine: out[t, i] = ((0 + y0*w0) + y1*w1) + ... (+ shared), products and
 // sums each rounded to f32 as in the MLX graph (bf16 * f32 -> f32).
 __global__ void __launch_bounds__(256)
+// rowmap (optional): y row of route slot t*k + j is rowmap[t*k + j] (rows in
+// dispatch order), else the slot itself.
 combine_kernel(const uint16_t* __restrict__ y, const float* __restrict__ w,
-               const uint16_t* __restrict__ ys, int M, int k, int d, float* __restrict__ out) {
+               const uint16_t* __restrict__ ys, int M, int k, int d, float* __restrict__ out,
+               const int* __restrict__ rowmap = nullptr) {
   const int d4 = d >> 2;
   const long long n = static_cast<long long>(M) * d4;
   for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += 256LL * gridDim.x) {
@@ -513,7 +516,9 @@ combine_kernel(const uint16_t* __restrict__ y, const float* __restrict__ w,
     float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
     for (int j = 0; j < k; ++j) {
       const float wj = w[static_cast<size_t>(t) * k + j];
-      const uint2 u = *reinterpret_cast<const uint2*>(y + (static_cast<size_t>(t) * k + j) * d + 4 * c);
+      const size_t slot = static_cast<size_t>(t) * k + j;
+      const size_t row = rowmap ? static_cast<size_t>(rowmap[slot]) : slot;
+      const uint2 u = *reinterpret_cast<const uint2*>(y + row * d + 4 * c);
       s0 = __fadd_rn(s0, __fmul_rn(bf16lo(u.x), wj));
       s1 = __fadd_rn(s1, __fmul_rn(bf16hi(u.x), wj));
       s2 = __fadd_rn(s2, __fmul_rn(bf16lo(u.y), wj));
@@ -527,6 +532,30 @@ combine_kernel(const uint16_t* __restrict__ y, const float* __restrict__ w,
       s3 = __fadd_rn(s3, bf16hi(u.y));
     }
     reinterpret_cast<float4*>(out)[i] = make_float4(s0, s1, s2, s3);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Expert-parallel send buffers: for dispatch position p (route slot
+// perm[p] = t*k + j, slots sorted by expert id, hence by owning rank)
+// x_send[p] = x[t], e_send[p] = expert id mod per_rank (local to the owner),
+// inv[perm[p]] = p.  One thread per 16-byte chunk of a row; d % 8 == 0.
+__global__ void __launch_bounds__(256)
+ep_pack_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ indices, const int* __restrict__ perm,
+               int R, int k, int d, int per_rank, uint16_t* __restrict__ x_send, int* __restrict__ e_send,
+               int* __restrict__ inv) {
+  const int per_row = d >> 3;
+  const long long n = static_cast<long long>(R) * per_row;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += 256LL * gridDim.x) {
+    const int p = static_cast<int>(i / per_row);
+    const int c = static_cast<int>(i - static_cast<long long>(p) * per_row);
+    const int slot = __ldg(perm + p);
+    reinterpret_cast<uint4*>(x_send + static_cast<size_t>(p) * d)[c] =
+        __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(slot / k) * d) + c);
+    if (c == 0) {
+      e_send[p] = static_cast<int>(__ldg(indices + slot) % static_cast<uint32_t>(per_rank));
+      inv[slot] = p;
+    }
   }
 }
 

@@ -16,8 +16,12 @@ are data-parallel (each rank brings its own rows).  One call:
    the exchange is in flight;
 4. run the received rows through the local experts (lg_moe_experts with
    top-k 1 over the E/W local experts);
-5. send the bf16 outputs back by the reverse all-to-all, put them back in
-   slot order and merge them with the local shared expert (lg_moe_combine).
+5. send the bf16 outputs back by the reverse all-to-all and merge them, read
+   through the inverse of the dispatch permutation, with the local shared
+   expert (lg_moe_combine_gather).
+
+The send buffers of step 3 (rows in destination order, local expert ids, the
+inverse permutation) come from one kernel, lg_moe_ep_pack.
 
 The per-route arithmetic is the single-GPU kernels' own, so the result equals
 ExpertSSDMoE on the same rows up to the batched kernels' rounding order.
@@ -45,41 +49,35 @@ def expert_owner(expert: torch.Tensor, n_experts: int, world: int) -> torch.Tens
     return torch.div(expert, n_experts // world, rounding_mode="floor")
 
 
-def exchange_routes(rows: torch.Tensor, slot_expert: torch.Tensor, perm: torch.Tensor,
-                    send_counts: torch.Tensor, n_experts: int, compute_local: LocalCompute,
-                    group=None, overlap: Callable[[], None] | None = None) -> torch.Tensor:
-    """Steps 2-5 above: ship route rows to the experts' owners and back.
+def exchange_rows(x_send: torch.Tensor, e_send: torch.Tensor, send_counts: torch.Tensor,
+                  compute_local: LocalCompute, group=None,
+                  overlap: Callable[[], None] | None = None) -> torch.Tensor:
+    """Steps 2-5 above on packed send buffers: ship route rows to the experts'
+    owners, run them there, ship the outputs back.
 
-    rows [M, d] (one row per token); slot_expert [M*k] int64 expert id of each
-    route slot; perm [M*k] int64 route slots sorted by expert id (stable);
-    send_counts [W] int64 slots bound for each rank, in perm order.
-    compute_local(x [N, d], local_expert [N] int64) -> [N, d] runs on the
-    received rows.  overlap(), if given, runs after the dispatch exchange is
-    issued and before it is waited for (the shared expert overlaps the
-    transfer that way).  Returns [M*k, d]: the output of every route slot.
+    x_send [N, d] route rows grouped by destination rank (rank order);
+    e_send [N] int32 expert id local to the destination; send_counts [W]
+    int64 rows bound for each rank.  compute_local(x [n, d], local_expert
+    [n] int32) -> [n, d] runs on the received rows.  overlap(), if given, runs
+    after the dispatch exchange is issued and before it is waited for (the
+    shared expert overlaps the transfer that way).  Returns [N, d]: the
+    output of every sent row, in send order.
 
     One all-to-all of W counts (whose values reach the host once: NCCL's
-    variable-size exchange takes host split sizes), one of the route rows and
-    one of their expert ids (both issued before overlap() runs), and one of
-    the outputs, which are put back in slot order by a gather through the
-    inverse of perm.
+    variable-size exchange takes host split sizes), one of the rows and one of
+    their expert ids (both issued before overlap() runs), and one of the
+    outputs.
     """
-    world = dist.get_world_size(group)
-    per_rank = n_experts // world
-    k = slot_expert.numel() // max(1, rows.shape[0])
-    d = rows.shape[1]
+    d = x_send.shape[1]
     recv_counts = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts, send_counts, group=group)
     counts = torch.stack([send_counts, recv_counts]).cpu()  # the split sizes, one host copy
     send_split, recv_split = counts[0].tolist(), counts[1].tolist()
     n_send, n_recv = sum(send_split), sum(recv_split)
-    if n_send != slot_expert.numel():
+    if n_send != x_send.shape[0] or e_send.shape[0] != n_send:
         raise ContractError("route counts do not cover every route slot")
-    token = torch.div(perm, max(1, k), rounding_mode="floor")
-    x_send = rows.index_select(0, token)
-    e_send = (slot_expert.index_select(0, perm) % per_rank).to(torch.int32)
-    x_recv = rows.new_empty((n_recv, d))
-    e_recv = torch.empty(n_recv, dtype=torch.int32, device=rows.device)
+    x_recv = x_send.new_empty((n_recv, d))
+    e_recv = torch.empty(n_recv, dtype=torch.int32, device=x_send.device)
     w_x = dist.all_to_all_single(x_recv, x_send, recv_split, send_split, group=group, async_op=True)
     w_e = dist.all_to_all_single(e_recv, e_send, recv_split, send_split, group=group, async_op=True)
     if overlap is not None:
@@ -87,13 +85,32 @@ def exchange_routes(rows: torch.Tensor, slot_expert: torch.Tensor, perm: torch.T
     w_x.wait()
     w_e.wait()
     if n_recv:
-        y_recv = compute_local(x_recv, e_recv.to(torch.int64)).reshape(n_recv, d).to(rows.dtype)
+        y_recv = compute_local(x_recv, e_recv).reshape(n_recv, d).to(x_send.dtype)
     else:
-        y_recv = rows.new_empty((0, d))
-    y_back = rows.new_empty((n_send, d))
+        y_recv = x_send.new_empty((0, d))
+    y_back = x_send.new_empty((n_send, d))
     dist.all_to_all_single(y_back, y_recv.contiguous(), send_split, recv_split, group=group)
+    return y_back
+
+
+def exchange_routes(rows: torch.Tensor, slot_expert: torch.Tensor, perm: torch.Tensor,
+                    send_counts: torch.Tensor, n_experts: int, compute_local: LocalCompute,
+                    group=None, overlap: Callable[[], None] | None = None) -> torch.Tensor:
+    """exchange_rows with the packing done by torch ops (any device): rows
+    [M, d] one per token, slot_expert [M*k] int64 expert id of each route
+    slot, perm [M*k] int64 route slots sorted by expert id (stable),
+    send_counts [W] int64.  Returns [M*k, d], the output of every route slot
+    in slot order.  ExpertParallelMoE does the same packing and unpacking
+    with lg_moe_ep_pack and lg_moe_combine_gather."""
+    world = dist.get_world_size(group)
+    per_rank = n_experts // world
+    k = slot_expert.numel() // max(1, rows.shape[0])
+    token = torch.div(perm, max(1, k), rounding_mode="floor")
+    x_send = rows.index_select(0, token)
+    e_send = (slot_expert.index_select(0, perm) % per_rank).to(torch.int32)
+    y_back = exchange_rows(x_send, e_send, send_counts, compute_local, group, overlap)
     inv = torch.empty_like(perm)
-    inv[perm] = torch.arange(n_send, dtype=perm.dtype, device=perm.device)
+    inv[perm] = torch.arange(perm.numel(), dtype=perm.dtype, device=perm.device)
     return y_back.index_select(0, inv)
 
 
@@ -162,28 +179,31 @@ class ExpertParallelMoE:
         """Local bf16 rows [..., d] -> f32 [..., d], as ExpertSSDMoE.__call__."""
         c = self.config
         rows = _rows_bf16(hidden_states, c.hidden_size)
-        M, dev, k, E = rows.shape[0], rows.device, c.num_experts_per_tok, c.n_routed_experts
+        M, dev, k, E, d = rows.shape[0], rows.device, c.num_experts_per_tok, c.n_routed_experts, c.hidden_size
         lib = _native.load()
         stream = _stream_ptr(dev)
+        R = M * k
+        x_send = torch.empty(R, d, dtype=torch.bfloat16, device=dev)
+        e_send = torch.empty(R, dtype=torch.int32, device=dev)
+        inv = torch.empty(R, dtype=torch.int32, device=dev)
         if M:
             _, weights, indices = self.gate(rows)
             counts = torch.empty(E, dtype=torch.int32, device=dev)
             offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
-            perm = torch.empty(M * k, dtype=torch.int32, device=dev)
+            perm = torch.empty(R, dtype=torch.int32, device=dev)
             ws, nbytes = self._ws.get(self._cfg, M, dev)
             _native.check(lib.lg_moe_dispatch(self._cfg, indices.data_ptr(), M, counts.data_ptr(),
                                               offsets.data_ptr(), perm.data_ptr(), ws, nbytes, stream),
                           "lg_moe_dispatch")
-            bounds = offsets[::self.per_rank].to(torch.int64)  # [W + 1] slot ranges per owner
+            _native.check(lib.lg_moe_ep_pack(self._cfg, rows.data_ptr(), M, indices.data_ptr(), perm.data_ptr(),
+                                             self.world, x_send.data_ptr(), e_send.data_ptr(), inv.data_ptr(),
+                                             stream), "lg_moe_ep_pack")
+            bounds = offsets[::self.per_rank].to(torch.int64)  # [W + 1] dispatch ranges per owner
             send_counts = bounds[1:] - bounds[:-1]
-            slot_expert = indices.reshape(-1).view(torch.int32).to(torch.int64)
-            perm64 = perm.to(torch.int64)
         else:
             weights = torch.empty(0, k, dtype=torch.float32, device=dev)
             indices = torch.empty(0, k, dtype=torch.uint32, device=dev)
             send_counts = torch.zeros(self.world, dtype=torch.int64, device=dev)
-            slot_expert = torch.empty(0, dtype=torch.int64, device=dev)
-            perm64 = torch.empty(0, dtype=torch.int64, device=dev)
         shared = None
 
         def run_shared() -> None:  # overlaps the dispatch exchange
@@ -191,14 +211,13 @@ class ExpertParallelMoE:
             if M and c.n_shared_experts > 0:
                 shared = self.shared_experts(rows)
 
-        y_slots = exchange_routes(rows, slot_expert, perm64, send_counts, E, self._local, self.group,
-                                  overlap=run_shared)
-        out = torch.empty(M, c.hidden_size, dtype=torch.float32, device=dev)
+        y_disp = exchange_rows(x_send, e_send, send_counts, self._local, self.group, overlap=run_shared)
+        out = torch.empty(M, d, dtype=torch.float32, device=dev)
         if M:
-            _native.check(lib.lg_moe_combine(self._cfg, y_slots.data_ptr(), weights.data_ptr(),
-                                             shared.data_ptr() if shared is not None else None, M,
-                                             out.data_ptr(), stream), "lg_moe_combine")
-        result = out.reshape(*hidden_states.shape[:-1], c.hidden_size)
+            _native.check(lib.lg_moe_combine_gather(self._cfg, y_disp.data_ptr(), inv.data_ptr(), weights.data_ptr(),
+                                                    shared.data_ptr() if shared is not None else None, M,
+                                                    out.data_ptr(), stream), "lg_moe_combine_gather")
+        result = out.reshape(*hidden_states.shape[:-1], d)
         if return_route:
             return result, weights, indices
         return result
