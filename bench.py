@@ -191,15 +191,40 @@ def layer_work(cfg, M: int, unique: float) -> dict:
             "flops": flops, "per_expert_bytes": 3 * per_proj}
 
 
-def kernels_per_layer(M: int, batched_tc: bool) -> int:
-    """Kernels of this library launched by one lg_moe_forward call."""
+def expert_path(cfg, M: int) -> str:
+    """The routed-expert path lg_moe_forward takes for M tokens (moe_capi.cu):
+    decode chain (M <= 4), CUDA-core grouped GEMV (5..63 tokens), tensor-core
+    grouped GEMMs with E2M1 activation terms (kind::mxf4), or with the weights
+    widened to bf16 (kind::f16) once experts average 128 routes."""
+    if M <= 4:
+        return "decode"
+    if M < 64:
+        return "gemv"
+    if M * cfg.num_experts_per_tok >= 128 * cfg.n_routed_experts:
+        return "bf16"
+    return "mxf4"
+
+
+def kernels_per_layer(M: int, path: str, ep: bool = False) -> int:
+    """Kernels of this library launched by one layer call (lg_moe_forward, or
+    the expert-parallel layer's entry points)."""
+    if ep:
+        # router logits, select, histogram, dispatch, send-buffer pack, shared
+        # gate/up and down, then on the received rows: histogram, dispatch,
+        # route chunks, SwiGLU table, row gather, routed gate/up, routed down;
+        # finally the merge through the inverse permutation
+        return 15
     if M == 1:
         return 6  # router logits, select+dispatch, gate/up, activation split, tensor-core down, combine
-    if M <= 4:
+    if path == "decode":
         return 5
-    if batched_tc:
+    if path == "mxf4":
         # router logits, select, dispatch, route tiles, inverse permutation,
         # route split, routed / shared gate/up, routed / shared down, combine
+        return 11
+    if path == "bf16":
+        # router logits, select, dispatch, route chunks, SwiGLU table, token
+        # gather, routed / shared gate/up, routed / shared down, combine
         return 11
     return 6  # router logits, select, dispatch, gate/up GEMV, down GEMV, combine
 
@@ -208,24 +233,28 @@ def kernels_per_layer(M: int, batched_tc: bool) -> int:
 
 def cpu_sample(cfg, tn: dict, x_bits, tokens_per_call: int, budget_s: float) -> dict:
     """Layer-tokens/s of the CPU restatement of the reference path on the host
-    cores: calls of `tokens_per_call` tokens through one layer until the budget
-    is spent (at least two calls)."""
+    cores (oracle/experts_ref.c + router_ref.c: MXFP4 decoded on the fly,
+    OpenMP over all host threads): calls of `tokens_per_call` tokens through
+    one layer until the budget is spent (at least two calls)."""
     from oracle import moe_oracle as mo
 
     n_threads = os.cpu_count() or 1
     n = max(1, tokens_per_call)
-    mo.moe_forward(x_bits[:n], tn, cfg)  # warm caches / build
+    mo.moe_forward_c(x_bits[:n], tn, cfg)  # warm caches / build
     t0 = time.perf_counter()
     calls = 0
     while True:
-        mo.moe_forward(x_bits[:n], tn, cfg)
+        mo.moe_forward_c(x_bits[:n], tn, cfg)
         calls += 1
         el = time.perf_counter() - t0
         if (el >= budget_s and calls >= 2) or calls >= 10_000:
             break
     return {"value": calls * n / el, "unit": "tokens/s", "cores": n_threads, "kind": "port",
-            "sample": f"{calls} calls of {n} token(s) through one cfg1-shaped layer with the NumPy/C "
-                      f"restatement (BLAS threads={n_threads}), {el:.1f} s"}
+            "sample": f"{calls} calls of {n} token(s) through one cfg1-shaped layer with the C restatement "
+                      f"(E2M1/E8M0 decoded on the fly, OpenMP threads={n_threads}), {el:.1f} s"}
+
+
+CPU_TOKENS_PER_CALL = 128  # the CPU arm's bounded sample of a batched workload
 
 
 def run_reference(args) -> None:
@@ -245,17 +274,17 @@ def run_reference(args) -> None:
     torch.set_num_threads(os.cpu_count() or 1)
     cfg = CONFIGS[wl["cfg"]]
     M = wl["M"]
-    n = min(M, 32)  # tokens per CPU call: a bounded sample of the workload
+    n = min(M, CPU_TOKENS_PER_CALL)  # tokens per CPU call: a bounded sample of the workload
     t = synthetic.layer_weights(cfg, seed=0, device="cpu")
     tn = bank_to_numpy(t)
     x = mo.f32_to_bf16_bits(np.random.default_rng(0).standard_normal((n, cfg.hidden_size)).astype(np.float32))
-    mo.moe_forward(x, tn, cfg)
+    mo.moe_forward_c(x, tn, cfg)
     budget = 60.0
     times = []
     t_all = time.perf_counter()
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        mo.moe_forward(x, tn, cfg)
+        mo.moe_forward_c(x, tn, cfg)
         times.append(time.perf_counter() - t0)
         if time.perf_counter() - t_all > budget:
             break
@@ -270,9 +299,10 @@ def run_reference(args) -> None:
                    "n_routed_experts": cfg.n_routed_experts, "num_experts_per_tok": cfg.num_experts_per_tok,
                    "moe_intermediate_size": cfg.moe_intermediate_size},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{len(times)} calls of {n} tokens through one layer of the NumPy/C "
-                                   "restatement of kg36/livglm moe.py/expert_ssd.py/layers.py (MLX, the "
-                                   "reference's own runtime, is not installable here)"},
+                         "sample": f"{len(times)} calls of {n} tokens through one layer of the C "
+                                   "restatement of kg36/livglm moe.py/expert_ssd.py/layers.py (E2M1/E8M0 "
+                                   f"decoded on the fly, OpenMP threads={cores}; MLX, the reference's own "
+                                   "runtime, is not installable here)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -448,7 +478,7 @@ def run_ours(args) -> None:
         t0 = synthetic.layer_weights(cfg, layer=0, seed=0, device=dev)
         tn = bank_to_numpy(t0)
         del t0
-        n_cpu = min(M, 32)
+        n_cpu = min(M, CPU_TOKENS_PER_CALL)
         cpu = cpu_sample(cfg, tn, to_numpy(synthetic.hidden_states(cfg, n_cpu, seed=0, device=dev)), n_cpu,
                          args.cpu_seconds)
 
@@ -460,8 +490,16 @@ def run_ours(args) -> None:
     peaks = measured_peaks()
     fp4 = fp4_peak_tflops()
     work = layer_work(cfg, M, U)
-    batched_tc = M >= 64
-    # dominant stage and its roofline: the larger of its HBM and FP4-tensor times
+    # the local experts of an expert-parallel rank see about M*k routes over E/world experts
+    path = expert_path(cfg.replace(n_routed_experts=cfg.n_routed_experts // world, num_experts_per_tok=1),
+                       M * cfg.num_experts_per_tok) if ep else expert_path(cfg, M)
+    # tensor peak of the MMA kind the path runs: kind::f16 (bf16) for the
+    # widened weights, kind::mxf4 (FP4) for the E2M1-term path
+    if path == "bf16":
+        tc_peak = {"tflops": peaks["bf16_tflops"], "source": f"{peaks['source']} (bf16 tensor, cuBLAS)"}
+    else:
+        tc_peak = fp4
+    # dominant stage and its roofline: the larger of its HBM and tensor times
     if stage:
         dominant = max(stage, key=stage.get)
         dom_ms = stage[dominant]
@@ -472,14 +510,14 @@ def run_ours(args) -> None:
                  "down": work["flops"]["down"] + work["flops"]["down_shared"],
                  "router": work["flops"]["router"]}.get(dominant, work["flops"]["layer"])
     t_hbm = dom_bytes / (peaks["hbm_gbs"] * 1e9)
-    t_tc = dom_flops / (fp4["tflops"] * 1e12)
+    t_tc = dom_flops / (tc_peak["tflops"] * 1e12)
     if t_tc > t_hbm:
-        bound, achieved, peak, unit = "tensor", dom_flops / (dom_ms * 1e-3) / 1e12, fp4["tflops"], "TFLOP/s"
+        bound, achieved, peak, unit = "tensor", dom_flops / (dom_ms * 1e-3) / 1e12, tc_peak["tflops"], "TFLOP/s"
     else:
         bound, achieved, peak, unit = "hbm", dom_bytes / (dom_ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s"
     layer_ms = ms_step / layers_per_step
     layer_t_hbm = work["bytes"]["layer"] / (peaks["hbm_gbs"] * 1e9)
-    layer_t_tc = work["flops"]["layer"] / (fp4["tflops"] * 1e12)
+    layer_t_tc = work["flops"]["layer"] / (tc_peak["tflops"] * 1e12)
     workload_name = {"cfg3": f"cfg3: {L} stacked layers, M={M} per rank",
                      "cfg4": f"cfg4: Zipf(1.2) bias, M={M} per rank",
                      "prefill256": "cfg2: M=256", "decode1": "cfg1: M=1", "decode2": "cfg1: M=2 (MTP verify)"}
@@ -488,8 +526,9 @@ def run_ours(args) -> None:
         "metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "strong" if (wl.get("zipf") and world > 1) else "weak", "vs_baseline": None,
-        "dtype": ("mxf4 (E2M1 weights x E2M1-term activations), f32 accumulate" if batched_tc
-                  else "fp4 weights x f16/bf16 activations, f32 accumulate"),
+        "dtype": {"mxf4": "mxf4 (E2M1 weights x E2M1-term activations), f32 accumulate",
+                  "bf16": "bf16 x bf16 (MXFP4 weights widened exactly to bf16 in shared memory), f32 accumulate",
+                  }.get(path, "fp4 weights x f16/bf16 activations, f32 accumulate"),
         "data": "synthetic (seeded N(0,1) bf16 tokens; N(0,0.02) weights, routed MXFP4 g32, shared bf16)",
         "config": {"workload": workload_name[args.workload], "M": M, "layers_per_step": layers_per_step,
                    "hidden_size": cfg.hidden_size, "n_routed_experts": cfg.n_routed_experts,
@@ -502,7 +541,7 @@ def run_ours(args) -> None:
         "roofline": {"bound": bound, "kernel": f"{dominant} stage", "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak if peak else None,
                      "traffic": MEASURED_TRAFFIC.get(args.workload) if dominant == "gate_up" else None,
-                     "peak_source": peaks["source"] if unit == "GB/s" else fp4["source"],
+                     "peak_source": peaks["source"] if unit == "GB/s" else tc_peak["source"],
                      "algorithmic_bytes_per_launch": dom_bytes, "algorithmic_flops_per_launch": dom_flops,
                      "launch_ms": dom_ms},
         "e2e": {"value": world * M * layers_per_step * K_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
@@ -510,13 +549,15 @@ def run_ours(args) -> None:
                 "steps": K_e2e,
                 "path": "pinned host tokens -> device copy -> public module call(s) -> f32 result copied to "
                         "pinned host memory, every step"},
-        "gpu_launches": kernels_per_layer(M, batched_tc) * layers_per_step * args.steps,
+        "gpu_launches": kernels_per_layer(M, path, ep) * layers_per_step * args.steps,
         "clocks": sampler.summary(),
         "extra": {"layer_ms": layer_ms,
-                  "layer_roofline": {"hbm_us": layer_t_hbm * 1e6, "fp4_us": layer_t_tc * 1e6,
+                  "expert_path": path,
+                  "layer_roofline": {"hbm_us": layer_t_hbm * 1e6, "tensor_us": layer_t_tc * 1e6,
                                      "frac": max(layer_t_hbm, layer_t_tc) / (layer_ms * 1e-3),
                                      "hbm_frac": layer_t_hbm / (layer_ms * 1e-3),
-                                     "fp4_frac": layer_t_tc / (layer_ms * 1e-3)},
+                                     "tensor_frac": layer_t_tc / (layer_ms * 1e-3),
+                                     "fp4_frac": work["flops"]["layer"] / (fp4["tflops"] * 1e12) / (layer_ms * 1e-3)},
                   "layer_bytes": work["bytes"]["layer"], "layer_flops": work["flops"]["layer"],
                   "fp4_peak_tflops": fp4["tflops"], "fp4_peak_source": fp4["source"],
                   "bf16_peak_tflops": peaks["bf16_tflops"],

@@ -60,6 +60,14 @@ def lib() -> ctypes.CDLL:
         ]
         _LIB.oracle_router.restype = ctypes.c_int
         _LIB.oracle_dispatch.argtypes = [u32p, ctypes.c_int64, ctypes.c_int, i32p, i32p, i32p]
+        u8p = np.ctypeslib.ndpointer(np.uint8, flags="C")
+        _LIB.oracle_moe_layer.argtypes = [
+            u16p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float, f32p, f32p,
+            u8p, u8p, u8p, u8p, u8p, u8p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+            f32p, f32p, u32p,
+        ]
+        _LIB.oracle_moe_layer.restype = ctypes.c_int
     return _LIB
 
 
@@ -274,3 +282,33 @@ def moe_forward(x: np.ndarray, bank: dict, cfg, tokens: np.ndarray | None = None
     out = combine(y, wts, sh)
     return {"logits": logits, "weights": wts, "indices": idx, "y": y, "shared": sh, "out": out,
             "tokens": sel}
+
+
+def moe_forward_c(x: np.ndarray, bank: dict, cfg) -> dict:
+    """The whole block through the C restatement (experts_ref.c: MXFP4 decoded
+    on the fly, OpenMP over weight rows) -> {"out", "weights", "indices"}.
+    Routing is the canonical router's (bit-identical to router()); outputs
+    agree with moe_forward() to within f32 summation order."""
+    g = geometry(cfg)
+    x = np.ascontiguousarray(x, dtype=np.uint16).reshape(-1, g.hidden_size)
+    M = x.shape[0]
+    d, F, E, k = g.hidden_size, g.moe_intermediate_size, g.n_routed_experts, g.num_experts_per_tok
+    Fs = F * g.n_shared_experts
+    out = np.zeros((M, d), np.float32)
+    wts = np.zeros((M, k), np.float32)
+    idx = np.zeros((M, k), np.uint32)
+    if M == 0:
+        return {"out": out, "weights": wts, "indices": idx}
+    c = np.ascontiguousarray
+    shared = [c(bank["shared_gate"], dtype=np.uint16), c(bank["shared_up"], dtype=np.uint16),
+              c(bank["shared_down"], dtype=np.uint16)] if Fs else [None, None, None]
+    rc = lib().oracle_moe_layer(
+        x, M, d, F, Fs, E, g.n_group, g.topk_group, k, int(g.norm_topk_prob), g.routed_scaling_factor,
+        g.swiglu_limit, c(bank["router_weight"], dtype=np.float32), c(bank["router_bias"], dtype=np.float32),
+        c(bank["gate_packed"], dtype=np.uint8), c(bank["gate_scale"], dtype=np.uint8),
+        c(bank["up_packed"], dtype=np.uint8), c(bank["up_scale"], dtype=np.uint8),
+        c(bank["down_packed"], dtype=np.uint8), c(bank["down_scale"], dtype=np.uint8),
+        *[a.ctypes.data if a is not None else None for a in shared], out, wts, idx)
+    if rc:
+        raise ValueError(f"C oracle rejected the call ({rc})")
+    return {"out": out, "weights": wts, "indices": idx}

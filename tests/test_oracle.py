@@ -160,3 +160,45 @@ def test_router_geometries_select_k_distinct_experts(k, E, G, g):
         groups = {int(e) // (E // G) for e in row}
         assert len(groups) <= g
     np.testing.assert_allclose(weights.sum(-1), cfg.routed_scaling_factor, rtol=1e-5)
+
+
+def test_c_restatement_matches_numpy_oracle_on_golden_cfg0(golden_cfg0):
+    """oracle/experts_ref.c (the timed CPU baseline: weights decoded on the
+    fly) against the NumPy oracle on the committed config-0 record: routing
+    bit-identical, outputs identical at this size."""
+    cfg = CONFIGS["cfg0"]
+    ref = mo.moe_forward(golden_cfg0["x"], golden_cfg0, cfg)
+    got = mo.moe_forward_c(golden_cfg0["x"], golden_cfg0, cfg)
+    np.testing.assert_array_equal(got["indices"], ref["indices"])
+    np.testing.assert_array_equal(got["weights"].view(np.uint32), ref["weights"].view(np.uint32))
+    np.testing.assert_array_equal(got["out"], ref["out"])
+
+
+def test_c_restatement_on_random_geometry_within_tolerance():
+    """A d=512, F=256, 32-expert layer with random MXFP4 bytes (scales
+    0..254 near 120) and 40 tokens: the C restatement and the NumPy oracle
+    differ only by f32 summation order before the bf16 roundings."""
+    from tests.helpers import assert_close
+
+    cfg = MoEConfig(hidden_size=512, moe_intermediate_size=256, n_routed_experts=32, num_experts_per_tok=4,
+                    n_shared_experts=1, n_group=4, topk_group=2)
+    rng = np.random.default_rng(9)
+    E, d, F = 32, 512, 256
+    bank = {
+        "router_weight": (rng.standard_normal((E, d)) * 0.05).astype(np.float32),
+        "router_bias": (rng.standard_normal(E) * 0.01).astype(np.float32),
+        "gate_packed": rng.integers(0, 256, (E, F, d // 2), dtype=np.uint8),
+        "gate_scale": rng.integers(116, 121, (E, F, d // 32), dtype=np.uint8),
+        "up_packed": rng.integers(0, 256, (E, F, d // 2), dtype=np.uint8),
+        "up_scale": rng.integers(116, 121, (E, F, d // 32), dtype=np.uint8),
+        "down_packed": rng.integers(0, 256, (E, d, F // 2), dtype=np.uint8),
+        "down_scale": rng.integers(116, 121, (E, d, F // 32), dtype=np.uint8),
+        "shared_gate": mo.f32_to_bf16_bits((rng.standard_normal((F, d)) * 0.02).astype(np.float32)),
+        "shared_up": mo.f32_to_bf16_bits((rng.standard_normal((F, d)) * 0.02).astype(np.float32)),
+        "shared_down": mo.f32_to_bf16_bits((rng.standard_normal((d, F)) * 0.02).astype(np.float32)),
+    }
+    x = mo.f32_to_bf16_bits(rng.standard_normal((40, d)).astype(np.float32))
+    ref = mo.moe_forward(x, bank, cfg)
+    got = mo.moe_forward_c(x, bank, cfg)
+    np.testing.assert_array_equal(got["indices"], ref["indices"])
+    assert_close(got["out"], ref["out"])
