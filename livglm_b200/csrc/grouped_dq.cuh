@@ -8,10 +8,10 @@
 //   routed gate/up   act[p]   = swiglu(bf16(Wg_e x_t), bf16(Wu_e x_t))
 //   routed down      y[s(p)]  = bf16(Wd_e act[p])
 //
-// as kind::f16 MMAs on bf16 operands.  The A operand is the weights: the TMA
-// brings each stage's checkpoint bytes (E2M1 nibbles, 64 values = 32 bytes a
-// row, 32-byte swizzle), and eight converter warps widen them to bf16 -- an
-// E2M1 value times a power-of-two scale is exact in bf16 -- straight into the
+// as kind::f16 MMAs on bf16 operands.  The A operand is the weights: worker
+// warps load each stage's checkpoint bytes (E2M1 nibbles, 64 values = 32 bytes
+// a row) from global memory into registers and widen them to bf16 -- an E2M1
+// value times a power-of-two scale is exact in bf16 -- straight into the
 // MMA's 128-byte-swizzled K-major layout.  The B operand is bf16 rows in
 // dispatch order: the tokens gathered once per call (gather_rows_kernel) or
 // act.  The products are then exactly those of a dequantised matmul, with no
