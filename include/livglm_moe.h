@@ -175,6 +175,18 @@ int lg_moe_combine_gather(const lg_moe_config *cfg, const uint16_t *y_disp,
                           const uint16_t *shared, int64_t M, float *out,
                           void *stream);
 
+/* Checkpoint loading: block-FP8 weights to bf16, the resident plan's
+ * block_fp8_to_bf16 transform for the shared expert (fp8.py:43-78,
+ * resident_plan.py:177-220).  weight: E4M3FN bytes [rows, cols] (device);
+ * scale_inv: f32 [rows/block, cols/block] (device); out: bf16 [rows, cols]
+ * (device), out = bf16_rn(e4m3fn(w) * scale) with the product in f32;
+ * *nonfinite (device int32) receives the number of non-finite products (the
+ * reference refuses such a checkpoint).  rows and cols multiples of block,
+ * block a multiple of 8. */
+int lg_fp8_block_dequant(const uint8_t *weight, const float *scale_inv,
+                         int64_t rows, int64_t cols, int32_t block,
+                         uint16_t *out, int32_t *nonfinite, void *stream);
+
 /*
  * Whole block.  Replaces ExpertSSDMoE.__call__ (moe.py:96-201) for bf16
  * hidden states: returns the f32 merge the MLX graph produces.

@@ -59,15 +59,20 @@ namespace gtc {
 constexpr int kThreads = 448;
 constexpr int kProdWarp = 0, kMmaWarp = 1, kSfWarp0 = 2, kEpiWarp0 = 6, kMathWarp0 = 10;
 constexpr int kMathWarps = 8;     // gate/up epilogue: warps 6-13 share the SwiGLU and split
-constexpr int kTerms = 5;         // E2M1 terms per bf16 activation
+constexpr int kTerms = 6;         // E2M1 terms per bf16 activation
 constexpr int kNtMax = 32;        // routes per routed tile
 constexpr int kNtShared = 128;    // tokens per shared tile
 constexpr int kMaxStages = 8;
-constexpr int kSfSlots = kMaxStages;  // tensor-memory scale-factor slots, one per ring stage: 2 * 160 + 8 * 24 = 512
+constexpr int kSfSlots = kMaxStages;
 constexpr int kSfaCols = 8;       // A: 2 MMA pairs x 4 row quarters
 constexpr int kSfbCols = 16;      // B: 2 MMA pairs x 8 row groups (N <= 256)
 constexpr int kSfSlotCols = kSfaCols + kSfbCols;
 constexpr int kABytes = 16384;    // 128 rows x 128 bytes
+// Routed kernels hold two accumulators of kTerms * kNtMax columns and one
+// scale-factor slot per ring stage in the 512 tensor-memory columns: 2 * 192 +
+// 5 * 24 = 504, so their ring has at most kRoutedStages stages.
+constexpr int kRoutedStages = (512 - 2 * kTerms * kNtMax) / kSfSlotCols;
+static_assert(kRoutedStages >= 2 && kRoutedStages <= kSfSlots, "tensor-memory plan of the routed kernels");
 constexpr int kEpiBar = 2;        // named barrier of the epilogue warps
 constexpr int kSiteFull = 40 << 8, kSiteEmpty = 41 << 8, kSiteSfFull = 42 << 8, kSiteSfEmpty = 43 << 8,
               kSiteScFull = 44 << 8, kSiteScFree = 45 << 8, kSiteAccFull = 46 << 8, kSiteAccEmpty = 47 << 8,

@@ -372,7 +372,7 @@ int launch_grouped(const lg::gtc::Args& a0, int items_max, const GgMaps& m, cuda
   const size_t budget = 227 * 1024 - 1024 - 1024;  // dynamic limit less alignment slack and static barriers
   if (fixed + 2 * static_cast<size_t>(a.stage_bytes) > budget)
     return fail(LG_ERR_UNSUPPORTED, "batched tensor-core plan does not fit in shared memory");
-  a.stages = static_cast<int>(std::min<size_t>(kMaxStages, (budget - fixed) / a.stage_bytes));
+  a.stages = static_cast<int>(std::min<size_t>(kRouted ? kRoutedStages : kMaxStages, (budget - fixed) / a.stage_bytes));
 
   a.ring_off = 0;
   a.sfa_off = a.stages * a.stage_bytes;
@@ -1196,6 +1196,23 @@ int lg_moe_ep_pack(const lg_moe_config* cfg, const uint16_t* x, int64_t M, const
   lg::ep_pack_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       x, indices, perm, static_cast<int>(R), k, d, cfg->n_routed_experts / n_ranks, x_send, e_send, inv);
   return cuda_check(cudaGetLastError(), "ep_pack launch");
+}
+
+int lg_fp8_block_dequant(const uint8_t* weight, const float* scale_inv, int64_t rows, int64_t cols, int32_t block,
+                         uint16_t* out, int32_t* nonfinite, void* stream) {
+  if (!weight || !scale_inv || !out || !nonfinite) return fail(LG_ERR_INVALID_ARG, "fp8 dequant: NULL pointer");
+  if (rows < 1 || cols < 8 || block < 8 || block % 8 || rows % block || cols % block)
+    return fail(LG_ERR_INVALID_ARG, "fp8 dequant: shape %lld x %lld not a multiple of block %d",
+                static_cast<long long>(rows), static_cast<long long>(cols), block);
+  if (!aligned(weight, 8) || !aligned(out, 16) || !aligned(scale_inv, 4))
+    return fail(LG_ERR_INVALID_ARG, "fp8 dequant: misaligned tensor");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(nonfinite, 0, sizeof(int32_t), s);
+  if (e != cudaSuccess) return cuda_check(e, "fp8 dequant memset");
+  const long long n = rows * (cols / 8);
+  const int grid = static_cast<int>(std::min<long long>((n + 255) / 256, 8LL * num_sms()));
+  lg::fp8_block_dequant_kernel<<<grid, 256, 0, s>>>(weight, scale_inv, rows, cols, block, out, nonfinite);
+  return cuda_check(cudaGetLastError(), "fp8 dequant launch");
 }
 
 int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint16_t* x, int64_t M, float* out,

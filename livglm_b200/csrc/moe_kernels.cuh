@@ -559,4 +559,45 @@ ep_pack_kernel(const uint16_t* __restrict__ x, const uint32_t* __restrict__ indi
   }
 }
 
+// --------------------------------------------------------------------------
+// Block-FP8 -> bf16 (checkpoint loading of the shared expert, the resident
+// plan's block_fp8_to_bf16 transform: kg36/livglm src/glm53flash/fp8.py:43-78,
+// resident_plan.py:177-220).  E4M3FN: sign, 4-bit exponent (bias 7), 3-bit
+// mantissa; exponent 0 is subnormal (m/8 * 2^-6); exponent 15 with mantissa 7
+// is NaN; there are no infinities.
+__device__ __forceinline__ float e4m3fn_to_f32(uint32_t b) {
+  const uint32_t e = (b >> 3) & 15u, m = b & 7u;
+  float v;
+  if (e == 0u) v = static_cast<float>(m) * 0x1p-9f;
+  else if (e == 15u && m == 7u) v = __uint_as_float(0x7FC00000u);
+  else v = __uint_as_float(((e + 120u) << 23) | (m << 20));
+  return (b & 0x80u) ? -v : v;
+}
+// out[r][c] = bf16(e4m3fn(w[r][c]) * scale[r / B][c / B]) with the product in
+// f32; *nonfinite counts the products that are not finite.  Thread per 8
+// consecutive values of a row; cols % 8 == 0.
+__global__ void __launch_bounds__(256)
+fp8_block_dequant_kernel(const uint8_t* __restrict__ w, const float* __restrict__ scale, long long rows,
+                         long long cols, int B, uint16_t* __restrict__ out, int* __restrict__ nonfinite) {
+  const long long per_row = cols / 8, n = rows * per_row;
+  const long long scols = cols / B;
+  int bad = 0;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += 256LL * gridDim.x) {
+    const long long r = i / per_row, c0 = (i - r * per_row) * 8;
+    const uint2 q = *reinterpret_cast<const uint2*>(w + r * cols + c0);
+    const float s = scale[(r / B) * scols + c0 / B];
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t word = j < 2 ? q.x : q.y;
+      const float v0 = __fmul_rn(e4m3fn_to_f32((word >> (16 * (j & 1))) & 0xFFu), s);
+      const float v1 = __fmul_rn(e4m3fn_to_f32((word >> (16 * (j & 1) + 8)) & 0xFFu), s);
+      bad += !isfinite(v0) + !isfinite(v1);
+      o[j] = static_cast<uint32_t>(f32_to_bf16(v0)) | (static_cast<uint32_t>(f32_to_bf16(v1)) << 16);
+    }
+    *reinterpret_cast<uint4*>(out + r * cols + c0) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if (bad) atomicAdd(nonfinite, bad);
+}
+
 }  // namespace lg

@@ -109,6 +109,37 @@ class Workspace:
         return int(self.buf[:4].view(torch.int32).item())
 
 
+FP8_BLOCK = 128  # block size of the checkpoint's block-FP8 weights (resident_plan.py:189-205)
+
+
+def widen_block_fp8(weight: torch.Tensor, scale_inv: torch.Tensor, block: int = FP8_BLOCK) -> torch.Tensor:
+    """Block-FP8 weight (float8_e4m3fn [rows, cols]) and its f32 block scales
+    ([rows/block, cols/block]) -> bf16 [rows, cols] on the weight's CUDA device
+    (lg_fp8_block_dequant; fp8.py:43-78).  Non-finite results are refused, as
+    the reference refuses them."""
+    if weight.dim() != 2 or weight.dtype != torch.float8_e4m3fn:
+        raise ContractError(f"block-FP8 weight must be a 2-D float8_e4m3fn tensor, got {weight.dtype}")
+    rows, cols = weight.shape
+    if rows % block or cols % block:
+        raise ContractError(f"block-FP8 shape must be divisible by {block}: {tuple(weight.shape)}")
+    if tuple(scale_inv.shape) != (rows // block, cols // block):
+        raise ContractError(f"block-FP8 scale shape mismatch: {tuple(scale_inv.shape)} != "
+                            f"{(rows // block, cols // block)}")
+    if weight.device.type != "cuda":
+        raise ContractError("block-FP8 weights are widened on the GPU: move them to a CUDA device first")
+    dev = weight.device
+    w = weight.contiguous().view(torch.uint8)
+    sc = scale_inv.to(device=dev, dtype=torch.float32).contiguous()
+    out = torch.empty(rows, cols, dtype=torch.bfloat16, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    lib = _native.load()
+    _native.check(lib.lg_fp8_block_dequant(w.data_ptr(), sc.data_ptr(), rows, cols, block, out.data_ptr(),
+                                           bad.data_ptr(), _stream_ptr(dev)), "lg_fp8_block_dequant")
+    if int(bad.item()):
+        raise ContractError("block-FP8 dequantization produced a non-finite weight")
+    return out
+
+
 def require_weight(value, name: str):
     """layers.py:12-15."""
     if value is None:
@@ -487,12 +518,27 @@ class ExpertSSDMoE:
             self.gate.weight = tensors[p + "gate.weight"].to(device=device, dtype=torch.float32).contiguous()
             self.gate.e_score_correction_bias = tensors[p + "gate.e_score_correction_bias"].to(
                 device=device, dtype=torch.float32).contiguous()
-            for name in ("gate_proj", "up_proj", "down_proj"):
-                getattr(self.shared_experts, name).weight = tensors[p + f"shared_experts.{name}.weight"].to(
-                    device=device, dtype=torch.bfloat16).contiguous()
+            for name in ("gate_proj", "up_proj", "down_proj") if self.config.n_shared_experts > 0 else ():
+                key = p + f"shared_experts.{name}.weight"
+                w = tensors[key]
+                if w.dtype == torch.float8_e4m3fn:  # block-FP8 with f32 block scales, widened on the GPU
+                    w = widen_block_fp8(w.to(device), tensors[key + "_scale_inv"])
+                getattr(self.shared_experts, name).weight = w.to(device=device, dtype=torch.bfloat16).contiguous()
         except KeyError as exc:
             raise ContractError(f"resident parameter was not loaded: {exc.args[0]}") from None
         self.experts.load_checkpoint(tensors, device=device)
+
+    @classmethod
+    def from_checkpoint(cls, path, config: MoEConfig, layer_idx: int, device="cuda") -> "ExpertSSDMoE":
+        """Construct layer `layer_idx` from a safetensors checkpoint directory
+        (index + shards) or file: routed experts bound byte for byte into HBM
+        banks, router in f32, shared expert in bf16 (block-FP8 widened)."""
+        from .safetensors import SafetensorsCheckpoint
+
+        ckpt = path if isinstance(path, SafetensorsCheckpoint) else SafetensorsCheckpoint(path)
+        moe = cls(config, layer_idx, lambda layer: ResidentExperts(config, layer=layer))
+        moe.load_checkpoint(ckpt.layer_tensors(layer_idx), device=device)
+        return moe
 
 
 def build_layer(config: MoEConfig, tensors: dict, layer_idx: int = 0) -> ExpertSSDMoE:

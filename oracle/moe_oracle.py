@@ -106,6 +106,25 @@ def e8m0_to_f32(s: np.ndarray) -> np.ndarray:
     return out
 
 
+def e4m3fn_to_f32(codes: np.ndarray) -> np.ndarray:
+    """E4M3FN bytes -> f32 (fp8.py:13-30): sign, 4-bit exponent (bias 7),
+    3-bit mantissa, exponent 0 subnormal, 0x7F / 0xFF NaN, no infinities."""
+    b = np.asarray(codes, np.uint8).astype(np.int64)
+    e, m = (b >> 3) & 15, b & 7
+    v = np.where(e == 0, np.ldexp(m / 8.0, -6), np.ldexp(1.0 + m / 8.0, e - 7))
+    v = np.where((e == 15) & (m == 7), np.nan, v)
+    return np.where(b & 0x80, -v, v).astype(np.float32)
+
+
+def fp8_block_dequant_bf16(weight: np.ndarray, scale_inv: np.ndarray, block: int = 128) -> np.ndarray:
+    """fp8.py:43-78 (decode, multiply the f32 block scale, f32 product), then
+    the resident plan's bf16 destination (resident_plan.py:206-214): bf16 bits."""
+    rows, cols = weight.shape
+    dec = e4m3fn_to_f32(weight).reshape(rows // block, block, cols // block, block)
+    prod = (dec * np.asarray(scale_inv, np.float32)[:, None, :, None]).astype(np.float32)
+    return f32_to_bf16_bits(prod.reshape(rows, cols))
+
+
 def mxfp4_dequant(packed: np.ndarray, scale: np.ndarray) -> np.ndarray:
     """U8 [rows, cols/2] nibbles (low nibble = even column) and U8 [rows,
     cols/32] E8M0 scales -> f32 [rows, cols] (value = E2M1 * 2^(s-127))."""

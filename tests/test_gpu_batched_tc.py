@@ -4,7 +4,7 @@ CPU oracle.
 Calls of at least 64 tokens whose geometry has d a multiple of 1024 and F a
 multiple of 512 run
 the routed experts as block-scaled kind::mxf4 grouped GEMMs (activations as
-five E2M1 terms) and the shared expert as kind::f16 GEMMs.  Bar as in
+six E2M1 terms) and the shared expert as kind::f16 GEMMs.  Bar as in
 test_gpu_parity.py: routing bit-exact, f32 output within max-abs 2e-2 and
 cosine >= 0.9995 of the oracle on every token checked.
 

@@ -1,0 +1,48 @@
+"""Checkpoint loading on the GPU: block-FP8 widening (lg_fp8_block_dequant)
+against the oracle's restatement of fp8.py:43-78, and a layer built with
+ExpertSSDMoE.from_checkpoint from a safetensors checkpoint (index + two
+shards, FP8 shared expert) against the oracle."""
+
+import numpy as np
+import pytest
+import torch
+
+from livglm_b200.config import CONFIGS, ContractError
+from livglm_b200.moe import ExpertSSDMoE, widen_block_fp8
+from oracle import moe_oracle as mo
+from tests import checkpoint_fixture as cf
+from tests.helpers import assert_close, to_numpy
+
+pytestmark = pytest.mark.gpu
+
+
+def test_fp8_widening_bit_exact(cuda, native_lib):
+    rng = np.random.default_rng(3)
+    w, s = cf.fp8_weight(rng, 384, 512)
+    w[0, :254] = np.array([c for c in range(256) if c & 0x7F != 0x7F], np.uint8)  # every finite code
+    got = widen_block_fp8(torch.from_numpy(w).to(cuda).view(torch.float8_e4m3fn), torch.from_numpy(s).to(cuda))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(to_numpy(got), mo.fp8_block_dequant_bf16(w, s))
+
+
+def test_fp8_widening_refuses_nan(cuda, native_lib):
+    rng = np.random.default_rng(4)
+    w, s = cf.fp8_weight(rng, 128, 128)
+    w[5, 7] = 0x7F
+    with pytest.raises(ContractError):
+        widen_block_fp8(torch.from_numpy(w).to(cuda).view(torch.float8_e4m3fn), torch.from_numpy(s).to(cuda))
+
+
+def test_layer_from_checkpoint_matches_oracle(tmp_path, cuda, native_lib, golden_cfg0):
+    cfg = CONFIGS["cfg0"]
+    bank = cf.build(tmp_path / "ckpt", golden_cfg0, cfg)
+    moe = ExpertSSDMoE.from_checkpoint(tmp_path / "ckpt", cfg, cf.LAYER, device=cuda)
+    for name in ("gate", "up", "down"):
+        np.testing.assert_array_equal(to_numpy(getattr(moe.shared_experts, f"{name}_proj").weight),
+                                      bank[f"shared_{name}"])
+    x = torch.from_numpy(golden_cfg0["x"].view(np.int16)).to(cuda).view(torch.bfloat16)
+    out, w, idx = moe(x, return_route=True)
+    torch.cuda.synchronize()
+    ref = mo.moe_forward(golden_cfg0["x"], bank, cfg)
+    np.testing.assert_array_equal(to_numpy(idx), ref["indices"])
+    assert_close(to_numpy(out), ref["out"])
