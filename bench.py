@@ -55,6 +55,8 @@ CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.a
 # kernel, from an ncu capture of this bench's command (workload -> bytes)
 MEASURED_TRAFFIC = {
     "decode1": 80.53e6,
+    # gate/up stage of one layer: route gather 287 MB + routed gate/up 1,227 MB + shared gate/up 60 MB
+    "cfg3": 1.574e9,
 }
 
 
@@ -326,9 +328,11 @@ def setup_dist():
     return world, rank, local, dev
 
 
-def timed_region(run_steps, steps: int, warmup: int, world: int, sampler=None) -> float:
+def timed_region(run_steps, steps: int, warmup: int, world: int, sampler=None, per_step: list | None = None) -> float:
     """Device time (ms, max over ranks) of exactly `steps` steps after
-    `warmup` untimed ones, bracketed by a barrier and synchronisation."""
+    `warmup` untimed ones, bracketed by a barrier and synchronisation.  With
+    `per_step` (a list), the device time of each step on this rank is appended
+    (events recorded between the steps on the same stream)."""
     import torch
     import torch.distributed as dist
 
@@ -341,13 +345,19 @@ def timed_region(run_steps, steps: int, warmup: int, world: int, sampler=None) -
     if sampler is not None:
         sampler.__enter__()
         time.sleep(0.2)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps)] if per_step is not None else None
     ev0.record()
-    run_steps(steps)
+    run_steps(steps, marks)
     ev1.record()
     torch.cuda.synchronize()
     if sampler is not None:
         sampler.__exit__(None, None, None)
     ms = ev0.elapsed_time(ev1)
+    if marks:
+        prev = ev0
+        for m in marks:
+            per_step.append(prev.elapsed_time(m))
+            prev = m
     if world > 1:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -429,15 +439,18 @@ def run_ours(args) -> None:
             graphs.append(g)
         torch.cuda.synchronize()
 
-    def run_steps(n: int) -> None:
+    def run_steps(n: int, marks=None) -> None:
         for i in range(n):
             if use_graph:
                 graphs[i % len(graphs)].replay()
             else:
                 forward(i)
+            if marks:
+                marks[i].record()
 
     sampler = ClockSampler(local)
-    ms = timed_region(run_steps, args.steps, args.warmup, world, sampler)
+    step_times: list = []
+    ms = timed_region(run_steps, args.steps, args.warmup, world, sampler, per_step=step_times)
     ms_step = ms / args.steps
     layers_per_step = L if stack_kind else 1
     value = world * M * layers_per_step * args.steps / (ms * 1e-3)
@@ -462,13 +475,13 @@ def run_ours(args) -> None:
     x_dev = torch.empty_like(xs[0])
     K_e2e = max(1, min(args.steps, 2000))
 
-    def e2e_steps(n: int) -> None:
+    def e2e_steps(n: int, marks=None) -> None:
         for i in range(n):
             x_dev.copy_(x_host, non_blocking=True)
             y = stack(x_dev) if stack_kind else layers[i % L](x_dev)
             out_host.copy_(y, non_blocking=True)
 
-    ms_e2e = timed_region(e2e_steps, K_e2e, 1, world)
+    ms_e2e = timed_region(e2e_steps, K_e2e, max(3, args.warmup), world)
 
     # ---- CPU baseline (rank 0, N=1 only) -------------------------------------
     cpu = None
@@ -562,6 +575,10 @@ def run_ours(args) -> None:
                   "fp4_peak_tflops": fp4["tflops"], "fp4_peak_source": fp4["source"],
                   "bf16_peak_tflops": peaks["bf16_tflops"],
                   "unique_experts_per_call": U, "stage_ms": stage,
+                  "step_ms": ({"median": statistics.median(step_times),
+                               "p99": sorted(step_times)[min(len(step_times) - 1, int(0.99 * len(step_times)))],
+                               "min": min(step_times), "max": max(step_times), "rank": 0}
+                              if step_times else None),
                   "stack_tokens_per_s": world * M * args.steps / (ms * 1e-3) if stack_kind else None,
                   "load": {k: v for k, v in stats.items() if k != "counts"},
                   "expert_counts": stats["counts"] if wl.get("zipf") else None},
