@@ -187,6 +187,15 @@ int lg_fp8_block_dequant(const uint8_t *weight, const float *scale_inv,
                          int64_t rows, int64_t cols, int32_t block,
                          uint16_t *out, int32_t *nonfinite, void *stream);
 
+/* Resident-linear quantisation (layers.py:67-104: mx.quantize with group
+ * size 32, mode "mxfp8" (bits 8) or "mxfp4" (bits 4)) of a bf16 [rows, cols]
+ * matrix: per 32-value group the shared exponent floor(log2 amax) - emax
+ * (8 for E4M3, 2 for E2M1), elements rounded to nearest even and saturated;
+ * out (bf16, may equal weight) holds the quantised values, which bf16 holds
+ * exactly.  cols % 32 == 0. */
+int lg_mx_requantize(const uint16_t *weight, int64_t rows, int64_t cols,
+                     int32_t bits, uint16_t *out, void *stream);
+
 /*
  * Whole block.  Replaces ExpertSSDMoE.__call__ (moe.py:96-201) for bf16
  * hidden states: returns the f32 merge the MLX graph produces.

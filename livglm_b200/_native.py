@@ -94,6 +94,7 @@ SIGNATURES = {
     "lg_moe_combine_gather": (ctypes.c_int, [_CFG, _P, _P, _P, _P, _I64, _P, _P]),
     "lg_moe_ep_pack": (ctypes.c_int, [_CFG, _P, _I64, _P, _P, ctypes.c_int32, _P, _P, _P, _P]),
     "lg_fp8_block_dequant": (ctypes.c_int, [_P, _P, _I64, _I64, ctypes.c_int32, _P, _P, _P]),
+    "lg_mx_requantize": (ctypes.c_int, [_P, _I64, _I64, ctypes.c_int32, _P, _P]),
     "lg_moe_forward": (ctypes.c_int, [_CFG, _W, _P, _I64, _P, _P, _P, _P, ctypes.c_size_t, _P]),
     "lg_moe_forward_static_scratch": (ctypes.c_int, [_CFG, _W, _P, _I64, _P, _P, _P, _P]),
     "lg_moe_static_scratch_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int32), _P]),

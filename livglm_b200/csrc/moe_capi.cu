@@ -1215,6 +1215,20 @@ int lg_fp8_block_dequant(const uint8_t* weight, const float* scale_inv, int64_t 
   return cuda_check(cudaGetLastError(), "fp8 dequant launch");
 }
 
+int lg_mx_requantize(const uint16_t* weight, int64_t rows, int64_t cols, int32_t bits, uint16_t* out, void* stream) {
+  if (!weight || !out) return fail(LG_ERR_INVALID_ARG, "mx requantize: NULL pointer");
+  if (bits != 4 && bits != 8) return fail(LG_ERR_INVALID_ARG, "mx requantize: bits %d not 4 or 8", bits);
+  if (rows < 1 || cols < 32 || cols % 32) return fail(LG_ERR_INVALID_ARG, "mx requantize: cols %lld not a multiple of 32",
+                                                      static_cast<long long>(cols));
+  if (!aligned(weight, 16) || !aligned(out, 16)) return fail(LG_ERR_INVALID_ARG, "mx requantize: misaligned tensor");
+  const long long groups = rows * (cols / 32);
+  const int grid = static_cast<int>(std::min<long long>((groups + 255) / 256, 8LL * num_sms()));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bits == 8) lg::mx_requantize_kernel<8><<<grid, 256, 0, s>>>(weight, groups, out);
+  else lg::mx_requantize_kernel<4><<<grid, 256, 0, s>>>(weight, groups, out);
+  return cuda_check(cudaGetLastError(), "mx requantize launch");
+}
+
 int lg_moe_forward(const lg_moe_config* cfg, const lg_moe_weights* w, const uint16_t* x, int64_t M, float* out,
                    float* weights_out, uint32_t* indices_out, void* workspace, size_t workspace_bytes,
                    void* stream) {

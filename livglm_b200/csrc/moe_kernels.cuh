@@ -7,6 +7,7 @@
 //   combine_kernel         weighted top-k sum + shared add           moe.py:199-201
 #pragma once
 #include "common.cuh"
+#include "umma.cuh"
 
 namespace lg {
 
@@ -598,6 +599,62 @@ fp8_block_dequant_kernel(const uint8_t* __restrict__ w, const float* __restrict_
     *reinterpret_cast<uint4*>(out + r * cols + c0) = make_uint4(o[0], o[1], o[2], o[3]);
   }
   if (bad) atomicAdd(nonfinite, bad);
+}
+
+// --------------------------------------------------------------------------
+// MX requantisation of a bf16 weight matrix: the resident-linear
+// quantisation of kg36/livglm layers.py:67-104 (mx.quantize, group_size 32,
+// mode "mxfp8" / "mxfp4") as the OCP MX rule: per 32-value group of a row the
+// shared exponent X = clamp(floor(log2(amax)) - emax, -127, 127) (emax 8 for
+// E4M3, 2 for E2M1; X = -127 for an all-zero group), each element the
+// round-to-nearest-even of v * 2^-X in the element format, saturated to its
+// largest finite value.  The output holds element * 2^X as bf16 -- exact, so
+// bf16 kernels compute the quantised products.  One thread per group.
+__device__ __forceinline__ float pow2_mx(int e) {  // 2^e, -127 <= e <= 127 (2^-127 is subnormal)
+  return e >= -126 ? pow2i(e) : __uint_as_float(0x00400000u);
+}
+__device__ __forceinline__ void e4m3x2_roundtrip(float& lo, float& hi) {
+  uint32_t h;
+  asm("{\n\t.reg .b16 b;\n\tcvt.rn.satfinite.e4m3x2.f32 b, %1, %2;\n\tcvt.rn.f16x2.e4m3x2 %0, b;\n\t}"
+      : "=r"(h)
+      : "f"(hi), "f"(lo));
+  lo = __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xFFFFu)));
+  hi = __half2float(__ushort_as_half(static_cast<unsigned short>(h >> 16)));
+}
+template <int kBits>
+__global__ void __launch_bounds__(256)
+mx_requantize_kernel(const uint16_t* __restrict__ w, long long groups, uint16_t* __restrict__ out) {
+  constexpr int kEmax = kBits == 8 ? 8 : 2;
+  for (long long g = blockIdx.x * 256LL + threadIdx.x; g < groups; g += 256LL * gridDim.x) {
+    const uint4* src = reinterpret_cast<const uint4*>(w + g * 32);
+    uint32_t u[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 q = src[i];
+      u[4 * i] = q.x; u[4 * i + 1] = q.y; u[4 * i + 2] = q.z; u[4 * i + 3] = q.w;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fmaxf(fabsf(bf16lo(u[i])), fabsf(bf16hi(u[i]))));
+    int X = amax > 0.f ? ilogbf(amax) - kEmax : -127;
+    X = X < -127 ? -127 : (X > 127 ? 127 : X);
+    const float down = pow2_mx(-X), up = pow2_mx(X);
+    uint32_t o[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float lo = __fmul_rn(bf16lo(u[i]), down), hi = __fmul_rn(bf16hi(u[i]), down);
+      if (kBits == 8) {
+        e4m3x2_roundtrip(lo, hi);
+      } else {
+        umma::e2m1x2_to_f32(umma::e2m1x2_rn(lo, hi), lo, hi);
+      }
+      o[i] = static_cast<uint32_t>(f32_to_bf16(__fmul_rn(lo, up))) |
+             (static_cast<uint32_t>(f32_to_bf16(__fmul_rn(hi, up))) << 16);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + g * 32);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+  }
 }
 
 }  // namespace lg

@@ -378,6 +378,42 @@ class DenseMLP:
         self._cfg = _native.LgConfig.from_config(config)
         self._ws = Workspace()
 
+    quantization_mode: str | None = None
+
+    def quantize_to_mxfp(self, bits: int) -> tuple[int, int]:
+        """The reference runtime's resident quantisation of the three linears
+        (layers.py:67-104, DeferredLinear.quantize_to_mxfp: mx.quantize with
+        group size 32, mode mxfp8 / mxfp4), done on the GPU by lg_mx_requantize.
+        The quantised values are kept as bf16 (bf16 holds every MXFP8 / MXFP4
+        value exactly), so the shared-expert kernels compute the quantised
+        products.  Returns (source bytes, bytes of the MX encoding) as the
+        reference does."""
+        if bits not in (4, 8):
+            raise ContractError(f"unsupported resident quantization: mxfp{bits}")
+        if self.quantization_mode is not None:
+            raise ContractError("deferred linear was already quantized")
+        source = dest = 0
+        for name, lin in (("gate_proj", self.gate_proj), ("up_proj", self.up_proj), ("down_proj", self.down_proj)):
+            t = require_weight(lin.weight, f"shared_experts.{name}.weight")
+            if t.dim() != 2 or t.shape[-1] % 32 or t.dtype != torch.bfloat16 or not t.is_cuda:
+                raise ContractError(f"resident MXFP{bits} requires a group-32 bf16 CUDA matrix: {tuple(t.shape)}")
+            t = t.contiguous()
+            out = torch.empty_like(t)
+            _native.check(_native.load().lg_mx_requantize(t.data_ptr(), t.shape[0], t.shape[1], bits,
+                                                          out.data_ptr(), _stream_ptr(t.device)),
+                          "lg_mx_requantize")
+            lin.weight = out
+            source += t.numel() * 2
+            dest += t.numel() * bits // 8 + t.numel() // 32
+        self.quantization_mode = f"mxfp{bits}"
+        return source, dest
+
+    def quantize_to_mxfp8(self) -> tuple[int, int]:
+        return self.quantize_to_mxfp(8)
+
+    def quantize_to_mxfp4(self) -> tuple[int, int]:
+        return self.quantize_to_mxfp(4)
+
     def native_into(self, w: _native.LgWeights) -> None:
         for name, lin in (("gate_proj", self.gate_proj), ("up_proj", self.up_proj),
                           ("down_proj", self.down_proj)):
@@ -527,6 +563,16 @@ class ExpertSSDMoE:
         except KeyError as exc:
             raise ContractError(f"resident parameter was not loaded: {exc.args[0]}") from None
         self.experts.load_checkpoint(tensors, device=device)
+
+    def quantize_resident_linears_mxfp(self, bits: int = 8) -> dict:
+        """The block's part of the reference runtime's resident quantisation
+        (model.py:240-262: every resident 2-D linear except the router gate,
+        resident_plan.py:77-86): the shared expert's linears to MXFP8 (the
+        runtime default) or MXFP4.  The routed experts are MXFP4 already."""
+        if self.config.n_shared_experts < 1:
+            return {"mode": f"mxfp{bits}", "linears": 0, "source_bytes": 0, "destination_bytes": 0}
+        source, dest = self.shared_experts.quantize_to_mxfp(bits)
+        return {"mode": f"mxfp{bits}", "linears": 3, "source_bytes": source, "destination_bytes": dest}
 
     @classmethod
     def from_checkpoint(cls, path, config: MoEConfig, layer_idx: int, device="cuda") -> "ExpertSSDMoE":

@@ -125,6 +125,33 @@ def fp8_block_dequant_bf16(weight: np.ndarray, scale_inv: np.ndarray, block: int
     return f32_to_bf16_bits(prod.reshape(rows, cols))
 
 
+def mx_requantize_bf16(w_bits: np.ndarray, bits: int) -> np.ndarray:
+    """Resident MXFP8 / MXFP4 quantisation of a bf16 matrix (layers.py:67-104,
+    mx.quantize group 32) by the OCP MX rule -> bf16 bits of the quantised
+    values: per 32-value group X = clamp(floor(log2 amax) - emax, -127, 127)
+    (emax 8 for E4M3, 2 for E2M1; -127 for an all-zero group); element =
+    round-to-nearest-even of v * 2^-X (f32 product) saturated to the largest
+    finite element; value = element * 2^X.  MLX's own quantiser is not
+    available here, so this restates the published rule."""
+    import ml_dtypes
+
+    v = bf16_bits_to_f32(np.asarray(w_bits, np.uint16))
+    rows, cols = v.shape
+    g = v.reshape(rows, cols // 32, 32)
+    amax = np.abs(g).max(axis=-1)
+    _, ex = np.frexp(amax)
+    emax = 8 if bits == 8 else 2
+    X = np.where(amax > 0, ex.astype(np.int64) - 1 - emax, -127).clip(-127, 127)
+    down = np.ldexp(np.float32(1.0), -X).astype(np.float32)[..., None]
+    up = np.ldexp(np.float32(1.0), X).astype(np.float32)[..., None]
+    q = (g * down).astype(np.float32)
+    if bits == 8:
+        el = np.clip(q, -448.0, 448.0).astype(ml_dtypes.float8_e4m3fn).astype(np.float32)
+    else:
+        el = np.clip(q, -6.0, 6.0).astype(ml_dtypes.float4_e2m1fn).astype(np.float32)
+    return f32_to_bf16_bits((el * up).astype(np.float32).reshape(rows, cols))
+
+
 def mxfp4_dequant(packed: np.ndarray, scale: np.ndarray) -> np.ndarray:
     """U8 [rows, cols/2] nibbles (low nibble = even column) and U8 [rows,
     cols/32] E8M0 scales -> f32 [rows, cols] (value = E2M1 * 2^(s-127))."""

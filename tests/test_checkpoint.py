@@ -77,3 +77,25 @@ def test_fp8_block_dequant_oracle_blocks():
     dec = w.view(ml_dtypes.float8_e4m3fn).astype(np.float32)
     ref = (dec * np.repeat(np.repeat(s, 128, 0), 128, 1)).astype(np.float32)
     np.testing.assert_array_equal(got, mo.bf16_bits_to_f32(mo.f32_to_bf16_bits(ref)))
+
+
+def test_mx_requantize_oracle_properties():
+    """The resident MXFP4 rule agrees with the independent quantizer used for
+    the synthetic routed weights (livglm_b200/mxfp4.py); both rules are
+    idempotent and keep every value on the element grid times 2^X."""
+    from livglm_b200.mxfp4 import dequantize_mxfp4, quantize_mxfp4
+
+    rng = np.random.default_rng(2)
+    w = (rng.standard_normal((48, 256)) * np.exp(rng.uniform(-6, 2, (48, 1)))).astype(np.float32)
+    w[3, 32:64] = 0.0  # an all-zero group
+    wb = mo.f32_to_bf16_bits(w)
+    q4 = mo.mx_requantize_bf16(wb, 4)
+    p, s = quantize_mxfp4(torch.from_numpy(mo.bf16_bits_to_f32(wb)))
+    np.testing.assert_array_equal(mo.bf16_bits_to_f32(q4), dequantize_mxfp4(p, s).numpy())
+    for bits in (4, 8):
+        q = mo.mx_requantize_bf16(wb, bits)
+        np.testing.assert_array_equal(mo.mx_requantize_bf16(q, bits), q)
+    q8 = mo.bf16_bits_to_f32(mo.mx_requantize_bf16(wb, 8))
+    assert np.all(q8[3, 32:64] == 0)
+    rel = np.abs(q8 - mo.bf16_bits_to_f32(wb)) / np.abs(mo.bf16_bits_to_f32(wb)).reshape(48, 8, 32).max(-1).repeat(32, 1)
+    assert np.nanmax(rel) <= 0.125 + 1e-6  # 3-bit mantissa, and the OCP rule may clamp a group max into 448

@@ -46,3 +46,41 @@ def test_layer_from_checkpoint_matches_oracle(tmp_path, cuda, native_lib, golden
     ref = mo.moe_forward(golden_cfg0["x"], bank, cfg)
     np.testing.assert_array_equal(to_numpy(idx), ref["indices"])
     assert_close(to_numpy(out), ref["out"])
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_mx_requantize_bit_exact(cuda, native_lib, bits):
+    from livglm_b200 import _native
+    from livglm_b200.moe import _stream_ptr
+
+    rng = np.random.default_rng(10 + bits)
+    w = (rng.standard_normal((96, 512)) * np.exp(rng.uniform(-8, 3, (96, 1)))).astype(np.float32)
+    w[5, :64] = 0.0
+    wb = mo.f32_to_bf16_bits(w)
+    t = torch.from_numpy(wb.view(np.int16)).to(cuda).view(torch.bfloat16)
+    out = torch.empty_like(t)
+    assert _native.load().lg_mx_requantize(t.data_ptr(), 96, 512, bits, out.data_ptr(), _stream_ptr(cuda)) == 0
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(to_numpy(out), mo.mx_requantize_bf16(wb, bits))
+
+
+def test_layer_with_mxfp8_shared_expert(cuda, native_lib, golden_cfg0):
+    """quantize_resident_linears_mxfp(8), the reference runtime's default
+    resident quantisation, against the oracle fed the same quantised shared
+    weights."""
+    from livglm_b200.moe import build_layer
+    from oracle.torch_bridge import bank_to_device
+
+    cfg = CONFIGS["cfg0"]
+    moe = build_layer(cfg, bank_to_device(golden_cfg0, cuda))
+    info = moe.quantize_resident_linears_mxfp(8)
+    assert info["linears"] == 3 and info["destination_bytes"] < info["source_bytes"]
+    bank = dict(golden_cfg0)
+    for name in ("gate", "up", "down"):
+        bank[f"shared_{name}"] = mo.mx_requantize_bf16(golden_cfg0[f"shared_{name}"], 8)
+        np.testing.assert_array_equal(to_numpy(getattr(moe.shared_experts, f"{name}_proj").weight),
+                                      bank[f"shared_{name}"])
+    x = torch.from_numpy(golden_cfg0["x"].view(np.int16)).to(cuda).view(torch.bfloat16)
+    out = moe(x)
+    torch.cuda.synchronize()
+    assert_close(to_numpy(out), mo.moe_forward(golden_cfg0["x"], bank, cfg)["out"])
