@@ -235,6 +235,9 @@ int launch_router(const lg_moe_config* c, const uint16_t* x, int M, const float*
   if (M <= 4) {
     dim3 grid((M + 0) / 1, (E + 7) / 8);
     router_logits_kernel<1, 1><<<grid, 256, 0, s>>>(x, Wr, M, d, E, logits);
+  } else if (d % 256 == 0 && M >= 8192) {  // 64 tokens x 16 experts per block: fewer re-reads of W_r
+    dim3 grid((M + 63) / 64, (E + kRlExperts - 1) / kRlExperts);
+    router_logits_tiled_kernel<8><<<grid, 256, 0, s>>>(x, Wr, M, d, E, logits);
   } else if (d % 256 == 0 && M >= 1024) {
     dim3 grid((M + 31) / 32, (E + kRlExperts - 1) / kRlExperts);
     router_logits_tiled_kernel<4><<<grid, 256, 0, s>>>(x, Wr, M, d, E, logits);

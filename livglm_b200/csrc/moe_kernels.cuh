@@ -83,52 +83,60 @@ router_logits_kernel(const uint16_t* __restrict__ x, const float* __restrict__ W
 // Router logits for many tokens, same arithmetic as router_logits_kernel
 // (lane l sums the 8-element chunks c = l, l + 32, ... in increasing order with
 // fma, then the 16/8/4/2/1 xor butterfly), with the operands staged through
-// shared memory: a block owns 8 * TW tokens x 16 experts and walks d in
+// shared memory: a block owns 8 * TW tokens x EW experts and walks d in
 // k-blocks of 256 elements (32 chunks, one per lane), so every staged x and
 // W_r element serves all the block's pairs instead of being re-read from L2
-// per warp.  Warp w owns tokens t0 + TW w .. + TW - 1 and all 16 experts.
+// per warp.  Warp w owns tokens t0 + TW w .. + TW - 1 and all EW experts.
+// W_r is staged as [expert][half][lane] float4 (lane l's chunk in two
+// consecutive-lane rows), so a warp's reads touch 32 consecutive 16-byte words.
 // d must be a multiple of 256.
 constexpr int kRlExperts = 16;
-template <int TW>
+template <int TW, int EW = kRlExperts>
 __global__ void __launch_bounds__(256)
 router_logits_tiled_kernel(const uint16_t* __restrict__ x, const float* __restrict__ W,
                            int M, int d, int E, float* __restrict__ logits) {
   constexpr int TB = 8 * TW;  // tokens per block
   __shared__ __align__(16) uint16_t xs[TB * 256];
-  __shared__ __align__(16) float ws[kRlExperts * 256];
+  __shared__ __align__(16) float4 ws[EW * 64];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int t0 = blockIdx.x * TB, e0 = blockIdx.y * kRlExperts;
-  float acc[TW][kRlExperts];
+  const int t0 = blockIdx.x * TB, e0 = blockIdx.y * EW;
+  float acc[TW][EW];
 #pragma unroll
   for (int a = 0; a < TW; ++a)
 #pragma unroll
-    for (int b = 0; b < kRlExperts; ++b) acc[a][b] = 0.0f;
+    for (int b = 0; b < EW; ++b) acc[a][b] = 0.0f;
   // the next k-block's share of this thread, loaded while the current one is
-  // multiplied: TB * 32 uint4 of x and 16 * 64 float4 of W_r over 256 threads
-  constexpr int XV = TB * 32 / 256, WV = kRlExperts * 64 / 256;
+  // multiplied: TB * 32 uint4 of x and EW * 64 float4 of W_r over 256 threads
+  constexpr int XV = (TB * 32 + 255) / 256, WV = (EW * 64 + 255) / 256;
   uint4 xr[XV];
   float4 wr[WV];
   auto fetch = [&](int k0) {
 #pragma unroll
     for (int u = 0; u < XV; ++u) {
       const int i = threadIdx.x + 256 * u, r = i >> 5, c = i & 31, t = t0 + r;
-      xr[u] = t < M ? *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * d + k0 + 8 * c)
-                    : make_uint4(0u, 0u, 0u, 0u);
+      xr[u] = (i < TB * 32 && t < M) ? *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * d + k0 + 8 * c)
+                                     : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
     for (int u = 0; u < WV; ++u) {
       const int i = threadIdx.x + 256 * u, r = i >> 6, c = i & 63, e = e0 + r;
-      wr[u] = e < E ? *reinterpret_cast<const float4*>(W + static_cast<size_t>(e) * d + k0 + 4 * c)
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      wr[u] = (i < EW * 64 && e < E) ? *reinterpret_cast<const float4*>(W + static_cast<size_t>(e) * d + k0 + 4 * c)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
   fetch(0);
   for (int k0 = 0; k0 < d; k0 += 256) {
     __syncthreads();  // the previous k-block's operands are consumed
 #pragma unroll
-    for (int u = 0; u < XV; ++u) reinterpret_cast<uint4*>(xs)[threadIdx.x + 256 * u] = xr[u];
+    for (int u = 0; u < XV; ++u) {
+      const int i = threadIdx.x + 256 * u;
+      if (i < TB * 32) reinterpret_cast<uint4*>(xs)[i] = xr[u];
+    }
 #pragma unroll
-    for (int u = 0; u < WV; ++u) reinterpret_cast<float4*>(ws)[threadIdx.x + 256 * u] = wr[u];
+    for (int u = 0; u < WV; ++u) {
+      const int i = threadIdx.x + 256 * u;  // expert i / 64, float4 c = i % 64 = lane c / 2, half c % 2
+      if (i < EW * 64) ws[(i >> 6) * 64 + (i & 1) * 32 + ((i & 63) >> 1)] = wr[u];
+    }
     __syncthreads();
     if (k0 + 256 < d) fetch(k0 + 256);
     // lane l: chunk c = k0 / 8 + l (elements 8 l .. 8 l + 7 of this k-block)
@@ -142,9 +150,9 @@ router_logits_tiled_kernel(const uint16_t* __restrict__ x, const float* __restri
       xv[a][6] = bf16lo(u.w); xv[a][7] = bf16hi(u.w);
     }
 #pragma unroll
-    for (int b = 0; b < kRlExperts; ++b) {
-      const float4 w0 = reinterpret_cast<const float4*>(ws)[b * 64 + 2 * lane];
-      const float4 w1 = reinterpret_cast<const float4*>(ws)[b * 64 + 2 * lane + 1];
+    for (int b = 0; b < EW; ++b) {
+      const float4 w0 = ws[b * 64 + lane];
+      const float4 w1 = ws[b * 64 + 32 + lane];
       const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
       for (int a = 0; a < TW; ++a)
@@ -157,16 +165,16 @@ router_logits_tiled_kernel(const uint16_t* __restrict__ x, const float* __restri
 #pragma unroll
     for (int a = 0; a < TW; ++a)
 #pragma unroll
-      for (int b = 0; b < kRlExperts; ++b)
+      for (int b = 0; b < EW; ++b)
         acc[a][b] = __fadd_rn(acc[a][b], __shfl_xor_sync(0xffffffffu, acc[a][b], off));
-  // lane b < 16 writes expert e0 + b of the warp's tokens
+  // lane b < EW writes expert e0 + b of the warp's tokens
 #pragma unroll
   for (int a = 0; a < TW; ++a) {
     const int t = t0 + warp * TW + a;
     float v = 0.f;
 #pragma unroll
-    for (int b = 0; b < kRlExperts; ++b) v = lane == b ? acc[a][b] : v;
-    if (t < M && lane < kRlExperts && e0 + lane < E) logits[static_cast<size_t>(t) * E + e0 + lane] = v;
+    for (int b = 0; b < EW; ++b) v = lane == b ? acc[a][b] : v;
+    if (t < M && lane < EW && e0 + lane < E) logits[static_cast<size_t>(t) * E + e0 + lane] = v;
   }
 }
 
@@ -264,7 +272,6 @@ dispatch_kernel(const uint32_t* __restrict__ idx, int S, int E,
                 const int* __restrict__ counts, int* __restrict__ offsets,
                 int* __restrict__ perm, int* __restrict__ active) {
   __shared__ int red[2][8];
-  __shared__ int wsum[8];
   const int e = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int start = 0, nz = 0;
@@ -290,20 +297,36 @@ dispatch_kernel(const uint32_t* __restrict__ idx, int S, int E,
     if (cnt > 0) active[1 + nz] = e;
   }
   if (cnt == 0) return;
-  int base = start;
-  for (int s0 = 0; s0 < S; s0 += 256) {
-    const int s = s0 + threadIdx.x;
-    const bool f = s < S && idx[s] == static_cast<uint32_t>(e);
-    const unsigned b = __ballot_sync(0xffffffffu, f);
-    __syncthreads();
-    if (lane == 0) wsum[warp] = __popc(b);
-    __syncthreads();
-    int wpre = 0, tot = 0;
+  // slots in blocks of 1024 (four 256-slot rows, thread t holds slot 256 j + t
+  // of row j): one ballot per row and warp, one barrier pair per block
+  __shared__ int rsum[2][4][8];
+  int base = start, par = 0;
+  for (int s0 = 0; s0 < S; s0 += 1024, par ^= 1) {
+    bool f[4];
+    unsigned b[4];
 #pragma unroll
-    for (int w = 0; w < 8; ++w) { const int v = wsum[w]; wpre += (w < warp) ? v : 0; tot += v; }
-    if (f) perm[base + wpre + __popc(b & ((1u << lane) - 1u))] = s;
+    for (int j = 0; j < 4; ++j) {
+      const int s = s0 + 256 * j + threadIdx.x;
+      f[j] = s < S && __ldg(idx + s) == static_cast<uint32_t>(e);
+      b[j] = __ballot_sync(0xffffffffu, f[j]);
+      if (lane == 0) rsum[par][j][warp] = __popc(b[j]);
+    }
+    __syncthreads();  // rsum[par] complete; rsum[par ^ 1] was read before the previous barrier
+    int tot = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int rpre = 0, rtot = 0;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const int v = rsum[par][j][w];
+        rpre += (w < warp) ? v : 0;
+        rtot += v;
+      }
+      if (f[j]) perm[base + tot + rpre + __popc(b[j] & ((1u << lane) - 1u))] = s0 + 256 * j + threadIdx.x;
+      tot += rtot;
+    }
     base += tot;
-    if (base - start >= cnt) break;
+    if (base - start >= cnt) break;  // every thread sees the same tot
   }
 }
 
