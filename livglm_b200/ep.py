@@ -3,12 +3,14 @@
 No counterpart in the reference (its experts stream from SSD on one device);
 this is the multi-GPU form of ExpertSSDMoE.__call__ (moe.py:96-201) for
 batched work.  Rank r of a W-rank process group holds the routed experts
-[r*E/W, (r+1)*E/W) and a replica of the router and the shared expert; tokens
+r, r + W, r + 2W, ... and a replica of the router and the shared expert; tokens
 are data-parallel (each rank brings its own rows).  One call:
 
-1. route the local rows (lg_moe_router) and sort the route slots t*k + j by
-   expert id (lg_moe_dispatch, a stable counting sort); because expert ranges
-   are contiguous per rank, that order also groups the slots by destination;
+1. route the local rows (lg_moe_router), renumber the chosen experts to
+   exchange ids (expert e lives on rank e mod W, as local expert e // W;
+   exchange id = owner * E/W + local index) and sort the route slots t*k + j
+   by exchange id (lg_moe_dispatch, a stable counting sort): that order groups
+   the slots by destination rank and, within it, by local expert;
 2. exchange the per-destination route counts (all-to-all of W integers; the
    split sizes go to the host once per call);
 3. send one bf16 row per route slot and its expert id local to the
@@ -45,8 +47,19 @@ LocalCompute = Callable[[torch.Tensor, torch.Tensor], torch.Tensor]
 
 
 def expert_owner(expert: torch.Tensor, n_experts: int, world: int) -> torch.Tensor:
-    """Rank that holds each expert id (contiguous ranges of E/W experts)."""
-    return torch.div(expert, n_experts // world, rounding_mode="floor")
+    """Rank that holds each expert id: round-robin, expert e on rank e mod W
+    (popular experts -- low ids under the Zipf workload -- spread over the
+    ranks instead of piling onto rank 0)."""
+    return torch.remainder(expert, world)
+
+
+def exchange_ids(n_experts: int, world: int, device=None) -> torch.Tensor:
+    """Expert id -> exchange id (int32 [E]): owner * (E/W) + local index, so
+    that sorting routes by exchange id groups them by owning rank, and the
+    exchange id mod E/W is the expert's index in its owner's bank (expert e is
+    local expert e // W of rank e mod W)."""
+    e = torch.arange(n_experts, dtype=torch.int64, device=device)
+    return ((e % world) * (n_experts // world) + e // world).to(torch.int32)
 
 
 def exchange_rows(x_send: torch.Tensor, e_send: torch.Tensor, send_counts: torch.Tensor,
@@ -97,8 +110,8 @@ def exchange_routes(rows: torch.Tensor, slot_expert: torch.Tensor, perm: torch.T
                     send_counts: torch.Tensor, n_experts: int, compute_local: LocalCompute,
                     group=None, overlap: Callable[[], None] | None = None) -> torch.Tensor:
     """exchange_rows with the packing done by torch ops (any device): rows
-    [M, d] one per token, slot_expert [M*k] int64 expert id of each route
-    slot, perm [M*k] int64 route slots sorted by expert id (stable),
+    [M, d] one per token, slot_expert [M*k] int64 exchange id of each route
+    slot (exchange_ids), perm [M*k] int64 route slots sorted by it (stable),
     send_counts [W] int64.  Returns [M*k, d], the output of every route slot
     in slot order.  ExpertParallelMoE does the same packing and unpacking
     with lg_moe_ep_pack and lg_moe_combine_gather."""
@@ -119,8 +132,8 @@ class ExpertParallelMoE:
 
     tensors: the layer's stacked tensors as built by synthetic.layer_weights
     (router_weight, router_bias, shared_*, and either the full expert banks,
-    of which this rank keeps its own slice, or banks already holding only the
-    E/W local experts).
+    of which this rank keeps experts rank, rank + W, ..., or banks already
+    holding only the E/W local experts in that order).
     """
 
     def __init__(self, config: MoEConfig, layer_idx: int, tensors: dict, *, group=None):
@@ -135,7 +148,6 @@ class ExpertParallelMoE:
         if E % self.world:
             raise ContractError(f"{E} routed experts do not split evenly over {self.world} ranks")
         self.per_rank = E // self.world
-        lo = self.rank * self.per_rank
         self.gate = TopKRouter(config)
         self.gate.weight = require_weight(tensors.get("router_weight"), "router.weight")
         self.gate.e_score_correction_bias = require_weight(tensors.get("router_bias"),
@@ -154,13 +166,14 @@ class ExpertParallelMoE:
         for name in ("gate_packed", "gate_scale", "up_packed", "up_scale", "down_packed", "down_scale"):
             t = tensors[name]
             if t.shape[0] == E:
-                t = t[lo:lo + self.per_rank]
+                t = t[self.rank::self.world]
             if t.shape[0] != self.per_rank:
                 raise ContractError(f"{name} holds {t.shape[0]} experts, expected {E} or {self.per_rank}")
             banks.append(t.contiguous())
         self.experts.set_banks(*banks)
         self._cfg = _native.LgConfig.from_config(config)
         self._ws = Workspace()
+        self._xid = exchange_ids(E, self.world, self.gate.weight.device)
 
     def use_workspace(self, ws: Workspace) -> None:
         """Share one scratch area with other layers run in order on one stream
@@ -188,14 +201,15 @@ class ExpertParallelMoE:
         inv = torch.empty(R, dtype=torch.int32, device=dev)
         if M:
             _, weights, indices = self.gate(rows)
+            xidx = self._xid[indices.view(torch.int32).long()].view(torch.uint32)  # exchange ids
             counts = torch.empty(E, dtype=torch.int32, device=dev)
             offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
             perm = torch.empty(R, dtype=torch.int32, device=dev)
             ws, nbytes = self._ws.get(self._cfg, M, dev)
-            _native.check(lib.lg_moe_dispatch(self._cfg, indices.data_ptr(), M, counts.data_ptr(),
+            _native.check(lib.lg_moe_dispatch(self._cfg, xidx.data_ptr(), M, counts.data_ptr(),
                                               offsets.data_ptr(), perm.data_ptr(), ws, nbytes, stream),
                           "lg_moe_dispatch")
-            _native.check(lib.lg_moe_ep_pack(self._cfg, rows.data_ptr(), M, indices.data_ptr(), perm.data_ptr(),
+            _native.check(lib.lg_moe_ep_pack(self._cfg, rows.data_ptr(), M, xidx.data_ptr(), perm.data_ptr(),
                                              self.world, x_send.data_ptr(), e_send.data_ptr(), inv.data_ptr(),
                                              stream), "lg_moe_ep_pack")
             bounds = offsets[::self.per_rank].to(torch.int64)  # [W + 1] dispatch ranges per owner

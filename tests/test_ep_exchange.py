@@ -18,7 +18,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from livglm_b200.config import CONFIGS
-from livglm_b200.ep import exchange_routes, expert_owner
+from livglm_b200.ep import exchange_ids, exchange_routes, expert_owner
 from oracle import moe_oracle as mo
 from tests.conftest import GOLDEN
 
@@ -46,20 +46,20 @@ def _worker(rank: int, world: int, port: int, shares: list, result_q):
         else:
             idx = np.zeros((0, k), np.uint32)
         slot_expert = torch.from_numpy(idx.reshape(-1).astype(np.int64))
-        perm = torch.from_numpy(np.argsort(slot_expert.numpy(), kind="stable").astype(np.int64))
+        slot_xid = exchange_ids(E, world)[slot_expert].to(torch.int64)
+        perm = torch.from_numpy(np.argsort(slot_xid.numpy(), kind="stable").astype(np.int64))
         owner = expert_owner(slot_expert, E, world)
         send_counts = torch.bincount(owner, minlength=world).to(torch.int64)
         rows = torch.from_numpy(mo.bf16_bits_to_f32(x_bits.astype(np.uint16)).reshape(M, d))
-        per_rank = E // world
         cfg1 = cfg.replace(num_experts_per_tok=1)
 
         def compute_local(x: torch.Tensor, local_expert: torch.Tensor) -> torch.Tensor:
             bits = mo.f32_to_bf16_bits(x.numpy())
-            glob = (local_expert.numpy() + rank * per_rank).astype(np.uint32).reshape(-1, 1)
+            glob = (local_expert.numpy() * world + rank).astype(np.uint32).reshape(-1, 1)
             y = mo.expert_outputs(bits, bank, glob, cfg1)
             return torch.from_numpy(y.reshape(-1, d))
 
-        y_slots = exchange_routes(rows, slot_expert, perm, send_counts, E, compute_local)
+        y_slots = exchange_routes(rows, slot_xid, perm, send_counts, E, compute_local)
         ref = mo.expert_outputs(x_bits, bank, idx, cfg).reshape(-1, d) if M else np.zeros((0, d), np.float32)
         result_q.put((rank, bool(np.array_equal(y_slots.numpy(), ref)), int(M)))
     finally:
@@ -85,4 +85,9 @@ def test_exchange_matches_single_process_experts(shares):
 
 def test_expert_owner_ranges():
     e = torch.arange(16)
-    assert expert_owner(e, 16, 4).tolist() == [0] * 4 + [1] * 4 + [2] * 4 + [3] * 4
+    assert expert_owner(e, 16, 4).tolist() == [0, 1, 2, 3] * 4
+    xid = exchange_ids(16, 4)
+    # sorted by exchange id = grouped by owner, then by local index e // W
+    assert torch.argsort(xid).tolist() == [0, 4, 8, 12, 1, 5, 9, 13, 2, 6, 10, 14, 3, 7, 11, 15]
+    assert (xid // 4).tolist() == expert_owner(e, 16, 4).tolist()
+    assert (xid % 4).tolist() == (e // 4).tolist()
