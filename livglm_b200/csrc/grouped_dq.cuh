@@ -115,6 +115,16 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
   }
 }
 
+// The shared expert's one-"expert" tables: offsets {0, M}, chunk_start {0, ceil(M / 256)}.
+__global__ void shared_table_kernel(int M, int* __restrict__ tab) {
+  if (threadIdx.x == 0) {
+    tab[0] = 0;
+    tab[1] = M;
+    tab[2] = 0;
+    tab[3] = (M + kNMax - 1) / kNMax;
+  }
+}
+
 // tab[b] = silu_bf16 of the bf16 value with bits b.
 __global__ void __launch_bounds__(256) silu_table_kernel(uint16_t* __restrict__ tab) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -252,7 +262,10 @@ __device__ __forceinline__ void prefetch_3d(const CUtensorMap* map, int x, int y
 // both freed by the MMAs' commit.  The packed weight bytes never pass
 // through shared memory: each worker loads its row's 32 bytes of a stage
 // from global memory into registers one of its stages (two stages) early.
-template <bool kGateUp>
+// kBf16A: the shared expert -- bf16 weight rows loaded by TMA straight into the
+// A slots (mA0 / mA1: 2-D [rows][K * 2 bytes], 128-byte x 128-row boxes, 128-byte
+// swizzle), no widening; the "routes" are the tokens in order (perm == nullptr).
+template <bool kGateUp, bool kBf16A = false>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_dq_kernel(Args a, const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mA1,
                       const __grid_constant__ CUtensorMap mB) {
@@ -273,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bempty[s], 1);
     }
     for (int c = 0; c < kConvSlots; ++c) {
-      mbar_init(&conv_full[c], kGroupWarps);
+      mbar_init(&conv_full[c], kBf16A ? 1 : kGroupWarps);
       mbar_init(&conv_empty[c], 1);
     }
     mbar_init(&acc_full, 1);
@@ -299,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pseq = 0, pks = 0;
       bool phave = next_item(0, pitem);
       auto pf_step = [&]() {
-        if (!phave) return;
+        if (kBf16A || !phave) return;
         prefetch_3d(&mA0, pks * 32, pitem.rb * a.rb_rows, pitem.e);
         prefetch_3d(&mA1, pks * 32, pitem.rb * a.rb_rows + a.acc1_rows, pitem.e);
         if (++pks == a.ks_count) {
@@ -315,6 +328,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (it_k >= kBStages) ok = dtc::wait1(&bempty[s], ((it_k / kBStages) - 1) & 1, a.status, kSiteBEmpty);
           if (!ok) break;
           unsigned char* bt = base + s * kBBytes;
+          if (kBf16A) {  // the stage's A tiles into widened slot it_k % kConvSlots
+            const int c = it_k % kConvSlots;
+            if (it_k >= kConvSlots)
+              ok = dtc::wait1(&conv_empty[c], ((it_k / kConvSlots) - 1) & 1, a.status, kSiteConvEmpty);
+            if (!ok) break;
+            unsigned char* at = conv + c * kConvBytes;
+            const int y0 = item.rb * a.rb_rows;
+            mbar_arrive_expect_tx(&conv_full[c], kConvBytes);
+            dtc::tma_2d(at, &mA0, ks * 128, y0, &conv_full[c]);
+            dtc::tma_2d(at + kConvBytes / 2, &mA1, ks * 128, y0 + a.acc1_rows, &conv_full[c]);
+          }
           mbar_arrive_expect_tx(&bfull[s], bytes);
           for (int b = 0; b < item.n / kBoxRows; ++b)
             dtc::tma_2d(bt + b * (kBoxRows * 128), &mB, ks * 128, item.p0 + b * kBoxRows, &bfull[s]);
@@ -324,6 +348,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) {  // let the copies in flight land before the CTA leaves
         for (int q = (it_k > kBStages ? it_k - kBStages : 0); q < it_k; ++q)
           dtc::wait1(&bfull[q % kBStages], (q / kBStages) & 1, a.status, kSiteBFull);
+        if (kBf16A)
+          for (int q = (it_k > kConvSlots ? it_k - kConvSlots : 0); q < it_k; ++q)
+            dtc::wait1(&conv_full[q % kConvSlots], (q / kConvSlots) & 1, a.status, kSiteConv);
       }
     }
     __syncwarp();
@@ -396,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int c = c_lo_d + 32 * k + lane;
-          if (32 * k < it.n / 2 && c < it.nt) slots[k] = __ldg(a.perm + it.p0 + c);
+          if (32 * k < it.n / 2 && c < it.nt) slots[k] = kBf16A ? it.p0 + c : __ldg(a.perm + it.p0 + c);
         }
       }
       if (ok) ok = dtc::wait_warp1(&acc_full, seq & 1, a.status, kSiteAccFull);
@@ -444,6 +471,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&acc_empty);
       return true;
     };
+    if (kBf16A) {  // the A tiles come by TMA: the workers only run the epilogues
+      Item it;
+      for (int seq = 0; next_item(seq, it); ++seq)
+        if (!epilogue(it, seq, true)) break;
+    } else {
     // This group's stages: ks = grp, grp + 2, ... of every item.  Weight bytes
     // and scales are loaded ahead along that sequence, across items; the
     // iterators keep row pointers only (items are recomputed where needed).
@@ -533,6 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       Item pv;
       next_item(seq - 1, pv);
       epilogue(pv, seq - 1, ok);
+    }
     }
   }
   __syncwarp();

@@ -109,7 +109,7 @@ int validate_tokens(int64_t M, const lg_moe_config* c) {
 
 struct Layout {
   size_t status, logits, weights, indices, counts, offsets, perm, active, act, act_s, y, ys, tickets, xs, bimg, bsc,
-      xterm, xtsc, aterm, atsc, tiles, inv, silu, total;
+      xterm, xtsc, aterm, atsc, tiles, inv, silu, shtab, total;
   bool tc;  // batched tensor-core buffers reserved
 };
 
@@ -174,6 +174,7 @@ Layout layout(const lg_moe_config* c, int64_t M) {
   L.tiles = o;   o += L.tc ? up((E + 1) * 4) : 0;
   L.inv = o;     o += L.tc ? up(m * k * 4) : 0;
   L.silu = o;    o += L.tc ? up(65536 * 2) : 0;  // SwiGLU factor table of the bf16 grouped GEMMs
+  L.shtab = o;   o += L.tc ? up(16) : 0;         // the shared expert's offsets and chunk table
   L.total = o;
   return L;
 }
@@ -414,13 +415,13 @@ bool dq_mode(const lg_moe_config* c, int M) {
          static_cast<long long>(kDqMinRoutesPerExpert) * c->n_routed_experts;
 }
 
-template <bool kGateUp>
+template <bool kGateUp, bool kBf16A = false>
 int launch_dq(const lg::gdq::Args& a0, long long items_max, const CUtensorMap& A0, const CUtensorMap& A1,
               const CUtensorMap& B, cudaStream_t s) {
   using namespace lg::gdq;
   Args a = a0;
   const size_t smem = 1024 + kSmemBytes;  // 1024-byte alignment slack
-  auto kern = grouped_dq_kernel<kGateUp>;
+  auto kern = grouped_dq_kernel<kGateUp, kBf16A>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return cuda_check(e, "grouped bf16 kernel smem attribute");
   long long grid = num_sms();
@@ -481,6 +482,41 @@ int launch_routed_dq(const lg_moe_config* c, const lg_moe_weights* w, const uint
   return launch_dq<false>(q, chunks_max * q.rb_count, A0, A0, B, s);
 }
 
+// The shared expert of a large batch on the same kernel (kBf16A): its bf16
+// weight rows TMA-loaded as the A tiles, the tokens (gate/up) or act_s (down)
+// in order as B, 256-token chunks.  Needs Fs % 128 == 0.
+int launch_shared_dq(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M, void* ws,
+                     const Layout& L, uint16_t* ys, bool gate_up, bool fill_silu, cudaStream_t s) {
+  const int d = c->hidden_size, Fs = c->moe_intermediate_size * c->n_shared_experts;
+  lg::gdq::Args q{};
+  int* tab = at<int>(ws, L.shtab);
+  q.d = d; q.F = Fs; q.E = 1; q.R = M;
+  q.limit = c->swiglu_limit;
+  q.offsets = tab; q.perm = nullptr; q.chunk_start = tab + 2;
+  q.silu = at<uint16_t>(ws, L.silu);
+  q.act = at<uint16_t>(ws, L.act_s); q.y = ys;
+  q.status = at<int>(ws, L.status);
+  const long long items_chunks = (M + lg::gdq::kNMax - 1) / lg::gdq::kNMax;
+  CUtensorMap A0, A1, B;
+  if (gate_up) {
+    lg::gdq::shared_table_kernel<<<1, 32, 0, s>>>(M, tab);
+    if (fill_silu) lg::gdq::silu_table_kernel<<<256, 256, 0, s>>>(at<uint16_t>(ws, L.silu));
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_check(e, "shared tables launch");
+    q.ks_count = d / 64; q.rb_count = Fs / 128; q.rb_rows = 128; q.acc1_rows = 0;
+    if (!map_2d(&A0, w->shared_gate, static_cast<uint64_t>(d) * 2, Fs, 128, 128, true) ||
+        !map_2d(&A1, w->shared_up, static_cast<uint64_t>(d) * 2, Fs, 128, 128, true) ||
+        !map_2d(&B, x, static_cast<uint64_t>(d) * 2, M, 128, lg::gdq::kBoxRows, true))
+      return fail(LG_ERR_CUDA, "batched shared gate/up: tensor map encoding failed");
+    return launch_dq<true, true>(q, items_chunks * q.rb_count, A0, A1, B, s);
+  }
+  q.ks_count = Fs / 64; q.rb_count = d / 256; q.rb_rows = 256; q.acc1_rows = 128;
+  if (!map_2d(&A0, w->shared_down, static_cast<uint64_t>(Fs) * 2, d, 128, 128, true) ||
+      !map_2d(&B, q.act, static_cast<uint64_t>(Fs) * 2, M, 128, lg::gdq::kBoxRows, true))
+    return fail(LG_ERR_CUDA, "batched shared down: tensor map encoding failed");
+  return launch_dq<false, true>(q, items_chunks * q.rb_count, A0, A0, B, s);
+}
+
 // The batched expert passes on the tensor core: token split, route tiles,
 // routed and/or shared gate/up, then routed and/or shared down.  Routing
 // tables (offsets, perm) must be ready; y gets the routed outputs in slot
@@ -534,7 +570,11 @@ int launch_experts_tc(const lg_moe_config* c, const lg_moe_weights* w, const uin
     const long long items = tiles_max * g.rb_count;
     if ((rc = launch_grouped<true, true>(g, static_cast<int>(std::min<long long>(items, 1 << 30)), m, s))) return rc;
   }
-  if (sh) {
+  // large batches: the shared expert on the widened-weight kernel (256-token tiles)
+  const bool sdq = sh && Fs % 128 == 0 && dq_mode(c, M);
+  if (sdq) {
+    if ((rc = launch_shared_dq(c, w, x, M, ws, L, ys, true, !dq, s))) return rc;
+  } else if (sh) {
     Args g = a;
     g.kb_count = d / 64; g.rb_count = Fs / 64; g.n_tok_tiles = tok_tiles;
     if (!map_2d(&m.A0, w->shared_gate, static_cast<uint64_t>(d) * 2, Fs, 128, 64, true) ||
@@ -561,7 +601,9 @@ int launch_experts_tc(const lg_moe_config* c, const lg_moe_weights* w, const uin
     const long long items = tiles_max * g.rb_count;
     if ((rc = launch_grouped<true, false>(g, static_cast<int>(std::min<long long>(items, 1 << 30)), m, s))) return rc;
   }
-  if (sh) {
+  if (sdq) {
+    if ((rc = launch_shared_dq(c, w, x, M, ws, L, ys, false, false, s))) return rc;
+  } else if (sh) {
     Args g = a;
     g.kb_count = Fs / 64; g.rb_count = d / 128; g.n_tok_tiles = tok_tiles;
     if (!map_2d(&m.A0, w->shared_down, static_cast<uint64_t>(Fs) * 2, d, 128, 128, true) ||
@@ -1156,11 +1198,11 @@ int lg_moe_combine(const lg_moe_config* cfg, const uint16_t* y, const float* wei
   if ((rc = validate_cfg(cfg)) || (rc = validate_tokens(M, cfg))) return rc;
   if (M == 0) return LG_OK;
   if (!y || !weights || !out) return fail(LG_ERR_INVALID_ARG, "combine: NULL tensor pointer");
-  if (!aligned(y, 8) || !aligned(out, 16) || (shared && !aligned(shared, 8)))
+  if (!aligned(y, 16) || !aligned(out, 16) || (shared && !aligned(shared, 16)))
     return fail(LG_ERR_INVALID_ARG, "combine: misaligned tensor");
   const int d = cfg->hidden_size;
-  const long long n4 = M * (d / 4);
-  const int grid = static_cast<int>(n4 / 256 + 1 < 4 * num_sms() ? n4 / 256 + 1 : 4 * num_sms());
+  const long long n8 = M * (d / 8);
+  const int grid = static_cast<int>(n8 / 256 + 1 < 8 * num_sms() ? n8 / 256 + 1 : 8 * num_sms());
   lg::combine_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       y, weights, shared, static_cast<int>(M), cfg->num_experts_per_tok, d, out);
   return cuda_check(cudaGetLastError(), "combine launch");
@@ -1172,11 +1214,11 @@ int lg_moe_combine_gather(const lg_moe_config* cfg, const uint16_t* y_disp, cons
   if ((rc = validate_cfg(cfg)) || (rc = validate_tokens(M, cfg))) return rc;
   if (M == 0) return LG_OK;
   if (!y_disp || !inv || !weights || !out) return fail(LG_ERR_INVALID_ARG, "combine_gather: NULL tensor pointer");
-  if (!aligned(y_disp, 8) || !aligned(out, 16) || (shared && !aligned(shared, 8)))
+  if (!aligned(y_disp, 16) || !aligned(out, 16) || (shared && !aligned(shared, 16)))
     return fail(LG_ERR_INVALID_ARG, "combine_gather: misaligned tensor");
   const int d = cfg->hidden_size;
-  const long long n4 = M * (d / 4);
-  const int grid = static_cast<int>(n4 / 256 + 1 < 4 * num_sms() ? n4 / 256 + 1 : 4 * num_sms());
+  const long long n8 = M * (d / 8);
+  const int grid = static_cast<int>(n8 / 256 + 1 < 8 * num_sms() ? n8 / 256 + 1 : 8 * num_sms());
   lg::combine_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       y_disp, weights, shared, static_cast<int>(M), cfg->num_experts_per_tok, d, out, inv);
   return cuda_check(cudaGetLastError(), "combine_gather launch");

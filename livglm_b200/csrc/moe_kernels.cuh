@@ -525,37 +525,44 @@ grouped_gemv_kernel(GemvArgs a) {
 
 // --------------------------------------------------------------------------
 // Combine: out[t, i] = ((0 + y0*w0) + y1*w1) + ... (+ shared), products and
-// sums each rounded to f32 as in the MLX graph (bf16 * f32 -> f32).
-__global__ void __launch_bounds__(256)
+// sums each rounded to f32 as in the MLX graph (bf16 * f32 -> f32).  A thread
+// owns 8 consecutive outputs of a token (16-byte loads of each route's row).
 // rowmap (optional): y row of route slot t*k + j is rowmap[t*k + j] (rows in
-// dispatch order), else the slot itself.
+// dispatch order), else the slot itself.  d % 8 == 0.
+__global__ void __launch_bounds__(256)
 combine_kernel(const uint16_t* __restrict__ y, const float* __restrict__ w,
                const uint16_t* __restrict__ ys, int M, int k, int d, float* __restrict__ out,
                const int* __restrict__ rowmap = nullptr) {
-  const int d4 = d >> 2;
-  const long long n = static_cast<long long>(M) * d4;
+  const int d8 = d >> 3;
+  const long long n = static_cast<long long>(M) * d8;
   for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += 256LL * gridDim.x) {
-    const int t = static_cast<int>(i / d4);
-    const int c = static_cast<int>(i - static_cast<long long>(t) * d4);
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    const int t = static_cast<int>(i / d8);
+    const int c = static_cast<int>(i - static_cast<long long>(t) * d8);
+    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < k; ++j) {
-      const float wj = w[static_cast<size_t>(t) * k + j];
+      const float wj = __ldg(w + static_cast<size_t>(t) * k + j);
       const size_t slot = static_cast<size_t>(t) * k + j;
-      const size_t row = rowmap ? static_cast<size_t>(rowmap[slot]) : slot;
-      const uint2 u = *reinterpret_cast<const uint2*>(y + row * d + 4 * c);
-      s0 = __fadd_rn(s0, __fmul_rn(bf16lo(u.x), wj));
-      s1 = __fadd_rn(s1, __fmul_rn(bf16hi(u.x), wj));
-      s2 = __fadd_rn(s2, __fmul_rn(bf16lo(u.y), wj));
-      s3 = __fadd_rn(s3, __fmul_rn(bf16hi(u.y), wj));
+      const size_t row = rowmap ? static_cast<size_t>(__ldg(rowmap + slot)) : slot;
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(y + row * d) + c);
+      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        s[2 * q] = __fadd_rn(s[2 * q], __fmul_rn(bf16lo(uw[q]), wj));
+        s[2 * q + 1] = __fadd_rn(s[2 * q + 1], __fmul_rn(bf16hi(uw[q]), wj));
+      }
     }
     if (ys) {
-      const uint2 u = *reinterpret_cast<const uint2*>(ys + static_cast<size_t>(t) * d + 4 * c);
-      s0 = __fadd_rn(s0, bf16lo(u.x));
-      s1 = __fadd_rn(s1, bf16hi(u.x));
-      s2 = __fadd_rn(s2, bf16lo(u.y));
-      s3 = __fadd_rn(s3, bf16hi(u.y));
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(ys + static_cast<size_t>(t) * d) + c);
+      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        s[2 * q] = __fadd_rn(s[2 * q], bf16lo(uw[q]));
+        s[2 * q + 1] = __fadd_rn(s[2 * q + 1], bf16hi(uw[q]));
+      }
     }
-    reinterpret_cast<float4*>(out)[i] = make_float4(s0, s1, s2, s3);
+    float4* o = reinterpret_cast<float4*>(out) + 2 * i;
+    o[0] = make_float4(s[0], s[1], s[2], s[3]);
+    o[1] = make_float4(s[4], s[5], s[6], s[7]);
   }
 }
 
