@@ -68,6 +68,8 @@ def parse_args(argv=None):
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--workload", choices=tuple(WORKLOADS), default="cfg3")
     p.add_argument("--layers", type=int, default=None, help="layers cycled (single-layer workloads)")
+    p.add_argument("--ep-impl", choices=("native", "python"), default="native",
+                   help="expert parallelism through lg_moe_ep_forward (native) or the torch.distributed steps")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU baseline sample")
     a = p.parse_args(argv)
@@ -207,15 +209,18 @@ def expert_path(cfg, M: int) -> str:
     return "mxf4"
 
 
-def kernels_per_layer(M: int, path: str, ep: bool = False) -> int:
+def kernels_per_layer(M: int, path: str, ep: bool = False, native_ep: bool = False,
+                      shared_dq: bool = False) -> int:
     """Kernels of this library launched by one layer call (lg_moe_forward, or
     the expert-parallel layer's entry points)."""
     if ep:
         # router logits, select, histogram, dispatch, send-buffer pack, shared
-        # gate/up and down, then on the received rows: histogram, dispatch,
-        # route chunks, SwiGLU table, row gather, routed gate/up, routed down;
-        # finally the merge through the inverse permutation
-        return 15
+        # gate/up and down (plus its chunk and SwiGLU tables on the
+        # widened-weight kernel), then on the received rows: histogram,
+        # dispatch, route chunks, SwiGLU table, row gather, routed gate/up,
+        # routed down; finally the merge through the inverse permutation.  The
+        # C call adds the exchange-id renumbering and the count message.
+        return 15 + (2 if shared_dq else 0) + (2 if native_ep else 0)
     if M == 1:
         return 6  # router logits, select+dispatch, gate/up, activation split, tensor-core down, combine
     if path == "decode":
@@ -365,7 +370,7 @@ def timed_region(run_steps, steps: int, warmup: int, world: int, sampler=None, p
     return ms
 
 
-def build_layers(args, wl, cfg, world, rank, dev):
+def build_layers(args, wl, cfg, world, rank, dev, M_rank):
     """The workload's layers on this rank: single-GPU ExpertSSDMoE layers, or
     ExpertParallelMoE layers holding E / world local experts."""
     from livglm_b200 import synthetic, workloads
@@ -374,6 +379,11 @@ def build_layers(args, wl, cfg, world, rank, dev):
     bias = workloads.cfg4_bias(dev) if wl.get("zipf") else None
     ep = world > 1 and (wl["kind"] == "stack" or bool(wl.get("zipf")))
     layers = []
+    comm = None
+    if ep and args.ep_impl == "native":
+        from livglm_b200.ep import EpCommunicator
+
+        comm = EpCommunicator(max_tokens=M_rank)
     for i in range(args.layers):
         if ep:
             from livglm_b200.ep import ExpertParallelMoE
@@ -381,7 +391,7 @@ def build_layers(args, wl, cfg, world, rank, dev):
             per = cfg.n_routed_experts // world
             t = synthetic.layer_weights(cfg, layer=i, seed=0, device=dev, router_bias=bias, experts=per,
                                         expert_seed=1 + rank)
-            layers.append(ExpertParallelMoE(cfg, i, t))
+            layers.append(ExpertParallelMoE(cfg, i, t, comm=comm))
         else:
             t = synthetic.layer_weights(cfg, layer=i, seed=rank, device=dev, router_bias=bias)
             layers.append(build_layer(cfg, t, layer_idx=i))
@@ -405,7 +415,7 @@ def run_ours(args) -> None:
     M = wl["M"]
     if wl.get("zipf") and world > 1:
         M = wl["M"] // world  # config 4: the 16384 tokens split over the ranks
-    layers, ep = build_layers(args, wl, cfg, world, rank, dev)
+    layers, ep = build_layers(args, wl, cfg, world, rank, dev, M)
     L = len(layers)
     xs = [synthetic.hidden_states(cfg, M, seed=1000 * rank + i, device=dev) for i in range(1 if stack_kind else L)]
     torch.cuda.synchronize()
@@ -562,10 +572,13 @@ def run_ours(args) -> None:
                 "steps": K_e2e,
                 "path": "pinned host tokens -> device copy -> public module call(s) -> f32 result copied to "
                         "pinned host memory, every step"},
-        "gpu_launches": kernels_per_layer(M, path, ep) * layers_per_step * args.steps,
+        "gpu_launches": kernels_per_layer(M, path, ep, ep and args.ep_impl == "native",
+                                          M * cfg.num_experts_per_tok >= 128 * cfg.n_routed_experts)
+                        * layers_per_step * args.steps,
         "clocks": sampler.summary(),
         "extra": {"layer_ms": layer_ms,
                   "expert_path": path,
+                  "ep_impl": args.ep_impl if ep else None,
                   "layer_roofline": {"hbm_us": layer_t_hbm * 1e6, "tensor_us": layer_t_tc * 1e6,
                                      "frac": max(layer_t_hbm, layer_t_tc) / (layer_ms * 1e-3),
                                      "hbm_frac": layer_t_hbm / (layer_ms * 1e-3),

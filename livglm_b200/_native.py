@@ -14,6 +14,7 @@ from .config import ContractError, MoEConfig
 
 LIB_DIR = Path(__file__).resolve().parent / "_lib"
 LIB_PATH = LIB_DIR / "liblivglm_moe.so"
+EP_LIB_PATH = LIB_DIR / "liblivglm_moe_ep.so"
 
 LG_OK = 0
 LG_ERR_INVALID_ARG = 1
@@ -103,6 +104,17 @@ SIGNATURES = {
     "lg_moe_trace_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_float), ctypes.c_int]),
 }
 
+# every symbol include/livglm_moe_ep.h declares.
+EP_SIGNATURES = {
+    "lg_ep_unique_id_bytes": (ctypes.c_int, []),
+    "lg_ep_get_unique_id": (ctypes.c_int, [_P]),
+    "lg_ep_comm_init": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32, _I64, ctypes.POINTER(_P)]),
+    "lg_ep_comm_destroy": (ctypes.c_int, [_P]),
+    "lg_ep_last_error": (ctypes.c_char_p, []),
+    "lg_moe_ep_workspace_size": (ctypes.c_size_t, [_CFG, _I64, ctypes.c_int32]),
+    "lg_moe_ep_forward": (ctypes.c_int, [_P, _CFG, _W, _P, _I64, _P, _P, _P, _P, ctypes.c_size_t, _P]),
+}
+
 TRACE_STAGES = ("router", "dispatch", "gate_up", "down", "combine")
 
 
@@ -138,6 +150,41 @@ def load() -> ctypes.CDLL:
             fn.argtypes = args
         _lib = lib
     return _lib
+
+
+_ep_lib: ctypes.CDLL | None = None
+
+
+def load_ep() -> ctypes.CDLL:
+    """Load the expert-parallel library (liblivglm_moe_ep.so).  torch is
+    imported first so that the libnccl.so.2 torch.distributed uses is the one
+    the library binds to; the main library is loaded first so that both share
+    one instance of it."""
+    global _ep_lib
+    if _ep_lib is None:
+        import torch  # noqa: F401  (loads torch's NCCL)
+
+        load()
+        if not EP_LIB_PATH.exists():
+            raise RuntimeError(f"livglm_b200 expert-parallel library missing at {EP_LIB_PATH}; build it with "
+                               "`python -m livglm_b200.build`")
+        lib = ctypes.CDLL(str(EP_LIB_PATH))
+        for name, (res, args) in EP_SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _ep_lib = lib
+    return _ep_lib
+
+
+def ep_check(rc: int, what: str) -> None:
+    if rc == LG_OK:
+        return
+    msg = load_ep().lg_ep_last_error()
+    text = f"{what}: {ERROR_NAMES.get(rc, rc)}: {msg.decode() if msg else ''}"
+    if rc in (LG_ERR_INVALID_ARG, LG_ERR_UNSUPPORTED, LG_ERR_WORKSPACE):
+        raise ContractError(text)
+    raise RuntimeError(text)
 
 
 def last_error() -> str:

@@ -28,10 +28,16 @@ inverse permutation) come from one kernel, lg_moe_ep_pack.
 The per-route arithmetic is the single-GPU kernels' own, so the result equals
 ExpertSSDMoE on the same rows up to the batched kernels' rounding order.
 Collectives run on the caller's process group (NCCL for CUDA tensors).
+
+The same layer is one C call in liblivglm_moe_ep.so (lg_moe_ep_forward,
+include/livglm_moe_ep.h): give ExpertParallelMoE an EpCommunicator and it
+runs that call instead of the steps above (same kernels, same order, its own
+NCCL communicator and exchange stream).
 """
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import replace
 from typing import Callable
 
@@ -127,6 +133,57 @@ def exchange_routes(rows: torch.Tensor, slot_expert: torch.Tensor, perm: torch.T
     return y_back.index_select(0, inv)
 
 
+class EpCommunicator:
+    """The C library's NCCL communicator over the ranks of a torch.distributed
+    group (lg_ep_comm_init): rank 0 makes the id, the group broadcasts it.
+    max_tokens bounds the rows any rank passes to one layer call.  Call on the
+    device the layers run on (torch.cuda.set_device first)."""
+
+    def __init__(self, max_tokens: int, group=None):
+        if not dist.is_initialized():
+            raise ContractError("EpCommunicator needs an initialised torch.distributed group")
+        lib = _native.load_ep()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.max_tokens = int(max_tokens)
+        n = lib.lg_ep_unique_id_bytes()
+        uid = (ctypes.c_uint8 * n)()
+        if self.rank == 0:
+            _native.ep_check(lib.lg_ep_get_unique_id(uid), "lg_ep_get_unique_id")
+        box = [bytes(uid)]
+        src = dist.get_global_rank(group, 0) if group is not None else 0
+        dist.broadcast_object_list(box, src=src, group=group)
+        ctypes.memmove(uid, box[0], n)
+        handle = ctypes.c_void_p()
+        _native.ep_check(lib.lg_ep_comm_init(uid, self.world, self.rank, self.max_tokens, ctypes.byref(handle)),
+                         "lg_ep_comm_init")
+        self.handle = handle
+        self._ws: torch.Tensor | None = None
+
+    def workspace(self, cfg: _native.LgConfig, device) -> torch.Tensor:
+        """Scratch of lg_moe_ep_forward, shared by every layer that uses this
+        communicator (their calls are ordered on one stream), grown to the
+        largest geometry asked for.  Zero-filled: the status word starts at 0."""
+        need = _native.load_ep().lg_moe_ep_workspace_size(cfg, self.max_tokens, self.world)
+        if need == 0:
+            _native.ep_check(_native.LG_ERR_INVALID_ARG, "lg_moe_ep_workspace_size")
+        if self._ws is None or self._ws.numel() < need or self._ws.device != torch.device(device):
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=device)
+        return self._ws
+
+    def close(self) -> None:
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            _native.load_ep().lg_ep_comm_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class ExpertParallelMoE:
     """ExpertSSDMoE with its routed experts sharded over a process group.
 
@@ -134,9 +191,14 @@ class ExpertParallelMoE:
     (router_weight, router_bias, shared_*, and either the full expert banks,
     of which this rank keeps experts rank, rank + W, ..., or banks already
     holding only the E/W local experts in that order).
+
+    comm: an EpCommunicator over the same group runs the layer as one C call
+    (lg_moe_ep_forward); without one the steps run from Python over
+    torch.distributed.
     """
 
-    def __init__(self, config: MoEConfig, layer_idx: int, tensors: dict, *, group=None):
+    def __init__(self, config: MoEConfig, layer_idx: int, tensors: dict, *, group=None,
+                 comm: EpCommunicator | None = None):
         if not dist.is_initialized():
             raise ContractError("expert parallelism needs an initialised torch.distributed group")
         self.config = config
@@ -174,6 +236,45 @@ class ExpertParallelMoE:
         self._cfg = _native.LgConfig.from_config(config)
         self._ws = Workspace()
         self._xid = exchange_ids(E, self.world, self.gate.weight.device)
+        self.comm = comm
+        if comm is not None and comm.world != self.world:
+            raise ContractError("communicator and process group differ in size")
+        self._ep_ws: torch.Tensor | None = None
+        self._native_w: _native.LgWeights | None = None
+
+    def _native_weights(self) -> _native.LgWeights:
+        if self._native_w is None:
+            w = _native.LgWeights()
+            local = self.experts.native_weights()
+            for name, _ in _native.LgWeights._fields_:
+                setattr(w, name, getattr(local, name))
+            w.router_weight = self.gate.weight.data_ptr()
+            w.router_bias = self.gate.e_score_correction_bias.data_ptr()
+            if self.config.n_shared_experts > 0:
+                self.shared_experts.native_into(w)
+            self._native_w = w
+        return self._native_w
+
+    def _forward_native(self, rows: torch.Tensor):
+        """lg_moe_ep_forward: the whole layer in one C call."""
+        c, comm = self.config, self.comm
+        M, dev, k, d = rows.shape[0], rows.device, c.num_experts_per_tok, c.hidden_size
+        lib = _native.load_ep()
+        self._ep_ws = comm.workspace(self._cfg, dev)
+        out = torch.empty(M, d, dtype=torch.float32, device=dev)
+        weights = torch.empty(M, k, dtype=torch.float32, device=dev)
+        indices = torch.empty(M, k, dtype=torch.uint32, device=dev)
+        _native.ep_check(lib.lg_moe_ep_forward(comm.handle, self._cfg, self._native_weights(), rows.data_ptr(), M,
+                                               out.data_ptr(), weights.data_ptr(), indices.data_ptr(),
+                                               self._ep_ws.data_ptr(), self._ep_ws.numel(), _stream_ptr(dev)),
+                         "lg_moe_ep_forward")
+        return out, weights, indices
+
+    def status(self) -> int:
+        """Device status word of the C call's workspace (0 = ok)."""
+        if self._ep_ws is None:
+            return self._ws.status()
+        return int(self._ep_ws[:4].view(torch.int32).item())
 
     def use_workspace(self, ws: Workspace) -> None:
         """Share one scratch area with other layers run in order on one stream
@@ -192,6 +293,10 @@ class ExpertParallelMoE:
         """Local bf16 rows [..., d] -> f32 [..., d], as ExpertSSDMoE.__call__."""
         c = self.config
         rows = _rows_bf16(hidden_states, c.hidden_size)
+        if self.comm is not None:
+            out, weights, indices = self._forward_native(rows)
+            result = out.reshape(*hidden_states.shape[:-1], c.hidden_size)
+            return (result, weights, indices) if return_route else result
         M, dev, k, E, d = rows.shape[0], rows.device, c.num_experts_per_tok, c.n_routed_experts, c.hidden_size
         lib = _native.load()
         stream = _stream_ptr(dev)

@@ -11,8 +11,8 @@ from livglm_b200.config import CONFIGS, ContractError, MoEConfig
 from tests.conftest import ROOT
 
 
-def declared_symbols() -> set[str]:
-    text = "\n".join(p.read_text() for p in (ROOT / "include").glob("*.h"))
+def declared_symbols(header: str = "livglm_moe.h") -> set[str]:
+    text = (ROOT / "include" / header).read_text()
     return set(re.findall(r"\b(lg_\w+)\s*\(", text))
 
 
@@ -21,8 +21,41 @@ def test_library_exports_every_declared_symbol(native_lib):
     assert "lg_moe_forward" in names
     for name in names:
         assert hasattr(native_lib, name), name
-    assert names <= set(_native.SIGNATURES), names - set(_native.SIGNATURES)
+    assert names == set(_native.SIGNATURES), names ^ set(_native.SIGNATURES)
     assert native_lib.lg_moe_abi_version() == 1
+
+
+def test_ep_library_exports_every_declared_symbol(native_lib):
+    headers = sorted(p.name for p in (ROOT / "include").glob("*.h"))
+    assert headers == ["livglm_moe.h", "livglm_moe_ep.h"], headers
+    ep = _native.load_ep()
+    names = declared_symbols("livglm_moe_ep.h")
+    assert "lg_moe_ep_forward" in names
+    for name in names:
+        assert hasattr(ep, name), name
+    assert names == set(_native.EP_SIGNATURES), names ^ set(_native.EP_SIGNATURES)
+    assert ep.lg_ep_unique_id_bytes() == 128
+
+
+def test_ep_workspace_and_argument_checks(native_lib):
+    ep = _native.load_ep()
+    c = cfg_of()  # 128 experts
+    one = native_lib.lg_moe_workspace_size(c, 64)
+    s2 = ep.lg_moe_ep_workspace_size(c, 64, 2)
+    s4 = ep.lg_moe_ep_workspace_size(c, 64, 4)
+    assert s2 > one and s4 > s2 and s4 % 256 == 0  # receive side grows with the ranks
+    assert ep.lg_moe_ep_workspace_size(c, 64, 3) == 0  # 128 experts do not split over 3 ranks
+    assert "world" in ep.lg_ep_last_error().decode()
+    assert ep.lg_moe_ep_workspace_size(c, 0, 2) == 0
+    rc = ep.lg_moe_ep_forward(None, c, None, None, 0, None, None, None, None, 0, None)
+    assert rc == _native.LG_ERR_INVALID_ARG
+    assert "communicator" in ep.lg_ep_last_error().decode()
+    handle = ctypes.c_void_p()
+    uid = (ctypes.c_uint8 * 128)()
+    assert ep.lg_ep_comm_init(uid, 2, 2, 64, ctypes.byref(handle)) == _native.LG_ERR_INVALID_ARG
+    assert ep.lg_ep_comm_init(uid, 2, 0, 0, ctypes.byref(handle)) == _native.LG_ERR_INVALID_ARG
+    assert not handle.value
+    assert ep.lg_ep_comm_destroy(None) == _native.LG_OK
 
 
 def cfg_of(**kw):
