@@ -46,6 +46,9 @@ WORKLOADS = {
     "prefill256": {"cfg": "cfg2", "M": 256, "layers": 8, "kind": "layer", "steps": 200},
     "decode1": {"cfg": "cfg1", "M": 1, "layers": 8, "kind": "layer", "steps": 4000},
     "decode2": {"cfg": "cfg1", "M": 2, "layers": 8, "kind": "layer", "steps": 4000},
+    # the MTP width-two verify at its call site: hyper-connections (4 streams)
+    # around the block, model.py:132-136
+    "site2": {"cfg": "cfg1", "M": 2, "layers": 8, "kind": "layer", "steps": 4000, "site": 4},
 }
 CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -394,7 +397,15 @@ def build_layers(args, wl, cfg, world, rank, dev, M_rank):
             layers.append(ExpertParallelMoE(cfg, i, t, comm=comm))
         else:
             t = synthetic.layer_weights(cfg, layer=i, seed=rank, device=dev, router_bias=bias)
-            layers.append(build_layer(cfg, t, layer_idx=i))
+            layer = build_layer(cfg, t, layer_idx=i)
+            if wl.get("site"):
+                from livglm_b200.ffn_site import HcConfig, HyperConnection, MoEFFNSite
+
+                sw = synthetic.ffn_site_weights(cfg, wl["site"], layer=i, seed=rank, device=dev)
+                hc = HyperConnection(HcConfig(hc_mult=wl["site"]), cfg.hidden_size)
+                hc.fn, hc.base, hc.scale = sw["fn"], sw["base"], sw["scale"]
+                layer = MoEFFNSite(layer, hc, sw["norm_weight"])
+            layers.append(layer)
         del t
     return layers, ep
 
@@ -417,7 +428,11 @@ def run_ours(args) -> None:
         M = wl["M"] // world  # config 4: the 16384 tokens split over the ranks
     layers, ep = build_layers(args, wl, cfg, world, rank, dev, M)
     L = len(layers)
-    xs = [synthetic.hidden_states(cfg, M, seed=1000 * rank + i, device=dev) for i in range(1 if stack_kind else L)]
+    if wl.get("site"):
+        xs = [synthetic.streams(cfg, M, wl["site"], seed=1000 * rank + i, device=dev) for i in range(L)]
+    else:
+        xs = [synthetic.hidden_states(cfg, M, seed=1000 * rank + i, device=dev)
+              for i in range(1 if stack_kind else L)]
     torch.cuda.synchronize()
 
     # routing statistics of one call (distinct experts, load per expert)
@@ -479,9 +494,9 @@ def run_ours(args) -> None:
         stage = {k: statistics.fmean(s_[k] for s_ in st) for k in _native.TRACE_STAGES}
 
     # ---- e2e: the public call with the tokens and the result on the host ----
-    x_host = torch.empty(M, cfg.hidden_size, dtype=torch.bfloat16, pin_memory=True)
+    x_host = torch.empty(xs[0].shape, dtype=torch.bfloat16, pin_memory=True)
     x_host.copy_(xs[0].cpu())
-    out_host = torch.empty(M, cfg.hidden_size, dtype=torch.float32, pin_memory=True)
+    out_host = torch.empty(xs[0].shape, dtype=torch.float32, pin_memory=True)
     x_dev = torch.empty_like(xs[0])
     K_e2e = max(1, min(args.steps, 2000))
 
@@ -543,7 +558,9 @@ def run_ours(args) -> None:
     layer_t_tc = work["flops"]["layer"] / (tc_peak["tflops"] * 1e12)
     workload_name = {"cfg3": f"cfg3: {L} stacked layers, M={M} per rank",
                      "cfg4": f"cfg4: Zipf(1.2) bias, M={M} per rank",
-                     "prefill256": "cfg2: M=256", "decode1": "cfg1: M=1", "decode2": "cfg1: M=2 (MTP verify)"}
+                     "prefill256": "cfg2: M=256", "decode1": "cfg1: M=1", "decode2": "cfg1: M=2 (MTP verify)",
+                     "site2": "cfg1: M=2 (MTP verify) at the FFN site: hyper-connections of 4 bf16 streams, "
+                              "RMSNorm, MoE block, hyper-residual (model.py:132-136)"}
     routed_gb = L * work["per_expert_bytes"] * cfg.n_routed_experts / world / 1e9
     line = {
         "metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -568,12 +585,13 @@ def run_ours(args) -> None:
                      "algorithmic_bytes_per_launch": dom_bytes, "algorithmic_flops_per_launch": dom_flops,
                      "launch_ms": dom_ms},
         "e2e": {"value": world * M * layers_per_step * K_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
-                "h2d_bytes_per_step": M * cfg.hidden_size * 2, "d2h_bytes_per_step": M * cfg.hidden_size * 4,
+                "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 4,
                 "steps": K_e2e,
                 "path": "pinned host tokens -> device copy -> public module call(s) -> f32 result copied to "
                         "pinned host memory, every step"},
-        "gpu_launches": kernels_per_layer(M, path, ep, ep and args.ep_impl == "native",
-                                          M * cfg.num_experts_per_tok >= 128 * cfg.n_routed_experts)
+        "gpu_launches": (kernels_per_layer(M, path, ep, ep and args.ep_impl == "native",
+                                           M * cfg.num_experts_per_tok >= 128 * cfg.n_routed_experts)
+                         + (3 if wl.get("site") else 0))  # hyper-connection mix, finish, residual
                         * layers_per_step * args.steps,
         "clocks": sampler.summary(),
         "extra": {"layer_ms": layer_ms,

@@ -286,6 +286,59 @@ int lg_moe_trace_enable(int capacity_calls);
  * the number of calls copied, or a negative LG_ERR_* code. */
 int lg_moe_trace_read(float *stage_ms /* host */, int max_calls);
 
+/*
+ * FFN site of a MoE decoder layer with manifold-constrained hyper-connections
+ * (kg36/livglm src/glm53flash/model.py:132-136; the width-two MTP verify,
+ * runtime.py:657-661, calls it with two tokens):
+ *   post, comb, collapsed = ffn_hc(streams)          (HyperConnection, mhc.py:23-48)
+ *   x   = post_attention_layernorm(collapsed)        (RMSNorm, layers.py:119-131)
+ *   out = hyper_residual(streams, moe(x), post, comb) (mhc.py:51-60)
+ * streams: bf16 [M, hc, d], the hc residual streams of M tokens.  Rounding
+ * points are MLX's for bf16 streams: the mix and gates in f32, collapsed
+ * cast to bf16, rms_norm's normalised value rounded to bf16 before and after
+ * the weight, bf16(post) * moe(x) in f32 plus the bf16 matmul comb^T @ streams.
+ */
+typedef struct lg_hc_config {
+  int32_t hc_mult;        /* streams per token, 1..4 (GLMTextConfig.hc_mult) */
+  int32_t sinkhorn_iters; /* hc_sinkhorn_iters, >= 1 */
+  float hc_eps;
+  float rms_norm_eps;
+} lg_hc_config;
+
+typedef struct lg_hc_weights {
+  const float *fn;             /* layers.{L}.hc_ffn_fn    f32 [hc*(hc+2), hc*d] */
+  const float *base;           /* layers.{L}.hc_ffn_base  f32 [hc*(hc+2)] */
+  const float *scale;          /* layers.{L}.hc_ffn_scale f32 [3] */
+  const uint16_t *norm_weight; /* layers.{L}.post_attention_layernorm.weight bf16 [d] */
+} lg_hc_weights;
+
+/* Scratch of lg_hc_pre for up to max_tokens tokens (0 on error). */
+size_t lg_hc_workspace_size(const lg_hc_config *hc /* host */, int32_t d, int64_t max_tokens);
+
+/* HyperConnection.__call__ (mhc.py:23-48) and, when x_norm is not NULL,
+ * the post-attention RMSNorm of its collapsed output (layers.py:126-131).
+ *   post f32 [M, hc]; comb f32 [M, hc, hc]; collapsed bf16 [M, d] (may be
+ *   NULL); x_norm bf16 [M, d] (may be NULL; needs w->norm_weight). */
+int lg_hc_pre(const lg_hc_config *hc, const lg_hc_weights *w, int32_t d, const uint16_t *streams, int64_t M,
+              float *post, float *comb, uint16_t *collapsed, uint16_t *x_norm, void *workspace,
+              size_t workspace_bytes, void *stream);
+
+/* hyper_residual (mhc.py:51-60): residual bf16 [M, hc, d], sublayer f32
+ * [M, d] (the MoE output), post / comb from lg_hc_pre -> out f32 [M, hc, d]. */
+int lg_hc_post(const lg_hc_config *hc, int32_t d, const uint16_t *residual, const float *sublayer,
+               const float *post, const float *comb, int64_t M, float *out, void *stream);
+
+/* Workspace of lg_moe_ffn_site (its first 4 bytes are the MoE status word). */
+size_t lg_moe_ffn_site_workspace_size(const lg_moe_config *cfg /* host */, const lg_hc_config *hc /* host */,
+                                      int64_t max_tokens);
+
+/* The whole FFN site: lg_hc_pre, lg_moe_forward on the normalised collapsed
+ * rows, lg_hc_post.  out f32 [M, hc, d]; weights_out / indices_out as in
+ * lg_moe_forward. */
+int lg_moe_ffn_site(const lg_moe_config *cfg, const lg_moe_weights *w, const lg_hc_config *hc,
+                    const lg_hc_weights *hw, const uint16_t *streams, int64_t M, float *out, float *weights_out,
+                    uint32_t *indices_out, void *workspace, size_t workspace_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,6 +56,24 @@ class LgConfig(ctypes.Structure):
                    float(c.swiglu_limit))
 
 
+class LgHcConfig(ctypes.Structure):
+    _fields_ = [
+        ("hc_mult", ctypes.c_int32),
+        ("sinkhorn_iters", ctypes.c_int32),
+        ("hc_eps", ctypes.c_float),
+        ("rms_norm_eps", ctypes.c_float),
+    ]
+
+
+class LgHcWeights(ctypes.Structure):
+    _fields_ = [
+        ("fn", ctypes.c_void_p),
+        ("base", ctypes.c_void_p),
+        ("scale", ctypes.c_void_p),
+        ("norm_weight", ctypes.c_void_p),
+    ]
+
+
 class LgWeights(ctypes.Structure):
     _fields_ = [
         ("router_weight", ctypes.c_void_p),
@@ -83,6 +101,8 @@ _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _CFG = ctypes.POINTER(LgConfig)
 _W = ctypes.POINTER(LgWeights)
+_HC = ctypes.POINTER(LgHcConfig)
+_HW = ctypes.POINTER(LgHcWeights)
 SIGNATURES = {
     "lg_moe_abi_version": (ctypes.c_int, []),
     "lg_moe_last_error": (ctypes.c_char_p, []),
@@ -101,6 +121,11 @@ SIGNATURES = {
     "lg_moe_static_scratch_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int32), _P]),
     "lg_moe_check_wait_timeout": (ctypes.c_int, [_I64, _P, _P]),
     "lg_moe_trace_enable": (ctypes.c_int, [ctypes.c_int]),
+    "lg_hc_workspace_size": (ctypes.c_size_t, [_HC, ctypes.c_int32, _I64]),
+    "lg_hc_pre": (ctypes.c_int, [_HC, _HW, ctypes.c_int32, _P, _I64, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
+    "lg_hc_post": (ctypes.c_int, [_HC, ctypes.c_int32, _P, _P, _P, _P, _I64, _P, _P]),
+    "lg_moe_ffn_site_workspace_size": (ctypes.c_size_t, [_CFG, _HC, _I64]),
+    "lg_moe_ffn_site": (ctypes.c_int, [_CFG, _W, _HC, _HW, _P, _I64, _P, _P, _P, _P, ctypes.c_size_t, _P]),
     "lg_moe_trace_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_float), ctypes.c_int]),
 }
 

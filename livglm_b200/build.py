@@ -22,7 +22,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OUT = PKG / "_lib" / "liblivglm_moe.so"
-SOURCES = ["moe_capi.cu", "moe_noalloc.cu"]
+SOURCES = ["moe_capi.cu", "moe_noalloc.cu", "ffn_site.cu"]
 EP_OUT = PKG / "_lib" / "liblivglm_moe_ep.so"
 EP_SOURCES = ["moe_ep.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -19,6 +19,7 @@ from .mxfp4 import quantize_mxfp4
 _TENSOR_IDS = {
     "hidden": 1, "router_weight": 2, "router_bias": 3, "gate": 4, "up": 5, "down": 6,
     "shared_gate": 7, "shared_up": 8, "shared_down": 9,
+    "streams": 10, "hc_fn": 11, "hc_base": 12, "norm_weight": 13,
 }
 
 
@@ -31,6 +32,27 @@ def _gen(device, seed: int, layer: int, name: str) -> torch.Generator:
 def hidden_states(cfg: MoEConfig, tokens: int, *, seed: int = 0, device="cuda") -> torch.Tensor:
     g = _gen(device, seed, 0, "hidden")
     return torch.randn(tokens, cfg.hidden_size, generator=g, device=device).to(torch.bfloat16)
+
+
+def streams(cfg: MoEConfig, tokens: int, hc_mult: int, *, seed: int = 0, device="cuda") -> torch.Tensor:
+    """Hyper-connection residual streams: bf16 N(0,1) [tokens, hc_mult, d]."""
+    g = _gen(device, seed, 0, "streams")
+    return torch.randn(tokens, hc_mult, cfg.hidden_size, generator=g, device=device).to(torch.bfloat16)
+
+
+def ffn_site_weights(cfg: MoEConfig, hc_mult: int, *, layer: int = 0, seed: int = 0, device="cuda") -> dict:
+    """The FFN site's hyper-connection and norm tensors (no checkpoint values
+    are reachable): fn f32 N(0, 1/(hc*d)) so the mixed logits are O(1) on
+    RMS-normalised streams, base f32 U(-0.2, 0.2), scale (0.5, 0.75, 1.25),
+    post-attention norm weight bf16 1 + N(0, 0.1)."""
+    d, R = cfg.hidden_size, hc_mult * (hc_mult + 2)
+    K = hc_mult * d
+    fn = torch.randn(R, K, generator=_gen(device, seed, layer, "hc_fn"), device=device) / K ** 0.5
+    base = torch.rand(R, generator=_gen(device, seed, layer, "hc_base"), device=device) * 0.4 - 0.2
+    norm = 1 + 0.1 * torch.randn(d, generator=_gen(device, seed, layer, "norm_weight"), device=device)
+    return {"fn": fn.contiguous(), "base": base.contiguous(),
+            "scale": torch.tensor([0.5, 0.75, 1.25], dtype=torch.float32, device=device),
+            "norm_weight": norm.to(torch.bfloat16).contiguous()}
 
 
 def layer_weights(cfg: MoEConfig, *, layer: int = 0, seed: int = 0, device="cuda",
