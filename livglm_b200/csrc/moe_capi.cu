@@ -136,6 +136,14 @@ bool tc_batched_env() {
   }();
   return on;
 }
+// LIVGLM_ROUTER_PIPE=0: large batches use the register-prefetch router kernel
+bool router_pipe_env() {
+  static const bool on = [] {
+    const char* v = std::getenv("LIVGLM_ROUTER_PIPE");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 Layout layout(const lg_moe_config* c, int64_t M) {
   const size_t E = c->n_routed_experts, k = c->num_experts_per_tok, d = c->hidden_size;
@@ -236,6 +244,15 @@ int launch_router(const lg_moe_config* c, const uint16_t* x, int M, const float*
   if (M <= 4) {
     dim3 grid((M + 0) / 1, (E + 7) / 8);
     router_logits_kernel<1, 1><<<grid, 256, 0, s>>>(x, Wr, M, d, E, logits);
+  } else if (d % 256 == 0 && M >= 1024 && router_pipe_env()) {
+    // 32 tokens x 16 experts per block, operands through a 3-stage cp.async ring
+    constexpr int kTW = 4, kST = 3;
+    const size_t smem = static_cast<size_t>(kST) * (8 * kTW * 512 + kRlExperts * 1024);
+    auto kern = router_logits_pipe_kernel<kTW, kRlExperts, kST>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_check(e, "router smem attribute");
+    dim3 grid((M + 8 * kTW - 1) / (8 * kTW), (E + kRlExperts - 1) / kRlExperts);
+    kern<<<grid, 256, smem, s>>>(x, Wr, M, d, E, logits);
   } else if (d % 256 == 0 && M >= 8192) {  // 64 tokens x 16 experts per block: fewer re-reads of W_r
     dim3 grid((M + 63) / 64, (E + kRlExperts - 1) / kRlExperts);
     router_logits_tiled_kernel<8><<<grid, 256, 0, s>>>(x, Wr, M, d, E, logits);

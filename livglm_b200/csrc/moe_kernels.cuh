@@ -179,6 +179,109 @@ router_logits_tiled_kernel(const uint16_t* __restrict__ x, const float* __restri
 }
 
 // --------------------------------------------------------------------------
+// router_logits_tiled_kernel's arithmetic (same lanes, chunks, fma order and
+// butterfly, so the logits are bit-identical) with the operands streamed into
+// an ST-stage shared-memory ring by cp.async instead of through registers:
+// no prefetch registers and no load latency between the k-block barriers, so
+// two CTAs fit per SM.  Stage layout: x [TB][32] uint4, then W_r as
+// [expert][half][lane] float4.  d must be a multiple of 256; x and W_r 16-byte
+// aligned.
+template <int TW, int EW, int ST>
+__global__ void __launch_bounds__(256, 2)
+router_logits_pipe_kernel(const uint16_t* __restrict__ x, const float* __restrict__ W,
+                          int M, int d, int E, float* __restrict__ logits) {
+  constexpr int TB = 8 * TW;
+  constexpr int XB = TB * 512;           // x bytes per stage
+  constexpr int SB = XB + EW * 1024;     // stage bytes
+  extern __shared__ __align__(16) unsigned char rl_smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * TB, e0 = blockIdx.y * EW;
+  const int nk = d / 256;
+  auto issue = [&](int kb, int st) {
+    const int k0 = kb * 256;
+    unsigned char* base = rl_smem + st * SB;
+#pragma unroll
+    for (int u = 0; u < (TB * 32 + 255) / 256; ++u) {
+      const int i = threadIdx.x + 256 * u;
+      if (i < TB * 32) {
+        const int r = i >> 5, c = i & 31, t = t0 + r;
+        const uint16_t* src = x + static_cast<size_t>(t < M ? t : 0) * d + k0 + 8 * c;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(base + 16 * i)), "l"(src),
+                     "r"(t < M ? 16 : 0)
+                     : "memory");
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < (EW * 64 + 255) / 256; ++u) {
+      const int i = threadIdx.x + 256 * u;
+      if (i < EW * 64) {
+        const int r = i >> 6, c = i & 63, e = e0 + r;
+        const float* src = W + static_cast<size_t>(e < E ? e : 0) * d + k0 + 4 * c;
+        const int slot = r * 64 + (i & 1) * 32 + ((i & 63) >> 1);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(base + XB + 16 * slot)),
+                     "l"(src), "r"(e < E ? 16 : 0)
+                     : "memory");
+      }
+    }
+  };
+  float acc[TW][EW];
+#pragma unroll
+  for (int a = 0; a < TW; ++a)
+#pragma unroll
+    for (int b = 0; b < EW; ++b) acc[a][b] = 0.0f;
+#pragma unroll
+  for (int st = 0; st < ST - 1; ++st) {
+    if (st < nk) issue(st, st);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  for (int kb = 0; kb < nk; ++kb) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(ST - 2) : "memory");
+    __syncthreads();  // k-block kb is in place; every warp is done with kb - 1
+    if (kb + ST - 1 < nk) issue(kb + ST - 1, (kb + ST - 1) % ST);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const unsigned char* base = rl_smem + (kb % ST) * SB;
+    const uint4* xs = reinterpret_cast<const uint4*>(base);
+    const float4* ws = reinterpret_cast<const float4*>(base + XB);
+    // lane l: chunk c = kb * 32 + l (elements 8 l .. 8 l + 7 of this k-block)
+    float xv[TW][8];
+#pragma unroll
+    for (int a = 0; a < TW; ++a) {
+      const uint4 u = xs[(warp * TW + a) * 32 + lane];
+      xv[a][0] = bf16lo(u.x); xv[a][1] = bf16hi(u.x);
+      xv[a][2] = bf16lo(u.y); xv[a][3] = bf16hi(u.y);
+      xv[a][4] = bf16lo(u.z); xv[a][5] = bf16hi(u.z);
+      xv[a][6] = bf16lo(u.w); xv[a][7] = bf16hi(u.w);
+    }
+#pragma unroll
+    for (int b = 0; b < EW; ++b) {
+      const float4 w0 = ws[b * 64 + lane];
+      const float4 w1 = ws[b * 64 + 32 + lane];
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int a = 0; a < TW; ++a)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[a][b] = __fmaf_rn(xv[a][q], wv[q], acc[a][b]);
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+    for (int a = 0; a < TW; ++a)
+#pragma unroll
+      for (int b = 0; b < EW; ++b)
+        acc[a][b] = __fadd_rn(acc[a][b], __shfl_xor_sync(0xffffffffu, acc[a][b], off));
+#pragma unroll
+  for (int a = 0; a < TW; ++a) {
+    const int t = t0 + warp * TW + a;
+    float v = 0.f;
+#pragma unroll
+    for (int b = 0; b < EW; ++b) v = lane == b ? acc[a][b] : v;
+    if (t < M && lane < EW && e0 + lane < E) logits[static_cast<size_t>(t) * E + e0 + lane] = v;
+  }
+}
+
+// --------------------------------------------------------------------------
 // Router selection: one warp per token.  E <= 1024 (32 experts per lane).
 // Shared memory per warp: scores[E], choice[E], gscore[G].
 constexpr int kSelectWarps = 4;

@@ -74,7 +74,7 @@ def test_golden_cfg0_expert_and_shared_entry_points(cuda, native_lib, golden_cfg
 
 # -------------------------------------------------------------- routing ---
 
-@pytest.mark.parametrize("M", [1, 2, 3, 256, 1031])
+@pytest.mark.parametrize("M", [1, 2, 3, 256, 1031, 4096])
 def test_router_bit_exact_cfg1(cfg1_layer, cuda, M):
     cfg, t, tn = cfg1_layer
     x = synthetic.hidden_states(cfg, M, seed=M, device=cuda)
