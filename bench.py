@@ -42,7 +42,7 @@ sys.path.insert(0, str(ROOT))
 
 WORKLOADS = {
     "cfg3": {"cfg": "cfg3", "M": 4096, "layers": 42, "kind": "stack", "steps": 10},
-    "cfg4": {"cfg": "cfg4", "M": 16384, "layers": 2, "kind": "layer", "steps": 20, "zipf": True},
+    "cfg4": {"cfg": "cfg4", "M": 16384, "layers": 2, "kind": "layer", "steps": 200, "zipf": True},
     "prefill256": {"cfg": "cfg2", "M": 256, "layers": 8, "kind": "layer", "steps": 200},
     "decode1": {"cfg": "cfg1", "M": 1, "layers": 8, "kind": "layer", "steps": 4000},
     "decode2": {"cfg": "cfg1", "M": 2, "layers": 8, "kind": "layer", "steps": 4000},
