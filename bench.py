@@ -58,8 +58,8 @@ CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.a
 # kernel, from an ncu capture of this bench's command (workload -> bytes)
 MEASURED_TRAFFIC = {
     "decode1": 80.53e6,
-    # gate/up stage of one layer: route gather 287 MB + routed gate/up 1,227 MB + shared gate/up 60 MB
-    "cfg3": 1.574e9,
+    # gate/up stage of one layer: route gather 291 MB + routed gate/up 1,221 MB + shared gate/up 61 MB
+    "cfg3": 1.572e9,
 }
 
 
