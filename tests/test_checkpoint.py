@@ -1,6 +1,9 @@
 """Checkpoint reading on the CPU: the safetensors reader against files
-written by tests/st_writer.py, its refusal of malformed files, and the
-oracle's E4M3FN decoding against ml_dtypes."""
+written by tests/st_writer.py, its refusal of malformed files, the oracle's
+E4M3FN decoding against ml_dtypes, and the oracle's block-FP8 and resident
+MXFP8 / MXFP4 transforms against the known answers and bounds of the
+reference's own tests (kg36/livglm tests/test_fp8.py,
+tests/test_resident_mxfp8.py)."""
 
 import json
 
@@ -99,3 +102,53 @@ def test_mx_requantize_oracle_properties():
     assert np.all(q8[3, 32:64] == 0)
     rel = np.abs(q8 - mo.bf16_bits_to_f32(wb)) / np.abs(mo.bf16_bits_to_f32(wb)).reshape(48, 8, 32).max(-1).repeat(32, 1)
     assert np.nanmax(rel) <= 0.125 + 1e-6  # 3-bit mantissa, and the OCP rule may clamp a group max into 448
+
+
+# ------------------------------------------- the reference's known answers ---
+
+def test_e4m3fn_reference_known_values():
+    """kg36/livglm tests/test_fp8.py:8-12."""
+    codes = np.array([0x00, 0x01, 0x38, 0x3C, 0x7E, 0xB8], np.uint8)
+    np.testing.assert_array_equal(mo.e4m3fn_to_f32(codes),
+                                  np.array([0.0, 2.0 ** -9, 1.0, 1.5, 448.0, -1.0], np.float32))
+
+
+def test_block_fp8_reference_scale_and_quadrants():
+    """kg36/livglm tests/test_fp8.py:15-29: one block times 2.5; a 2 x 2 scale
+    grid maps onto the matrix quadrants."""
+    one = np.full((128, 128), 0x38, np.uint8)
+    got = mo.bf16_bits_to_f32(mo.fp8_block_dequant_bf16(one, np.array([[2.5]], np.float32)))
+    np.testing.assert_array_equal(got, np.full((128, 128), 2.5, np.float32))
+    four = np.full((256, 256), 0x38, np.uint8)
+    got = mo.bf16_bits_to_f32(mo.fp8_block_dequant_bf16(four, np.array([[1.0, 2.0], [3.0, 4.0]], np.float32)))
+    assert np.all(got[:128, :128] == 1.0) and np.all(got[:128, 128:] == 2.0)
+    assert np.all(got[128:, :128] == 3.0) and np.all(got[128:, 128:] == 4.0)
+
+
+def test_block_fp8_reference_non_finite_code():
+    """kg36/livglm tests/test_fp8.py:32-36: code 0x7F is NaN (the GPU widening
+    refuses it, tests/test_gpu_checkpoint.py)."""
+    assert np.isnan(mo.e4m3fn_to_f32(np.array([0x7F, 0xFF], np.uint8))).all()
+    got = mo.bf16_bits_to_f32(mo.fp8_block_dequant_bf16(np.full((128, 128), 0x7F, np.uint8),
+                                                        np.array([[1.0]], np.float32)))
+    assert np.isnan(got).all()
+
+
+@pytest.mark.parametrize("bits,seed,rtol,atol", [(8, 5308, 0.03, 0.015), (4, 5304, 0.20, 0.04)])
+def test_resident_mx_reference_closeness(bits, seed, rtol, atol):
+    """kg36/livglm tests/test_resident_mxfp8.py: a 64 x 32 bf16 linear of N(0,
+    0.05) weights on two N(0, 0.2) rows stays within the reference test's
+    tolerance after resident MXFP8 (rtol 0.03, atol 0.015) / MXFP4 (0.20,
+    0.04) quantisation (the byte counts it also checks are checked on the GPU
+    module, tests/test_gpu_checkpoint.py)."""
+    rng = np.random.default_rng(seed)
+    w = mo.f32_to_bf16_bits(rng.normal(0, 0.05, (64, 32)).astype(np.float32))
+    x = mo.f32_to_bf16_bits(rng.normal(0, 0.2, (2, 32)).astype(np.float32))
+
+    def linear(wb):  # bf16 x @ W^T with f32 sums, rounded to bf16
+        return mo.round_bf16((mo.bf16_bits_to_f32(x).astype(np.float64) @ mo.bf16_bits_to_f32(wb).T
+                              .astype(np.float64)).astype(np.float32))
+
+    expected = linear(w)
+    actual = linear(mo.mx_requantize_bf16(w, bits))
+    np.testing.assert_allclose(actual, expected, rtol=rtol, atol=atol)

@@ -25,6 +25,20 @@ def test_fp8_widening_bit_exact(cuda, native_lib):
     np.testing.assert_array_equal(to_numpy(got), mo.fp8_block_dequant_bf16(w, s))
 
 
+def test_fp8_widening_reference_known_answers(cuda, native_lib):
+    """kg36/livglm tests/test_fp8.py:15-29 on the GPU: code 0x38 (1.0) times a
+    block scale of 2.5, and a 2 x 2 scale grid over four 128 x 128 quadrants."""
+    one = torch.full((128, 128), 0x38, dtype=torch.uint8, device=cuda).view(torch.float8_e4m3fn)
+    got = widen_block_fp8(one, torch.tensor([[2.5]], device=cuda))
+    four = torch.full((256, 256), 0x38, dtype=torch.uint8, device=cuda).view(torch.float8_e4m3fn)
+    quad = widen_block_fp8(four, torch.tensor([[1.0, 2.0], [3.0, 4.0]], device=cuda))
+    torch.cuda.synchronize()
+    assert torch.all(got.float() == 2.5)
+    q = quad.float().cpu()
+    assert torch.all(q[:128, :128] == 1.0) and torch.all(q[:128, 128:] == 2.0)
+    assert torch.all(q[128:, :128] == 3.0) and torch.all(q[128:, 128:] == 4.0)
+
+
 def test_fp8_widening_refuses_nan(cuda, native_lib):
     rng = np.random.default_rng(4)
     w, s = cf.fp8_weight(rng, 128, 128)
@@ -75,6 +89,10 @@ def test_layer_with_mxfp8_shared_expert(cuda, native_lib, golden_cfg0):
     moe = build_layer(cfg, bank_to_device(golden_cfg0, cuda))
     info = moe.quantize_resident_linears_mxfp(8)
     assert info["linears"] == 3 and info["destination_bytes"] < info["source_bytes"]
+    # per linear: 2 bytes per bf16 value before, one E4M3 byte per value and
+    # one scale byte per 32 after (kg36/livglm tests/test_resident_mxfp8.py:21-22)
+    n = 3 * cfg.hidden_size * cfg.shared_intermediate_size
+    assert (info["source_bytes"], info["destination_bytes"]) == (2 * n, n + n // 32)
     bank = dict(golden_cfg0)
     for name in ("gate", "up", "down"):
         bank[f"shared_{name}"] = mo.mx_requantize_bf16(golden_cfg0[f"shared_{name}"], 8)
