@@ -116,12 +116,12 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
 }
 
 // The shared expert's one-"expert" tables: offsets {0, M}, chunk_start {0, ceil(M / 256)}.
-__global__ void shared_table_kernel(int M, int* __restrict__ tab) {
+__global__ void shared_table_kernel(int M, int nch, int* __restrict__ tab) {
   if (threadIdx.x == 0) {
     tab[0] = 0;
     tab[1] = M;
     tab[2] = 0;
-    tab[3] = (M + kNMax - 1) / kNMax;
+    tab[3] = nch;
   }
 }
 

@@ -499,9 +499,31 @@ int launch_routed_dq(const lg_moe_config* c, const lg_moe_weights* w, const uint
   return launch_dq<false>(q, chunks_max * q.rb_count, A0, A0, B, s);
 }
 
+// Token chunks of the shared expert on the widened-weight kernel: every chunk
+// makes rb_count work items for `grid` CTAs, so the chunk width that costs
+// the fewest rounds x MMA cycles wins (118 cycles per M = 128 MMA up to
+// N = 160, rising to 166 at N = 256, measured), larger chunks on a tie.  The
+// chunk count returned is ceil(M / width), so that no chunk is empty.
+int shared_chunks(int M, int rb_count, int grid) {
+  int best_n = (M + lg::gdq::kNMax - 1) / lg::gdq::kNMax;
+  double best = 1e300;
+  for (int c = lg::gdq::kNMax; c >= 128; c -= lg::gdq::kBoxRows) {
+    const int n = (M + c - 1) / c;
+    const int width = ((M + n - 1) / n + lg::gdq::kBoxRows - 1) / lg::gdq::kBoxRows * lg::gdq::kBoxRows;
+    const long long rounds = (static_cast<long long>(n) * rb_count + grid - 1) / grid;
+    const double cost = static_cast<double>(rounds) * (width <= 160 ? 118.0 : 118.0 + 0.5 * (width - 160));
+    if (cost < best - 1e-9) {
+      best = cost;
+      best_n = n;
+    }
+  }
+  return best_n;
+}
+
 // The shared expert of a large batch on the same kernel (kBf16A): its bf16
 // weight rows TMA-loaded as the A tiles, the tokens (gate/up) or act_s (down)
-// in order as B, 256-token chunks.  Needs Fs % 128 == 0.
+// in order as B, token chunks of at most 256 (shared_chunks).  Needs
+// Fs % 128 == 0.
 int launch_shared_dq(const lg_moe_config* c, const lg_moe_weights* w, const uint16_t* x, int M, void* ws,
                      const Layout& L, uint16_t* ys, bool gate_up, bool fill_silu, cudaStream_t s) {
   const int d = c->hidden_size, Fs = c->moe_intermediate_size * c->n_shared_experts;
@@ -513,10 +535,10 @@ int launch_shared_dq(const lg_moe_config* c, const lg_moe_weights* w, const uint
   q.silu = at<uint16_t>(ws, L.silu);
   q.act = at<uint16_t>(ws, L.act_s); q.y = ys;
   q.status = at<int>(ws, L.status);
-  const long long items_chunks = (M + lg::gdq::kNMax - 1) / lg::gdq::kNMax;
   CUtensorMap A0, A1, B;
   if (gate_up) {
-    lg::gdq::shared_table_kernel<<<1, 32, 0, s>>>(M, tab);
+    const int nch = shared_chunks(M, Fs / 128, num_sms());
+    lg::gdq::shared_table_kernel<<<1, 32, 0, s>>>(M, nch, tab);
     if (fill_silu) lg::gdq::silu_table_kernel<<<256, 256, 0, s>>>(at<uint16_t>(ws, L.silu));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_check(e, "shared tables launch");
@@ -525,13 +547,17 @@ int launch_shared_dq(const lg_moe_config* c, const lg_moe_weights* w, const uint
         !map_2d(&A1, w->shared_up, static_cast<uint64_t>(d) * 2, Fs, 128, 128, true) ||
         !map_2d(&B, x, static_cast<uint64_t>(d) * 2, M, 128, lg::gdq::kBoxRows, true))
       return fail(LG_ERR_CUDA, "batched shared gate/up: tensor map encoding failed");
-    return launch_dq<true, true>(q, items_chunks * q.rb_count, A0, A1, B, s);
+    return launch_dq<true, true>(q, static_cast<long long>(nch) * q.rb_count, A0, A1, B, s);
   }
   q.ks_count = Fs / 64; q.rb_count = d / 256; q.rb_rows = 256; q.acc1_rows = 128;
+  const int nch = shared_chunks(M, q.rb_count, num_sms());
+  lg::gdq::shared_table_kernel<<<1, 32, 0, s>>>(M, nch, tab);  // after the gate/up kernel read it
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_check(e, "shared table launch");
   if (!map_2d(&A0, w->shared_down, static_cast<uint64_t>(Fs) * 2, d, 128, 128, true) ||
       !map_2d(&B, q.act, static_cast<uint64_t>(Fs) * 2, M, 128, lg::gdq::kBoxRows, true))
     return fail(LG_ERR_CUDA, "batched shared down: tensor map encoding failed");
-  return launch_dq<false, true>(q, items_chunks * q.rb_count, A0, A0, B, s);
+  return launch_dq<false, true>(q, static_cast<long long>(nch) * q.rb_count, A0, A0, B, s);
 }
 
 // The batched expert passes on the tensor core: token split, route tiles,
