@@ -98,20 +98,34 @@ struct Args {
 };
 
 // ---- operands in dispatch order --------------------------------------------------
-// xp[p] = x[perm[p] / k] for every dispatched position p; d % 8 == 0.
+// xp[p] = x[perm[p] / k] for every dispatched position p; d % 8 == 0.  A warp
+// per row: one perm read, then the row's 16-byte words with eight loads in
+// flight per lane.
 __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __restrict__ x, int d, int k,
                                                           const int* __restrict__ perm,
                                                           const int* __restrict__ offsets, int E,
                                                           uint16_t* __restrict__ xp) {
-  const long long n = offsets[E];
+  const int n = offsets[E];
   const int per_row = d / 8;
-  const long long total = n * per_row;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long p = i / per_row;
-    const int c = static_cast<int>(i - p * per_row);
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < n; p += warps) {
     const int t = __ldg(perm + p) / k;
-    reinterpret_cast<uint4*>(xp + p * d)[c] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * d) + c);
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * d);
+    uint4* dst = reinterpret_cast<uint4*>(xp + static_cast<size_t>(p) * d);
+    for (int c0 = 0; c0 < per_row; c0 += 8 * 32) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < per_row) v[u] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < per_row) dst[c] = v[u];
+      }
+    }
   }
 }
 

@@ -467,8 +467,8 @@ int launch_routed_dq(const lg_moe_config* c, const lg_moe_weights* w, const uint
   if (gate_up) {
     lg::gdq::chunk_table_kernel<<<1, 1024, 0, s>>>(offsets, E, at<int>(ws, L.tiles));
     lg::gdq::silu_table_kernel<<<256, 256, 0, s>>>(at<uint16_t>(ws, L.silu));
-    const long long vec = static_cast<long long>(R) * (d / 8);
-    lg::gdq::gather_rows_kernel<<<static_cast<int>(std::min<long long>((vec + 255) / 256, 8LL * num_sms())), 256, 0,
+    // a warp per dispatched row, eight warps per CTA
+    lg::gdq::gather_rows_kernel<<<static_cast<int>(std::min<long long>((R + 7) / 8, 8LL * num_sms())), 256, 0,
                                   s>>>(x, d, k, perm, offsets, E, xp);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_check(e, "route gather launch");
