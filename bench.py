@@ -58,8 +58,13 @@ CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.a
 # kernel, from an ncu capture of this bench's command (workload -> bytes)
 MEASURED_TRAFFIC = {
     "decode1": 80.53e6,
-    # gate/up stage of one layer: route gather 291 MB + routed gate/up 1,221 MB + shared gate/up 61 MB
-    "cfg3": 1.572e9,
+    "decode2": 119.0e6,  # gate_up_stream_kernel<2>, 16 distinct experts' gate/up + shared
+    # gate/up stage of one layer: route split 2 MB + routed gate/up 891 MB + shared gate/up 27 MB
+    "prefill256": 920.7e6,
+    # gate/up stage of one layer: route gather 298 MB + routed gate/up 1,230 MB + shared gate/up 59 MB
+    "cfg3": 1.587e9,
+    # gate/up stage at M = 16384: gather 1,895 MB + routed gate/up 2,053 MB + shared gate/up 200 MB
+    "cfg4": 4.148e9,
 }
 
 
@@ -589,7 +594,8 @@ def run_ours(args) -> None:
                                    "all-to-all)") if ep else (f"replicas x{world}" if world > 1 else "single GPU")},
         "roofline": {"bound": bound, "kernel": f"{dominant} stage", "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak if peak else None,
-                     "traffic": MEASURED_TRAFFIC.get(args.workload) if dominant == "gate_up" else None,
+                     # captured on one GPU; the expert-parallel ranks run other shapes
+                     "traffic": MEASURED_TRAFFIC.get(args.workload) if dominant == "gate_up" and world == 1 else None,
                      "peak_source": peaks["source"] if unit == "GB/s" else tc_peak["source"],
                      "algorithmic_bytes_per_launch": dom_bytes, "algorithmic_flops_per_launch": dom_flops,
                      "launch_ms": dom_ms},

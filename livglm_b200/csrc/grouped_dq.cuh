@@ -235,10 +235,15 @@ struct Item {
   int nt;  // routes in the chunk (>= 1)
   int n;   // nt rounded up to kBoxRows: MMA N and B rows loaded
 };
-// Item i: expert e owns items [RB * cs[e], RB * cs[e + 1]), ordered (row
-// block, chunk), chunk fastest.  An expert's count c splits into
+constexpr int kChunkMajorMin = 4;  // chunks of an expert from which its items go chunk-major
+
+// Item i: expert e owns items [RB * cs[e], RB * cs[e + 1]), ordered (chunk,
+// row block), row block fastest, when the expert has kChunkMajorMin chunks or
+// more, else (row block, chunk), chunk fastest.  A routed expert's count c splits into
 // nch = ceil(c / 256) chunks of cs = ceil(c / nch) rounded up to 32 routes
-// (cs <= 256, and every chunk is nonempty: (nch - 1) * 256 < c).
+// (cs <= 256, and every chunk is nonempty: (nch - 1) * 256 < c); the shared
+// expert's chunk count comes from the host (shared_chunks), also with no
+// empty chunk.
 __device__ __forceinline__ bool item_of(const Args& a, const int* cs, int i, Item& it) {
   const int RB = a.rb_count;
   if (i >= RB * cs[a.E]) return false;
@@ -250,7 +255,14 @@ __device__ __forceinline__ bool item_of(const Args& a, const int* cs, int i, Ite
   }
   const int nch = cs[lo + 1] - cs[lo];
   const int local = i - RB * cs[lo];
-  const int rb = local / nch, j = local - rb * nch;
+  // An expert of many chunks goes chunk-major: consecutive items (co-scheduled
+  // CTAs) take every row block of one route chunk, so the chunk's B rows are
+  // read from HBM once and then served by L2 however many chunks the expert
+  // has.  With few chunks, row-block-major keeps a weight block's re-reads
+  // adjacent instead.
+  const bool chunk_major = nch >= kChunkMajorMin;
+  const int j = chunk_major ? local / RB : local % nch;
+  const int rb = chunk_major ? local - j * RB : local / nch;
   const int cnt = a.offsets[lo + 1] - a.offsets[lo];
   const int csz = ((cnt + nch - 1) / nch + kBoxRows - 1) / kBoxRows * kBoxRows;
   it.e = lo;
