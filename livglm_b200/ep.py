@@ -241,18 +241,27 @@ class ExpertParallelMoE:
             raise ContractError("communicator and process group differ in size")
         self._ep_ws: torch.Tensor | None = None
         self._native_w: _native.LgWeights | None = None
+        self._native_key: tuple = ()
 
     def _native_weights(self) -> _native.LgWeights:
-        if self._native_w is None:
+        """The C call's weight table, rebuilt whenever a bound tensor changed
+        (the expert banks' own table, the router, the shared expert)."""
+        local = self.experts.native_weights()
+        tensors = [require_weight(self.gate.weight, "router.weight"),
+                   require_weight(self.gate.e_score_correction_bias, "router.e_score_correction_bias")]
+        if self.config.n_shared_experts > 0:
+            tensors += [self.shared_experts.gate_proj.weight, self.shared_experts.up_proj.weight,
+                        self.shared_experts.down_proj.weight]
+        key = (id(local),) + tuple(t.data_ptr() if t is not None else 0 for t in tensors)
+        if self._native_w is None or self._native_key != key:
             w = _native.LgWeights()
-            local = self.experts.native_weights()
             for name, _ in _native.LgWeights._fields_:
                 setattr(w, name, getattr(local, name))
-            w.router_weight = self.gate.weight.data_ptr()
-            w.router_bias = self.gate.e_score_correction_bias.data_ptr()
+            w.router_weight = tensors[0].data_ptr()
+            w.router_bias = tensors[1].data_ptr()
             if self.config.n_shared_experts > 0:
                 self.shared_experts.native_into(w)
-            self._native_w = w
+            self._native_w, self._native_key, self._native_refs = w, key, (local, tensors)
         return self._native_w
 
     def _forward_native(self, rows: torch.Tensor):
