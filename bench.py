@@ -99,10 +99,12 @@ def measured_peaks() -> dict:
     if path.exists():
         try:
             d = json.loads(path.read_text())
-            return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+            sus = d.get("bf16_tflops_sustained")
+            return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                    "bf16_tflops_sustained": float(sus) if sus else None, "source": "measured"}
         except (KeyError, ValueError):
             pass
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 def fp4_peak_tflops() -> dict:
@@ -598,7 +600,14 @@ def run_ours(args) -> None:
                      "traffic": MEASURED_TRAFFIC.get(args.workload) if dominant == "gate_up" and world == 1 else None,
                      "peak_source": peaks["source"] if unit == "GB/s" else tc_peak["source"],
                      "algorithmic_bytes_per_launch": dom_bytes, "algorithmic_flops_per_launch": dom_flops,
-                     "launch_ms": dom_ms},
+                     "launch_ms": dom_ms,
+                     # the bf16 GEMM peak measured over seconds at the power cap, for a
+                     # stage timed right after the long timed region
+                     "peak_sustained": (peaks["bf16_tflops_sustained"]
+                                        if unit == "TFLOP/s" and path == "bf16" else None),
+                     "frac_sustained": (achieved / peaks["bf16_tflops_sustained"]
+                                        if unit == "TFLOP/s" and path == "bf16"
+                                        and peaks.get("bf16_tflops_sustained") else None)},
         "e2e": {"value": world * M * layers_per_step * K_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 4,
                 "steps": K_e2e,
